@@ -1,0 +1,301 @@
+"""Benchmark of the B200 quantized matvec path (one JSON line on rank 0).
+
+Workload: Q4_K weight 11008 x 4096 in GGUF blocks,
+f32 activations x[1, 4096] ~ N(0, 1), batch 1, float path
+(c = x . dequant(W)^T).  Synthetic seeded blocks with the benchmark's value
+distributions (tcb_b200/synth.py); no model files exist on the box.
+
+A step is one pass over a cold ring of R distinct weight copies (together
+well above the 126 MB L2), i.e. R matvecs, so every launch streams its
+weight from HBM.  The ring sweep is captured once in a CUDA graph and
+replayed.  `value` is the algorithmic bytes (weight blocks + x + y) of all
+ranks / the max over ranks of the device time.  `e2e` repeats the metric
+through the public C ABI with host buffers: every step copies x from
+pinned host memory, runs tcb_qgemm and copies y back.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+    torchrun --nproc-per-node N bench.py --gpus N   (one process per GPU)
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Q4_K matvec HBM GB/s (% of peak); 8B-shape Q4_K_M decode tokens/sec @ batch 1"
+WORKLOAD = {"workload": "q4_k_matvec", "wtype": "q4_k", "N": 11008, "K": 4096, "batch": 1,
+            "x_dtype": "f32", "path": "float"}
+Q4_K = 12
+
+
+def algorithmic_bytes(N: int, K: int, M: int = 1) -> int:
+    """weight blocks + x (f32) + y (f32), SURVEY/BASELINE accounting."""
+    return N * K // 256 * 144 + M * K * 4 + M * N * 4
+
+
+def load_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def load_traffic(name: str):
+    """dram bytes per launch from the committed ncu summary, if present."""
+    p = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(p):
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", open(p).read())
+    return int(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    def __init__(self, device: int):
+        self.device = device
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+
+    def __enter__(self):
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.device)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            names = {
+                "hw_slowdown": getattr(pynvml, "nvmlClocksEventReasonHwSlowdown", 0x8),
+                "hw_thermal_slowdown": getattr(pynvml, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+                "sw_thermal_slowdown": getattr(pynvml, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+                "sw_power_cap": getattr(pynvml, "nvmlClocksEventReasonSwPowerCap", 0x4),
+            }
+
+            def run():
+                while not self._stop.is_set():
+                    try:
+                        self.samples.append(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                        r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        for k, bit in names.items():
+                            if r & bit:
+                                self.reasons.add(k)
+                    except Exception:
+                        pass
+                    time.sleep(0.01)
+
+            self._t = threading.Thread(target=run, daemon=True)
+            self._t.start()
+        except Exception:
+            self._t = None
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def cpu_baseline(seconds: float = 12.0) -> dict:
+    """TR's AVX2 float path restated (oracle, all host threads) on a bounded
+    sample of the same workload: repeated 11008 x 4096 Q4_K matvecs."""
+    from oracle import oracle as O
+    from tcb_b200 import synth
+
+    N, K = WORKLOAD["N"], WORKLOAD["K"]
+    w = synth.weight(Q4_K, N, K, seed=7)
+    x = synth.activations(1, K, seed=8)
+    threads = os.cpu_count() or 1
+    O.qgemm_float(Q4_K, x, w, N, nthreads=threads)  # warm
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        O.qgemm_float(Q4_K, x, w, N, nthreads=threads)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(algorithmic_bytes(N, K) * n / dt / 1e9, 3), "unit": "GB/s", "cores": threads,
+            "kind": "port", "sample": f"{n} matvecs of Q4_K 11008x4096 (float path, oracle AVX2 restatement) "
+                                      f"in {dt:.1f} s"}
+
+
+def dist_init():
+    if "RANK" not in os.environ:
+        return 0, 1, 0
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def run_reference(args, rank: int):
+    if rank != 0:
+        return
+    cb = cpu_baseline()
+    line = {"metric": METRIC, "value": cb["value"], "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "impl": "reference", "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": WORKLOAD, "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank, world, local = dist_init()
+    if args.impl == "reference":
+        run_reference(args, rank)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
+
+    import torch
+
+    import tcb_b200 as T
+    from tcb_b200 import synth
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    N, K = WORKLOAD["N"], WORKLOAD["K"]
+    wbytes = N * K // 256 * 144
+    ring = max(4, -(-512 * 2 ** 20 // wbytes))  # >= 512 MiB of distinct weights
+    ctx = T.Context(local)
+    base = torch.from_numpy(synth.weight(Q4_K, N, K, seed=1 + rank)).to(dev)
+    weights = [base]
+    for i in range(1, ring):
+        # distinct copies: flip the nibbles of one byte per block row so no two are equal
+        w = base.clone()
+        w[16 + (i % 128)::144] ^= 0x11
+        weights.append(w)
+    x = torch.from_numpy(synth.activations(1, K, seed=2 + rank)).to(dev)
+    ys = [torch.empty((1, N), dtype=torch.float32, device=dev) for _ in range(ring)]
+    stream = torch.cuda.Stream(dev)
+
+    def sweep():
+        for i in range(ring):
+            ctx.qgemm(Q4_K, weights[i], x, ys[i], accumulate=False, stream=stream)
+
+    with torch.cuda.stream(stream):
+        sweep()  # first call outside capture (lazy attributes)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            sweep()
+    for _ in range(args.warmup):
+        g.replay()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with ClockSampler(local) as clk:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(args.steps):
+                g.replay()
+            stop.record(stream)
+        stop.synchronize()
+    barrier()
+    ms = start.elapsed_time(stop)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    launches = args.steps * ring
+    per_launch_bytes = algorithmic_bytes(N, K)
+    value = per_launch_bytes * launches * world / (ms_max / 1e3) / 1e9
+    kernel_s = ms / 1e3 / launches  # this rank's average duration per launch
+    peaks = load_peaks()
+    achieved = per_launch_bytes / kernel_s / 1e9
+
+    # e2e through the public API with host buffers (eager calls)
+    xh = torch.from_numpy(synth.activations(1, K, seed=2 + rank)).pin_memory()
+    yh = torch.empty((1, N), dtype=torch.float32).pin_memory()
+    e2e_steps = max(200, args.steps // 4)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        for i in range(20):
+            x.copy_(xh, non_blocking=True)
+            ctx.qgemm(Q4_K, weights[i % ring], x, ys[0], accumulate=False, stream=stream)
+            yh.copy_(ys[0], non_blocking=True)
+        barrier()
+        e0.record(stream)
+        for i in range(e2e_steps):
+            x.copy_(xh, non_blocking=True)
+            ctx.qgemm(Q4_K, weights[i % ring], x, ys[0], accumulate=False, stream=stream)
+            yh.copy_(ys[0], non_blocking=True)
+        e1.record(stream)
+        e1.synchronize()
+    et = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(et, op=dist.ReduceOp.MAX)
+    e2e_value = per_launch_bytes * e2e_steps * world / (float(et.item()) / 1e3) / 1e9
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 6), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "pct_of_peak": round(100 * value / world / peaks["hbm_gbs"], 2),
+            "config": dict(WORKLOAD, ring=ring, ring_bytes=ring * wbytes, l2="inputs larger than L2 (cold ring)",
+                           parallelism=f"replicas{world}"),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
+                         "traffic": load_traffic("q4k_matvec_11008x4096.md"),
+                         "algorithmic_bytes_per_launch": per_launch_bytes},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": K * 4,
+                    "d2h_bytes_per_step": N * 4, "steps": e2e_steps},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline()
+        print(json.dumps(line), flush=True)
+    del g
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

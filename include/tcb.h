@@ -1,0 +1,131 @@
+/*
+ * tcb.h - C ABI of the B200 (sm_100a) quantized-tensor path of TR
+ * (sekerahmet/TCB): GGUF block-quantized matvec/matmul, dequantisation,
+ * embedding rows and verbatim block upload.
+ *
+ * Every entry point here replaces one call of TR's tensor.Backend quant
+ * branch (internal/compute/gpu/...) and is what a cgo/purego binding in
+ * TR's gpu package binds.  Conventions:
+ *  - device pointers are plain addresses; a stream is a cudaStream_t passed
+ *    as void* (NULL = the legacy default stream);
+ *  - w is the [N, K] block store of a quantized tensor, rows of K/blk
+ *    blocks laid out exactly as in the GGUF file (tensor/quant.go:14-29);
+ *  - dtypes use GGUF type ids (internal/compute/gguf/types.go:12-16);
+ *  - every call returns a tcb_status; nothing panics, nothing is freed that
+ *    the caller owns.  Scratch memory is owned by the context.
+ *  - results do not depend on the GPU's SM count or on launch timing: no
+ *    float atomics, fixed reduction order (TR spec 15.22a).
+ */
+#ifndef TCB_H
+#define TCB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum tcb_status {
+  TCB_OK = 0,
+  TCB_ERR_NULL = 1,        /* a required pointer is NULL */
+  TCB_ERR_DTYPE = 2,       /* weight or activation/output type not supported */
+  TCB_ERR_SHAPE = 3,       /* K not a multiple of the block, negative size, ... */
+  TCB_ERR_ALIGN = 4,       /* offset not on a block boundary */
+  TCB_ERR_CUDA = 5,        /* a CUDA runtime call failed (see tcb_last_cuda_error) */
+  TCB_ERR_NOMEM = 6,       /* scratch allocation failed */
+  TCB_ERR_TIMEOUT = 7,     /* a bounded device-side wait gave up */
+  TCB_ERR_UNSUPPORTED = 8, /* combination not provided (e.g. Q8_0 act8 off) */
+  TCB_ERR_BOUNDS = 9,      /* an index outside the table */
+  TCB_ERR_SCALE = 10       /* a NaN/Inf block scale (tensor/quant.go:108-128) */
+} tcb_status;
+
+/* weight block types (GGUF ids) */
+enum { TCB_Q4_0 = 2, TCB_Q8_0 = 8, TCB_Q4_K = 12, TCB_Q6_K = 14 };
+/* activation / output element types (GGUF ids) */
+enum { TCB_F32 = 0, TCB_F16 = 1, TCB_BF16 = 30 };
+
+typedef struct tcb_ctx tcb_ctx;
+
+/* Bind to a CUDA device (the primary context, shared with TR's purego
+ * driver).  Replaces the lazy backend init of gpu/cuda.go:134-166,241-290. */
+int tcb_ctx_create(int device, tcb_ctx **out);
+int tcb_ctx_destroy(tcb_ctx *ctx);
+
+/* Message for a status code; never NULL. */
+const char *tcb_strerror(int status);
+/* The last CUDA error string seen by this context (for TCB_ERR_CUDA). */
+const char *tcb_last_cuda_error(tcb_ctx *ctx);
+
+/* elements and bytes of one block; 0,0 for an unknown type
+ * (tensor.DType.QuantBlock, tensor/quant.go:35-47) */
+int tcb_block_shape(int wtype, int *elems, int *bytes);
+
+/* c[m, n] (+)= sum_k x[m, k] * dequant(w)[n, k]  for m < M, n < N.
+ * Replaces gpu/backend_quant.go:43-65 (quantGemm, reached from
+ * Backend.Gemm / GemmSet through gemmOuter, backend_gemm.go:132-158).
+ *   w       device, [N, K] blocks, K a multiple of the block
+ *   x       device, M rows of K elements, row stride ldx elements, xdtype
+ *           F32, BF16 or F16 (converted to f32 inside the kernel)
+ *   c       device, M rows of N elements, row stride ldc, cdtype F32, BF16
+ *           or F16: computed in f32, rounded once
+ *   accumulate  1 = Backend.Gemm (C +=), 0 = GemmSet (C =; old C unread)
+ * K == 0 is the empty sum (C unchanged, or zeroed when accumulate == 0). */
+int tcb_qgemm(tcb_ctx *ctx, int wtype, int M, int N, int K, const void *w,
+              const void *x, int xdtype, long ldx, void *c, int cdtype,
+              long ldc, int accumulate, void *stream);
+
+/* The int8-activation product of TR's TR_quantized_activations block:
+ * every finite row of x is quantised per weight block (quantizeQ8,
+ * tensor/cpu_quant_q8.go:39-68), dotted in integers per block and folded
+ * in block order bit-exactly as TR's CPU kernels do
+ * (cpu_quant_q8.go:74-116,378-407); a row holding NaN/Inf takes the float
+ * path (cpu_quant_q8.go:157-174).  Replaces ActQuantGemmer.GemmActQuant
+ * (tensor/matmul.go:59-61, CPU-only in TR).  Q8_0 weights are an extension
+ * (TR refuses them, H6723) with dotQ4Q8Go's fold.  Same arguments as
+ * tcb_qgemm; TR's method accumulates, pass accumulate = 1 for it. */
+int tcb_qgemm_act8(tcb_ctx *ctx, int wtype, int M, int N, int K,
+                   const void *w, const void *x, int xdtype, long ldx,
+                   void *c, int cdtype, long ldc, int accumulate,
+                   void *stream);
+
+/* out[i] = dequant(w)[i] for i < n: the first n elements of the block
+ * store at w (n a multiple of the block), bit-identical to TR's CPU dequant
+ * for every fp16 scale pattern including NaN and Inf (x86 NaN rule).
+ * odtype F32, BF16 or F16 (rounded from f32 as TR's Cast does).
+ * Replaces QuantOpener.OpenQuant (tensor/quant.go:103-105,
+ * gpu/backend_quant.go:117-134). */
+int tcb_qdequant(tcb_ctx *ctx, int wtype, const void *w, long n, void *out,
+                 int odtype, void *stream);
+
+/* out[i, :] = dequant(w)[idx[i], :]  for a [V, D] table on the device;
+ * idx is a HOST array of nidx row numbers (TR passes a Go []int) and out a
+ * device [nidx, D] f32 array.  An index outside [0, V) is refused
+ * (TCB_ERR_BOUNDS) before anything is launched.  Replaces
+ * Backend.Embedding with quantized w (tensor/limits.go:15-45,
+ * gpu/backend_row.go:186). */
+int tcb_qembed(tcb_ctx *ctx, int wtype, const void *w, long V, int D,
+               const int64_t *idx, int nidx, float *out, void *stream);
+
+/* Verbatim block upload/download (FromRaw / ToRaw, gpu/typed.go:24-55):
+ * the bytes cross unchanged.  tcb_quant_upload refuses a block whose
+ * fp16 scale is NaN/Inf (CheckQuantScales, tensor/quant.go:108-128) and
+ * reports its index in *bad_block (-1 when all are finite). */
+int tcb_quant_upload(tcb_ctx *ctx, int wtype, const void *host, size_t nbytes,
+                     void *dev, long *bad_block, void *stream);
+int tcb_quant_download(tcb_ctx *ctx, const void *dev, size_t nbytes,
+                       void *host, void *stream);
+
+/* Zero blocks on the device: Q4_0 codes 0x88, every other byte 0
+ * (QuantZeroRaw, tensor/quant.go:416-427; gpu/backend_memory.go:131-152). */
+int tcb_quant_zero(tcb_ctx *ctx, int wtype, void *dev, long nblocks,
+                   void *stream);
+
+/* host-side scale check (CheckQuantScales); *bad_block = -1 if clean */
+int tcb_check_scales(int wtype, const void *host, size_t nbytes,
+                     long *bad_block);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

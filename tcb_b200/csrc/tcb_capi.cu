@@ -1,0 +1,297 @@
+// tcb_capi.cu - the C ABI of include/tcb.h: argument checks that TR's
+// backend performs before a launch (shapes, dtypes, block alignment), the
+// per-context scratch, and dispatch to the kernels.
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "../../include/tcb.h"
+#include "tcb_common.cuh"
+#include "tcb_launch.h"
+#include "tcb_matvec.h"
+
+struct tcb_ctx {
+  int dev = 0;
+  int sms = 148;
+  void *ws = nullptr;  // scratch owned by the context, grown on demand
+  size_t ws_cap = 0;
+  int *derr = nullptr;  // device error word (bounded waits that gave up)
+  std::mutex mu;
+  char err[256] = {0};
+};
+
+namespace {
+
+int cuda_fail(tcb_ctx *ctx, cudaError_t e) {
+  if (ctx) snprintf(ctx->err, sizeof ctx->err, "%s: %s", cudaGetErrorName(e), cudaGetErrorString(e));
+  return TCB_ERR_CUDA;
+}
+
+#define TCB_CU(ctx, call)                          \
+  do {                                             \
+    cudaError_t e_ = (call);                       \
+    if (e_ != cudaSuccess) return cuda_fail(ctx, e_); \
+  } while (0)
+
+bool act_type_ok(int dt) { return dt == TCB_F32 || dt == TCB_BF16 || dt == TCB_F16; }
+size_t elem_size(int dt) { return dt == TCB_F32 ? 4 : 2; }
+
+int bind(tcb_ctx *ctx) {
+  int cur = -1;
+  TCB_CU(ctx, cudaGetDevice(&cur));
+  if (cur != ctx->dev) TCB_CU(ctx, cudaSetDevice(ctx->dev));
+  return TCB_OK;
+}
+
+// grow the context's scratch; freeing the old buffer waits for the device
+int ensure_ws(tcb_ctx *ctx, size_t bytes) {
+  if (bytes <= ctx->ws_cap) return TCB_OK;
+  if (ctx->ws) {
+    cudaError_t e = cudaFree(ctx->ws);
+    ctx->ws = nullptr;
+    ctx->ws_cap = 0;
+    if (e != cudaSuccess) return cuda_fail(ctx, e);
+  }
+  size_t cap = bytes < (1u << 20) ? (1u << 20) : bytes;
+  cudaError_t e = cudaMalloc(&ctx->ws, cap);
+  if (e != cudaSuccess) {
+    cuda_fail(ctx, e);
+    (void)cudaGetLastError();
+    return TCB_ERR_NOMEM;
+  }
+  ctx->ws_cap = cap;
+  return TCB_OK;
+}
+
+// the batch-1 tensor-core path: plan, scratch, launch.  *taken = false when
+// the shape goes to the portable kernel instead.
+int run_matvec(tcb_ctx *ctx, int wtype, int act8, int M, int N, int K, const void *w, const void *x, int xdt,
+               void *c, int cdt, int accumulate, cudaStream_t s, bool *taken) {
+  *taken = false;
+  tcb::MvPlan pl = tcb::matvec_plan(wtype, act8, M, N, K, w, ctx->sms);
+  if (!pl.ok) return TCB_OK;
+  *taken = true;
+  cudaError_t e = tcb::matvec_launch(pl, wtype, act8, N, K, w, x, xdt, c, cdt, accumulate, ctx->derr, s);
+  return e == cudaSuccess ? TCB_OK : cuda_fail(ctx, e);
+}
+
+// the checks TR makes before the quant product (gpu/backend_quant.go:43-65,
+// tensor/quant.go:240-247, spec 15.51-15.53)
+int check_gemm_args(int wtype, int M, int N, int K, const void *w, const void *x, int xdt, long ldx, void *c,
+                    int cdt, long ldc) {
+  int E = tcb::block_elems(wtype);
+  if (!E) return TCB_ERR_DTYPE;
+  if (!act_type_ok(xdt) || !act_type_ok(cdt)) return TCB_ERR_DTYPE;
+  if (M < 0 || N < 0 || K < 0 || K % E) return TCB_ERR_SHAPE;
+  if (M == 0 || N == 0) return TCB_OK;
+  if (ldc < N || (K > 0 && ldx < K)) return TCB_ERR_SHAPE;
+  if (!c || (K > 0 && (!w || !x))) return TCB_ERR_NULL;
+  uintptr_t wa = reinterpret_cast<uintptr_t>(w);
+  if (wa % (wtype == TCB_Q4_K ? 4 : 2)) return TCB_ERR_ALIGN;
+  if (reinterpret_cast<uintptr_t>(x) % elem_size(xdt) || reinterpret_cast<uintptr_t>(c) % elem_size(cdt))
+    return TCB_ERR_ALIGN;
+  return TCB_OK;
+}
+
+// K == 0: the empty sum; GemmSet zeroes C, Gemm leaves it
+int empty_sum(tcb_ctx *ctx, int M, int N, void *c, int cdt, long ldc, int accumulate, cudaStream_t s) {
+  if (accumulate || M == 0 || N == 0) return TCB_OK;
+  size_t es = elem_size(cdt);
+  TCB_CU(ctx, cudaMemset2DAsync(c, (size_t)ldc * es, 0, (size_t)N * es, (size_t)M, s));
+  return TCB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *tcb_strerror(int status) {
+  switch (status) {
+  case TCB_OK: return "ok";
+  case TCB_ERR_NULL: return "a required pointer is NULL";
+  case TCB_ERR_DTYPE: return "unsupported weight, activation or output type";
+  case TCB_ERR_SHAPE: return "invalid shape (negative size, K not a multiple of the block, or stride too small)";
+  case TCB_ERR_ALIGN: return "pointer or offset not aligned to its element or block";
+  case TCB_ERR_CUDA: return "CUDA runtime error";
+  case TCB_ERR_NOMEM: return "device scratch allocation failed";
+  case TCB_ERR_TIMEOUT: return "a bounded device-side wait gave up";
+  case TCB_ERR_UNSUPPORTED: return "unsupported combination";
+  case TCB_ERR_BOUNDS: return "index outside the table";
+  case TCB_ERR_SCALE: return "NaN or Inf block scale";
+  }
+  return "unknown status";
+}
+
+const char *tcb_last_cuda_error(tcb_ctx *ctx) { return ctx ? ctx->err : ""; }
+
+int tcb_block_shape(int wtype, int *elems, int *bytes) {
+  if (elems) *elems = tcb::block_elems(wtype);
+  if (bytes) *bytes = tcb::block_bytes(wtype);
+  return tcb::block_elems(wtype) ? TCB_OK : TCB_ERR_DTYPE;
+}
+
+int tcb_ctx_create(int device, tcb_ctx **out) {
+  if (!out) return TCB_ERR_NULL;
+  *out = nullptr;
+  tcb_ctx *ctx = new (std::nothrow) tcb_ctx;
+  if (!ctx) return TCB_ERR_NOMEM;
+  ctx->dev = device;
+  cudaError_t e = cudaSetDevice(device);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&ctx->sms, cudaDevAttrMultiProcessorCount, device);
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->derr, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(ctx->derr, 0, sizeof(int));
+  if (e != cudaSuccess) {
+    if (ctx->derr) cudaFree(ctx->derr);
+    delete ctx;
+    (void)cudaGetLastError();
+    return TCB_ERR_CUDA;
+  }
+  *out = ctx;
+  return TCB_OK;
+}
+
+int tcb_ctx_destroy(tcb_ctx *ctx) {
+  if (!ctx) return TCB_OK;
+  int rc = TCB_OK;
+  if (cudaSetDevice(ctx->dev) != cudaSuccess) rc = TCB_ERR_CUDA;
+  for (void *p : {ctx->ws, (void *)ctx->derr})
+    if (p && cudaFree(p) != cudaSuccess) rc = TCB_ERR_CUDA;
+  delete ctx;
+  return rc;
+}
+
+int tcb_qgemm(tcb_ctx *ctx, int wtype, int M, int N, int K, const void *w, const void *x, int xdtype, long ldx,
+              void *c, int cdtype, long ldc, int accumulate, void *stream) {
+  if (!ctx) return TCB_ERR_NULL;
+  int rc = check_gemm_args(wtype, M, N, K, w, x, xdtype, ldx, c, cdtype, ldc);
+  if (rc != TCB_OK || M == 0 || N == 0) return rc;
+  if ((rc = bind(ctx)) != TCB_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (K == 0) return empty_sum(ctx, M, N, c, cdtype, ldc, accumulate, s);
+  bool taken = false;
+  rc = run_matvec(ctx, wtype, 0, M, N, K, w, x, xdtype, c, cdtype, accumulate, s, &taken);
+  if (taken || rc != TCB_OK) return rc;
+  cudaError_t e = tcb::launch_qgemm_simt(wtype, w, M, N, K, x, xdtype, ldx, c, cdtype, ldc, accumulate, ctx->sms, s);
+  if (e != cudaSuccess) return cuda_fail(ctx, e);
+  return TCB_OK;
+}
+
+int tcb_qgemm_act8(tcb_ctx *ctx, int wtype, int M, int N, int K, const void *w, const void *x, int xdtype, long ldx,
+                   void *c, int cdtype, long ldc, int accumulate, void *stream) {
+  if (!ctx) return TCB_ERR_NULL;
+  int rc = check_gemm_args(wtype, M, N, K, w, x, xdtype, ldx, c, cdtype, ldc);
+  if (rc != TCB_OK || M == 0 || N == 0) return rc;
+  if ((rc = bind(ctx)) != TCB_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (K == 0) return empty_sum(ctx, M, N, c, cdtype, ldc, accumulate, s);
+  bool taken = false;
+  rc = run_matvec(ctx, wtype, 1, M, N, K, w, x, xdtype, c, cdtype, accumulate, s, &taken);
+  if (taken || rc != TCB_OK) return rc;
+  const int blk = tcb::block_elems(wtype);
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  if ((rc = ensure_ws(ctx, tcb::act8_scratch_bytes(M, K, blk))) != TCB_OK) return rc;
+  tcb::Act8Scratch sc = tcb::act8_scratch_carve(ctx->ws, M, K, blk);
+  cudaError_t e = tcb::launch_act8_quantize(blk, M, K, x, xdtype, ldx, sc, ctx->sms, s);
+  if (e == cudaSuccess)
+    e = tcb::launch_act8_dot(wtype, w, M, N, K, sc, x, xdtype, ldx, c, cdtype, ldc, accumulate, ctx->sms, s);
+  if (e != cudaSuccess) return cuda_fail(ctx, e);
+  return TCB_OK;
+}
+
+int tcb_qdequant(tcb_ctx *ctx, int wtype, const void *w, long n, void *out, int odtype, void *stream) {
+  if (!ctx) return TCB_ERR_NULL;
+  int E = tcb::block_elems(wtype);
+  if (!E || !act_type_ok(odtype)) return TCB_ERR_DTYPE;
+  if (n < 0 || n % E) return TCB_ERR_SHAPE;
+  if (n == 0) return TCB_OK;
+  if (!w || !out) return TCB_ERR_NULL;
+  if (reinterpret_cast<uintptr_t>(w) % 2 || reinterpret_cast<uintptr_t>(out) % elem_size(odtype)) return TCB_ERR_ALIGN;
+  int rc = bind(ctx);
+  if (rc != TCB_OK) return rc;
+  cudaError_t e = tcb::launch_dequant_rows(wtype, w, n / E, E, nullptr, out, odtype, ctx->sms,
+                                           static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TCB_OK : cuda_fail(ctx, e);
+}
+
+int tcb_qembed(tcb_ctx *ctx, int wtype, const void *w, long V, int D, const int64_t *idx, int nidx, float *out,
+               void *stream) {
+  if (!ctx) return TCB_ERR_NULL;
+  int E = tcb::block_elems(wtype);
+  if (!E) return TCB_ERR_DTYPE;
+  if (V < 0 || D < 0 || nidx < 0 || D % E) return TCB_ERR_SHAPE;
+  if (nidx == 0 || D == 0) return TCB_OK;
+  if (!w || !idx || !out) return TCB_ERR_NULL;
+  for (int i = 0; i < nidx; i++)
+    if (idx[i] < 0 || idx[i] >= V) return TCB_ERR_BOUNDS;  // tensor/limits.go:30-34 (H3043)
+  if (reinterpret_cast<uintptr_t>(w) % 2 || reinterpret_cast<uintptr_t>(out) % 4) return TCB_ERR_ALIGN;
+  int rc = bind(ctx);
+  if (rc != TCB_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  if ((rc = ensure_ws(ctx, (size_t)nidx * sizeof(int64_t))) != TCB_OK) return rc;
+  int64_t *didx = static_cast<int64_t *>(ctx->ws);
+  TCB_CU(ctx, cudaMemcpyAsync(didx, idx, (size_t)nidx * sizeof(int64_t), cudaMemcpyHostToDevice, s));
+  cudaError_t e = tcb::launch_dequant_rows(wtype, w, nidx, D, didx, out, TCB_F32, ctx->sms, s);
+  return e == cudaSuccess ? TCB_OK : cuda_fail(ctx, e);
+}
+
+int tcb_check_scales(int wtype, const void *host, size_t nbytes, long *bad_block) {
+  if (bad_block) *bad_block = -1;
+  int B = tcb::block_bytes(wtype);
+  if (!B) return TCB_ERR_DTYPE;
+  if (nbytes % B) return TCB_ERR_SHAPE;
+  if (nbytes && !host) return TCB_ERR_NULL;
+  const uint8_t *p = static_cast<const uint8_t *>(host);
+  int at0 = wtype == TCB_Q6_K ? 208 : 0, at1 = wtype == TCB_Q4_K ? 2 : -1;
+  for (size_t b = 0; b < nbytes / B; b++) {
+    const uint8_t *blk = p + b * B;
+    uint32_t s0 = blk[at0] | (blk[at0 + 1] << 8);
+    bool bad = (s0 & 0x7C00u) == 0x7C00u;
+    if (at1 >= 0) bad = bad || ((blk[at1] | (blk[at1 + 1] << 8)) & 0x7C00u) == 0x7C00u;
+    if (bad) {
+      if (bad_block) *bad_block = (long)b;
+      return TCB_ERR_SCALE;
+    }
+  }
+  return TCB_OK;
+}
+
+int tcb_quant_upload(tcb_ctx *ctx, int wtype, const void *host, size_t nbytes, void *dev, long *bad_block,
+                     void *stream) {
+  if (!ctx) return TCB_ERR_NULL;
+  int rc = tcb_check_scales(wtype, host, nbytes, bad_block);
+  if (rc != TCB_OK || nbytes == 0) return rc;
+  if (!dev) return TCB_ERR_NULL;
+  if ((rc = bind(ctx)) != TCB_OK) return rc;
+  TCB_CU(ctx, cudaMemcpyAsync(dev, host, nbytes, cudaMemcpyHostToDevice, static_cast<cudaStream_t>(stream)));
+  return TCB_OK;
+}
+
+int tcb_quant_download(tcb_ctx *ctx, const void *dev, size_t nbytes, void *host, void *stream) {
+  if (!ctx) return TCB_ERR_NULL;
+  if (nbytes == 0) return TCB_OK;
+  if (!dev || !host) return TCB_ERR_NULL;
+  int rc = bind(ctx);
+  if (rc != TCB_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  TCB_CU(ctx, cudaMemcpyAsync(host, dev, nbytes, cudaMemcpyDeviceToHost, s));
+  TCB_CU(ctx, cudaStreamSynchronize(s));
+  return TCB_OK;
+}
+
+int tcb_quant_zero(tcb_ctx *ctx, int wtype, void *dev, long nblocks, void *stream) {
+  if (!ctx) return TCB_ERR_NULL;
+  if (!tcb::block_bytes(wtype)) return TCB_ERR_DTYPE;
+  if (nblocks < 0) return TCB_ERR_SHAPE;
+  if (nblocks == 0) return TCB_OK;
+  if (!dev) return TCB_ERR_NULL;
+  int rc = bind(ctx);
+  if (rc != TCB_OK) return rc;
+  cudaError_t e = tcb::launch_quant_zero(wtype, dev, nblocks, ctx->sms, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TCB_OK : cuda_fail(ctx, e);
+}
+
+}  // extern "C"

@@ -1,0 +1,854 @@
+// tcb_matvec.cu - batch-1 quantized matvec on sm_100a tensor cores.
+//
+//   y[n] (+)= sum_k x[k] * dequant(W)[n, k]     W: [N, K] GGUF blocks
+//
+// Design (memory-bound at batch 1: every weight byte is read once):
+//  * Weights stream from HBM into shared memory through 2-D TMA tensor
+//    copies (cp.async.bulk.tensor, 8-byte elements, no multicast) issued by
+//    a producer warp: a stage is 16 rows x 2 boxes of ~1.1-1.7 KB per row,
+//    two TMA instructions per ~40 KB, so DRAM sees long runs and the copy
+//    engine few requests; the box width is padded so the staged rows fall on
+//    different shared-memory banks; rows past N and bytes past the row end
+//    arrive as zeros.  Eight consumer warps split each stage's blocks.
+//  * Launched with programmatic stream serialization: the producer starts
+//    streaming weights while the previous kernel of the stream drains; the
+//    consumers wait for it (griddepcontrol.wait) before reading x or
+//    writing c.  Weights are only read, never written, by these kernels.
+//  * The dot products run on the int8 tensor-core path (mma.sync
+//    m16n8k32 / m16n8k16, u8/s8 -> s32): the weight codes are exact small
+//    integers, so the A fragment is the raw code bytes after one LOP3 per
+//    four codes (no per-element dequantisation).  The 8 columns of the MMA
+//    are not batch rows: column j carries scale group j (a Q4_K sub-block,
+//    a Q6_K 16-element group, a whole Q8_0/Q4_0 block), so one MMA chain
+//    leaves every (row, group) integer dot in its own accumulator and each
+//    lane applies the scales of exactly four (row, group) pairs.
+//  * Float path: x is split per 32-element group into int8 digits,
+//    x ~= sigma * (h + l1/254 + l2/254^2), |digits| <= 127, sigma =
+//    amax/127; the digit products are exact int32 and are recombined in
+//    fp32 (relative error of the x representation ~1e-7).  A row of x with
+//    NaN/Inf takes an fp32 SIMT path instead (NaN/Inf propagate as in TR).
+//  * Int8-activation path (TR_quantized_activations): x is quantised with
+//    TR's quantizeQ8 and each block term is formed exactly as TR's CPU
+//    kernels do, then folded in block order: bit-exact.
+//  * Work split: a CTA owns whole 16-row tiles; warp w takes the blocks (or
+//    8-block rounds) w, w+8, ... of every chunk, and the eight warp
+//    partials of a row are added in warp order (float path) or every block
+//    term is folded in block order (int8 path) in shared memory.  Results
+//    do not depend on the SM count or on timing.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <string.h>
+
+#include "tcb_common.cuh"
+#include "tcb_matvec.h"
+#include "tcb_simt.cuh"
+
+namespace tcb {
+namespace mv {
+
+// ----------------------------------------------------------------- PTX
+
+__device__ __forceinline__ uint32_t sa(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(sa(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sa(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(sa(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   sa(dst)),
+               "l"(src), "r"(bytes), "r"(sa(bar))
+               : "memory");
+}
+
+// 2-D tensor copy of one box into shared memory (no multicast)
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, int x, int y, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(sa(dst)),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(sa(bar))
+      : "memory");
+}
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// D += A(16x32 u8) * B(32x8 s8)
+__device__ __forceinline__ void imma_u8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+  asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+               : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+               : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// D += A(16x32 s8) * B(32x8 s8)
+__device__ __forceinline__ void imma_s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+  asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+               : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+               : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// D += A(16x16 u8) * B(16x8 s8)
+__device__ __forceinline__ void imma_u8_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+               : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+               : "r"(a0), "r"(a1), "r"(b0));
+}
+
+__device__ __forceinline__ uint32_t lds32(const uint8_t *p) { return *reinterpret_cast<const uint32_t *>(p); }
+__device__ __forceinline__ uint32_t lds16(const uint8_t *p) { return *reinterpret_cast<const uint16_t *>(p); }
+// 4 bytes at a 2-byte aligned shared address
+__device__ __forceinline__ uint32_t lds32_a2(const uint8_t *p) {
+  uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  if ((a & 2) == 0) return lds32(p);
+  const uint8_t *q = p - 2;
+  return __byte_perm(lds32(q), lds32(q + 4), 0x5432);
+}
+
+constexpr uint32_t M4 = 0x0F0F0F0Fu;
+
+// ----------------------------------------------------------------- formats
+// GRP: elements per scale group (one MMA k); GPB: groups per block; RB:
+// blocks per warp work item (a Q8_0/Q4_0 round fills the 8 MMA columns
+// with 8 blocks); BPB: blocks per TMA box (box starts 16-byte aligned, 8
+// work items per box); BOX8: box width in 8-byte elements, the BPB blocks
+// plus padding that makes the staged row pitch 32 or 96 mod 128 bytes;
+// NDIG: digits of x on the float path (2 for Q6_K, whose k16 groups take
+// twice the MMAs).  A stage is NBOX boxes.
+template <int W> struct Pol;
+template <> struct Pol<TCB_Q4_K> { static constexpr int E = 256, B = 144, GRP = 32, GPB = 8, RB = 1, BPB = 8, BOX8 = 148, NDIG = 3; };
+template <> struct Pol<TCB_Q6_K> { static constexpr int E = 256, B = 210, GRP = 16, GPB = 16, RB = 1, BPB = 8, BOX8 = 212, NDIG = 2; };
+template <> struct Pol<TCB_Q8_0> { static constexpr int E = 32, B = 34, GRP = 32, GPB = 1, RB = 8, BPB = 32, BOX8 = 140, NDIG = 3; };
+template <> struct Pol<TCB_Q4_0> { static constexpr int E = 32, B = 18, GRP = 32, GPB = 1, RB = 8, BPB = 64, BOX8 = 148, NDIG = 3; };
+constexpr int NBOX = 2;
+
+constexpr int kConsumers = 8;          // consumer warps; warp 8 produces
+constexpr int kThreads = 32 * (kConsumers + 1);
+
+struct Params {
+  const uint8_t *w;
+  long rowBytes;
+  int N, K, nb;
+  const void *x;
+  int xdt;
+  void *c;
+  int cdt;
+  int accumulate;
+  int tiles, cbc, nch;    // 16-row tiles; blocks per chunk (NBOX boxes); chunks per row
+  int *err;               // sticky error word (timeouts)
+  int S;                  // stages
+  int xoff, toff, soff;   // shared-memory offsets: x region, int8 terms, stages
+};
+
+// x region layout (float path): NDIG digit planes of K int8, then per group
+// sg (sigma / 254^(NDIG-1)), S (sum of x), Sd (digit sum in recombined units).
+// int8 path: q8 codes K int8, d8 per block, bs (int16 sums of 16 codes).
+struct XF {
+  const int8_t *dig;  // plane p at dig + p*K
+  const float *sg, *sx, *sd;
+};
+struct XQ {
+  const int8_t *q;
+  const float *d8;
+  const int16_t *bs;
+};
+
+template <int W, bool ACT8>
+__host__ __device__ inline int x_region_bytes(int K) {
+  using P = Pol<W>;
+  auto up = [](int v) { return (v + 15) & ~15; };
+  if (ACT8) return up(K) + up(K / P::E * 4) + up(K / 16 * 2) + 16;
+  int ng = K / P::GRP;
+  return up(P::NDIG * K) + 3 * up(ng * 4) + 16;
+}
+
+// ----------------------------------------------------------------- x prep
+
+// float path: each thread takes 4 consecutive elements (8 threads per
+// 32-element group, 4 per 16-element Q6_K group); loads are issued in
+// batches of four so the L2 latency is paid once per batch.
+template <int W>
+__device__ void prep_float(const Params &a, uint8_t *xr, int *flag) {
+  using P = Pol<W>;
+  constexpr int ND = P::NDIG, G = P::GRP, LPG = G / 4, NB = 4;
+  const int K = a.K, ng = K / G;
+  auto up = [](int v) { return (v + 15) & ~15; };
+  int8_t *dig = reinterpret_cast<int8_t *>(xr);
+  float *sg = reinterpret_cast<float *>(xr + up(ND * K));
+  float *sx = sg + up(ng * 4) / 4;
+  float *sd = sx + up(ng * 4) / 4;
+  const int tid = threadIdx.x, nthr = 32 * kConsumers;
+  const bool vec = a.xdt == TCB_F32 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
+  bool fin_all = true;
+  for (int base = 0; base < K; base += 4 * nthr * NB) {
+    float4 v[NB];
+#pragma unroll
+    for (int i = 0; i < NB; i++) {
+      const int e = base + 4 * (tid + i * nthr);
+      v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (e < K) {
+        if (vec) {
+          v[i] = *reinterpret_cast<const float4 *>(static_cast<const float *>(a.x) + e);
+        } else {
+          v[i].x = load_act(a.x, e, a.xdt);
+          v[i].y = load_act(a.x, e + 1, a.xdt);
+          v[i].z = load_act(a.x, e + 2, a.xdt);
+          v[i].w = load_act(a.x, e + 3, a.xdt);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < NB; i++) {
+      const int e = base + 4 * (tid + i * nthr);
+      float xv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+      float am = 0.f;
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const bool fin = __fsub_rn(xv[q], xv[q]) == 0.0f;
+        fin_all = fin_all && fin;
+        if (!fin) xv[q] = 0.f;
+        am = fmaxf(am, fabsf(xv[q]));
+      }
+#pragma unroll
+      for (int o = LPG / 2; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xFFFFFFFFu, am, o));
+      float id = 0.f, pre = 1.f, sigma = 0.f;
+      if (am > 0.f) {
+        // tiny groups are lifted by 2^64 first so 127/amax stays finite;
+        // sigma * id = 1 to a few ulp, which is all the representation needs
+        pre = am < 1e-30f ? 18446744073709551616.0f : 1.0f;
+        const float s = am * pre * (1.0f / 127.0f);
+        id = __frcp_rn(s);
+        sigma = s * (pre == 1.0f ? 1.0f : 5.421010862427522e-20f);
+      }
+      uint32_t ph = 0, p1 = 0, p2 = 0;
+      int dh = 0, d1 = 0, d2 = 0;
+      float s = 0.f;
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        int h = 0, l1 = 0, l2 = 0;
+        if (am > 0.f) {
+          const float y = (xv[q] * pre) * id;
+          h = max(-127, min(127, __float2int_rn(y)));
+          const float r1 = (y - (float)h) * 254.0f;
+          l1 = max(-127, min(127, __float2int_rn(r1)));
+          if (ND > 2) l2 = max(-127, min(127, __float2int_rn((r1 - (float)l1) * 254.0f)));
+        }
+        ph |= (uint32_t)(h & 0xFF) << (8 * q);
+        p1 |= (uint32_t)(l1 & 0xFF) << (8 * q);
+        p2 |= (uint32_t)(l2 & 0xFF) << (8 * q);
+        dh += h;
+        d1 += l1;
+        d2 += l2;
+        s += xv[q];
+      }
+#pragma unroll
+      for (int o = LPG / 2; o > 0; o >>= 1) {
+        s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+        dh += __shfl_xor_sync(0xFFFFFFFFu, dh, o);
+        d1 += __shfl_xor_sync(0xFFFFFFFFu, d1, o);
+        d2 += __shfl_xor_sync(0xFFFFFFFFu, d2, o);
+      }
+      if (e < K) {
+        *reinterpret_cast<uint32_t *>(dig + e) = ph;
+        *reinterpret_cast<uint32_t *>(dig + K + e) = p1;
+        if (ND > 2) *reinterpret_cast<uint32_t *>(dig + 2 * K + e) = p2;
+        if ((tid & (LPG - 1)) == 0) {
+          const int gi = e / G;
+          sg[gi] = ND > 2 ? sigma * (1.0f / 64516.0f) : sigma * (1.0f / 254.0f);
+          sx[gi] = s;
+          sd[gi] = ND > 2 ? fmaf(fmaf((float)dh, 254.0f, (float)d1), 254.0f, (float)d2)
+                          : fmaf((float)dh, 254.0f, (float)d1);
+        }
+      }
+    }
+  }
+  if (!fin_all) *flag = 1;
+}
+
+// int8 path: TR's quantizeQ8 (tensor/cpu_quant_q8.go:39-68), one warp per
+// activation block of E (= weight block) elements.
+template <int W>
+__device__ void prep_act8(const Params &a, uint8_t *xr, int *flag) {
+  using P = Pol<W>;
+  constexpr int E = P::E, PER = E / 32;
+  const int K = a.K, nbk = K / E;
+  auto up = [](int v) { return (v + 15) & ~15; };
+  int8_t *q8 = reinterpret_cast<int8_t *>(xr);
+  float *d8 = reinterpret_cast<float *>(xr + up(K));
+  int16_t *bs = reinterpret_cast<int16_t *>(xr + up(K) + up(nbk * 4));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = kConsumers;
+  for (int bi = warp; bi < nbk; bi += nw) {
+    float v[PER];
+    float amax = 0.0f;
+    bool fin = true;
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+      v[i] = load_act(a.x, (long)bi * E + lane * PER + i, a.xdt);
+      float t = fabsf(v[i]);
+      amax = t > amax ? t : amax;
+      fin = fin && (__fsub_rn(v[i], v[i]) == 0.0f);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float t = __shfl_xor_sync(0xFFFFFFFFu, amax, o);
+      amax = t > amax ? t : amax;
+    }
+    if (!__all_sync(0xFFFFFFFFu, fin) && lane == 0) *flag = 1;
+    const float id = __fdiv_rn(127.0f, amax);
+    const bool zero = !(amax > 0.0f) || (__fsub_rn(id, id) != 0.0f);
+    int part = 0;
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+      int q = 0;
+      if (!zero) q = max(-127, min(127, __float2int_rn(__fmul_rn(v[i], id))));
+      q8[bi * E + lane * PER + i] = (int8_t)q;
+      part += q;
+    }
+    if constexpr (PER == 8) {
+      part += __shfl_xor_sync(0xFFFFFFFFu, part, 1);
+      if ((lane & 1) == 0) bs[(bi * E + lane * PER) / 16] = (int16_t)part;
+    } else {
+#pragma unroll
+      for (int o = 1; o < 16; o <<= 1) part += __shfl_xor_sync(0xFFFFFFFFu, part, o);
+      if ((lane & 15) == 0) bs[(bi * E + lane) / 16] = (int16_t)part;
+    }
+    if (lane == 0) d8[bi] = zero ? 0.0f : __fdiv_rn(amax, 127.0f);
+  }
+}
+
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sa(bar)) : "memory");
+}
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(32 * kConsumers) : "memory"); }
+
+__device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t phase, int *err) {
+  for (uint32_t i = 0; i < (1u << 20); i++)
+    if (mbar_try_wait(bar, phase)) return true;
+  atomicExch(err, TCB_ERR_TIMEOUT);
+  return false;
+}
+
+// ----------------------------------------------------------------- format bodies
+// A body consumes one work item of a staged chunk (a Q4_K/Q6_K block, or a
+// Q8_0/Q4_0 round of 8 blocks) for the tile's 16 rows: rows g and g+8 of
+// lane (g = lane/4, t = lane%4).  Float path: acc[4] accumulates
+// (row g, MMA column 2t), (g, 2t+1), (g+8, 2t), (g+8, 2t+1).  Int8 path:
+// the block terms go to tb[row * cbc + local block].
+
+struct Lane {
+  int g, t;
+};
+
+// B fragment of group G for MMA column `col`: only the lanes of that column
+// carry digits, the others stay zero.
+__device__ __forceinline__ uint2 bfrag8(const int8_t *plane, int G, int col, const Lane &L) {
+  uint2 b = make_uint2(0u, 0u);
+  if (L.g == col) b = *reinterpret_cast<const uint2 *>(plane + G * 32 + 8 * L.t);
+  return b;
+}
+
+// Q4_K block: 8 sub-blocks of 32, two per 32-byte code group
+template <bool ACT8>
+__device__ __forceinline__ void body_q4k(const uint8_t *r0, const uint8_t *r1, int bg, int lb, const Lane &L,
+                                         const uint8_t *xr, int K, float (&acc)[4], float *tb, int cbc) {
+  constexpr int ND = ACT8 ? 1 : 3;
+  auto up = [](int v) { return (v + 15) & ~15; };
+  int D[ND][4];
+#pragma unroll
+  for (int p = 0; p < ND; p++) D[p][0] = D[p][1] = D[p][2] = D[p][3] = 0;
+#pragma unroll
+  for (int gq = 0; gq < 4; gq++) {
+    const uint2 q0 = *reinterpret_cast<const uint2 *>(r0 + 16 + 32 * gq + 8 * L.t);
+    const uint2 q1 = *reinterpret_cast<const uint2 *>(r1 + 16 + 32 * gq + 8 * L.t);
+    const uint32_t la0 = q0.x & M4, la1 = q1.x & M4, la2 = q0.y & M4, la3 = q1.y & M4;
+    const uint32_t ha0 = (q0.x >> 4) & M4, ha1 = (q1.x >> 4) & M4, ha2 = (q0.y >> 4) & M4, ha3 = (q1.y >> 4) & M4;
+    const int Glo = bg * 8 + 2 * gq;
+#pragma unroll
+    for (int p = 0; p < ND; p++) {
+      const int8_t *plane = reinterpret_cast<const int8_t *>(xr) + p * K;
+      uint2 b = bfrag8(plane, Glo, 2 * gq, L);
+      imma_u8(D[p], la0, la1, la2, la3, b.x, b.y);
+      b = bfrag8(plane, Glo + 1, 2 * gq + 1, L);
+      imma_u8(D[p], ha0, ha1, ha2, ha3, b.x, b.y);
+    }
+  }
+  // scales of sub-blocks j = 2t, 2t+1 for rows g, g+8 (get_scale_min_k4)
+  const uint4 h0 = *reinterpret_cast<const uint4 *>(r0);
+  const uint4 h1 = *reinterpret_cast<const uint4 *>(r1);
+  const int sh = (L.t & 1) * 16;
+  uint32_t sc2[2], mm2[2];
+  float dd[2], dm[2];
+#pragma unroll
+  for (int r = 0; r < 2; r++) {
+    const uint4 h = r ? h1 : h0;
+    const uint32_t A = h.y >> sh, Bq = h.z >> sh, C = h.w >> sh;
+    const uint32_t lo_sc = A & 0x3F3Fu, lo_m = Bq & 0x3F3Fu;
+    const uint32_t hi_sc = (C & 0x0F0Fu) | ((A >> 2) & 0x3030u);
+    const uint32_t hi_m = ((C >> 4) & 0x0F0Fu) | ((Bq >> 2) & 0x3030u);
+    sc2[r] = L.t < 2 ? lo_sc : hi_sc;
+    mm2[r] = L.t < 2 ? lo_m : hi_m;
+    dd[r] = half_exact(h.x & 0xFFFFu);
+    dm[r] = half_exact(h.x >> 16);
+  }
+  if constexpr (!ACT8) {
+    const float *sg = reinterpret_cast<const float *>(xr + up(3 * K));
+    const float *sx = sg + up(K / 32 * 4) / 4;
+    const int G0 = bg * 8 + 2 * L.t;
+    const float sg0 = sg[G0], sg1 = sg[G0 + 1], sx0 = sx[G0], sx1 = sx[G0 + 1];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int r = i >> 1, j = i & 1;
+      const float v = fmaf(fmaf((float)D[0][i], 254.0f, (float)D[1][i]), 254.0f, (float)D[2][i]);
+      const float sc = (float)((sc2[r] >> (8 * j)) & 0xFFu), m = (float)((mm2[r] >> (8 * j)) & 0xFFu);
+      acc[i] = fmaf(dd[r] * sc * (j ? sg1 : sg0), v, acc[i]);
+      acc[i] = fmaf(-(dm[r] * m), j ? sx1 : sx0, acc[i]);
+    }
+  } else {
+    // TR dotQ4KQ8Go (cpu_quant_q8.go:91-116): isum = sum sc_j * dot_j,
+    // msum = sum m_j * (bs pair); t = d*isum - dmin*msum; term = t * d8
+    const int16_t *bs = reinterpret_cast<const int16_t *>(xr + up(K) + up(K / 256 * 4)) + bg * 16 + 4 * L.t;
+    const float d8 = reinterpret_cast<const float *>(xr + up(K))[bg];
+    const int p0 = (int)(int16_t)(bs[0] + bs[1]), p1 = (int)(int16_t)(bs[2] + bs[3]);
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+      int is = (int)(sc2[r] & 0xFFu) * D[0][2 * r] + (int)((sc2[r] >> 8) & 0xFFu) * D[0][2 * r + 1];
+      int ms = (int)(mm2[r] & 0xFFu) * p0 + (int)((mm2[r] >> 8) & 0xFFu) * p1;
+#pragma unroll
+      for (int o = 1; o < 4; o <<= 1) {
+        is += __shfl_xor_sync(0xFFFFFFFFu, is, o);
+        ms += __shfl_xor_sync(0xFFFFFFFFu, ms, o);
+      }
+      const float tt = __fsub_rn(__fmul_rn(dd[r], (float)is), __fmul_rn(dm[r], (float)ms));
+      if (L.t == 0) tb[(L.g + 8 * r) * cbc + lb] = __fmul_rn(tt, d8);
+    }
+  }
+}
+
+// Q6_K block: 16 groups of 16 (k16 MMAs), two rounds (halves n = 0, 1)
+template <bool ACT8>
+__device__ __forceinline__ void body_q6k(const uint8_t *r0, const uint8_t *r1, int bg, int lb, const Lane &L,
+                                         const uint8_t *xr, int K, float (&acc)[4], float *tb, int cbc) {
+  constexpr int ND = ACT8 ? 1 : 2;
+  auto up = [](int v) { return (v + 15) & ~15; };
+  int is[2] = {0, 0}, ms[2] = {0, 0};
+  const float dd[2] = {half_exact(lds16(r0 + 208)), half_exact(lds16(r1 + 208))};
+#pragma unroll
+  for (int n = 0; n < 2; n++) {
+    int D[ND][4];
+#pragma unroll
+    for (int p = 0; p < ND; p++) D[p][0] = D[p][1] = D[p][2] = D[p][3] = 0;
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+      const int off = 64 * n + 16 * i + 4 * L.t, offh = 128 + 32 * n + 16 * i + 4 * L.t;
+      const uint32_t qa0 = lds32_a2(r0 + off), qb0 = lds32_a2(r0 + off + 32), qh0 = lds32_a2(r0 + offh);
+      const uint32_t qa1 = lds32_a2(r1 + off), qb1 = lds32_a2(r1 + off + 32), qh1 = lds32_a2(r1 + offh);
+      uint32_t A0[4], A1[4];
+      A0[0] = (qa0 & M4) | ((qh0 << 4) & 0x30303030u);
+      A0[1] = (qb0 & M4) | ((qh0 << 2) & 0x30303030u);
+      A0[2] = ((qa0 >> 4) & M4) | (qh0 & 0x30303030u);
+      A0[3] = ((qb0 >> 4) & M4) | ((qh0 >> 2) & 0x30303030u);
+      A1[0] = (qa1 & M4) | ((qh1 << 4) & 0x30303030u);
+      A1[1] = (qb1 & M4) | ((qh1 << 2) & 0x30303030u);
+      A1[2] = ((qa1 >> 4) & M4) | (qh1 & 0x30303030u);
+      A1[3] = ((qb1 >> 4) & M4) | ((qh1 >> 2) & 0x30303030u);
+#pragma unroll
+      for (int cq = 0; cq < 4; cq++) {
+        const int col = 2 * cq + i;
+        const int e0 = bg * 256 + 128 * n + 32 * cq + 16 * i;  // first element of the group
+#pragma unroll
+        for (int p = 0; p < ND; p++) {
+          uint32_t b = 0;
+          if (L.g == col) b = *reinterpret_cast<const uint32_t *>(reinterpret_cast<const int8_t *>(xr) + p * K + e0 + 4 * L.t);
+          imma_u8_k16(D[p], A0[cq], A1[cq], b);
+        }
+      }
+    }
+    // lane groups: j = 8n + 2t + jj, sc index 8n + 2t + jj
+    const uint32_t scw0 = lds16(r0 + 192 + 8 * n + 2 * L.t), scw1 = lds16(r1 + 192 + 8 * n + 2 * L.t);
+    if constexpr (!ACT8) {
+      const int ng = K / 16;
+      const float *sg = reinterpret_cast<const float *>(xr + up(2 * K));
+      const float *sd = sg + 2 * (up(ng * 4) / 4);
+      const int G0 = bg * 16 + 8 * n + 2 * L.t;
+#pragma unroll
+      for (int ii = 0; ii < 4; ii++) {
+        const int r = ii >> 1, jj = ii & 1;
+        const uint32_t scw = r ? scw1 : scw0;
+        const float sc = (float)(int8_t)((scw >> (8 * jj)) & 0xFFu);
+        const float v = fmaf((float)D[0][ii], 254.0f, (float)D[1][ii]);
+        acc[ii] = fmaf(dd[r] * sc * sg[G0 + jj], fmaf(-32.0f, sd[G0 + jj], v), acc[ii]);
+      }
+    } else {
+      const int16_t *bs = reinterpret_cast<const int16_t *>(xr + up(K) + up(K / 256 * 4)) + bg * 16 + 8 * n + 2 * L.t;
+#pragma unroll
+      for (int r = 0; r < 2; r++) {
+        const uint32_t scw = r ? scw1 : scw0;
+        const int s0 = (int)(int8_t)(scw & 0xFFu), s1 = (int)(int8_t)((scw >> 8) & 0xFFu);
+        is[r] += s0 * D[0][2 * r] + s1 * D[0][2 * r + 1];
+        ms[r] += s0 * (int)bs[0] + s1 * (int)bs[1];
+      }
+    }
+  }
+  if constexpr (ACT8) {
+    // TR dotQ6KQ8Go (cpu_quant_q8.go:378-407): t = d*(isum - 32*msum); term = t*d8
+    const float d8 = reinterpret_cast<const float *>(xr + up(K))[bg];
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+#pragma unroll
+      for (int o = 1; o < 4; o <<= 1) {
+        is[r] += __shfl_xor_sync(0xFFFFFFFFu, is[r], o);
+        ms[r] += __shfl_xor_sync(0xFFFFFFFFu, ms[r], o);
+      }
+      const float tt = __fmul_rn(dd[r], (float)(is[r] - 32 * ms[r]));
+      if (L.t == 0) tb[(L.g + 8 * r) * cbc + lb] = __fmul_rn(tt, d8);
+    }
+  }
+}
+
+// Q8_0 / Q4_0 round: 8 consecutive blocks, block j of the round in MMA
+// column j.  Rounds start 16-byte aligned (8 blocks = 272 / 144 bytes).
+template <int W, bool ACT8>
+__device__ __forceinline__ void body_q32(const uint8_t *s0, const uint8_t *s1, int bg0, int lb0, const Lane &L,
+                                         const uint8_t *xr, int K, float (&acc)[4], float *tb, int cbc) {
+  using P = Pol<W>;
+  constexpr int ND = ACT8 ? 1 : 3;
+  constexpr int B = P::B;
+  auto up = [](int v) { return (v + 15) & ~15; };
+  int D[ND][4];
+#pragma unroll
+  for (int p = 0; p < ND; p++) D[p][0] = D[p][1] = D[p][2] = D[p][3] = 0;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const uint8_t *b0 = s0 + j * B, *b1 = s1 + j * B;
+    const int G = bg0 + j;
+    if constexpr (W == TCB_Q8_0) {
+      const uint32_t w00 = lds32_a2(b0 + 2 + 8 * L.t), w01 = lds32_a2(b0 + 6 + 8 * L.t);
+      const uint32_t w10 = lds32_a2(b1 + 2 + 8 * L.t), w11 = lds32_a2(b1 + 6 + 8 * L.t);
+#pragma unroll
+      for (int p = 0; p < ND; p++) {
+        const uint2 b = bfrag8(reinterpret_cast<const int8_t *>(xr) + p * K, G, j, L);
+        imma_s8(D[p], w00, w10, w01, w11, b.x, b.y);
+      }
+    } else {
+      const uint32_t q0 = lds32_a2(b0 + 2 + 4 * L.t), q1 = lds32_a2(b1 + 2 + 4 * L.t);
+      const uint32_t a0 = q0 & M4, a1 = q1 & M4, a2 = (q0 >> 4) & M4, a3 = (q1 >> 4) & M4;
+#pragma unroll
+      for (int p = 0; p < ND; p++) {
+        uint32_t bx = 0, by = 0;
+        if (L.g == j) {
+          const int8_t *pl = reinterpret_cast<const int8_t *>(xr) + p * K + G * 32;
+          bx = *reinterpret_cast<const uint32_t *>(pl + 4 * L.t);
+          by = *reinterpret_cast<const uint32_t *>(pl + 16 + 4 * L.t);
+        }
+        imma_u8(D[p], a0, a1, a2, a3, bx, by);
+      }
+    }
+  }
+  // lane blocks: 2t, 2t+1 of the round, rows g, g+8
+  float dw[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) dw[i] = half_exact(lds16((i >> 1 ? s1 : s0) + (2 * L.t + (i & 1)) * B));
+  const int G0 = bg0 + 2 * L.t;
+  if constexpr (!ACT8) {
+    const float *sg = reinterpret_cast<const float *>(xr + up(3 * K));
+    const float *sd = sg + 2 * (up(K / 32 * 4) / 4);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int j = i & 1;
+      float v = fmaf(fmaf((float)D[0][i], 254.0f, (float)D[1][i]), 254.0f, (float)D[2][i]);
+      if (W == TCB_Q4_0) v = fmaf(-8.0f, sd[G0 + j], v);
+      acc[i] = fmaf(dw[i] * sg[G0 + j], v, acc[i]);
+    }
+  } else {
+    // TR dotQ4Q8Go (cpu_quant_q8.go:74-87), the same fold for Q8_0:
+    // t = dw*d8; term = t*isum
+    const float *d8 = reinterpret_cast<const float *>(xr + up(K));
+    const int16_t *bs = reinterpret_cast<const int16_t *>(xr + up(K) + up(K / 32 * 4));
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int j = i & 1;
+      int isum = D[0][i];
+      if (W == TCB_Q4_0) isum -= 8 * ((int)bs[2 * (G0 + j)] + (int)bs[2 * (G0 + j) + 1]);
+      tb[(L.g + 8 * (i >> 1)) * cbc + lb0 + 2 * L.t + j] = __fmul_rn(__fmul_rn(dw[i], d8[G0 + j]), (float)isum);
+    }
+  }
+}
+
+// ----------------------------------------------------------------- kernel
+// Shared memory: [full bars | empty bars | flag | warp partials | x region |
+// int8-path terms | stages].  CTA b owns tiles b, b + grid, ...
+
+template <int W, bool ACT8>
+__global__ void __launch_bounds__(kThreads, 2) k_mv1(const __grid_constant__ CUtensorMap tmap, const Params a) {
+  using P = Pol<W>;
+  constexpr int pitch = P::BOX8 * 8, box_bytes = 16 * pitch;
+  extern __shared__ __align__(128) uint8_t sm[];
+  uint64_t *full = reinterpret_cast<uint64_t *>(sm), *empty = full + 8;
+  int *flag = reinterpret_cast<int *>(sm + 128);
+  float *part = reinterpret_cast<float *>(sm + 256);  // [kConsumers][16]
+  uint8_t *xr = sm + a.xoff;
+  float *terms = reinterpret_cast<float *>(sm + a.toff);
+  uint8_t *stages = sm + a.soff;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int stage_bytes = NBOX * box_bytes;
+  const int my_tiles = (a.tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int nstages = my_tiles * a.nch;
+
+  if (threadIdx.x == 0) {
+    *flag = 0;
+    for (int s = 0; s < a.S; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumers);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) pdl_launch_dependents();
+
+  if (warp == kConsumers) {
+    // producer: a stage is NBOX boxes of 16 rows; rows past N and bytes
+    // past the row end are zero-filled by the copy engine
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
+      for (int it = 0; it < nstages; it++) {
+        const int buf = it % a.S;
+        if (!wait_bar(&empty[buf], (uint32_t)(((it / a.S) & 1) ^ 1), a.err)) return;
+        const int tile = (int)blockIdx.x + (it / a.nch) * (int)gridDim.x, ch = it % a.nch;
+        const int b0 = ch * a.cbc;
+        const int nbox = min(NBOX, (a.nb - b0 + P::BPB - 1) / P::BPB);
+        mbar_expect_tx(&full[buf], (uint32_t)(nbox * box_bytes));
+        for (int k = 0; k < nbox; k++)
+          tma_load_2d(stages + buf * stage_bytes + k * box_bytes, &tmap, (b0 + k * P::BPB) * P::B / 8, tile * 16,
+                      &full[buf]);
+      }
+    }
+    return;
+  }
+
+  // consumers: x (and c) may be written by the previous kernel of the stream
+  pdl_wait();
+  if constexpr (ACT8) prep_act8<W>(a, xr, flag);
+  else prep_float<W>(a, xr, flag);
+  consumers_sync();
+  const bool slow = *flag != 0;
+  const Lane L{lane >> 2, lane & 3};
+  int it = 0;
+  for (int ti = 0; ti < my_tiles; ti++) {
+    const int tile = (int)blockIdx.x + ti * (int)gridDim.x;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    float frow = 0.f;  // int8 path: running fold of row `lane` (warp 0, lanes < 16)
+    for (int ch = 0; ch < a.nch; ch++, it++) {
+      const int buf = it % a.S;
+      if (!wait_bar(&full[buf], (uint32_t)((it / a.S) & 1), a.err)) return;
+      const uint8_t *st = stages + buf * stage_bytes;
+      const int b0 = ch * a.cbc, nblk = min(a.nb, b0 + a.cbc) - b0;
+      float *tb = terms + (it & 1) * 16 * a.cbc;
+      if (!slow) {
+        for (int lb = warp * P::RB; lb < nblk; lb += kConsumers * P::RB) {
+          const uint8_t *r0 = st + (lb / P::BPB) * box_bytes + L.g * pitch + (lb % P::BPB) * P::B;
+          const uint8_t *r1 = r0 + 8 * pitch;
+          if constexpr (W == TCB_Q4_K) body_q4k<ACT8>(r0, r1, b0 + lb, lb, L, xr, a.K, acc, tb, a.cbc);
+          else if constexpr (W == TCB_Q6_K) body_q6k<ACT8>(r0, r1, b0 + lb, lb, L, xr, a.K, acc, tb, a.cbc);
+          else body_q32<W, ACT8>(r0, r1, b0 + lb, lb, L, xr, a.K, acc, tb, a.cbc);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[buf]);
+      if (ACT8 && !slow) {
+        consumers_sync();  // every term of this chunk is in tb
+        if (warp == 0 && lane < 16)
+          for (int lb = 0; lb < nblk; lb++) frow = __fadd_rn(frow, tb[lane * a.cbc + lb]);
+      }
+    }
+    if (slow) continue;
+    const int row = tile * 16 + lane;
+    if constexpr (!ACT8) {
+      float s0 = acc[0] + acc[1], s1 = acc[2] + acc[3];
+      s0 += __shfl_xor_sync(0xFFFFFFFFu, s0, 1);
+      s1 += __shfl_xor_sync(0xFFFFFFFFu, s1, 1);
+      s0 += __shfl_xor_sync(0xFFFFFFFFu, s0, 2);
+      s1 += __shfl_xor_sync(0xFFFFFFFFu, s1, 2);
+      if (L.t == 0) {
+        part[warp * 16 + L.g] = s0;
+        part[warp * 16 + L.g + 8] = s1;
+      }
+      consumers_sync();
+      if (warp == 0 && lane < 16 && row < a.N) {
+        float v = 0.f;
+#pragma unroll
+        for (int w2 = 0; w2 < kConsumers; w2++) v += part[w2 * 16 + lane];
+        store_out(a.c, row, a.cdt, v, a.accumulate != 0);
+      }
+      consumers_sync();
+    } else {
+      if (warp == 0 && lane < 16 && row < a.N) store_out(a.c, row, a.cdt, frow, a.accumulate != 0);
+    }
+  }
+  if (slow) {
+    // NaN/Inf in x: TR's float path (the int8 path also falls back to it,
+    // cpu_quant_q8.go:157-163), one warp per row
+    for (int n = (int)blockIdx.x * kConsumers + warp; n < a.N; n += (int)gridDim.x * kConsumers) {
+      float accs[1] = {0.0f};
+      lane_row_float<W, 1>(a.w + (long)n * a.rowBytes, a.K, lane, XGlobal{a.x, 0, a.xdt}, accs);
+      const float v = warp_sum(accs[0]);
+      if (lane == 0) store_out(a.c, n, a.cdt, v, a.accumulate != 0);
+    }
+  }
+}
+
+}  // namespace mv
+
+// ----------------------------------------------------------------- host
+
+namespace {
+
+constexpr int kSmemMax = 227 * 1024;
+constexpr int kSmemHalf = 113 * 1024;  // two CTAs per SM
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// [N rows, rowBytes/8 eight-byte elements] view of the block store
+template <int W>
+bool encode_weight_map(CUtensorMap *tm, const void *w, int N, long rowBytes) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  cuuint64_t gdim[2] = {(cuuint64_t)(rowBytes / 8), (cuuint64_t)N};
+  cuuint64_t gstride[1] = {(cuuint64_t)rowBytes};
+  cuuint32_t box[2] = {(cuuint32_t)mv::Pol<W>::BOX8, 16};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void *>(w), gdim, gstride, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int W, bool ACT8>
+cudaError_t plan_launch(const MvPlan &pl, const void *w, int N, int K, const void *x, int xdt, void *c, int cdt,
+                        int accumulate, int *err, cudaStream_t s) {
+  mv::Params a{};
+  a.w = static_cast<const uint8_t *>(w);
+  a.nb = K / mv::Pol<W>::E;
+  a.rowBytes = (long)a.nb * mv::Pol<W>::B;
+  a.N = N;
+  a.K = K;
+  a.x = x;
+  a.xdt = xdt;
+  a.c = c;
+  a.cdt = cdt;
+  a.accumulate = accumulate;
+  a.tiles = pl.tiles;
+  a.cbc = pl.cbc;
+  a.nch = pl.nch;
+  a.err = err;
+  a.S = pl.stages;
+  a.xoff = pl.xoff;
+  a.toff = pl.toff;
+  a.soff = pl.soff;
+  CUtensorMap tm;
+  static_assert(sizeof(tm) == sizeof(pl.tmap), "CUtensorMap size");
+  memcpy(&tm, pl.tmap, sizeof tm);
+  auto kern = mv::k_mv1<W, ACT8>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.grid);
+  cfg.blockDim = dim3(mv::kThreads);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, tm, a);
+}
+
+template <int W, bool ACT8>
+MvPlan plan_w(int N, int K, const void *w, int sms) {
+  using P = mv::Pol<W>;
+  MvPlan pl{};
+  const int nb = K / P::E;
+  const long rowBytes = (long)nb * P::B;
+  if (rowBytes % 16 || reinterpret_cast<uintptr_t>(w) % 16 || nb == 0) return pl;
+  if (P::RB == 8 && nb % 8) return pl;  // Q8_0 / Q4_0 rounds are 8 blocks
+  if (!tensor_map_encoder()) return pl;
+  pl.cbc = mv::NBOX * P::BPB;
+  pl.nch = (nb + pl.cbc - 1) / pl.cbc;
+  pl.pitch = P::BOX8 * 8;
+  pl.xoff = 1024;
+  pl.toff = pl.xoff + ((mv::x_region_bytes<W, ACT8>(K) + 127) & ~127);
+  const int tbytes = ACT8 ? 2 * 16 * pl.cbc * 4 : 0;
+  pl.soff = (pl.toff + tbytes + 127) & ~127;
+  const int stage_bytes = mv::NBOX * 16 * pl.pitch;
+  // two stages when that leaves room for a second CTA on the SM: the next
+  // launch of the stream (programmatic serialization) then starts streaming
+  // its weights beside this one; otherwise as many stages as fit
+  int S = (kSmemHalf - pl.soff) / stage_bytes;
+  if (S >= 2) S = 2;
+  else S = (kSmemMax - pl.soff) / stage_bytes;
+  if (S > 6) S = 6;
+  if (S < 2) return pl;
+  pl.stages = S;
+  pl.smem = pl.soff + S * stage_bytes;
+  pl.tiles = (N + 15) / 16;
+  pl.grid = pl.tiles < sms ? pl.tiles : sms;
+  CUtensorMap tm;
+  if (!encode_weight_map<W>(&tm, w, N, rowBytes)) return pl;
+  memcpy(pl.tmap, &tm, sizeof tm);
+  pl.ok = true;
+  return pl;
+}
+
+}  // namespace
+
+MvPlan matvec_plan(int wtype, int act8, int M, int N, int K, const void *w, int sms) {
+  MvPlan none{};
+  if (M != 1 || N <= 0 || K <= 0) return none;
+  switch (wtype) {
+  case TCB_Q4_K: return act8 ? plan_w<TCB_Q4_K, true>(N, K, w, sms) : plan_w<TCB_Q4_K, false>(N, K, w, sms);
+  case TCB_Q6_K: return act8 ? plan_w<TCB_Q6_K, true>(N, K, w, sms) : plan_w<TCB_Q6_K, false>(N, K, w, sms);
+  case TCB_Q8_0: return act8 ? plan_w<TCB_Q8_0, true>(N, K, w, sms) : plan_w<TCB_Q8_0, false>(N, K, w, sms);
+  case TCB_Q4_0: return act8 ? plan_w<TCB_Q4_0, true>(N, K, w, sms) : plan_w<TCB_Q4_0, false>(N, K, w, sms);
+  }
+  return none;
+}
+
+cudaError_t matvec_launch(const MvPlan &pl, int wtype, int act8, int N, int K, const void *w, const void *x, int xdt,
+                          void *c, int cdt, int accumulate, int *err, cudaStream_t s) {
+#define TCB_MV(WT)                                                                             \
+  return act8 ? plan_launch<WT, true>(pl, w, N, K, x, xdt, c, cdt, accumulate, err, s)        \
+              : plan_launch<WT, false>(pl, w, N, K, x, xdt, c, cdt, accumulate, err, s)
+  switch (wtype) {
+  case TCB_Q4_K: TCB_MV(TCB_Q4_K);
+  case TCB_Q6_K: TCB_MV(TCB_Q6_K);
+  case TCB_Q8_0: TCB_MV(TCB_Q8_0);
+  case TCB_Q4_0: TCB_MV(TCB_Q4_0);
+  }
+#undef TCB_MV
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace tcb

@@ -1,0 +1,25 @@
+// tcb_matvec.h - the tensor-core matvec path (batch 1) of libtcb.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+namespace tcb {
+
+// launch plan of the batch-1 tensor-core kernel; ok == false when the
+// shape is not taken by it (the caller then runs the portable kernel)
+struct MvPlan {
+  bool ok;
+  int tiles, cbc, nch;         // 16-row tiles, blocks per staged chunk, chunks per row
+  int stages, pitch;           // TMA stages, bytes per staged row
+  int xoff, toff, soff, smem;  // shared-memory layout
+  int grid;
+  alignas(64) unsigned char tmap[128];  // TMA descriptor of the weight (CUtensorMap)
+};
+
+MvPlan matvec_plan(int wtype, int act8, int M, int N, int K, const void *w, int sms);
+
+cudaError_t matvec_launch(const MvPlan &pl, int wtype, int act8, int N, int K, const void *w, const void *x, int xdt,
+                          void *c, int cdt, int accumulate, int *err, cudaStream_t s);
+
+}  // namespace tcb
