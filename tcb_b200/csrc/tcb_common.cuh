@@ -114,6 +114,21 @@ __device__ __forceinline__ void store_out(void *c, long i, int dt, float v, bool
   }
 }
 
+// the old value of one output as f32 (for accumulation), read ahead of use
+__device__ __forceinline__ float load_out(const void *c, long i, int dt) {
+  if (dt == TCB_F32) return static_cast<const float *>(c)[i];
+  const uint16_t h = static_cast<const uint16_t *>(c)[i];
+  return dt == TCB_BF16 ? bf16_to_f32(h) : half_exact(h);
+}
+
+// store one output whose old value (if accumulating) was loaded earlier
+__device__ __forceinline__ void store_out_old(void *c, long i, int dt, float v, bool accumulate, float old) {
+  const float r = accumulate ? __fadd_rn(old, v) : v;
+  if (dt == TCB_F32) static_cast<float *>(c)[i] = r;
+  else if (dt == TCB_BF16) static_cast<uint16_t *>(c)[i] = f32_to_bf16(r);
+  else static_cast<uint16_t *>(c)[i] = f32_to_f16(r);
+}
+
 // Q4_K packed 6-bit scale/min of sub-block j (TR tensor/quant.go:158-163)
 __device__ __forceinline__ void q4k_scale(int j, const uint8_t *q, uint32_t &sc, uint32_t &m) {
   if (j < 4) {

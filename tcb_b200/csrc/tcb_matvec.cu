@@ -5,11 +5,11 @@
 // Design (memory-bound at batch 1: every weight byte is read once):
 //  * Weights stream from HBM into shared memory through 2-D TMA tensor
 //    copies (cp.async.bulk.tensor, 8-byte elements, no multicast) issued by
-//    a producer warp: a stage is 16 rows x 2 boxes of ~1.1-1.7 KB per row,
-//    two TMA instructions per ~40 KB, so DRAM sees long runs and the copy
+//    a producer warp: a stage is 16 rows x 2-4 boxes of ~1.1-1.7 KB per row,
+//    a few TMA instructions per ~40-70 KB, so DRAM sees long runs and the copy
 //    engine few requests; the box width is padded so the staged rows fall on
 //    different shared-memory banks; rows past N and bytes past the row end
-//    arrive as zeros.  Eight consumer warps split each stage's blocks.
+//    arrive as zeros.  Sixteen consumer warps split each stage's blocks.
 //  * Launched with programmatic stream serialization: the producer starts
 //    streaming weights while the previous kernel of the stream drains; the
 //    consumers wait for it (griddepcontrol.wait) before reading x or
@@ -23,15 +23,16 @@
 //    leaves every (row, group) integer dot in its own accumulator and each
 //    lane applies the scales of exactly four (row, group) pairs.
 //  * Float path: x is split per 32-element group into int8 digits,
-//    x ~= sigma * (h + l1/254 + l2/254^2), |digits| <= 127, sigma =
-//    amax/127; the digit products are exact int32 and are recombined in
-//    fp32 (relative error of the x representation ~1e-7).  A row of x with
+//    x ~= sigma * (h + l/254), |digits| <= 127, sigma = amax/127; the digit
+//    products are exact int32 and recombine exactly (relative error of the
+//    x representation <= 1/(2*127*254) of the group maximum, ~4e-5 rel-L2
+//    on the outputs).  A row of x with
 //    NaN/Inf takes an fp32 SIMT path instead (NaN/Inf propagate as in TR).
 //  * Int8-activation path (TR_quantized_activations): x is quantised with
 //    TR's quantizeQ8 and each block term is formed exactly as TR's CPU
 //    kernels do, then folded in block order: bit-exact.
-//  * Work split: a CTA owns whole 16-row tiles; warp w takes the blocks (or
-//    8-block rounds) w, w+8, ... of every chunk, and the eight warp
+//  * Work split: a CTA owns whole 16-row tiles; warp w takes block (or
+//    8-block round) w of every chunk, and the sixteen warp
 //    partials of a row are added in warp order (float path) or every block
 //    term is folded in block order (int8 path) in shared memory.  Results
 //    do not depend on the SM count or on timing.
@@ -90,20 +91,20 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 // D += A(16x32 u8) * B(32x8 s8)
 __device__ __forceinline__ void imma_u8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                         uint32_t b1) {
-  asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
                : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 // D += A(16x32 s8) * B(32x8 s8)
 __device__ __forceinline__ void imma_s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                         uint32_t b1) {
-  asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
                : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 // D += A(16x16 u8) * B(16x8 s8)
 __device__ __forceinline__ void imma_u8_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
-  asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+  asm("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
                : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
                : "r"(a0), "r"(a1), "r"(b0));
 }
@@ -127,16 +128,15 @@ constexpr uint32_t M4 = 0x0F0F0F0Fu;
 // work items per box); BOX8: box width in 8-byte elements, the BPB blocks
 // plus padding that makes the staged row pitch 32 or 96 mod 128 bytes;
 // NDIG: digits of x on the float path (2 for Q6_K, whose k16 groups take
-// twice the MMAs).  A stage is NBOX boxes.
+// twice the MMAs).  A stage is NBOX boxes: 16 work items, one per consumer
+// warp.
 template <int W> struct Pol;
-template <> struct Pol<TCB_Q4_K> { static constexpr int E = 256, B = 144, GRP = 32, GPB = 8, RB = 1, BPB = 8, BOX8 = 148, NDIG = 3; };
-template <> struct Pol<TCB_Q6_K> { static constexpr int E = 256, B = 210, GRP = 16, GPB = 16, RB = 1, BPB = 8, BOX8 = 212, NDIG = 2; };
-template <> struct Pol<TCB_Q8_0> { static constexpr int E = 32, B = 34, GRP = 32, GPB = 1, RB = 8, BPB = 32, BOX8 = 140, NDIG = 3; };
-template <> struct Pol<TCB_Q4_0> { static constexpr int E = 32, B = 18, GRP = 32, GPB = 1, RB = 8, BPB = 64, BOX8 = 148, NDIG = 3; };
-constexpr int NBOX = 2;
+template <> struct Pol<TCB_Q4_K> { static constexpr int E = 256, B = 144, GRP = 32, GPB = 8, RB = 1, BPB = 8, BOX8 = 148, NBOX = 2, NDIG = 2; };
+template <> struct Pol<TCB_Q6_K> { static constexpr int E = 256, B = 210, GRP = 16, GPB = 16, RB = 1, BPB = 8, BOX8 = 212, NBOX = 2, NDIG = 2; };
+template <> struct Pol<TCB_Q8_0> { static constexpr int E = 32, B = 34, GRP = 32, GPB = 1, RB = 8, BPB = 32, BOX8 = 140, NBOX = 4, NDIG = 2; };
+template <> struct Pol<TCB_Q4_0> { static constexpr int E = 32, B = 18, GRP = 32, GPB = 1, RB = 8, BPB = 64, BOX8 = 148, NBOX = 2, NDIG = 2; };
 
-constexpr int kConsumers = 8;          // consumer warps; warp 8 produces
-constexpr int kThreads = 32 * (kConsumers + 1);
+constexpr int kConsumers = 16;         // compute warps; warp 16 produces, warp 17 finishes
 
 struct Params {
   const uint8_t *w;
@@ -179,11 +179,16 @@ __host__ __device__ inline int x_region_bytes(int K) {
 
 // float path: each thread takes 4 consecutive elements (8 threads per
 // 32-element group, 4 per 16-element Q6_K group); loads are issued in
-// batches of four so the L2 latency is paid once per batch.
+// batches of four so the L2 latency is paid once per batch.  Digits are
+// rounded with the 1.5*2^23 trick (the integer lands in the low mantissa
+// bits, ties to even) and packed with byte permutes.
 template <int W>
 __device__ void prep_float(const Params &a, uint8_t *xr, int *flag) {
   using P = Pol<W>;
   constexpr int ND = P::NDIG, G = P::GRP, LPG = G / 4, NB = 4;
+  constexpr bool NEED_SX = W == TCB_Q4_K;                    // the min term uses sum(x)
+  constexpr bool NEED_SD = W == TCB_Q4_0 || W == TCB_Q6_K;  // the code offset uses sum(digits)
+  constexpr float MAGIC = 12582912.0f;
   const int K = a.K, ng = K / G;
   auto up = [](int v) { return (v + 15) & ~15; };
   int8_t *dig = reinterpret_cast<int8_t *>(xr);
@@ -217,49 +222,57 @@ __device__ void prep_float(const Params &a, uint8_t *xr, int *flag) {
       float am = 0.f;
 #pragma unroll
       for (int q = 0; q < 4; q++) {
-        const bool fin = __fsub_rn(xv[q], xv[q]) == 0.0f;
-        fin_all = fin_all && fin;
-        if (!fin) xv[q] = 0.f;
+        if ((__float_as_uint(xv[q]) & 0x7F800000u) == 0x7F800000u) {
+          fin_all = false;
+          xv[q] = 0.f;
+        }
         am = fmaxf(am, fabsf(xv[q]));
       }
 #pragma unroll
       for (int o = LPG / 2; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xFFFFFFFFu, am, o));
-      float id = 0.f, pre = 1.f, sigma = 0.f;
+      // y = x * 127/amax in [-127, 127]; tiny groups are lifted by 2^64 so
+      // the reciprocal stays finite; sigma * id = 1 to a few ulp
+      float id = 0.f, sigma = 0.f;
       if (am > 0.f) {
-        // tiny groups are lifted by 2^64 first so 127/amax stays finite;
-        // sigma * id = 1 to a few ulp, which is all the representation needs
-        pre = am < 1e-30f ? 18446744073709551616.0f : 1.0f;
-        const float s = am * pre * (1.0f / 127.0f);
-        id = __frcp_rn(s);
-        sigma = s * (pre == 1.0f ? 1.0f : 5.421010862427522e-20f);
+        const bool tiny = am < 1e-30f;
+        const float sc = (tiny ? am * 18446744073709551616.0f : am) * (1.0f / 127.0f);
+        id = __frcp_rn(sc) * (tiny ? 18446744073709551616.0f : 1.0f);
+        sigma = tiny ? sc * 5.421010862427522e-20f : sc;
       }
-      uint32_t ph = 0, p1 = 0, p2 = 0;
-      int dh = 0, d1 = 0, d2 = 0;
-      float s = 0.f;
+      uint32_t bh[4], b1[4], b2[4];
+      float fh = 0.f, f1 = 0.f, f2 = 0.f, s = 0.f;
 #pragma unroll
       for (int q = 0; q < 4; q++) {
-        int h = 0, l1 = 0, l2 = 0;
-        if (am > 0.f) {
-          const float y = (xv[q] * pre) * id;
-          h = max(-127, min(127, __float2int_rn(y)));
-          const float r1 = (y - (float)h) * 254.0f;
-          l1 = max(-127, min(127, __float2int_rn(r1)));
-          if (ND > 2) l2 = max(-127, min(127, __float2int_rn((r1 - (float)l1) * 254.0f)));
+        const float y = __fmul_rn(xv[q], id);
+        const float t0 = __fadd_rn(y, MAGIC), h = __fsub_rn(t0, MAGIC);
+        const float r1 = __fmul_rn(__fsub_rn(y, h), 254.0f);
+        const float t1 = __fadd_rn(r1, MAGIC), l1 = __fsub_rn(t1, MAGIC);
+        bh[q] = __float_as_uint(t0);
+        b1[q] = __float_as_uint(t1);
+        if (ND > 2) {
+          const float r2 = __fmul_rn(__fsub_rn(r1, l1), 254.0f);
+          const float t2 = __fadd_rn(r2, MAGIC);
+          b2[q] = __float_as_uint(t2);
+          if (NEED_SD) f2 += __fsub_rn(t2, MAGIC);
         }
-        ph |= (uint32_t)(h & 0xFF) << (8 * q);
-        p1 |= (uint32_t)(l1 & 0xFF) << (8 * q);
-        p2 |= (uint32_t)(l2 & 0xFF) << (8 * q);
-        dh += h;
-        d1 += l1;
-        d2 += l2;
-        s += xv[q];
+        if (NEED_SD) {
+          fh += h;
+          f1 += l1;
+        }
+        if (NEED_SX) s += xv[q];
       }
+      const uint32_t ph = __byte_perm(__byte_perm(bh[0], bh[1], 0x0040), __byte_perm(bh[2], bh[3], 0x0040), 0x5410);
+      const uint32_t p1 = __byte_perm(__byte_perm(b1[0], b1[1], 0x0040), __byte_perm(b1[2], b1[3], 0x0040), 0x5410);
+      uint32_t p2 = 0;
+      if (ND > 2) p2 = __byte_perm(__byte_perm(b2[0], b2[1], 0x0040), __byte_perm(b2[2], b2[3], 0x0040), 0x5410);
 #pragma unroll
       for (int o = LPG / 2; o > 0; o >>= 1) {
-        s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
-        dh += __shfl_xor_sync(0xFFFFFFFFu, dh, o);
-        d1 += __shfl_xor_sync(0xFFFFFFFFu, d1, o);
-        d2 += __shfl_xor_sync(0xFFFFFFFFu, d2, o);
+        if (NEED_SX) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+        if (NEED_SD) {
+          fh += __shfl_xor_sync(0xFFFFFFFFu, fh, o);
+          f1 += __shfl_xor_sync(0xFFFFFFFFu, f1, o);
+          if (ND > 2) f2 += __shfl_xor_sync(0xFFFFFFFFu, f2, o);
+        }
       }
       if (e < K) {
         *reinterpret_cast<uint32_t *>(dig + e) = ph;
@@ -268,9 +281,8 @@ __device__ void prep_float(const Params &a, uint8_t *xr, int *flag) {
         if ((tid & (LPG - 1)) == 0) {
           const int gi = e / G;
           sg[gi] = ND > 2 ? sigma * (1.0f / 64516.0f) : sigma * (1.0f / 254.0f);
-          sx[gi] = s;
-          sd[gi] = ND > 2 ? fmaf(fmaf((float)dh, 254.0f, (float)d1), 254.0f, (float)d2)
-                          : fmaf((float)dh, 254.0f, (float)d1);
+          if (NEED_SX) sx[gi] = s;
+          if (NEED_SD) sd[gi] = ND > 2 ? fmaf(fmaf(fh, 254.0f, f1), 254.0f, f2) : fmaf(fh, 254.0f, f1);
         }
       }
     }
@@ -333,11 +345,43 @@ __device__ void prep_act8(const Params &a, uint8_t *xr, int *flag) {
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sa(bar)) : "memory");
 }
-__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(32 * kConsumers) : "memory"); }
 
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(sa(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes (the copy engine's completion wakes it) or ~0.5 ms pass
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t *bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(sa(bar)), "r"(phase), "r"(500000u)
+      : "memory");
+  return ok != 0;
+}
+
+// a barrier completed by the copy engine (bounded: ~2 s at most)
 __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t phase, int *err) {
-  for (uint32_t i = 0; i < (1u << 20); i++)
-    if (mbar_try_wait(bar, phase)) return true;
+  for (uint32_t i = 0; i < 4096u; i++)
+    if (mbar_try_wait_hint(bar, phase)) return true;
+  atomicExch(err, TCB_ERR_TIMEOUT);
+  return false;
+}
+
+// A barrier completed by other warps' arrives: a sleeping try_wait is not
+// woken promptly by them, so poll with a short backoff (bounded: ~1 s).
+__device__ __forceinline__ bool spin_bar(uint64_t *bar, uint32_t phase, int *err) {
+  for (uint32_t i = 0; i < (1u << 24); i++) {
+    if (mbar_test_wait(bar, phase)) return true;
+    __nanosleep(32);
+  }
   atomicExch(err, TCB_ERR_TIMEOUT);
   return false;
 }
@@ -345,46 +389,56 @@ __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t phase, int *err
 // ----------------------------------------------------------------- format bodies
 // A body consumes one work item of a staged chunk (a Q4_K/Q6_K block, or a
 // Q8_0/Q4_0 round of 8 blocks) for the tile's 16 rows: rows g and g+8 of
-// lane (g = lane/4, t = lane%4).  Float path: acc[4] accumulates
-// (row g, MMA column 2t), (g, 2t+1), (g+8, 2t), (g+8, 2t+1).  Int8 path:
-// the block terms go to tb[row * cbc + local block].
+// lane (g = lane/4, t = lane%4).  MMA column c carries scale group c: lane
+// g supplies the B operand of column g only, so each lane loads the digits
+// of its own group once and masks them with mk[c] = (g == c ? ~0 : 0).
+// Float path: acc[4] accumulates (row g, column 2t), (g, 2t+1),
+// (g+8, 2t), (g+8, 2t+1).  Int8 path: block terms go to
+// tb[row * cbc + local block].
 
 struct Lane {
   int g, t;
 };
 
-// B fragment of group G for MMA column `col`: only the lanes of that column
-// carry digits, the others stay zero.
-__device__ __forceinline__ uint2 bfrag8(const int8_t *plane, int G, int col, const Lane &L) {
-  uint2 b = make_uint2(0u, 0u);
-  if (L.g == col) b = *reinterpret_cast<const uint2 *>(plane + G * 32 + 8 * L.t);
-  return b;
-}
-
 // Q4_K block: 8 sub-blocks of 32, two per 32-byte code group
 template <bool ACT8>
 __device__ __forceinline__ void body_q4k(const uint8_t *r0, const uint8_t *r1, int bg, int lb, const Lane &L,
-                                         const uint8_t *xr, int K, float (&acc)[4], float *tb, int cbc) {
-  constexpr int ND = ACT8 ? 1 : 3;
+                                         const uint32_t (&mk)[8], const uint8_t *xr, int K, float (&acc)[4],
+                                         float *tb, int cbc) {
+  constexpr int ND = ACT8 ? 1 : 2;
   auto up = [](int v) { return (v + 15) & ~15; };
-  int D[ND][4];
+  uint2 own[ND];
 #pragma unroll
-  for (int p = 0; p < ND; p++) D[p][0] = D[p][1] = D[p][2] = D[p][3] = 0;
+  for (int p = 0; p < ND; p++)
+    own[p] = *reinterpret_cast<const uint2 *>(xr + p * K + (bg * 8 + L.g) * 32 + 8 * L.t);
+  // four independent accumulator chains per digit (the MMA latency is long):
+  // set (gq & 1) * 2 + h for code group gq, nibble half h.  Lane column 2t
+  // (2t+1) is written only by group gq = t, low (high) half.
+  int Ds[ND][4][4];
+#pragma unroll
+  for (int p = 0; p < ND; p++)
+#pragma unroll
+    for (int q = 0; q < 4; q++) Ds[p][q][0] = Ds[p][q][1] = Ds[p][q][2] = Ds[p][q][3] = 0;
 #pragma unroll
   for (int gq = 0; gq < 4; gq++) {
     const uint2 q0 = *reinterpret_cast<const uint2 *>(r0 + 16 + 32 * gq + 8 * L.t);
     const uint2 q1 = *reinterpret_cast<const uint2 *>(r1 + 16 + 32 * gq + 8 * L.t);
     const uint32_t la0 = q0.x & M4, la1 = q1.x & M4, la2 = q0.y & M4, la3 = q1.y & M4;
     const uint32_t ha0 = (q0.x >> 4) & M4, ha1 = (q1.x >> 4) & M4, ha2 = (q0.y >> 4) & M4, ha3 = (q1.y >> 4) & M4;
-    const int Glo = bg * 8 + 2 * gq;
 #pragma unroll
     for (int p = 0; p < ND; p++) {
-      const int8_t *plane = reinterpret_cast<const int8_t *>(xr) + p * K;
-      uint2 b = bfrag8(plane, Glo, 2 * gq, L);
-      imma_u8(D[p], la0, la1, la2, la3, b.x, b.y);
-      b = bfrag8(plane, Glo + 1, 2 * gq + 1, L);
-      imma_u8(D[p], ha0, ha1, ha2, ha3, b.x, b.y);
+      imma_u8(Ds[p][(gq & 1) * 2], la0, la1, la2, la3, own[p].x & mk[2 * gq], own[p].y & mk[2 * gq]);
+      imma_u8(Ds[p][(gq & 1) * 2 + 1], ha0, ha1, ha2, ha3, own[p].x & mk[2 * gq + 1], own[p].y & mk[2 * gq + 1]);
     }
+  }
+  const int odd = L.t & 1;
+  int D[ND][4];
+#pragma unroll
+  for (int p = 0; p < ND; p++) {
+    D[p][0] = odd ? Ds[p][2][0] : Ds[p][0][0];
+    D[p][1] = odd ? Ds[p][3][1] : Ds[p][1][1];
+    D[p][2] = odd ? Ds[p][2][2] : Ds[p][0][2];
+    D[p][3] = odd ? Ds[p][3][3] : Ds[p][1][3];
   }
   // scales of sub-blocks j = 2t, 2t+1 for rows g, g+8 (get_scale_min_k4)
   const uint4 h0 = *reinterpret_cast<const uint4 *>(r0);
@@ -405,14 +459,14 @@ __device__ __forceinline__ void body_q4k(const uint8_t *r0, const uint8_t *r1, i
     dm[r] = half_exact(h.x >> 16);
   }
   if constexpr (!ACT8) {
-    const float *sg = reinterpret_cast<const float *>(xr + up(3 * K));
+    const float *sg = reinterpret_cast<const float *>(xr + up(2 * K));
     const float *sx = sg + up(K / 32 * 4) / 4;
     const int G0 = bg * 8 + 2 * L.t;
     const float sg0 = sg[G0], sg1 = sg[G0 + 1], sx0 = sx[G0], sx1 = sx[G0 + 1];
 #pragma unroll
     for (int i = 0; i < 4; i++) {
       const int r = i >> 1, j = i & 1;
-      const float v = fmaf(fmaf((float)D[0][i], 254.0f, (float)D[1][i]), 254.0f, (float)D[2][i]);
+      const float v = (float)(D[0][i] * 254 + D[1][i]);  // |.| < 2^24: exact
       const float sc = (float)((sc2[r] >> (8 * j)) & 0xFFu), m = (float)((mm2[r] >> (8 * j)) & 0xFFu);
       acc[i] = fmaf(dd[r] * sc * (j ? sg1 : sg0), v, acc[i]);
       acc[i] = fmaf(-(dm[r] * m), j ? sx1 : sx0, acc[i]);
@@ -438,19 +492,31 @@ __device__ __forceinline__ void body_q4k(const uint8_t *r0, const uint8_t *r1, i
   }
 }
 
-// Q6_K block: 16 groups of 16 (k16 MMAs), two rounds (halves n = 0, 1)
+// Q6_K block: 16 groups of 16 (k16 MMAs), two rounds (halves n = 0, 1);
+// round n, column c = 2*cq + i holds group 8n + c
 template <bool ACT8>
 __device__ __forceinline__ void body_q6k(const uint8_t *r0, const uint8_t *r1, int bg, int lb, const Lane &L,
-                                         const uint8_t *xr, int K, float (&acc)[4], float *tb, int cbc) {
+                                         const uint32_t (&mk)[8], const uint8_t *xr, int K, float (&acc)[4],
+                                         float *tb, int cbc) {
   constexpr int ND = ACT8 ? 1 : 2;
   auto up = [](int v) { return (v + 15) & ~15; };
   int is[2] = {0, 0}, ms[2] = {0, 0};
   const float dd[2] = {half_exact(lds16(r0 + 208)), half_exact(lds16(r1 + 208))};
 #pragma unroll
   for (int n = 0; n < 2; n++) {
-    int D[ND][4];
+    // own group 8n + g: elements 128n + 32*(g/2) + 16*(g%2) + [0, 16)
+    uint32_t own[ND];
 #pragma unroll
-    for (int p = 0; p < ND; p++) D[p][0] = D[p][1] = D[p][2] = D[p][3] = 0;
+    for (int p = 0; p < ND; p++)
+      own[p] = *reinterpret_cast<const uint32_t *>(xr + p * K + bg * 256 + 128 * n + 32 * (L.g >> 1) +
+                                                    16 * (L.g & 1) + 4 * L.t);
+    // four accumulator chains per digit: set col & 3 for MMA column col;
+    // lane columns 2t, 2t+1 live in sets (2t) & 3, (2t+1) & 3
+    int Ds[ND][4][4];
+#pragma unroll
+    for (int p = 0; p < ND; p++)
+#pragma unroll
+      for (int q = 0; q < 4; q++) Ds[p][q][0] = Ds[p][q][1] = Ds[p][q][2] = Ds[p][q][3] = 0;
 #pragma unroll
     for (int i = 0; i < 2; i++) {
       const int off = 64 * n + 16 * i + 4 * L.t, offh = 128 + 32 * n + 16 * i + 4 * L.t;
@@ -466,16 +532,18 @@ __device__ __forceinline__ void body_q6k(const uint8_t *r0, const uint8_t *r1, i
       A1[2] = ((qa1 >> 4) & M4) | (qh1 & 0x30303030u);
       A1[3] = ((qb1 >> 4) & M4) | ((qh1 >> 2) & 0x30303030u);
 #pragma unroll
-      for (int cq = 0; cq < 4; cq++) {
-        const int col = 2 * cq + i;
-        const int e0 = bg * 256 + 128 * n + 32 * cq + 16 * i;  // first element of the group
+      for (int cq = 0; cq < 4; cq++)
 #pragma unroll
-        for (int p = 0; p < ND; p++) {
-          uint32_t b = 0;
-          if (L.g == col) b = *reinterpret_cast<const uint32_t *>(reinterpret_cast<const int8_t *>(xr) + p * K + e0 + 4 * L.t);
-          imma_u8_k16(D[p], A0[cq], A1[cq], b);
-        }
-      }
+        for (int p = 0; p < ND; p++) imma_u8_k16(Ds[p][(2 * cq + i) & 3], A0[cq], A1[cq], own[p] & mk[2 * cq + i]);
+    }
+    const int odd = L.t & 1;
+    int D[ND][4];
+#pragma unroll
+    for (int p = 0; p < ND; p++) {
+      D[p][0] = odd ? Ds[p][2][0] : Ds[p][0][0];
+      D[p][1] = odd ? Ds[p][3][1] : Ds[p][1][1];
+      D[p][2] = odd ? Ds[p][2][2] : Ds[p][0][2];
+      D[p][3] = odd ? Ds[p][3][3] : Ds[p][1][3];
     }
     // lane groups: j = 8n + 2t + jj, sc index 8n + 2t + jj
     const uint32_t scw0 = lds16(r0 + 192 + 8 * n + 2 * L.t), scw1 = lds16(r1 + 192 + 8 * n + 2 * L.t);
@@ -489,7 +557,7 @@ __device__ __forceinline__ void body_q6k(const uint8_t *r0, const uint8_t *r1, i
         const int r = ii >> 1, jj = ii & 1;
         const uint32_t scw = r ? scw1 : scw0;
         const float sc = (float)(int8_t)((scw >> (8 * jj)) & 0xFFu);
-        const float v = fmaf((float)D[0][ii], 254.0f, (float)D[1][ii]);
+        const float v = (float)(D[0][ii] * 254 + D[1][ii]);
         acc[ii] = fmaf(dd[r] * sc * sg[G0 + jj], fmaf(-32.0f, sd[G0 + jj], v), acc[ii]);
       }
     } else {
@@ -523,40 +591,50 @@ __device__ __forceinline__ void body_q6k(const uint8_t *r0, const uint8_t *r1, i
 // column j.  Rounds start 16-byte aligned (8 blocks = 272 / 144 bytes).
 template <int W, bool ACT8>
 __device__ __forceinline__ void body_q32(const uint8_t *s0, const uint8_t *s1, int bg0, int lb0, const Lane &L,
-                                         const uint8_t *xr, int K, float (&acc)[4], float *tb, int cbc) {
+                                         const uint32_t (&mk)[8], const uint8_t *xr, int K, float (&acc)[4],
+                                         float *tb, int cbc) {
   using P = Pol<W>;
-  constexpr int ND = ACT8 ? 1 : 3;
+  constexpr int ND = ACT8 ? 1 : 2;
   constexpr int B = P::B;
   auto up = [](int v) { return (v + 15) & ~15; };
-  int D[ND][4];
+  // own block bg0 + g: Q8_0 k-slots 4t.. <- codes 8t.., 4t+16.. <- 8t+4..;
+  // Q4_0 k-slots 4t.. <- low nibbles 4t.., 4t+16.. <- high nibbles (16+4t..)
+  uint2 own[ND];
 #pragma unroll
-  for (int p = 0; p < ND; p++) D[p][0] = D[p][1] = D[p][2] = D[p][3] = 0;
+  for (int p = 0; p < ND; p++) {
+    const uint8_t *pl = xr + p * K + (bg0 + L.g) * 32;
+    if constexpr (W == TCB_Q8_0) own[p] = *reinterpret_cast<const uint2 *>(pl + 8 * L.t);
+    else own[p] = make_uint2(*reinterpret_cast<const uint32_t *>(pl + 4 * L.t), *reinterpret_cast<const uint32_t *>(pl + 16 + 4 * L.t));
+  }
+  // four accumulator chains per digit: set j & 3 for block j of the round
+  int Ds[ND][4][4];
+#pragma unroll
+  for (int p = 0; p < ND; p++)
+#pragma unroll
+    for (int q = 0; q < 4; q++) Ds[p][q][0] = Ds[p][q][1] = Ds[p][q][2] = Ds[p][q][3] = 0;
 #pragma unroll
   for (int j = 0; j < 8; j++) {
     const uint8_t *b0 = s0 + j * B, *b1 = s1 + j * B;
-    const int G = bg0 + j;
     if constexpr (W == TCB_Q8_0) {
       const uint32_t w00 = lds32_a2(b0 + 2 + 8 * L.t), w01 = lds32_a2(b0 + 6 + 8 * L.t);
       const uint32_t w10 = lds32_a2(b1 + 2 + 8 * L.t), w11 = lds32_a2(b1 + 6 + 8 * L.t);
 #pragma unroll
-      for (int p = 0; p < ND; p++) {
-        const uint2 b = bfrag8(reinterpret_cast<const int8_t *>(xr) + p * K, G, j, L);
-        imma_s8(D[p], w00, w10, w01, w11, b.x, b.y);
-      }
+      for (int p = 0; p < ND; p++) imma_s8(Ds[p][j & 3], w00, w10, w01, w11, own[p].x & mk[j], own[p].y & mk[j]);
     } else {
       const uint32_t q0 = lds32_a2(b0 + 2 + 4 * L.t), q1 = lds32_a2(b1 + 2 + 4 * L.t);
       const uint32_t a0 = q0 & M4, a1 = q1 & M4, a2 = (q0 >> 4) & M4, a3 = (q1 >> 4) & M4;
 #pragma unroll
-      for (int p = 0; p < ND; p++) {
-        uint32_t bx = 0, by = 0;
-        if (L.g == j) {
-          const int8_t *pl = reinterpret_cast<const int8_t *>(xr) + p * K + G * 32;
-          bx = *reinterpret_cast<const uint32_t *>(pl + 4 * L.t);
-          by = *reinterpret_cast<const uint32_t *>(pl + 16 + 4 * L.t);
-        }
-        imma_u8(D[p], a0, a1, a2, a3, bx, by);
-      }
+      for (int p = 0; p < ND; p++) imma_u8(Ds[p][j & 3], a0, a1, a2, a3, own[p].x & mk[j], own[p].y & mk[j]);
     }
+  }
+  const int odd = L.t & 1;
+  int D[ND][4];
+#pragma unroll
+  for (int p = 0; p < ND; p++) {
+    D[p][0] = odd ? Ds[p][2][0] : Ds[p][0][0];
+    D[p][1] = odd ? Ds[p][3][1] : Ds[p][1][1];
+    D[p][2] = odd ? Ds[p][2][2] : Ds[p][0][2];
+    D[p][3] = odd ? Ds[p][3][3] : Ds[p][1][3];
   }
   // lane blocks: 2t, 2t+1 of the round, rows g, g+8
   float dw[4];
@@ -564,12 +642,12 @@ __device__ __forceinline__ void body_q32(const uint8_t *s0, const uint8_t *s1, i
   for (int i = 0; i < 4; i++) dw[i] = half_exact(lds16((i >> 1 ? s1 : s0) + (2 * L.t + (i & 1)) * B));
   const int G0 = bg0 + 2 * L.t;
   if constexpr (!ACT8) {
-    const float *sg = reinterpret_cast<const float *>(xr + up(3 * K));
+    const float *sg = reinterpret_cast<const float *>(xr + up(2 * K));
     const float *sd = sg + 2 * (up(K / 32 * 4) / 4);
 #pragma unroll
     for (int i = 0; i < 4; i++) {
       const int j = i & 1;
-      float v = fmaf(fmaf((float)D[0][i], 254.0f, (float)D[1][i]), 254.0f, (float)D[2][i]);
+      float v = (float)(D[0][i] * 254 + D[1][i]);
       if (W == TCB_Q4_0) v = fmaf(-8.0f, sd[G0 + j], v);
       acc[i] = fmaf(dw[i] * sg[G0 + j], v, acc[i]);
     }
@@ -589,19 +667,33 @@ __device__ __forceinline__ void body_q32(const uint8_t *s0, const uint8_t *s1, i
 }
 
 // ----------------------------------------------------------------- kernel
-// Shared memory: [full bars | empty bars | flag | warp partials | x region |
-// int8-path terms | stages].  CTA b owns tiles b, b + grid, ...
+// Warps: 0..15 compute, 16 produces (TMA), 17 finishes outputs.  The
+// compute warps run through the stages on their own (no CTA-wide barrier
+// per stage); tile partials (float path) and block terms (int8 path) reach
+// the epilogue warp through shared memory guarded by mbarriers.
+// Shared memory: [barriers (1 KB) | flag | tile partials | x region |
+// int8 terms | stages].  CTA b owns tiles b, b + grid, ...
+
+constexpr int kEpi = kConsumers + 1;      // epilogue warp
+constexpr int kWarpsAll = kConsumers + 2;
+constexpr int kPartSlots = 8;             // tile partial slots in flight
+constexpr int kBarBytes = 1024;
 
 template <int W, bool ACT8>
-__global__ void __launch_bounds__(kThreads, 2) k_mv1(const __grid_constant__ CUtensorMap tmap, const Params a) {
+__global__ void __launch_bounds__(32 * kWarpsAll, 1) k_mv1(const __grid_constant__ CUtensorMap tmap, const Params a) {
   using P = Pol<W>;
-  constexpr int pitch = P::BOX8 * 8, box_bytes = 16 * pitch;
+  constexpr int pitch = P::BOX8 * 8, box_bytes = 16 * pitch, NBOX = P::NBOX;
   extern __shared__ __align__(128) uint8_t sm[];
-  uint64_t *full = reinterpret_cast<uint64_t *>(sm), *empty = full + 8;
-  int *flag = reinterpret_cast<int *>(sm + 128);
-  float *part = reinterpret_cast<float *>(sm + 256);  // [kConsumers][16]
+  uint64_t *full = reinterpret_cast<uint64_t *>(sm);  // [S]     copy engine -> compute
+  uint64_t *empty = full + 8;                         // [S]     compute -> producer
+  uint64_t *sdone = full + 16;                        // [S]     int8 terms of a stage ready
+  uint64_t *sfree = full + 24;                        // [S]     int8 terms folded
+  uint64_t *tdone = full + 32;                        // [slots] tile partials ready
+  uint64_t *tfree = full + 40;                        // [slots] tile partials summed
+  int *flag = reinterpret_cast<int *>(sm + 512);
+  float *part = reinterpret_cast<float *>(sm + kBarBytes);  // [slots][kConsumers][16]
   uint8_t *xr = sm + a.xoff;
-  float *terms = reinterpret_cast<float *>(sm + a.toff);
+  float *terms = reinterpret_cast<float *>(sm + a.toff);  // [S][16][cbc]
   uint8_t *stages = sm + a.soff;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int stage_bytes = NBOX * box_bytes;
@@ -613,6 +705,12 @@ __global__ void __launch_bounds__(kThreads, 2) k_mv1(const __grid_constant__ CUt
     for (int s = 0; s < a.S; s++) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumers);
+      mbar_init(&sdone[s], kConsumers);
+      mbar_init(&sfree[s], 1);
+    }
+    for (int s = 0; s < kPartSlots; s++) {
+      mbar_init(&tdone[s], kConsumers);
+      mbar_init(&tfree[s], 1);
     }
     fence_barrier_init();
   }
@@ -626,7 +724,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_mv1(const __grid_constant__ CUt
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
       for (int it = 0; it < nstages; it++) {
         const int buf = it % a.S;
-        if (!wait_bar(&empty[buf], (uint32_t)(((it / a.S) & 1) ^ 1), a.err)) return;
+        if (!spin_bar(&empty[buf], (uint32_t)(((it / a.S) & 1) ^ 1), a.err)) return;
         const int tile = (int)blockIdx.x + (it / a.nch) * (int)gridDim.x, ch = it % a.nch;
         const int b0 = ch * a.cbc;
         const int nbox = min(NBOX, (a.nb - b0 + P::BPB - 1) / P::BPB);
@@ -639,69 +737,111 @@ __global__ void __launch_bounds__(kThreads, 2) k_mv1(const __grid_constant__ CUt
     return;
   }
 
-  // consumers: x (and c) may be written by the previous kernel of the stream
+  // compute and epilogue warps: x (and c) may be written by the previous
+  // kernel of the stream
   pdl_wait();
-  if constexpr (ACT8) prep_act8<W>(a, xr, flag);
-  else prep_float<W>(a, xr, flag);
-  consumers_sync();
+  if (warp < kConsumers) {
+    if constexpr (ACT8) prep_act8<W>(a, xr, flag);
+    else prep_float<W>(a, xr, flag);
+  }
+  asm volatile("bar.sync 1, %0;" ::"n"(32 * (kConsumers + 1)) : "memory");
   const bool slow = *flag != 0;
-  const Lane L{lane >> 2, lane & 3};
-  int it = 0;
-  for (int ti = 0; ti < my_tiles; ti++) {
-    const int tile = (int)blockIdx.x + ti * (int)gridDim.x;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    float frow = 0.f;  // int8 path: running fold of row `lane` (warp 0, lanes < 16)
-    for (int ch = 0; ch < a.nch; ch++, it++) {
-      const int buf = it % a.S;
-      if (!wait_bar(&full[buf], (uint32_t)((it / a.S) & 1), a.err)) return;
-      const uint8_t *st = stages + buf * stage_bytes;
-      const int b0 = ch * a.cbc, nblk = min(a.nb, b0 + a.cbc) - b0;
-      float *tb = terms + (it & 1) * 16 * a.cbc;
-      if (!slow) {
-        for (int lb = warp * P::RB; lb < nblk; lb += kConsumers * P::RB) {
-          const uint8_t *r0 = st + (lb / P::BPB) * box_bytes + L.g * pitch + (lb % P::BPB) * P::B;
-          const uint8_t *r1 = r0 + 8 * pitch;
-          if constexpr (W == TCB_Q4_K) body_q4k<ACT8>(r0, r1, b0 + lb, lb, L, xr, a.K, acc, tb, a.cbc);
-          else if constexpr (W == TCB_Q6_K) body_q6k<ACT8>(r0, r1, b0 + lb, lb, L, xr, a.K, acc, tb, a.cbc);
-          else body_q32<W, ACT8>(r0, r1, b0 + lb, lb, L, xr, a.K, acc, tb, a.cbc);
+
+  if (!slow && warp == kEpi) {
+    // epilogue: sum the sixteen warp partials of each tile in warp order
+    // (float path) or fold every block term in block order (int8 path)
+    int it = 0;
+    for (int ti = 0; ti < my_tiles; ti++) {
+      const int tile = (int)blockIdx.x + ti * (int)gridDim.x;
+      const int row = tile * 16 + lane;
+      const bool mine = lane < 16 && row < a.N;
+      const float cold = (a.accumulate && mine) ? load_out(a.c, row, a.cdt) : 0.f;
+      float v = 0.f;
+      if constexpr (!ACT8) {
+        const int slot = ti % kPartSlots;
+        if (!spin_bar(&tdone[slot], (uint32_t)((ti / kPartSlots) & 1), a.err)) return;
+        const float *pt = part + slot * kConsumers * 16;
+        if (lane < 16)
+#pragma unroll
+          for (int w2 = 0; w2 < kConsumers; w2++) v += pt[w2 * 16 + lane];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tfree[slot]);
+        it += a.nch;
+      } else {
+        for (int ch = 0; ch < a.nch; ch++, it++) {
+          const int buf = it % a.S;
+          if (!spin_bar(&sdone[buf], (uint32_t)((it / a.S) & 1), a.err)) return;
+          const int nblk = min(a.nb, (ch + 1) * a.cbc) - ch * a.cbc;
+          const float *tb = terms + buf * 16 * a.cbc;
+          if (lane < 16)
+            for (int lb = 0; lb < nblk; lb++) v = __fadd_rn(v, tb[lane * a.cbc + lb]);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sfree[buf]);
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[buf]);
-      if (ACT8 && !slow) {
-        consumers_sync();  // every term of this chunk is in tb
-        if (warp == 0 && lane < 16)
-          for (int lb = 0; lb < nblk; lb++) frow = __fadd_rn(frow, tb[lane * a.cbc + lb]);
-      }
+      if (mine) store_out_old(a.c, row, a.cdt, v, a.accumulate != 0, cold);
     }
-    if (slow) continue;
-    const int row = tile * 16 + lane;
-    if constexpr (!ACT8) {
-      float s0 = acc[0] + acc[1], s1 = acc[2] + acc[3];
-      s0 += __shfl_xor_sync(0xFFFFFFFFu, s0, 1);
-      s1 += __shfl_xor_sync(0xFFFFFFFFu, s1, 1);
-      s0 += __shfl_xor_sync(0xFFFFFFFFu, s0, 2);
-      s1 += __shfl_xor_sync(0xFFFFFFFFu, s1, 2);
-      if (L.t == 0) {
-        part[warp * 16 + L.g] = s0;
-        part[warp * 16 + L.g + 8] = s1;
-      }
-      consumers_sync();
-      if (warp == 0 && lane < 16 && row < a.N) {
-        float v = 0.f;
+    return;
+  }
+
+  if (warp < kConsumers) {
+    const Lane L{lane >> 2, lane & 3};
+    uint32_t mk[8];
 #pragma unroll
-        for (int w2 = 0; w2 < kConsumers; w2++) v += part[w2 * 16 + lane];
-        store_out(a.c, row, a.cdt, v, a.accumulate != 0);
+    for (int c = 0; c < 8; c++) mk[c] = L.g == c ? 0xFFFFFFFFu : 0u;
+    int it = 0;
+    for (int ti = 0; ti < my_tiles; ti++) {
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int ch = 0; ch < a.nch; ch++, it++) {
+        const int buf = it % a.S;
+        const uint32_t ph = (uint32_t)((it / a.S) & 1);
+        bool ok = true;
+        if (lane == 0) ok = wait_bar(&full[buf], ph, a.err);
+        if (ACT8 && !slow && lane == 0 && ok) ok = spin_bar(&sfree[buf], ph ^ 1, a.err);
+        if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) return;
+        if (!slow) {
+          const uint8_t *st = stages + buf * stage_bytes;
+          const int b0 = ch * a.cbc, nblk = min(a.nb, b0 + a.cbc) - b0;
+          float *tb = terms + buf * 16 * a.cbc;
+          for (int lb = warp * P::RB; lb < nblk; lb += kConsumers * P::RB) {
+            const uint8_t *r0 = st + (lb / P::BPB) * box_bytes + L.g * pitch + (lb % P::BPB) * P::B;
+            const uint8_t *r1 = r0 + 8 * pitch;
+            if constexpr (W == TCB_Q4_K) body_q4k<ACT8>(r0, r1, b0 + lb, lb, L, mk, xr, a.K, acc, tb, a.cbc);
+            else if constexpr (W == TCB_Q6_K) body_q6k<ACT8>(r0, r1, b0 + lb, lb, L, mk, xr, a.K, acc, tb, a.cbc);
+            else body_q32<W, ACT8>(r0, r1, b0 + lb, lb, L, mk, xr, a.K, acc, tb, a.cbc);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&empty[buf]);
+          if (ACT8 && !slow) mbar_arrive(&sdone[buf]);
+        }
       }
-      consumers_sync();
-    } else {
-      if (warp == 0 && lane < 16 && row < a.N) store_out(a.c, row, a.cdt, frow, a.accumulate != 0);
+      if (!ACT8 && !slow) {
+        float s0 = acc[0] + acc[1], s1 = acc[2] + acc[3];
+        s0 += __shfl_xor_sync(0xFFFFFFFFu, s0, 1);
+        s1 += __shfl_xor_sync(0xFFFFFFFFu, s1, 1);
+        s0 += __shfl_xor_sync(0xFFFFFFFFu, s0, 2);
+        s1 += __shfl_xor_sync(0xFFFFFFFFu, s1, 2);
+        const int slot = ti % kPartSlots;
+        bool ok = true;
+        if (lane == 0) ok = spin_bar(&tfree[slot], (uint32_t)(((ti / kPartSlots) & 1) ^ 1), a.err);
+        if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) return;
+        float *pt = part + slot * kConsumers * 16;
+        if (L.t == 0) {
+          pt[warp * 16 + L.g] = s0;
+          pt[warp * 16 + L.g + 8] = s1;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tdone[slot]);
+      }
     }
   }
   if (slow) {
     // NaN/Inf in x: TR's float path (the int8 path also falls back to it,
     // cpu_quant_q8.go:157-163), one warp per row
-    for (int n = (int)blockIdx.x * kConsumers + warp; n < a.N; n += (int)gridDim.x * kConsumers) {
+    const int widx = warp == kEpi ? kConsumers : warp;  // 0..16 over the compute and epilogue warps
+    for (int n = (int)blockIdx.x * (kConsumers + 1) + widx; n < a.N; n += (int)gridDim.x * (kConsumers + 1)) {
       float accs[1] = {0.0f};
       lane_row_float<W, 1>(a.w + (long)n * a.rowBytes, a.K, lane, XGlobal{a.x, 0, a.xdt}, accs);
       const float v = warp_sum(accs[0]);
@@ -717,7 +857,6 @@ __global__ void __launch_bounds__(kThreads, 2) k_mv1(const __grid_constant__ CUt
 namespace {
 
 constexpr int kSmemMax = 227 * 1024;
-constexpr int kSmemHalf = 113 * 1024;  // two CTAs per SM
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
@@ -775,7 +914,7 @@ cudaError_t plan_launch(const MvPlan &pl, const void *w, int N, int K, const voi
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.grid);
-  cfg.blockDim = dim3(mv::kThreads);
+  cfg.blockDim = dim3(32 * mv::kWarpsAll);
   cfg.dynamicSmemBytes = pl.smem;
   cfg.stream = s;
   cudaLaunchAttribute at[1];
@@ -795,21 +934,16 @@ MvPlan plan_w(int N, int K, const void *w, int sms) {
   if (rowBytes % 16 || reinterpret_cast<uintptr_t>(w) % 16 || nb == 0) return pl;
   if (P::RB == 8 && nb % 8) return pl;  // Q8_0 / Q4_0 rounds are 8 blocks
   if (!tensor_map_encoder()) return pl;
-  pl.cbc = mv::NBOX * P::BPB;
+  pl.cbc = P::NBOX * P::BPB;
   pl.nch = (nb + pl.cbc - 1) / pl.cbc;
   pl.pitch = P::BOX8 * 8;
-  pl.xoff = 1024;
+  pl.xoff = mv::kBarBytes + mv::kPartSlots * mv::kConsumers * 16 * 4;
   pl.toff = pl.xoff + ((mv::x_region_bytes<W, ACT8>(K) + 127) & ~127);
-  const int tbytes = ACT8 ? 2 * 16 * pl.cbc * 4 : 0;
-  pl.soff = (pl.toff + tbytes + 127) & ~127;
-  const int stage_bytes = mv::NBOX * 16 * pl.pitch;
-  // two stages when that leaves room for a second CTA on the SM: the next
-  // launch of the stream (programmatic serialization) then starts streaming
-  // its weights beside this one; otherwise as many stages as fit
-  int S = (kSmemHalf - pl.soff) / stage_bytes;
-  if (S >= 2) S = 2;
-  else S = (kSmemMax - pl.soff) / stage_bytes;
+  const int tbytes_per_stage = ACT8 ? 16 * pl.cbc * 4 : 0;
+  const int stage_bytes = P::NBOX * 16 * pl.pitch;
+  int S = (kSmemMax - pl.toff - 128) / (stage_bytes + tbytes_per_stage);
   if (S > 6) S = 6;
+  pl.soff = (pl.toff + S * tbytes_per_stage + 127) & ~127;
   if (S < 2) return pl;
   pl.stages = S;
   pl.smem = pl.soff + S * stage_bytes;
