@@ -37,7 +37,8 @@ typedef enum tcb_status {
   TCB_ERR_TIMEOUT = 7,     /* a bounded device-side wait gave up */
   TCB_ERR_UNSUPPORTED = 8, /* combination not provided (e.g. Q8_0 act8 off) */
   TCB_ERR_BOUNDS = 9,      /* an index outside the table */
-  TCB_ERR_SCALE = 10       /* a NaN/Inf block scale (tensor/quant.go:108-128) */
+  TCB_ERR_SCALE = 10,      /* a NaN/Inf block scale (tensor/quant.go:108-128) */
+  TCB_ERR_TOO_LARGE = 11   /* the problem does not fit the fixed static scratch */
 } tcb_status;
 
 /* weight block types (GGUF ids) */
@@ -124,6 +125,37 @@ int tcb_quant_zero(tcb_ctx *ctx, int wtype, void *dev, long nblocks,
 /* host-side scale check (CheckQuantScales); *bad_block = -1 if clean */
 int tcb_check_scales(int wtype, const void *host, size_t nbytes,
                      long *bad_block);
+
+/* Size of the device array that tcb_qgemm_act8_static works in. */
+#define TCB_STATIC_SCRATCH_BYTES (4u << 20)
+
+/* tcb_qgemm_act8 for callers that must not allocate device memory.
+ *
+ * No counterpart in TR: TR's int8-activation product runs on the CPU.
+ * This entry point exists for hosts that reserve all device memory up
+ * front or must never enter the CUDA allocator on this path (for example
+ * an embedding runtime with a fixed memory plan, or a caller on a
+ * latency-critical thread that must not take the allocator's locks).  It
+ * takes no context and calls no cudaMalloc, cudaFree or other allocating
+ * routine: the quantised activations live in one file-scope device array
+ * of TCB_STATIC_SCRATCH_BYTES that every GPU loading libtcb holds until the
+ * process exits.
+ *   - It runs on the calling thread's current device.  The first call on a
+ *     device looks up the array's device address (cudaGetSymbolAddress);
+ *     make that first call before any stream capture.
+ *   - Problems needing more than TCB_STATIC_SCRATCH_BYTES of scratch
+ *     (about 1.28 bytes per element of x, M*K in all) are refused with
+ *     TCB_ERR_TOO_LARGE before anything is launched.
+ *   - Every call shares the one array: calls whose work overlaps on the GPU
+ *     (different streams, or different host threads without ordering)
+ *     race and may return wrong results.  Order them on one stream.
+ *   - The array keeps the last call's contents; each call writes every
+ *     scratch byte it reads before reading it.
+ * Results are bit-identical to tcb_qgemm_act8 (same arguments, same
+ * int8-activation semantics, NaN/Inf rows on the float path). */
+int tcb_qgemm_act8_static(int wtype, int M, int N, int K, const void *w,
+                          const void *x, int xdtype, long ldx, void *c,
+                          int cdtype, long ldc, int accumulate, void *stream);
 
 #ifdef __cplusplus
 }

@@ -31,7 +31,7 @@ NAMES = {Q8_0: "q8_0", Q4_0: "q4_0", Q4_K: "q4_k", Q6_K: "q6_k"}
 STATUS = {
     0: "TCB_OK", 1: "TCB_ERR_NULL", 2: "TCB_ERR_DTYPE", 3: "TCB_ERR_SHAPE", 4: "TCB_ERR_ALIGN",
     5: "TCB_ERR_CUDA", 6: "TCB_ERR_NOMEM", 7: "TCB_ERR_TIMEOUT", 8: "TCB_ERR_UNSUPPORTED",
-    9: "TCB_ERR_BOUNDS", 10: "TCB_ERR_SCALE",
+    9: "TCB_ERR_BOUNDS", 10: "TCB_ERR_SCALE", 11: "TCB_ERR_TOO_LARGE",
 }
 
 
@@ -73,6 +73,7 @@ def lib() -> ctypes.CDLL:
     L.tcb_block_shape.argtypes = [I, ctypes.POINTER(I), ctypes.POINTER(I)]
     L.tcb_qgemm.argtypes = [P, I, I, I, I, P, P, I, Lg, P, I, Lg, I, P]
     L.tcb_qgemm_act8.argtypes = [P, I, I, I, I, P, P, I, Lg, P, I, Lg, I, P]
+    L.tcb_qgemm_act8_static.argtypes = [I, I, I, I, P, P, I, Lg, P, I, Lg, I, P]
     L.tcb_qdequant.argtypes = [P, I, P, Lg, P, I, P]
     L.tcb_qembed.argtypes = [P, I, P, Lg, I, P, I, P, P]
     L.tcb_quant_upload.argtypes = [P, I, P, Z, P, ctypes.POINTER(Lg), P]
@@ -203,3 +204,20 @@ def check_scales(wtype: int, host) -> int:
     if rc not in (0, 10):
         raise TcbError(rc, "tcb_check_scales")
     return bad.value
+
+
+STATIC_SCRATCH_BYTES = 4 << 20
+
+
+def qgemm_act8_static(wtype, w, x, c, accumulate=True, stream=None):
+    """tcb_qgemm_act8_static: Context.qgemm_act8 without a context, for
+    callers that must not allocate device memory; its scratch is a fixed
+    STATIC_SCRATCH_BYTES device array shared by all calls (order calls on
+    one stream).  Runs on the current CUDA device."""
+    M, K = x.shape
+    N = c.shape[1]
+    rc = lib().tcb_qgemm_act8_static(wtype, M, N, K, _ptr(w), _ptr(x), _dtype_code(x), x.stride(0), _ptr(c),
+                                     _dtype_code(c), c.stride(0), int(bool(accumulate)), _stream(stream))
+    if rc != 0:
+        raise TcbError(rc, "tcb_qgemm_act8_static")
+    return c

@@ -78,6 +78,9 @@ int run_matvec(tcb_ctx *ctx, int wtype, int act8, int M, int N, int K, const voi
   return e == cudaSuccess ? TCB_OK : cuda_fail(ctx, e);
 }
 
+}  // namespace
+
+namespace tcb {
 // the checks TR makes before the quant product (gpu/backend_quant.go:43-65,
 // tensor/quant.go:240-247, spec 15.51-15.53)
 int check_gemm_args(int wtype, int M, int N, int K, const void *w, const void *x, int xdt, long ldx, void *c,
@@ -95,6 +98,10 @@ int check_gemm_args(int wtype, int M, int N, int K, const void *w, const void *x
     return TCB_ERR_ALIGN;
   return TCB_OK;
 }
+}  // namespace tcb
+
+namespace {
+using tcb::check_gemm_args;
 
 // K == 0: the empty sum; GemmSet zeroes C, Gemm leaves it
 int empty_sum(tcb_ctx *ctx, int M, int N, void *c, int cdt, long ldc, int accumulate, cudaStream_t s) {
@@ -121,6 +128,7 @@ const char *tcb_strerror(int status) {
   case TCB_ERR_UNSUPPORTED: return "unsupported combination";
   case TCB_ERR_BOUNDS: return "index outside the table";
   case TCB_ERR_SCALE: return "NaN or Inf block scale";
+  case TCB_ERR_TOO_LARGE: return "problem larger than the static scratch (TCB_STATIC_SCRATCH_BYTES)";
   }
   return "unknown status";
 }

@@ -16,6 +16,9 @@ struct Act8Scratch {
   uint8_t *flags;  // [M][K/blk] 1 = block finite
 };
 size_t act8_scratch_bytes(int M, int K, int blk);
+// argument checks shared by the products' entry points (TCB_OK or an error)
+int check_gemm_args(int wtype, int M, int N, int K, const void *w, const void *x, int xdt, long ldx, void *c,
+                    int cdt, long ldc);
 Act8Scratch act8_scratch_carve(void *base, int M, int K, int blk);
 
 cudaError_t launch_dequant_rows(int wtype, const void *w, long rows, int D, const int64_t *idx, void *out,
