@@ -42,84 +42,12 @@
 
 #include "tcb_common.cuh"
 #include "tcb_matvec.h"
+#include "tcb_mv_ptx.cuh"
 #include "tcb_simt.cuh"
 
 namespace tcb {
 namespace mv {
 
-// ----------------------------------------------------------------- PTX
-
-__device__ __forceinline__ uint32_t sa(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(sa(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void fence_barrier_init() {
-  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sa(bar)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(sa(bar)), "r"(phase)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   sa(dst)),
-               "l"(src), "r"(bytes), "r"(sa(bar))
-               : "memory");
-}
-
-// 2-D tensor copy of one box into shared memory (no multicast)
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, int x, int y, uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-          "r"(sa(dst)),
-      "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(sa(bar))
-      : "memory");
-}
-__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
-// D += A(16x32 u8) * B(32x8 s8)
-__device__ __forceinline__ void imma_u8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                        uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-               : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-               : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-// D += A(16x32 s8) * B(32x8 s8)
-__device__ __forceinline__ void imma_s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                        uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-               : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-               : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-// D += A(16x16 u8) * B(16x8 s8)
-__device__ __forceinline__ void imma_u8_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
-  asm("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
-               : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-               : "r"(a0), "r"(a1), "r"(b0));
-}
-
-__device__ __forceinline__ uint32_t lds32(const uint8_t *p) { return *reinterpret_cast<const uint32_t *>(p); }
-__device__ __forceinline__ uint32_t lds16(const uint8_t *p) { return *reinterpret_cast<const uint16_t *>(p); }
-// 4 bytes at a 2-byte aligned shared address
-__device__ __forceinline__ uint32_t lds32_a2(const uint8_t *p) {
-  uintptr_t a = reinterpret_cast<uintptr_t>(p);
-  if ((a & 2) == 0) return lds32(p);
-  const uint8_t *q = p - 2;
-  return __byte_perm(lds32(q), lds32(q + 4), 0x5432);
-}
-
-constexpr uint32_t M4 = 0x0F0F0F0Fu;
 
 // ----------------------------------------------------------------- formats
 // GRP: elements per scale group (one MMA k); GPB: groups per block; RB:
@@ -341,50 +269,6 @@ __device__ void prep_act8(const Params &a, uint8_t *xr, int *flag) {
   }
 }
 
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sa(bar)) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t phase) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(sa(bar)), "r"(phase)
-      : "memory");
-  return ok != 0;
-}
-// try_wait with a suspend-time hint: the thread sleeps until the phase
-// completes (the copy engine's completion wakes it) or ~0.5 ms pass
-__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t *bar, uint32_t phase) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(sa(bar)), "r"(phase), "r"(500000u)
-      : "memory");
-  return ok != 0;
-}
-
-// a barrier completed by the copy engine (bounded: ~2 s at most)
-__device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t phase, int *err) {
-  for (uint32_t i = 0; i < 4096u; i++)
-    if (mbar_try_wait_hint(bar, phase)) return true;
-  atomicExch(err, TCB_ERR_TIMEOUT);
-  return false;
-}
-
-// A barrier completed by other warps' arrives: a sleeping try_wait is not
-// woken promptly by them, so poll with a short backoff (bounded: ~1 s).
-__device__ __forceinline__ bool spin_bar(uint64_t *bar, uint32_t phase, int *err) {
-  for (uint32_t i = 0; i < (1u << 24); i++) {
-    if (mbar_test_wait(bar, phase)) return true;
-    __nanosleep(32);
-  }
-  atomicExch(err, TCB_ERR_TIMEOUT);
-  return false;
-}
 
 // ----------------------------------------------------------------- format bodies
 // A body consumes one work item of a staged chunk (a Q4_K/Q6_K block, or a
@@ -858,20 +742,8 @@ namespace {
 
 constexpr int kSmemMax = 227 * 1024;
 
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-    void *p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      p = nullptr;
-    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }();
-  return fn;
-}
-
 // [N rows, rowBytes/8 eight-byte elements] view of the block store
-template <int W>
+template <int W, bool ACT8>
 bool encode_weight_map(CUtensorMap *tm, const void *w, int N, long rowBytes) {
   auto enc = tensor_map_encoder();
   if (!enc) return false;
@@ -936,7 +808,7 @@ MvPlan plan_w(int N, int K, const void *w, int sms) {
   if (!tensor_map_encoder()) return pl;
   pl.cbc = P::NBOX * P::BPB;
   pl.nch = (nb + pl.cbc - 1) / pl.cbc;
-  pl.pitch = P::BOX8 * 8;
+  pl.pitch = mv::Pol<W>::BOX8 * 8;
   pl.xoff = mv::kBarBytes + mv::kPartSlots * mv::kConsumers * 16 * 4;
   pl.toff = pl.xoff + ((mv::x_region_bytes<W, ACT8>(K) + 127) & ~127);
   const int tbytes_per_stage = ACT8 ? 16 * pl.cbc * 4 : 0;
@@ -950,7 +822,7 @@ MvPlan plan_w(int N, int K, const void *w, int sms) {
   pl.tiles = (N + 15) / 16;
   pl.grid = pl.tiles < sms ? pl.tiles : sms;
   CUtensorMap tm;
-  if (!encode_weight_map<W>(&tm, w, N, rowBytes)) return pl;
+  if (!encode_weight_map<W, ACT8>(&tm, w, N, rowBytes)) return pl;
   memcpy(pl.tmap, &tm, sizeof tm);
   pl.ok = true;
   return pl;
@@ -962,7 +834,7 @@ MvPlan matvec_plan(int wtype, int act8, int M, int N, int K, const void *w, int 
   MvPlan none{};
   if (M != 1 || N <= 0 || K <= 0) return none;
   switch (wtype) {
-  case TCB_Q4_K: return act8 ? plan_w<TCB_Q4_K, true>(N, K, w, sms) : plan_w<TCB_Q4_K, false>(N, K, w, sms);
+  case TCB_Q4_K: return act8 ? plan_w<TCB_Q4_K, true>(N, K, w, sms) : q4k_plan(N, K, w, sms);
   case TCB_Q6_K: return act8 ? plan_w<TCB_Q6_K, true>(N, K, w, sms) : plan_w<TCB_Q6_K, false>(N, K, w, sms);
   case TCB_Q8_0: return act8 ? plan_w<TCB_Q8_0, true>(N, K, w, sms) : plan_w<TCB_Q8_0, false>(N, K, w, sms);
   case TCB_Q4_0: return act8 ? plan_w<TCB_Q4_0, true>(N, K, w, sms) : plan_w<TCB_Q4_0, false>(N, K, w, sms);
@@ -975,6 +847,7 @@ cudaError_t matvec_launch(const MvPlan &pl, int wtype, int act8, int N, int K, c
 #define TCB_MV(WT)                                                                             \
   return act8 ? plan_launch<WT, true>(pl, w, N, K, x, xdt, c, cdt, accumulate, err, s)        \
               : plan_launch<WT, false>(pl, w, N, K, x, xdt, c, cdt, accumulate, err, s)
+  if (pl.kind == 1) return q4k_launch(pl, N, K, w, x, xdt, c, cdt, accumulate, err, s);
   switch (wtype) {
   case TCB_Q4_K: TCB_MV(TCB_Q4_K);
   case TCB_Q6_K: TCB_MV(TCB_Q6_K);

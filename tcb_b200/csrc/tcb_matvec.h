@@ -10,7 +10,8 @@ namespace tcb {
 // shape is not taken by it (the caller then runs the portable kernel)
 struct MvPlan {
   bool ok;
-  int tiles, cbc, nch;         // 16-row tiles, blocks per staged chunk, chunks per row
+  int kind;                    // 0: generic kernel (16-row tiles), 1: Q4_K float kernel (32-row tiles)
+  int tiles, cbc, nch;         // tiles, blocks per staged chunk, chunks per row
   int stages, pitch;           // TMA stages, bytes per staged row
   int xoff, toff, soff, smem;  // shared-memory layout
   int grid;
@@ -18,6 +19,11 @@ struct MvPlan {
 };
 
 MvPlan matvec_plan(int wtype, int act8, int M, int N, int K, const void *w, int sms);
+
+// Q4_K float path (kind 1)
+MvPlan q4k_plan(int N, int K, const void *w, int sms);
+cudaError_t q4k_launch(const MvPlan &pl, int N, int K, const void *w, const void *x, int xdt, void *c, int cdt,
+                       int accumulate, int *err, cudaStream_t s);
 
 cudaError_t matvec_launch(const MvPlan &pl, int wtype, int act8, int N, int K, const void *w, const void *x, int xdt,
                           void *c, int cdt, int accumulate, int *err, cudaStream_t s);
