@@ -126,6 +126,59 @@ int tcb_quant_zero(tcb_ctx *ctx, int wtype, void *dev, long nblocks,
 int tcb_check_scales(int wtype, const void *host, size_t nbytes,
                      long *bad_block);
 
+/* ---- Llama-shaped decoder, batch 1 (the callers either side of the path) ----
+ *
+ * A decode step of TR's GPT (lib/layers.tr: GPT.single_step 658-666, block
+ * residuals 348-389, RMSNorm 68-79, rotary table and apply_rotary 85-107,
+ * grouped-query causal attention 126-215, merged SwiGLU 224-276) over
+ * quantized weights,
+ * with an fp16 KV cache.  Every launch of a step runs on the caller's stream
+ * and the step can be captured once into a CUDA graph: the current token,
+ * the position and the prompt live on the device, so a prompt and the
+ * greedy continuation are the same graph replayed, with no host round trip.
+ * Weights are device block stores ([rows, K] GGUF blocks); the engine keeps
+ * the pointers (the caller owns and keeps the memory). */
+typedef struct tcb_llama tcb_llama;
+
+typedef struct tcb_llama_config {
+  int n_layers, d_model, n_heads, n_kv_heads, head_dim, ffn_dim, vocab;
+  int max_ctx;        /* KV-cache positions (prompt + generated) */
+  float eps;          /* RMSNorm epsilon */
+  float rope_theta;   /* rotary frequency base */
+} tcb_llama_config;
+
+typedef struct tcb_llama_weights {
+  const void *tok_emb;  int tok_emb_type;  /* [vocab, d] blocks */
+  const float *final_norm;                  /* [d] */
+  const void *head;     int head_type;      /* [vocab, d] blocks */
+  /* arrays of n_layers pointers */
+  const float *const *attn_norm;            /* [d] */
+  const float *const *ffn_norm;             /* [d] */
+  const void *const *qkv;  int qkv_type;    /* [(H + 2*KVH)*hd, d]: q rows, k rows, v rows */
+  const void *const *o;    int o_type;      /* [d, H*hd] */
+  const void *const *gate_up; int gate_up_type; /* [2*ffn, d]: gate rows, then up rows */
+  const void *const *down; int down_type;   /* [d, ffn] */
+} tcb_llama_weights;
+
+int tcb_llama_create(tcb_ctx *ctx, const tcb_llama_config *cfg, const tcb_llama_weights *w, tcb_llama **out);
+int tcb_llama_destroy(tcb_llama *m);
+/* Start a sequence: copies the n prompt token ids (host, n >= 1) to the
+ * device and sets position 0 with prompt[0] as the current token.  Steps
+ * 0..n-2 then feed the prompt; later steps feed their own greedy token. */
+int tcb_llama_start(tcb_llama *m, const int64_t *prompt, int n, void *stream);
+/* One step: embed the current token, run every layer at the current
+ * position (appending its K/V), score the vocabulary, take the greedy
+ * token (first maximum), store it at tokens[pos + 1], advance.  Replays the
+ * captured graph when tcb_llama_capture has made one. */
+int tcb_llama_step(tcb_llama *m, void *stream);
+/* Capture one step into a CUDA graph (on a stream of the engine's own,
+ * after the caller's stream has drained); tcb_llama_step replays it on the
+ * caller's stream from then on. */
+int tcb_llama_capture(tcb_llama *m, void *stream);
+/* Device pointers of the token history (int64 [max_ctx]) and the logits of
+ * the last step (float [vocab]). */
+int tcb_llama_buffers(tcb_llama *m, int64_t **tokens, float **logits);
+
 /* Size of the device array that tcb_qgemm_act8_static works in. */
 #define TCB_STATIC_SCRATCH_BYTES (4u << 20)
 

@@ -11,17 +11,9 @@
 #include "../../include/tcb.h"
 #include "tcb_common.cuh"
 #include "tcb_launch.h"
+#include "tcb_ctx.h"
 #include "tcb_matvec.h"
 
-struct tcb_ctx {
-  int dev = 0;
-  int sms = 148;
-  void *ws = nullptr;  // scratch owned by the context, grown on demand
-  size_t ws_cap = 0;
-  int *derr = nullptr;  // device error word (bounded waits that gave up)
-  std::mutex mu;
-  char err[256] = {0};
-};
 
 namespace {
 

@@ -1,0 +1,16 @@
+// tcb_ctx.h - the context behind the opaque tcb_ctx handle (internal).
+#pragma once
+
+#include <stddef.h>
+
+#include <mutex>
+
+struct tcb_ctx {
+  int dev = 0;
+  int sms = 148;
+  void *ws = nullptr;  // scratch owned by the context, grown on demand
+  size_t ws_cap = 0;
+  int *derr = nullptr;  // device error word (bounded waits that gave up)
+  std::mutex mu;
+  char err[256] = {0};
+};

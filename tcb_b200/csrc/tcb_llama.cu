@@ -1,0 +1,606 @@
+// tcb_llama.cu - batch-1 decode step of a Llama-shaped model over quantized
+// weights: the callers on either side of the quantized product (embedding
+// lookup, RMSNorm, rotary position, grouped-query attention over an fp16 KV
+// cache, SwiGLU, greedy token) around the batch-1 matvec kernels.
+//
+// Follows TR's GPT (lib/layers.tr): x = embed(token); per block
+// h = x + attn(rms(x)); x = h + ffn(rms(h)) (348-389); logits =
+// head(rms(x)) (658-666).  RMSNorm is x / sqrt(mean(x^2) + eps) * w
+// (68-79); the rotary table uses theta^(-2i/hd) and rotates the two halves
+// (a, b) of a head to (a cos - b sin, a sin + b cos) (85-107); attention is
+// causal softmax(q.k / sqrt(hd)) v with consecutive query heads sharing a KV
+// head (126-215); the merged SwiGLU is silu(g) * u over [G | U] (224-276).
+// The K/V cache is fp16.
+//
+// Every step runs on the caller's stream.  The current token, the position
+// and the prompt live in device memory, so one captured CUDA graph serves
+// every step of a sequence (prompt feeding and greedy decoding alike).  The
+// launches use programmatic dependent launch: each kernel waits
+// (griddepcontrol.wait) before reading what the previous kernel wrote, and
+// lets the next kernel start its independent prologue (the weight stream of
+// a matvec) early.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <stdio.h>
+
+#include <utility>
+#include <vector>
+
+#include "../../include/tcb.h"
+#include "tcb_common.cuh"
+#include "tcb_ctx.h"
+#include "tcb_launch.h"
+#include "tcb_matvec.h"
+#include "tcb_mv_ptx.cuh"
+
+namespace tcb {
+namespace ll {
+
+constexpr int kHd = 128;        // head dimension supported by the attention kernel
+constexpr int kChunk = 128;     // positions per attention CTA (4 warps x 32 lanes)
+constexpr int kArgBlocks = 148;
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_add(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+
+// out = x / sqrt(mean(x^2) + eps) * w   (one CTA)
+__global__ void k_rmsnorm(const float *x, const float *w, float *out, int D, float eps) {
+  __shared__ float red[32];
+  mv::pdl_wait();
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
+  ss = warp_add(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    v = warp_add(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  mv::pdl_launch_dependents();
+  const float s = sqrtf(__fdiv_rn(red[0], (float)D) + eps);
+  for (int i = threadIdx.x; i < D; i += blockDim.x) out[i] = __fmul_rn(__fdiv_rn(x[i], s), w[i]);
+}
+
+// Rotary position on q (heads 0..H-1, in place) and k (heads H..H+KVH-1,
+// into the fp16 cache); v (heads H+KVH..) into the fp16 cache; all at *pos.
+// CTA per head.
+__global__ void k_rope_cache(float *qkv, const float *cosT, const float *sinT, const int *pos, __half *kc,
+                             __half *vc, int H, int KVH, int hd, int max_ctx) {
+  mv::pdl_wait();
+  const int p = *pos, half = hd / 2, head = blockIdx.x;
+  float *row = qkv + (size_t)head * hd;
+  if (head < H + KVH) {
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+      const float a = row[i], b = row[i + half], c = cosT[(size_t)p * half + i], s = sinT[(size_t)p * half + i];
+      const float ra = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+      const float rb = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+      if (head < H) {
+        row[i] = ra;
+        row[i + half] = rb;
+      } else {
+        __half *k = kc + ((size_t)(head - H) * max_ctx + p) * hd;
+        k[i] = __float2half_rn(ra);
+        k[i + half] = __float2half_rn(rb);
+      }
+    }
+  } else {
+    __half *v = vc + ((size_t)(head - H - KVH) * max_ctx + p) * hd;
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) v[i] = __float2half_rn(row[i]);
+  }
+  mv::pdl_launch_dependents();
+}
+
+// Attention of the G query heads of KV head blockIdx.x over the positions
+// [blockIdx.y * 128, +128) that are <= *pos: lane = position for the scores
+// (a whole K row per lane), then the probabilities are broadcast per
+// position for V (lane = 4 dimensions).  Writes the chunk's (max, sum,
+// unnormalised output) per query head to part[h][chunk][2 + hd].
+template <int G>
+__global__ void __launch_bounds__(128) k_attn_part(const float *q, const __half *kc, const __half *vc, const int *pos,
+                                                   float *part, int max_ctx, int nch_max, float scale) {
+  __shared__ float qs[G][kHd];
+  __shared__ float ps[4][G][32];
+  __shared__ float wm[4][G], wl[4][G];
+  __shared__ float wo[4][G][kHd];
+  mv::pdl_wait();
+  const int n = *pos + 1, kh = blockIdx.x, c = blockIdx.y, t0 = c * kChunk;
+  if (t0 >= n) return;
+  for (int i = threadIdx.x; i < G * kHd; i += blockDim.x) qs[i / kHd][i % kHd] = q[(size_t)kh * G * kHd + i];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tw = t0 + warp * 32;  // first position of this warp
+  if (tw < n) {
+    const int t = tw + lane;
+    float s[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) s[g] = 0.f;
+    if (t < n) {
+      const __half *kr = kc + ((size_t)kh * max_ctx + t) * kHd;
+#pragma unroll 4
+      for (int d = 0; d < kHd; d += 8) {
+        const uint4 raw = *reinterpret_cast<const uint4 *>(kr + d);
+        const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
+        float kv[8];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const float2 f = __half22float2(h2[j]);
+          kv[2 * j] = f.x;
+          kv[2 * j + 1] = f.y;
+        }
+#pragma unroll
+        for (int g = 0; g < G; g++)
+#pragma unroll
+          for (int j = 0; j < 8; j++) s[g] = fmaf(qs[g][d + j], kv[j], s[g]);
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+      const float sv = t < n ? s[g] * scale : -INFINITY;
+      const float m = warp_max(sv);
+      const float e = t < n ? __expf(sv - m) : 0.f;
+      const float l = warp_add(e);
+      ps[warp][g][lane] = e;
+      if (lane == 0) {
+        wm[warp][g] = m;
+        wl[warp][g] = l;
+      }
+    }
+    __syncwarp();
+    float o[G][4];
+#pragma unroll
+    for (int g = 0; g < G; g++) o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
+    const int nt = min(32, n - tw);
+    for (int j = 0; j < nt; j++) {
+      const uint2 raw = *reinterpret_cast<const uint2 *>(vc + ((size_t)kh * max_ctx + tw + j) * kHd + 4 * lane);
+      const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
+      const float2 v01 = __half22float2(h2[0]), v23 = __half22float2(h2[1]);
+#pragma unroll
+      for (int g = 0; g < G; g++) {
+        const float pj = ps[warp][g][j];
+        o[g][0] = fmaf(pj, v01.x, o[g][0]);
+        o[g][1] = fmaf(pj, v01.y, o[g][1]);
+        o[g][2] = fmaf(pj, v23.x, o[g][2]);
+        o[g][3] = fmaf(pj, v23.y, o[g][3]);
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++)
+#pragma unroll
+      for (int i = 0; i < 4; i++) wo[warp][g][4 * lane + i] = o[g][i];
+  } else if (lane < G) {
+    wm[warp][lane] = -INFINITY;
+    wl[warp][lane] = 0.f;
+  }
+  __syncthreads();
+  mv::pdl_launch_dependents();
+  for (int i = threadIdx.x; i < G * kHd; i += blockDim.x) {
+    const int g = i / kHd, d = i % kHd;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; w++) M = fmaxf(M, wm[w][g]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; w++) {
+      if (t0 + w * 32 >= n) continue;
+      const float f = __expf(wm[w][g] - M);
+      L = fmaf(wl[w][g], f, L);
+      O = fmaf(wo[w][g][d], f, O);
+    }
+    float *pp = part + ((size_t)(kh * G + g) * nch_max + c) * (2 + kHd);
+    pp[2 + d] = O;
+    if (d == 0) {
+      pp[0] = M;
+      pp[1] = L;
+    }
+  }
+}
+
+// out[h] = sum over chunks of the partial outputs, rescaled to the global
+// maximum, divided by the total sum.  CTA per query head.
+__global__ void k_attn_combine(const float *part, const int *pos, float *out, int nch_max) {
+  mv::pdl_wait();
+  const int h = blockIdx.x, n = *pos + 1, nch = (n + kChunk - 1) / kChunk;
+  const float *ph = part + (size_t)h * nch_max * (2 + kHd);
+  float M = -INFINITY;
+  for (int c = 0; c < nch; c++) M = fmaxf(M, ph[(size_t)c * (2 + kHd)]);
+  mv::pdl_launch_dependents();
+  for (int d = threadIdx.x; d < kHd; d += blockDim.x) {
+    float L = 0.f, O = 0.f;
+    for (int c = 0; c < nch; c++) {
+      const float *pc = ph + (size_t)c * (2 + kHd);
+      const float f = __expf(pc[0] - M);
+      L = fmaf(pc[1], f, L);
+      O = fmaf(pc[2 + d], f, O);
+    }
+    out[(size_t)h * kHd + d] = __fdiv_rn(O, L);
+  }
+}
+
+// a = silu(g) * u over the merged [G | U] rows
+__global__ void k_swiglu(const float *gu, float *a, int F) {
+  mv::pdl_wait();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  mv::pdl_launch_dependents();
+  if (i < F) {
+    const float g = gu[i], u = gu[F + i];
+    a[i] = __fmul_rn(__fmul_rn(g, __frcp_rn(__fadd_rn(1.0f, expf(-g)))), u);
+  }
+}
+
+// (max, first index) per CTA
+__global__ void k_argmax_part(const float *v, int n, float *pm, int *pi) {
+  __shared__ float sm_v[32];
+  __shared__ int sm_i[32];
+  mv::pdl_wait();
+  float best = -INFINITY;
+  int bi = 0x7FFFFFFF;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const float x = v[i];
+    if (x > best) {
+      best = x;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+    const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+    if (ob > best || (ob == best && oi < bi)) {
+      best = ob;
+      bi = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sm_v[threadIdx.x >> 5] = best;
+    sm_i[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  mv::pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++)
+      if (sm_v[w] > best || (sm_v[w] == best && sm_i[w] < bi)) {
+        best = sm_v[w];
+        bi = sm_i[w];
+      }
+    pm[blockIdx.x] = best;
+    pi[blockIdx.x] = bi;
+  }
+}
+
+// The next token: the prompt's next id while the prompt lasts, else the
+// first maximum of the logits; recorded at tokens[pos + 1]; pos advances.
+__global__ void k_next_token(const float *pm, const int *pi, int nb, int *pos, int64_t *tok, int64_t *hist,
+                             const int64_t *prompt, const int *nprompt, int max_ctx) {
+  mv::pdl_wait();
+  if (threadIdx.x != 0) return;
+  float best = -INFINITY;
+  int bi = 0;
+  bool any = false;
+  for (int b = 0; b < nb; b++)
+    if (pi[b] != 0x7FFFFFFF && (!any || pm[b] > best || (pm[b] == best && pi[b] < bi))) {
+      best = pm[b];
+      bi = pi[b];
+      any = true;
+    }
+  const int p = *pos;
+  const int64_t next = (p + 1 < *nprompt) ? prompt[p + 1] : (int64_t)bi;
+  if (p + 1 < max_ctx) hist[p + 1] = next;
+  *tok = next;
+  *pos = p + 1;
+  mv::pdl_launch_dependents();
+}
+
+template <typename... Exp, typename... Act>
+cudaError_t launch(void (*k)(Exp...), dim3 grid, dim3 block, cudaStream_t s, Act &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, std::forward<Act>(args)...);
+}
+
+}  // namespace ll
+}  // namespace tcb
+
+// ----------------------------------------------------------------- engine
+
+namespace {
+
+struct Mat {
+  const void *w = nullptr;
+  int type = 0, N = 0, K = 0;
+  tcb::MvPlan plan{};
+};
+
+}  // namespace
+
+struct tcb_llama {
+  tcb_ctx *ctx = nullptr;
+  tcb_llama_config cfg{};
+  const void *tok_emb = nullptr;
+  int tok_emb_type = 0;
+  const float *final_norm = nullptr;
+  std::vector<const float *> attn_norm, ffn_norm;
+  Mat head;
+  std::vector<Mat> qkv, o, gu, down;
+  // device state
+  float *x = nullptr, *h = nullptr, *qkvb = nullptr, *att = nullptr, *gub = nullptr, *a = nullptr, *logits = nullptr;
+  float *part = nullptr, *am_v = nullptr, *cosT = nullptr, *sinT = nullptr;
+  int *am_i = nullptr, *pos = nullptr, *nprompt = nullptr;
+  __half *kc = nullptr, *vc = nullptr;
+  int64_t *tok = nullptr, *hist = nullptr, *prompt = nullptr;
+  int nch_max = 0;
+  int host_pos = 0;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  cudaStream_t cap = nullptr;  // capture stream (the caller's may be the legacy default stream)
+  std::vector<void *> allocs;
+};
+
+namespace {
+
+int fail(tcb_llama *m, cudaError_t e) {
+  if (m && m->ctx) snprintf(m->ctx->err, sizeof m->ctx->err, "%s", cudaGetErrorString(e));
+  return TCB_ERR_CUDA;
+}
+
+template <class T>
+cudaError_t alloc(tcb_llama *m, T **p, size_t n) {
+  void *q = nullptr;
+  cudaError_t e = cudaMalloc(&q, n * sizeof(T) + 16);
+  if (e == cudaSuccess) {
+    m->allocs.push_back(q);
+    *p = static_cast<T *>(q);
+  }
+  return e;
+}
+
+bool wtype_ok(int t) { return t == TCB_Q4_0 || t == TCB_Q8_0 || t == TCB_Q4_K || t == TCB_Q6_K; }
+
+Mat make_mat(const void *w, int type, int N, int K, int sms) {
+  Mat mt;
+  mt.w = w;
+  mt.type = type;
+  mt.N = N;
+  mt.K = K;
+  mt.plan = tcb::matvec_plan(type, 0, 1, N, K, w, sms);
+  return mt;
+}
+
+// y (+)= W x for one row of activations (f32 in, f32 out)
+cudaError_t matvec(tcb_llama *m, const Mat &mt, const float *x, float *y, int accumulate, cudaStream_t s) {
+  if (mt.plan.ok)
+    return tcb::matvec_launch(mt.plan, mt.type, 0, mt.N, mt.K, mt.w, x, TCB_F32, y, TCB_F32, accumulate,
+                              m->ctx->derr, s);
+  return tcb::launch_qgemm_simt(mt.type, mt.w, 1, mt.N, mt.K, x, TCB_F32, mt.K, y, TCB_F32, mt.N, accumulate,
+                                m->ctx->sms, s);
+}
+
+cudaError_t issue_step(tcb_llama *m, cudaStream_t s) {
+  using namespace tcb::ll;
+  const tcb_llama_config &c = m->cfg;
+  const int H = c.n_heads, KVH = c.n_kv_heads, hd = c.head_dim, D = c.d_model, F = c.ffn_dim;
+  const int G = H / KVH;
+  const float scale = 1.0f / sqrtf((float)hd);
+  const size_t cache_layer = (size_t)KVH * c.max_ctx * hd;
+  cudaError_t e = tcb::launch_dequant_rows(m->tok_emb_type, m->tok_emb, 1, D, m->tok, m->x, TCB_F32, m->ctx->sms, s);
+  for (int l = 0; l < c.n_layers && e == cudaSuccess; l++) {
+    __half *kc = m->kc + l * cache_layer, *vc = m->vc + l * cache_layer;
+    if ((e = launch(k_rmsnorm, dim3(1), dim3(1024), s, m->x, m->attn_norm[l], m->h, D, c.eps)) != cudaSuccess) break;
+    if ((e = matvec(m, m->qkv[l], m->h, m->qkvb, 0, s)) != cudaSuccess) break;
+    if ((e = launch(k_rope_cache, dim3(H + 2 * KVH), dim3(64), s, m->qkvb, m->cosT, m->sinT, m->pos, kc, vc, H, KVH,
+                    hd, c.max_ctx)) != cudaSuccess)
+      break;
+    const dim3 ag(KVH, m->nch_max);
+    switch (G) {
+    case 1: e = launch(k_attn_part<1>, ag, dim3(128), s, m->qkvb, kc, vc, m->pos, m->part, c.max_ctx, m->nch_max, scale); break;
+    case 2: e = launch(k_attn_part<2>, ag, dim3(128), s, m->qkvb, kc, vc, m->pos, m->part, c.max_ctx, m->nch_max, scale); break;
+    case 4: e = launch(k_attn_part<4>, ag, dim3(128), s, m->qkvb, kc, vc, m->pos, m->part, c.max_ctx, m->nch_max, scale); break;
+    case 8: e = launch(k_attn_part<8>, ag, dim3(128), s, m->qkvb, kc, vc, m->pos, m->part, c.max_ctx, m->nch_max, scale); break;
+    default: e = cudaErrorInvalidValue;
+    }
+    if (e != cudaSuccess) break;
+    if ((e = launch(k_attn_combine, dim3(H), dim3(128), s, m->part, m->pos, m->att, m->nch_max)) != cudaSuccess) break;
+    if ((e = matvec(m, m->o[l], m->att, m->x, 1, s)) != cudaSuccess) break;
+    if ((e = launch(k_rmsnorm, dim3(1), dim3(1024), s, m->x, m->ffn_norm[l], m->h, D, c.eps)) != cudaSuccess) break;
+    if ((e = matvec(m, m->gu[l], m->h, m->gub, 0, s)) != cudaSuccess) break;
+    if ((e = launch(k_swiglu, dim3((F + 255) / 256), dim3(256), s, m->gub, m->a, F)) != cudaSuccess) break;
+    e = matvec(m, m->down[l], m->a, m->x, 1, s);
+  }
+  if (e != cudaSuccess) return e;
+  if ((e = launch(k_rmsnorm, dim3(1), dim3(1024), s, m->x, m->final_norm, m->h, D, c.eps)) != cudaSuccess) return e;
+  if ((e = matvec(m, m->head, m->h, m->logits, 0, s)) != cudaSuccess) return e;
+  if ((e = launch(k_argmax_part, dim3(kArgBlocks), dim3(256), s, m->logits, c.vocab, m->am_v, m->am_i)) != cudaSuccess)
+    return e;
+  return launch(k_next_token, dim3(1), dim3(32), s, m->am_v, m->am_i, kArgBlocks, m->pos, m->tok, m->hist, m->prompt,
+                m->nprompt, c.max_ctx);
+}
+
+}  // namespace
+
+extern "C" {
+
+int tcb_llama_create(tcb_ctx *ctx, const tcb_llama_config *cfg, const tcb_llama_weights *w, tcb_llama **out) {
+  if (!ctx || !cfg || !w || !out) return TCB_ERR_NULL;
+  *out = nullptr;
+  const tcb_llama_config &c = *cfg;
+  if (c.n_layers < 1 || c.d_model < 1 || c.n_heads < 1 || c.n_kv_heads < 1 || c.head_dim != tcb::ll::kHd ||
+      c.n_heads % c.n_kv_heads || c.ffn_dim < 1 || c.vocab < 1 || c.max_ctx < 2 || !(c.eps > 0.f) ||
+      !(c.rope_theta > 0.f))
+    return TCB_ERR_SHAPE;
+  const int G = c.n_heads / c.n_kv_heads;
+  if (G != 1 && G != 2 && G != 4 && G != 8) return TCB_ERR_UNSUPPORTED;
+  if (!w->tok_emb || !w->final_norm || !w->head || !w->attn_norm || !w->ffn_norm || !w->qkv || !w->o ||
+      !w->gate_up || !w->down)
+    return TCB_ERR_NULL;
+  if (!wtype_ok(w->tok_emb_type) || !wtype_ok(w->head_type) || !wtype_ok(w->qkv_type) || !wtype_ok(w->o_type) ||
+      !wtype_ok(w->gate_up_type) || !wtype_ok(w->down_type))
+    return TCB_ERR_DTYPE;
+  const int D = c.d_model, H = c.n_heads, KVH = c.n_kv_heads, hd = c.head_dim, F = c.ffn_dim;
+  auto kok = [](int type, int K) { return K % tcb::block_elems(type) == 0; };
+  if (!kok(w->tok_emb_type, D) || !kok(w->head_type, D) || !kok(w->qkv_type, D) || !kok(w->o_type, H * hd) ||
+      !kok(w->gate_up_type, D) || !kok(w->down_type, F))
+    return TCB_ERR_SHAPE;
+  cudaError_t e = cudaSetDevice(ctx->dev);
+  if (e != cudaSuccess) return TCB_ERR_CUDA;
+  tcb_llama *m = new tcb_llama();
+  m->ctx = ctx;
+  m->cfg = c;
+  m->tok_emb = w->tok_emb;
+  m->tok_emb_type = w->tok_emb_type;
+  m->final_norm = w->final_norm;
+  m->head = make_mat(w->head, w->head_type, c.vocab, D, ctx->sms);
+  for (int l = 0; l < c.n_layers; l++) {
+    if (!w->attn_norm[l] || !w->ffn_norm[l] || !w->qkv[l] || !w->o[l] || !w->gate_up[l] || !w->down[l]) {
+      tcb_llama_destroy(m);
+      return TCB_ERR_NULL;
+    }
+    m->attn_norm.push_back(w->attn_norm[l]);
+    m->ffn_norm.push_back(w->ffn_norm[l]);
+    m->qkv.push_back(make_mat(w->qkv[l], w->qkv_type, (H + 2 * KVH) * hd, D, ctx->sms));
+    m->o.push_back(make_mat(w->o[l], w->o_type, D, H * hd, ctx->sms));
+    m->gu.push_back(make_mat(w->gate_up[l], w->gate_up_type, 2 * F, D, ctx->sms));
+    m->down.push_back(make_mat(w->down[l], w->down_type, D, F, ctx->sms));
+  }
+  m->nch_max = (c.max_ctx + tcb::ll::kChunk - 1) / tcb::ll::kChunk;
+  const size_t cache = (size_t)c.n_layers * KVH * c.max_ctx * hd;
+  const int qkvn = (H + 2 * KVH) * hd;
+  if ((e = alloc(m, &m->x, D)) != cudaSuccess || (e = alloc(m, &m->h, D)) != cudaSuccess ||
+      (e = alloc(m, &m->qkvb, qkvn)) != cudaSuccess || (e = alloc(m, &m->att, H * hd)) != cudaSuccess ||
+      (e = alloc(m, &m->gub, 2 * (size_t)F)) != cudaSuccess || (e = alloc(m, &m->a, F)) != cudaSuccess ||
+      (e = alloc(m, &m->logits, c.vocab)) != cudaSuccess ||
+      (e = alloc(m, &m->part, (size_t)H * m->nch_max * (2 + hd))) != cudaSuccess ||
+      (e = alloc(m, &m->am_v, tcb::ll::kArgBlocks)) != cudaSuccess ||
+      (e = alloc(m, &m->am_i, tcb::ll::kArgBlocks)) != cudaSuccess ||
+      (e = alloc(m, &m->cosT, (size_t)c.max_ctx * hd / 2)) != cudaSuccess ||
+      (e = alloc(m, &m->sinT, (size_t)c.max_ctx * hd / 2)) != cudaSuccess || (e = alloc(m, &m->kc, cache)) != cudaSuccess ||
+      (e = alloc(m, &m->vc, cache)) != cudaSuccess || (e = alloc(m, &m->pos, 1)) != cudaSuccess ||
+      (e = alloc(m, &m->nprompt, 1)) != cudaSuccess || (e = alloc(m, &m->tok, 1)) != cudaSuccess ||
+      (e = alloc(m, &m->hist, c.max_ctx)) != cudaSuccess || (e = alloc(m, &m->prompt, c.max_ctx)) != cudaSuccess) {
+    tcb_llama_destroy(m);
+    return e == cudaErrorMemoryAllocation ? TCB_ERR_NOMEM : TCB_ERR_CUDA;
+  }
+  // rotary table (TR's rotary_table: theta^(-2i/hd) in double, then float32
+  // angles t * f and their cosine / sine)
+  const int half = hd / 2;
+  std::vector<float> ct((size_t)c.max_ctx * half), st((size_t)c.max_ctx * half);
+  for (int i = 0; i < half; i++) {
+    const float f = (float)pow((double)c.rope_theta, -2.0 * i / hd);
+    for (int t = 0; t < c.max_ctx; t++) {
+      const float ang = (float)t * f;
+      ct[(size_t)t * half + i] = (float)cos((double)ang);
+      st[(size_t)t * half + i] = (float)sin((double)ang);
+    }
+  }
+  if ((e = cudaMemcpy(m->cosT, ct.data(), ct.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
+      (e = cudaMemcpy(m->sinT, st.data(), st.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
+      (e = cudaMemset(m->kc, 0, cache * 2)) != cudaSuccess || (e = cudaMemset(m->vc, 0, cache * 2)) != cudaSuccess) {
+    tcb_llama_destroy(m);
+    return TCB_ERR_CUDA;
+  }
+  *out = m;
+  return TCB_OK;
+}
+
+int tcb_llama_destroy(tcb_llama *m) {
+  if (!m) return TCB_ERR_NULL;
+  if (m->exec) cudaGraphExecDestroy(m->exec);
+  if (m->graph) cudaGraphDestroy(m->graph);
+  if (!m->allocs.empty()) cudaDeviceSynchronize();
+  if (m->cap) cudaStreamDestroy(m->cap);
+  for (void *p : m->allocs) cudaFree(p);
+  delete m;
+  return TCB_OK;
+}
+
+int tcb_llama_start(tcb_llama *m, const int64_t *prompt, int n, void *stream) {
+  if (!m || !prompt) return TCB_ERR_NULL;
+  if (n < 1 || n > m->cfg.max_ctx) return TCB_ERR_SHAPE;
+  for (int i = 0; i < n; i++)
+    if (prompt[i] < 0 || prompt[i] >= m->cfg.vocab) return TCB_ERR_BOUNDS;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int zero = 0;
+  cudaError_t e;
+  // synchronous copies from pageable host memory: the caller's buffers may
+  // go away after the call
+  if ((e = cudaSetDevice(m->ctx->dev)) != cudaSuccess || (e = cudaStreamSynchronize(s)) != cudaSuccess ||
+      (e = cudaMemcpy(m->prompt, prompt, (size_t)n * 8, cudaMemcpyHostToDevice)) != cudaSuccess ||
+      (e = cudaMemcpy(m->hist, prompt, 8, cudaMemcpyHostToDevice)) != cudaSuccess ||
+      (e = cudaMemcpy(m->tok, prompt, 8, cudaMemcpyHostToDevice)) != cudaSuccess ||
+      (e = cudaMemcpy(m->nprompt, &n, 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
+      (e = cudaMemcpy(m->pos, &zero, 4, cudaMemcpyHostToDevice)) != cudaSuccess)
+    return fail(m, e);
+  m->host_pos = 0;
+  return TCB_OK;
+}
+
+int tcb_llama_step(tcb_llama *m, void *stream) {
+  if (!m) return TCB_ERR_NULL;
+  if (m->host_pos + 1 >= m->cfg.max_ctx) return TCB_ERR_BOUNDS;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = m->exec ? cudaGraphLaunch(m->exec, s) : issue_step(m, s);
+  if (e != cudaSuccess) return fail(m, e);
+  m->host_pos++;
+  return TCB_OK;
+}
+
+int tcb_llama_capture(tcb_llama *m, void *stream) {
+  if (!m) return TCB_ERR_NULL;
+  cudaError_t e = cudaSetDevice(m->ctx->dev);
+  if (e == cudaSuccess && !m->cap) e = cudaStreamCreateWithFlags(&m->cap, cudaStreamNonBlocking);
+  // the capture stream starts after the caller's work
+  if (e == cudaSuccess) e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(m, e);
+  cudaStream_t s = m->cap;
+  if (m->exec) {
+    cudaGraphExecDestroy(m->exec);
+    m->exec = nullptr;
+  }
+  if (m->graph) {
+    cudaGraphDestroy(m->graph);
+    m->graph = nullptr;
+  }
+  e = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
+  if (e != cudaSuccess) return fail(m, e);
+  cudaError_t ei = issue_step(m, s);
+  cudaGraph_t g = nullptr;
+  e = cudaStreamEndCapture(s, &g);
+  if (ei != cudaSuccess || e != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    return fail(m, ei != cudaSuccess ? ei : e);
+  }
+  m->graph = g;
+  if ((e = cudaGraphInstantiate(&m->exec, g, 0)) != cudaSuccess) {
+    m->exec = nullptr;
+    return fail(m, e);
+  }
+  return TCB_OK;
+}
+
+int tcb_llama_buffers(tcb_llama *m, int64_t **tokens, float **logits) {
+  if (!m || !tokens || !logits) return TCB_ERR_NULL;
+  *tokens = m->hist;
+  *logits = m->logits;
+  return TCB_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,233 @@
+"""Llama-shaped batch-1 decoder over quantized weights (include/tcb.h,
+tcb_llama_*): a thin ctypes view plus seeded synthetic models.
+
+Layout of a model's weights (all device tensors):
+  tok_emb   [vocab, d]            Q4_K blocks
+  qkv[l]    [(H + 2 KVH) hd, d]   Q4_K   (q rows, then k rows, then v rows)
+  o[l]      [d, H hd]             Q6_K
+  gate_up[l][2 ffn, d]            Q4_K   (gate rows, then up rows)
+  down[l]   [d, ffn]              Q6_K
+  head      [vocab, d]            Q6_K
+  attn_norm[l], ffn_norm[l], final_norm: float32 [d]
+This is the Q4_K_M assignment of the benchmark's 8B configuration (Q4_K for
+attention and MLP weights, Q6_K for o_proj, down_proj and the head).
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import BLOCK, Q4_K, Q6_K, TcbError, _stream, lib
+from . import synth
+
+
+@dataclass(frozen=True)
+class LlamaConfig:
+    n_layers: int
+    d_model: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    ffn_dim: int
+    vocab: int
+    max_ctx: int
+    eps: float = 1e-5
+    rope_theta: float = 500000.0
+
+
+LLAMA3_8B = LlamaConfig(32, 4096, 32, 8, 128, 14336, 128256, 768)
+TYPES = {"tok_emb": Q4_K, "qkv": Q4_K, "o": Q6_K, "gate_up": Q4_K, "down": Q6_K, "head": Q6_K}
+# Standard deviation of the fp16 block scales of a random-init decoder.  The
+# matvec benchmark's |N(0, 0.01)| scales give weights of standard deviation
+# 2.6 (Q4_K) and 13 (Q6_K), and 32 such layers overflow float32; these give
+# weights of standard deviation ~0.02 (TR's default init_std, layers.tr
+# Linear), so activations stay of order one through the stack.
+D_STD = {Q4_K: 7.6e-5, Q6_K: 1.5e-5}
+
+
+def shapes(cfg: LlamaConfig) -> dict:
+    """(rows, K) of every quantized tensor kind."""
+    H, KVH, hd, D, F = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.d_model, cfg.ffn_dim
+    return {"tok_emb": (cfg.vocab, D), "qkv": ((H + 2 * KVH) * hd, D), "o": (D, H * hd),
+            "gate_up": (2 * F, D), "down": (D, F), "head": (cfg.vocab, D)}
+
+
+def weight_bytes_per_token(cfg: LlamaConfig) -> int:
+    """Quantized weight bytes a decode step streams (every layer + head + one
+    embedding row)."""
+    sh = shapes(cfg)
+    tot = 0
+    for k in ("qkv", "o", "gate_up", "down"):
+        n, kk = sh[k]
+        tot += cfg.n_layers * n * kk // BLOCK[TYPES[k]][0] * BLOCK[TYPES[k]][1]
+    n, kk = sh["head"]
+    tot += n * kk // 256 * BLOCK[Q6_K][1]
+    tot += cfg.d_model // 256 * BLOCK[Q4_K][1]
+    return tot
+
+
+def host_model(cfg: LlamaConfig, seed: int) -> dict:
+    """Seeded model as numpy arrays (small configurations: parity tests)."""
+    sh = shapes(cfg)
+    m = {"cfg": cfg}
+    rng = np.random.default_rng(seed)
+    s = seed * 1000
+    m["tok_emb"] = synth.weight(TYPES["tok_emb"], *sh["tok_emb"], s + 1, D_STD[TYPES["tok_emb"]])
+    m["head"] = synth.weight(TYPES["head"], *sh["head"], s + 2, D_STD[TYPES["head"]])
+    m["final_norm"] = (1.0 + 0.1 * rng.standard_normal(cfg.d_model)).astype(np.float32)
+    for k in ("attn_norm", "ffn_norm"):
+        m[k] = [(1.0 + 0.1 * rng.standard_normal(cfg.d_model)).astype(np.float32) for _ in range(cfg.n_layers)]
+    for j, k in enumerate(("qkv", "o", "gate_up", "down")):
+        m[k] = [synth.weight(TYPES[k], *sh[k], s + 10 + 4 * l + j, D_STD[TYPES[k]]) for l in range(cfg.n_layers)]
+    return m
+
+
+def device_model(cfg: LlamaConfig, seed: int, host: dict | None = None) -> dict:
+    """The model on cuda:0: uploads `host` if given, else generates the
+    blocks on the GPU (fp16 block scales |N(0, D_STD)|, every other byte
+    uniform, as host_model)."""
+    import torch
+
+    def up(a):
+        return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+    if host is not None:
+        d = {"cfg": cfg}
+        for k, v in host.items():
+            if k == "cfg":
+                continue
+            d[k] = [up(x) for x in v] if isinstance(v, list) else up(v)
+        return d
+    sh = shapes(cfg)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
+
+    def blocks(kind):
+        wt = TYPES[kind]
+        n, k = sh[kind]
+        e, size = BLOCK[wt]
+        nb = n * k // e
+        out = torch.randint(0, 256, (nb, size), dtype=torch.uint8, device="cuda", generator=gen)
+        if wt == Q4_K:
+            out[:, 0:4] = (torch.randn(nb, 2, device="cuda", generator=gen).abs() * D_STD[wt]).half().view(torch.uint8)
+        elif wt == Q6_K:
+            out[:, 208:210] = (torch.randn(nb, 1, device="cuda", generator=gen).abs() * D_STD[wt]).half().view(torch.uint8)
+        return out.reshape(-1)
+
+    def norm():
+        return 1.0 + 0.1 * torch.randn(cfg.d_model, device="cuda", generator=gen)
+
+    d = {"cfg": cfg, "tok_emb": blocks("tok_emb"), "head": blocks("head"), "final_norm": norm()}
+    d["attn_norm"] = [norm() for _ in range(cfg.n_layers)]
+    d["ffn_norm"] = [norm() for _ in range(cfg.n_layers)]
+    for k in ("qkv", "o", "gate_up", "down"):
+        d[k] = [blocks(k) for _ in range(cfg.n_layers)]
+    return d
+
+
+class _Cfg(ctypes.Structure):
+    _fields_ = [("n_layers", ctypes.c_int), ("d_model", ctypes.c_int), ("n_heads", ctypes.c_int),
+                ("n_kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int), ("ffn_dim", ctypes.c_int),
+                ("vocab", ctypes.c_int), ("max_ctx", ctypes.c_int), ("eps", ctypes.c_float),
+                ("rope_theta", ctypes.c_float)]
+
+
+_PP = ctypes.POINTER(ctypes.c_void_p)
+
+
+class _Weights(ctypes.Structure):
+    _fields_ = [("tok_emb", ctypes.c_void_p), ("tok_emb_type", ctypes.c_int), ("final_norm", ctypes.c_void_p),
+                ("head", ctypes.c_void_p), ("head_type", ctypes.c_int), ("attn_norm", _PP), ("ffn_norm", _PP),
+                ("qkv", _PP), ("qkv_type", ctypes.c_int), ("o", _PP), ("o_type", ctypes.c_int),
+                ("gate_up", _PP), ("gate_up_type", ctypes.c_int), ("down", _PP), ("down_type", ctypes.c_int)]
+
+
+def _bind():
+    L = lib()
+    if getattr(L, "_llama_bound", False):
+        return L
+    P = ctypes.c_void_p
+    L.tcb_llama_create.argtypes = [P, ctypes.POINTER(_Cfg), ctypes.POINTER(_Weights), ctypes.POINTER(P)]
+    L.tcb_llama_destroy.argtypes = [P]
+    L.tcb_llama_start.argtypes = [P, P, ctypes.c_int, P]
+    L.tcb_llama_step.argtypes = [P, P]
+    L.tcb_llama_capture.argtypes = [P, P]
+    L.tcb_llama_buffers.argtypes = [P, ctypes.POINTER(P), ctypes.POINTER(P)]
+    L._llama_bound = True
+    return L
+
+
+class Llama:
+    """A decoder engine over a device model (keeps the model alive)."""
+
+    def __init__(self, ctx, model: dict):
+        L = _bind()
+        cfg = model["cfg"]
+        self.cfg, self.model, self._L = cfg, model, L
+        c = _Cfg(cfg.n_layers, cfg.d_model, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn_dim, cfg.vocab,
+                 cfg.max_ctx, cfg.eps, cfg.rope_theta)
+
+        def arr(ts):
+            return (ctypes.c_void_p * len(ts))(*[t.data_ptr() for t in ts])
+
+        self._arrs = {k: arr(model[k]) for k in ("attn_norm", "ffn_norm", "qkv", "o", "gate_up", "down")}
+        w = _Weights(model["tok_emb"].data_ptr(), TYPES["tok_emb"], model["final_norm"].data_ptr(),
+                     model["head"].data_ptr(), TYPES["head"],
+                     ctypes.cast(self._arrs["attn_norm"], _PP), ctypes.cast(self._arrs["ffn_norm"], _PP),
+                     ctypes.cast(self._arrs["qkv"], _PP), TYPES["qkv"], ctypes.cast(self._arrs["o"], _PP),
+                     TYPES["o"], ctypes.cast(self._arrs["gate_up"], _PP), TYPES["gate_up"],
+                     ctypes.cast(self._arrs["down"], _PP), TYPES["down"])
+        h = ctypes.c_void_p()
+        self._check(L.tcb_llama_create(ctx.handle, ctypes.byref(c), ctypes.byref(w), ctypes.byref(h)), "create")
+        self._h = h
+        self._ctx = ctx
+
+    def _check(self, rc, what):
+        if rc != 0:
+            err = TcbError(rc, f"tcb_llama_{what}")
+            if rc == 5:
+                err.args = (err.args[0] + ": " + self._L.tcb_last_cuda_error(self._ctx.handle).decode(),)
+            raise err
+
+    def start(self, prompt, stream=None):
+        p = np.ascontiguousarray(prompt, dtype=np.int64)
+        self._check(self._L.tcb_llama_start(self._h, p.ctypes.data, p.size, _stream(stream)), "start")
+
+    def step(self, n: int = 1, stream=None):
+        s = _stream(stream)
+        for _ in range(n):
+            self._check(self._L.tcb_llama_step(self._h, s), "step")
+
+    def capture(self, stream=None):
+        self._check(self._L.tcb_llama_capture(self._h, _stream(stream)), "capture")
+
+    def _buffers(self):
+        t, lg = ctypes.c_void_p(), ctypes.c_void_p()
+        self._check(self._L.tcb_llama_buffers(self._h, ctypes.byref(t), ctypes.byref(lg)), "buffers")
+        return t.value, lg.value
+
+    def _download(self, ptr: int, out: np.ndarray, stream=None) -> np.ndarray:
+        rc = self._L.tcb_quant_download(self._ctx.handle, ptr, out.nbytes, out.ctypes.data, _stream(stream))
+        self._check(rc, "download")
+        return out
+
+    def tokens(self, n: int, stream=None) -> np.ndarray:
+        """The first n entries of the token history (prompt, then greedy)."""
+        return self._download(self._buffers()[0], np.empty(n, np.int64), stream)
+
+    def logits(self, stream=None) -> np.ndarray:
+        """The logits of the last step."""
+        return self._download(self._buffers()[1], np.empty(self.cfg.vocab, np.float32), stream)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._L.tcb_llama_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -34,8 +34,10 @@ def pack_q4k_scales(sc: np.ndarray, m: np.ndarray) -> np.ndarray:
     return q
 
 
-def blocks(wtype: int, nblocks: int, seed: int) -> np.ndarray:
-    """nblocks blocks of wtype as a flat uint8 array."""
+def blocks(wtype: int, nblocks: int, seed: int, d_std: float | None = None) -> np.ndarray:
+    """nblocks blocks of wtype as a flat uint8 array; d_std replaces the
+    standard deviation of the K-quant fp16 block scales (Q4_K d and dmin,
+    Q6_K d) when given."""
     rng = np.random.default_rng(seed)
     e, size = BLOCK[wtype]
     out = np.empty((nblocks, size), np.uint8)
@@ -46,24 +48,25 @@ def blocks(wtype: int, nblocks: int, seed: int) -> np.ndarray:
         out[:, 0:2] = _f16_bytes(np.abs(rng.normal(0, 0.02, nblocks)) / 127)
         out[:, 2:] = rng.integers(0, 256, (nblocks, 16), dtype=np.uint8)
     elif wtype == Q4_K:
-        out[:, 0:2] = _f16_bytes(np.abs(rng.normal(0, 0.01, nblocks)))
-        out[:, 2:4] = _f16_bytes(np.abs(rng.normal(0, 0.01, nblocks)))
+        ds = 0.01 if d_std is None else d_std
+        out[:, 0:2] = _f16_bytes(np.abs(rng.normal(0, ds, nblocks)))
+        out[:, 2:4] = _f16_bytes(np.abs(rng.normal(0, ds, nblocks)))
         out[:, 4:16] = pack_q4k_scales(rng.integers(0, 64, (nblocks, 8)), rng.integers(0, 64, (nblocks, 8)))
         out[:, 16:] = rng.integers(0, 256, (nblocks, 128), dtype=np.uint8)
     elif wtype == Q6_K:
         out[:, 0:192] = rng.integers(0, 256, (nblocks, 192), dtype=np.uint8)
         out[:, 192:208] = rng.integers(-128, 128, (nblocks, 16), dtype=np.int8).view(np.uint8)
-        out[:, 208:210] = _f16_bytes(np.abs(rng.normal(0, 0.01, nblocks)))
+        out[:, 208:210] = _f16_bytes(np.abs(rng.normal(0, 0.01 if d_std is None else d_std, nblocks)))
     else:
         raise ValueError(wtype)
     return out.reshape(-1)
 
 
-def weight(wtype: int, N: int, K: int, seed: int) -> np.ndarray:
+def weight(wtype: int, N: int, K: int, seed: int, d_std: float | None = None) -> np.ndarray:
     """An [N, K] weight as its block store."""
     e, _ = BLOCK[wtype]
     assert K % e == 0
-    return blocks(wtype, N * K // e, seed)
+    return blocks(wtype, N * K // e, seed, d_std)
 
 
 def activations(M: int, K: int, seed: int) -> np.ndarray:
