@@ -41,7 +41,7 @@ namespace tcb {
 namespace ll {
 
 constexpr int kHd = 128;        // head dimension supported by the attention kernel
-constexpr int kChunk = 128;     // positions per attention CTA (4 warps x 32 lanes)
+constexpr int kChunk = 64;      // positions per attention CTA
 constexpr int kArgBlocks = 148;
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -75,159 +75,193 @@ __global__ void k_rmsnorm(const float *x, const float *w, float *out, int D, flo
   for (int i = threadIdx.x; i < D; i += blockDim.x) out[i] = __fmul_rn(__fdiv_rn(x[i], s), w[i]);
 }
 
-// Rotary position on q (heads 0..H-1, in place) and k (heads H..H+KVH-1,
-// into the fp16 cache); v (heads H+KVH..) into the fp16 cache; all at *pos.
-// CTA per head.
-__global__ void k_rope_cache(float *qkv, const float *cosT, const float *sinT, const int *pos, __half *kc,
-                             __half *vc, int H, int KVH, int hd, int max_ctx) {
-  mv::pdl_wait();
-  const int p = *pos, half = hd / 2, head = blockIdx.x;
-  float *row = qkv + (size_t)head * hd;
-  if (head < H + KVH) {
-    for (int i = threadIdx.x; i < half; i += blockDim.x) {
-      const float a = row[i], b = row[i + half], c = cosT[(size_t)p * half + i], s = sinT[(size_t)p * half + i];
-      const float ra = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
-      const float rb = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
-      if (head < H) {
-        row[i] = ra;
-        row[i + half] = rb;
-      } else {
-        __half *k = kc + ((size_t)(head - H) * max_ctx + p) * hd;
-        k[i] = __float2half_rn(ra);
-        k[i + half] = __float2half_rn(rb);
-      }
-    }
-  } else {
-    __half *v = vc + ((size_t)(head - H - KVH) * max_ctx + p) * hd;
-    for (int i = threadIdx.x; i < hd; i += blockDim.x) v[i] = __float2half_rn(row[i]);
-  }
-  mv::pdl_launch_dependents();
-}
-
-// Attention of the G query heads of KV head blockIdx.x over the positions
-// [blockIdx.y * 128, +128) that are <= *pos: lane = position for the scores
-// (a whole K row per lane), then the probabilities are broadcast per
-// position for V (lane = 4 dimensions).  Writes the chunk's (max, sum,
-// unnormalised output) per query head to part[h][chunk][2 + hd].
+// One layer's attention at position *pos: CTA (KV head blockIdx.x, chunk
+// blockIdx.y of kChunk positions), 256 threads.  Every K and V byte of the
+// chunk is requested right after the dependency wait (K: thread = (position
+// t/4, 32 dimensions (t%4)*32); V: thread = (dimensions (t%32)*4, positions
+// t/32 + 8j)), so a layer costs one memory round trip.  The CTA rotates the
+// query rows of its G query heads; the CTA whose chunk holds pos also
+// rotates the new key, stores it and the new value into the fp16 cache and
+// uses them from shared memory for that position.  Each CTA writes its
+// chunk's (max, sum, unnormalised output) per query head; the last CTA of a
+// KV head to finish (a counter per KV head, reset by that CTA) merges the
+// chunks in chunk order, so the result does not depend on timing.
 template <int G>
-__global__ void __launch_bounds__(128) k_attn_part(const float *q, const __half *kc, const __half *vc, const int *pos,
-                                                   float *part, int max_ctx, int nch_max, float scale) {
+__global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cosT, const float *sinT, const int *pos,
+                                              __half *kc, __half *vc, float *part, unsigned *count, float *out, int H,
+                                              int KVH, int max_ctx, int nch_max, float scale) {
+  constexpr int half = kHd / 2;
   __shared__ float qs[G][kHd];
-  __shared__ float ps[4][G][32];
-  __shared__ float wm[4][G], wl[4][G];
-  __shared__ float wo[4][G][kHd];
+  __shared__ float knew[kHd], vnew[kHd];
+  __shared__ float sc[G][kChunk];
+  __shared__ float gm[G], gl[G];
+  __shared__ float wo[8][G][kHd];
+  __shared__ int last;
   mv::pdl_wait();
-  const int n = *pos + 1, kh = blockIdx.x, c = blockIdx.y, t0 = c * kChunk;
+  const int p = *pos, n = p + 1, kh = blockIdx.x, c = blockIdx.y, t0 = c * kChunk;
   if (t0 >= n) return;
-  for (int i = threadIdx.x; i < G * kHd; i += blockDim.x) qs[i / kHd][i % kHd] = q[(size_t)kh * G * kHd + i];
+  const int tid = threadIdx.x;
+  const __half *kbase = kc + (size_t)kh * max_ctx * kHd, *vbase = vc + (size_t)kh * max_ctx * kHd;
+  // K: position tk, dims 32*sk..; V: dims 4*(tid%32).., positions tv + 8j
+  const int tk = t0 + (tid >> 2), sk = tid & 3, dv = 4 * (tid & 31), tv = t0 + (tid >> 5);
+  uint4 kr[4];
+  uint2 vr[kChunk / 8];
+  const bool kok = tk < n && tk != p;
+  if (kok) {
+#pragma unroll
+    for (int j = 0; j < 4; j++) kr[j] = __ldcg(reinterpret_cast<const uint4 *>(kbase + (size_t)tk * kHd + 32 * sk) + j);
+  }
+#pragma unroll
+  for (int j = 0; j < kChunk / 8; j++) {
+    const int t = tv + 8 * j;
+    if (t < n && t != p) vr[j] = __ldcg(reinterpret_cast<const uint2 *>(vbase + (size_t)t * kHd + dv));
+  }
+  const float *cs = cosT + (size_t)p * half, *sn = sinT + (size_t)p * half;
+  for (int i = tid; i < G * half; i += blockDim.x) {
+    const int g = i / half, j = i % half;
+    const float *row = qkv + (size_t)(kh * G + g) * kHd;
+    const float a = row[j], b = row[j + half];
+    qs[g][j] = __fsub_rn(__fmul_rn(a, cs[j]), __fmul_rn(b, sn[j]));
+    qs[g][j + half] = __fadd_rn(__fmul_rn(a, sn[j]), __fmul_rn(b, cs[j]));
+  }
+  const bool tail = p < t0 + kChunk;
+  if (tail) {
+    const float *krow = qkv + (size_t)(H + kh) * kHd, *vrow = qkv + (size_t)(H + KVH + kh) * kHd;
+    __half *kd = kc + ((size_t)kh * max_ctx + p) * kHd, *vd = vc + ((size_t)kh * max_ctx + p) * kHd;
+    if (tid < half) {
+      const float a = krow[tid], b = krow[tid + half];
+      const __half ka = __float2half_rn(__fsub_rn(__fmul_rn(a, cs[tid]), __fmul_rn(b, sn[tid])));
+      const __half kb = __float2half_rn(__fadd_rn(__fmul_rn(a, sn[tid]), __fmul_rn(b, cs[tid])));
+      kd[tid] = ka;
+      kd[tid + half] = kb;
+      knew[tid] = __half2float(ka);
+      knew[tid + half] = __half2float(kb);
+    } else if (tid < half + kHd) {
+      const __half v = __float2half_rn(vrow[tid - half]);
+      vd[tid - half] = v;
+      vnew[tid - half] = __half2float(v);
+    }
+  }
   __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tw = t0 + warp * 32;  // first position of this warp
-  if (tw < n) {
-    const int t = tw + lane;
+  // scores: four threads per position, 32 dimensions each
+  {
     float s[G];
 #pragma unroll
     for (int g = 0; g < G; g++) s[g] = 0.f;
-    if (t < n) {
-      const __half *kr = kc + ((size_t)kh * max_ctx + t) * kHd;
-#pragma unroll 4
-      for (int d = 0; d < kHd; d += 8) {
-        const uint4 raw = *reinterpret_cast<const uint4 *>(kr + d);
-        const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
-        float kv[8];
+    if (tk < n) {
+      float kv[32];
+      if (tk == p) {
+#pragma unroll
+        for (int i = 0; i < 32; i++) kv[i] = knew[32 * sk + i];
+      } else {
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-          const float2 f = __half22float2(h2[j]);
-          kv[2 * j] = f.x;
-          kv[2 * j + 1] = f.y;
+          const __half2 *h2 = reinterpret_cast<const __half2 *>(&kr[j]);
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            const float2 f = __half22float2(h2[i]);
+            kv[8 * j + 2 * i] = f.x;
+            kv[8 * j + 2 * i + 1] = f.y;
+          }
         }
-#pragma unroll
-        for (int g = 0; g < G; g++)
-#pragma unroll
-          for (int j = 0; j < 8; j++) s[g] = fmaf(qs[g][d + j], kv[j], s[g]);
       }
+#pragma unroll
+      for (int g = 0; g < G; g++)
+#pragma unroll
+        for (int i = 0; i < 32; i++) s[g] = fmaf(qs[g][32 * sk + i], kv[i], s[g]);
     }
 #pragma unroll
     for (int g = 0; g < G; g++) {
-      const float sv = t < n ? s[g] * scale : -INFINITY;
-      const float m = warp_max(sv);
-      const float e = t < n ? __expf(sv - m) : 0.f;
-      const float l = warp_add(e);
-      ps[warp][g][lane] = e;
+      s[g] += __shfl_xor_sync(0xFFFFFFFFu, s[g], 1);
+      s[g] += __shfl_xor_sync(0xFFFFFFFFu, s[g], 2);
+      if (sk == 0) sc[g][tid >> 2] = tk < n ? s[g] * scale : -INFINITY;
+    }
+  }
+  __syncthreads();
+  // chunk softmax: warp g, two positions per lane
+  {
+    const int w = tid >> 5, lane = tid & 31;
+    if (w < G) {
+      const float a = sc[w][lane], b = sc[w][lane + 32];
+      const float m = warp_max(fmaxf(a, b));
+      const float ea = a == -INFINITY ? 0.f : __expf(a - m), eb = b == -INFINITY ? 0.f : __expf(b - m);
+      const float l = warp_add(ea + eb);
+      sc[w][lane] = ea;
+      sc[w][lane + 32] = eb;
       if (lane == 0) {
-        wm[warp][g] = m;
-        wl[warp][g] = l;
+        gm[w] = m;
+        gl[w] = l;
       }
     }
-    __syncwarp();
+  }
+  __syncthreads();
+  // values: thread = 4 dimensions x positions tv + 8j
+  {
     float o[G][4];
 #pragma unroll
     for (int g = 0; g < G; g++) o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
-    const int nt = min(32, n - tw);
-    for (int j = 0; j < nt; j++) {
-      const uint2 raw = *reinterpret_cast<const uint2 *>(vc + ((size_t)kh * max_ctx + tw + j) * kHd + 4 * lane);
-      const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
-      const float2 v01 = __half22float2(h2[0]), v23 = __half22float2(h2[1]);
+#pragma unroll
+    for (int j = 0; j < kChunk / 8; j++) {
+      const int t = tv + 8 * j;
+      if (t >= n) break;
+      float v[4];
+      if (t == p) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) v[i] = vnew[dv + i];
+      } else {
+        const __half2 *h2 = reinterpret_cast<const __half2 *>(&vr[j]);
+        const float2 a = __half22float2(h2[0]), b = __half22float2(h2[1]);
+        v[0] = a.x, v[1] = a.y, v[2] = b.x, v[3] = b.y;
+      }
 #pragma unroll
       for (int g = 0; g < G; g++) {
-        const float pj = ps[warp][g][j];
-        o[g][0] = fmaf(pj, v01.x, o[g][0]);
-        o[g][1] = fmaf(pj, v01.y, o[g][1]);
-        o[g][2] = fmaf(pj, v23.x, o[g][2]);
-        o[g][3] = fmaf(pj, v23.y, o[g][3]);
+        const float pj = sc[g][t - t0];
+#pragma unroll
+        for (int i = 0; i < 4; i++) o[g][i] = fmaf(pj, v[i], o[g][i]);
       }
     }
 #pragma unroll
     for (int g = 0; g < G; g++)
 #pragma unroll
-      for (int i = 0; i < 4; i++) wo[warp][g][4 * lane + i] = o[g][i];
-  } else if (lane < G) {
-    wm[warp][lane] = -INFINITY;
-    wl[warp][lane] = 0.f;
+      for (int i = 0; i < 4; i++) wo[tid >> 5][g][dv + i] = o[g][i];
   }
   __syncthreads();
-  mv::pdl_launch_dependents();
-  for (int i = threadIdx.x; i < G * kHd; i += blockDim.x) {
+  for (int i = tid; i < G * kHd; i += blockDim.x) {
     const int g = i / kHd, d = i % kHd;
-    float M = -INFINITY;
+    float O = 0.f;
 #pragma unroll
-    for (int w = 0; w < 4; w++) M = fmaxf(M, wm[w][g]);
-    float L = 0.f, O = 0.f;
-#pragma unroll
-    for (int w = 0; w < 4; w++) {
-      if (t0 + w * 32 >= n) continue;
-      const float f = __expf(wm[w][g] - M);
-      L = fmaf(wl[w][g], f, L);
-      O = fmaf(wo[w][g][d], f, O);
-    }
+    for (int w = 0; w < 8; w++) O += wo[w][g][d];
     float *pp = part + ((size_t)(kh * G + g) * nch_max + c) * (2 + kHd);
     pp[2 + d] = O;
     if (d == 0) {
-      pp[0] = M;
-      pp[1] = L;
+      pp[0] = gm[g];
+      pp[1] = gl[g];
     }
   }
-}
-
-// out[h] = sum over chunks of the partial outputs, rescaled to the global
-// maximum, divided by the total sum.  CTA per query head.
-__global__ void k_attn_combine(const float *part, const int *pos, float *out, int nch_max) {
-  mv::pdl_wait();
-  const int h = blockIdx.x, n = *pos + 1, nch = (n + kChunk - 1) / kChunk;
-  const float *ph = part + (size_t)h * nch_max * (2 + kHd);
-  float M = -INFINITY;
-  for (int c = 0; c < nch; c++) M = fmaxf(M, ph[(size_t)c * (2 + kHd)]);
-  mv::pdl_launch_dependents();
-  for (int d = threadIdx.x; d < kHd; d += blockDim.x) {
+  // the last CTA of this KV head merges the chunks
+  __threadfence();
+  __syncthreads();
+  const int nch = (n + kChunk - 1) / kChunk;
+  if (tid == 0) last = atomicAdd(&count[kh], 1u) == (unsigned)(nch - 1);
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  for (int i = tid; i < G * kHd; i += blockDim.x) {
+    const int g = i / kHd, d = i % kHd;
+    const float *ph = part + (size_t)(kh * G + g) * nch_max * (2 + kHd);
+    float M = -INFINITY;
+    for (int cc = 0; cc < nch; cc++) M = fmaxf(M, __ldcg(ph + (size_t)cc * (2 + kHd)));
     float L = 0.f, O = 0.f;
-    for (int c = 0; c < nch; c++) {
-      const float *pc = ph + (size_t)c * (2 + kHd);
-      const float f = __expf(pc[0] - M);
-      L = fmaf(pc[1], f, L);
-      O = fmaf(pc[2 + d], f, O);
+    for (int cc = 0; cc < nch; cc++) {
+      const float *pc = ph + (size_t)cc * (2 + kHd);
+      const float f = __expf(__ldcg(pc) - M);
+      L = fmaf(__ldcg(pc + 1), f, L);
+      O = fmaf(__ldcg(pc + 2 + d), f, O);
     }
-    out[(size_t)h * kHd + d] = __fdiv_rn(O, L);
+    out[(size_t)(kh * G + g) * kHd + d] = __fdiv_rn(O, L);
   }
+  if (tid == 0) count[kh] = 0u;
+  mv::pdl_launch_dependents();
 }
 
 // a = silu(g) * u over the merged [G | U] rows
@@ -283,24 +317,37 @@ __global__ void k_argmax_part(const float *v, int n, float *pm, int *pi) {
 
 // The next token: the prompt's next id while the prompt lasts, else the
 // first maximum of the logits; recorded at tokens[pos + 1]; pos advances.
+// One warp.
 __global__ void k_next_token(const float *pm, const int *pi, int nb, int *pos, int64_t *tok, int64_t *hist,
                              const int64_t *prompt, const int *nprompt, int max_ctx) {
   mv::pdl_wait();
-  if (threadIdx.x != 0) return;
+  const int lane = threadIdx.x;
   float best = -INFINITY;
-  int bi = 0;
-  bool any = false;
-  for (int b = 0; b < nb; b++)
-    if (pi[b] != 0x7FFFFFFF && (!any || pm[b] > best || (pm[b] == best && pi[b] < bi))) {
-      best = pm[b];
-      bi = pi[b];
-      any = true;
+  int bi = 0x7FFFFFFF;
+  for (int b = lane; b < nb; b += 32) {
+    const float v = pm[b];
+    const int i = pi[b];
+    if (i != 0x7FFFFFFF && (bi == 0x7FFFFFFF || v > best || (v == best && i < bi))) {
+      best = v;
+      bi = i;
     }
-  const int p = *pos;
-  const int64_t next = (p + 1 < *nprompt) ? prompt[p + 1] : (int64_t)bi;
-  if (p + 1 < max_ctx) hist[p + 1] = next;
-  *tok = next;
-  *pos = p + 1;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+    const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+    if (oi != 0x7FFFFFFF && (bi == 0x7FFFFFFF || ob > best || (ob == best && oi < bi))) {
+      best = ob;
+      bi = oi;
+    }
+  }
+  if (lane == 0) {
+    const int p = *pos;
+    const int64_t next = (p + 1 < *nprompt) ? prompt[p + 1] : (int64_t)(bi == 0x7FFFFFFF ? 0 : bi);
+    if (p + 1 < max_ctx) hist[p + 1] = next;
+    *tok = next;
+    *pos = p + 1;
+  }
   mv::pdl_launch_dependents();
 }
 
@@ -329,6 +376,9 @@ struct Mat {
   const void *w = nullptr;
   int type = 0, N = 0, K = 0;
   tcb::MvPlan plan{};
+  const void *pf = nullptr;  // the next matvec's weights in the step (L2 prefetch while this one runs)
+  size_t pf_bytes = 0;
+  size_t bytes() const { return (size_t)N * K / tcb::block_elems(type) * tcb::block_bytes(type); }
 };
 
 }  // namespace
@@ -346,6 +396,7 @@ struct tcb_llama {
   float *x = nullptr, *h = nullptr, *qkvb = nullptr, *att = nullptr, *gub = nullptr, *a = nullptr, *logits = nullptr;
   float *part = nullptr, *am_v = nullptr, *cosT = nullptr, *sinT = nullptr;
   int *am_i = nullptr, *pos = nullptr, *nprompt = nullptr;
+  unsigned *acount = nullptr;  // per KV head: attention chunks finished
   __half *kc = nullptr, *vc = nullptr;
   int64_t *tok = nullptr, *hist = nullptr, *prompt = nullptr;
   int nch_max = 0;
@@ -390,9 +441,20 @@ Mat make_mat(const void *w, int type, int N, int K, int sms) {
 cudaError_t matvec(tcb_llama *m, const Mat &mt, const float *x, float *y, int accumulate, cudaStream_t s) {
   if (mt.plan.ok)
     return tcb::matvec_launch(mt.plan, mt.type, 0, mt.N, mt.K, mt.w, x, TCB_F32, y, TCB_F32, accumulate,
-                              m->ctx->derr, s);
+                              m->ctx->derr, s, mt.pf, mt.pf_bytes);
   return tcb::launch_qgemm_simt(mt.type, mt.w, 1, mt.N, mt.K, x, TCB_F32, mt.K, y, TCB_F32, mt.N, accumulate,
                                 m->ctx->sms, s);
+}
+
+// y = W rms(x) * w: the RMSNorm is fused into the Q4_K matvec's prologue
+// when that kernel takes the weight, else a separate pass into h
+cudaError_t norm_matvec(tcb_llama *m, const Mat &mt, const float *nw, float *y, cudaStream_t s) {
+  const tcb_llama_config &c = m->cfg;
+  if (mt.plan.ok && mt.plan.kind == 1)
+    return tcb::q4k_launch(mt.plan, mt.N, mt.K, mt.w, m->x, TCB_F32, y, TCB_F32, 0, m->ctx->derr, s, nw, c.eps, mt.pf,
+                           mt.pf_bytes);
+  cudaError_t e = tcb::ll::launch(tcb::ll::k_rmsnorm, dim3(1), dim3(1024), s, m->x, nw, m->h, c.d_model, c.eps);
+  return e == cudaSuccess ? matvec(m, mt, m->h, y, 0, s) : e;
 }
 
 cudaError_t issue_step(tcb_llama *m, cudaStream_t s) {
@@ -405,24 +467,24 @@ cudaError_t issue_step(tcb_llama *m, cudaStream_t s) {
   cudaError_t e = tcb::launch_dequant_rows(m->tok_emb_type, m->tok_emb, 1, D, m->tok, m->x, TCB_F32, m->ctx->sms, s);
   for (int l = 0; l < c.n_layers && e == cudaSuccess; l++) {
     __half *kc = m->kc + l * cache_layer, *vc = m->vc + l * cache_layer;
-    if ((e = launch(k_rmsnorm, dim3(1), dim3(1024), s, m->x, m->attn_norm[l], m->h, D, c.eps)) != cudaSuccess) break;
-    if ((e = matvec(m, m->qkv[l], m->h, m->qkvb, 0, s)) != cudaSuccess) break;
-    if ((e = launch(k_rope_cache, dim3(H + 2 * KVH), dim3(64), s, m->qkvb, m->cosT, m->sinT, m->pos, kc, vc, H, KVH,
-                    hd, c.max_ctx)) != cudaSuccess)
-      break;
+    if ((e = norm_matvec(m, m->qkv[l], m->attn_norm[l], m->qkvb, s)) != cudaSuccess) break;
     const dim3 ag(KVH, m->nch_max);
     switch (G) {
-    case 1: e = launch(k_attn_part<1>, ag, dim3(128), s, m->qkvb, kc, vc, m->pos, m->part, c.max_ctx, m->nch_max, scale); break;
-    case 2: e = launch(k_attn_part<2>, ag, dim3(128), s, m->qkvb, kc, vc, m->pos, m->part, c.max_ctx, m->nch_max, scale); break;
-    case 4: e = launch(k_attn_part<4>, ag, dim3(128), s, m->qkvb, kc, vc, m->pos, m->part, c.max_ctx, m->nch_max, scale); break;
-    case 8: e = launch(k_attn_part<8>, ag, dim3(128), s, m->qkvb, kc, vc, m->pos, m->part, c.max_ctx, m->nch_max, scale); break;
+#define TCB_ATTN(GG)                                                                                              \
+  case GG:                                                                                                        \
+    e = launch(k_attn<GG>, ag, dim3(256), s, m->qkvb, m->cosT, m->sinT, m->pos, kc, vc, m->part, m->acount, m->att, H, \
+               KVH, c.max_ctx, m->nch_max, scale);                                                                \
+    break;
+      TCB_ATTN(1)
+      TCB_ATTN(2)
+      TCB_ATTN(4)
+      TCB_ATTN(8)
+#undef TCB_ATTN
     default: e = cudaErrorInvalidValue;
     }
     if (e != cudaSuccess) break;
-    if ((e = launch(k_attn_combine, dim3(H), dim3(128), s, m->part, m->pos, m->att, m->nch_max)) != cudaSuccess) break;
     if ((e = matvec(m, m->o[l], m->att, m->x, 1, s)) != cudaSuccess) break;
-    if ((e = launch(k_rmsnorm, dim3(1), dim3(1024), s, m->x, m->ffn_norm[l], m->h, D, c.eps)) != cudaSuccess) break;
-    if ((e = matvec(m, m->gu[l], m->h, m->gub, 0, s)) != cudaSuccess) break;
+    if ((e = norm_matvec(m, m->gu[l], m->ffn_norm[l], m->gub, s)) != cudaSuccess) break;
     if ((e = launch(k_swiglu, dim3((F + 255) / 256), dim3(256), s, m->gub, m->a, F)) != cudaSuccess) break;
     e = matvec(m, m->down[l], m->a, m->x, 1, s);
   }
@@ -481,6 +543,25 @@ int tcb_llama_create(tcb_ctx *ctx, const tcb_llama_config *cfg, const tcb_llama_
     m->gu.push_back(make_mat(w->gate_up[l], w->gate_up_type, 2 * F, D, ctx->sms));
     m->down.push_back(make_mat(w->down[l], w->down_type, D, F, ctx->sms));
   }
+  // each matvec streams the next one's weights into L2 (qkv -> o -> gate_up
+  // -> down -> next layer's qkv ... -> head -> layer 0's qkv), at most
+  // kPrefetchMax bytes of them, half the L2
+  {
+    constexpr size_t kPrefetchMax = 64u << 20;
+    std::vector<Mat *> chain;
+    for (int l = 0; l < c.n_layers; l++) {
+      chain.push_back(&m->qkv[l]);
+      chain.push_back(&m->o[l]);
+      chain.push_back(&m->gu[l]);
+      chain.push_back(&m->down[l]);
+    }
+    chain.push_back(&m->head);
+    for (size_t i = 0; i < chain.size(); i++) {
+      const Mat *nx = chain[(i + 1) % chain.size()];
+      chain[i]->pf = nx->w;
+      chain[i]->pf_bytes = nx->bytes() < kPrefetchMax ? nx->bytes() : kPrefetchMax;
+    }
+  }
   m->nch_max = (c.max_ctx + tcb::ll::kChunk - 1) / tcb::ll::kChunk;
   const size_t cache = (size_t)c.n_layers * KVH * c.max_ctx * hd;
   const int qkvn = (H + 2 * KVH) * hd;
@@ -495,7 +576,8 @@ int tcb_llama_create(tcb_ctx *ctx, const tcb_llama_config *cfg, const tcb_llama_
       (e = alloc(m, &m->sinT, (size_t)c.max_ctx * hd / 2)) != cudaSuccess || (e = alloc(m, &m->kc, cache)) != cudaSuccess ||
       (e = alloc(m, &m->vc, cache)) != cudaSuccess || (e = alloc(m, &m->pos, 1)) != cudaSuccess ||
       (e = alloc(m, &m->nprompt, 1)) != cudaSuccess || (e = alloc(m, &m->tok, 1)) != cudaSuccess ||
-      (e = alloc(m, &m->hist, c.max_ctx)) != cudaSuccess || (e = alloc(m, &m->prompt, c.max_ctx)) != cudaSuccess) {
+      (e = alloc(m, &m->hist, c.max_ctx)) != cudaSuccess || (e = alloc(m, &m->prompt, c.max_ctx)) != cudaSuccess ||
+      (e = alloc(m, &m->acount, KVH)) != cudaSuccess) {
     tcb_llama_destroy(m);
     return e == cudaErrorMemoryAllocation ? TCB_ERR_NOMEM : TCB_ERR_CUDA;
   }
@@ -513,7 +595,8 @@ int tcb_llama_create(tcb_ctx *ctx, const tcb_llama_config *cfg, const tcb_llama_
   }
   if ((e = cudaMemcpy(m->cosT, ct.data(), ct.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
       (e = cudaMemcpy(m->sinT, st.data(), st.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
-      (e = cudaMemset(m->kc, 0, cache * 2)) != cudaSuccess || (e = cudaMemset(m->vc, 0, cache * 2)) != cudaSuccess) {
+      (e = cudaMemset(m->kc, 0, cache * 2)) != cudaSuccess || (e = cudaMemset(m->vc, 0, cache * 2)) != cudaSuccess ||
+      (e = cudaMemset(m->acount, 0, KVH * sizeof(unsigned))) != cudaSuccess) {
     tcb_llama_destroy(m);
     return TCB_ERR_CUDA;
   }

@@ -79,6 +79,8 @@ struct Params {
   int *err;               // sticky error word (timeouts)
   int S;                  // stages
   int xoff, toff, soff;   // shared-memory offsets: x region, int8 terms, stages
+  const void *pf;         // weights of the next kernel of a chain, prefetched into L2 (or nullptr)
+  size_t pf_bytes;
 };
 
 // x region layout (float path): NDIG digit planes of K int8, then per group
@@ -616,6 +618,7 @@ __global__ void __launch_bounds__(32 * kWarpsAll, 1) k_mv1(const __grid_constant
         for (int k = 0; k < nbox; k++)
           tma_load_2d(stages + buf * stage_bytes + k * box_bytes, &tmap, (b0 + k * P::BPB) * P::B / 8, tile * 16,
                       &full[buf]);
+        if (it == (nstages < a.S ? nstages : a.S) - 1) prefetch_slice_l2(a.pf, a.pf_bytes);
       }
     }
     return;
@@ -758,7 +761,7 @@ bool encode_weight_map(CUtensorMap *tm, const void *w, int N, long rowBytes) {
 
 template <int W, bool ACT8>
 cudaError_t plan_launch(const MvPlan &pl, const void *w, int N, int K, const void *x, int xdt, void *c, int cdt,
-                        int accumulate, int *err, cudaStream_t s) {
+                        int accumulate, int *err, cudaStream_t s, const void *pf, size_t pf_bytes) {
   mv::Params a{};
   a.w = static_cast<const uint8_t *>(w);
   a.nb = K / mv::Pol<W>::E;
@@ -778,6 +781,8 @@ cudaError_t plan_launch(const MvPlan &pl, const void *w, int N, int K, const voi
   a.xoff = pl.xoff;
   a.toff = pl.toff;
   a.soff = pl.soff;
+  a.pf = pf;
+  a.pf_bytes = pf_bytes;
   CUtensorMap tm;
   static_assert(sizeof(tm) == sizeof(pl.tmap), "CUtensorMap size");
   memcpy(&tm, pl.tmap, sizeof tm);
@@ -843,11 +848,11 @@ MvPlan matvec_plan(int wtype, int act8, int M, int N, int K, const void *w, int 
 }
 
 cudaError_t matvec_launch(const MvPlan &pl, int wtype, int act8, int N, int K, const void *w, const void *x, int xdt,
-                          void *c, int cdt, int accumulate, int *err, cudaStream_t s) {
-#define TCB_MV(WT)                                                                             \
-  return act8 ? plan_launch<WT, true>(pl, w, N, K, x, xdt, c, cdt, accumulate, err, s)        \
-              : plan_launch<WT, false>(pl, w, N, K, x, xdt, c, cdt, accumulate, err, s)
-  if (pl.kind == 1) return q4k_launch(pl, N, K, w, x, xdt, c, cdt, accumulate, err, s);
+                          void *c, int cdt, int accumulate, int *err, cudaStream_t s, const void *pf, size_t pf_bytes) {
+#define TCB_MV(WT)                                                                                    \
+  return act8 ? plan_launch<WT, true>(pl, w, N, K, x, xdt, c, cdt, accumulate, err, s, pf, pf_bytes) \
+              : plan_launch<WT, false>(pl, w, N, K, x, xdt, c, cdt, accumulate, err, s, pf, pf_bytes)
+  if (pl.kind == 1) return q4k_launch(pl, N, K, w, x, xdt, c, cdt, accumulate, err, s, nullptr, 0.f, pf, pf_bytes);
   switch (wtype) {
   case TCB_Q4_K: TCB_MV(TCB_Q4_K);
   case TCB_Q6_K: TCB_MV(TCB_Q6_K);

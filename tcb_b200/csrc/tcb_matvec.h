@@ -20,12 +20,18 @@ struct MvPlan {
 
 MvPlan matvec_plan(int wtype, int act8, int M, int N, int K, const void *w, int sms);
 
-// Q4_K float path (kind 1)
+// Q4_K float path (kind 1).  With nw, the product is W * rms(x): an
+// RMSNorm (x / sqrt(mean(x^2) + eps) * nw, K elements, f32 x, finite x
+// assumed) is fused into the prologue.
 MvPlan q4k_plan(int N, int K, const void *w, int sms);
 cudaError_t q4k_launch(const MvPlan &pl, int N, int K, const void *w, const void *x, int xdt, void *c, int cdt,
-                       int accumulate, int *err, cudaStream_t s);
+                       int accumulate, int *err, cudaStream_t s, const float *nw = nullptr, float eps = 0.f,
+                       const void *pf = nullptr, size_t pf_bytes = 0);
 
+// pf / pf_bytes: the weights of the next kernel of a chain, streamed into L2
+// by this launch's producers (a hint; nullptr for none)
 cudaError_t matvec_launch(const MvPlan &pl, int wtype, int act8, int N, int K, const void *w, const void *x, int xdt,
-                          void *c, int cdt, int accumulate, int *err, cudaStream_t s);
+                          void *c, int cdt, int accumulate, int *err, cudaStream_t s, const void *pf = nullptr,
+                          size_t pf_bytes = 0);
 
 }  // namespace tcb

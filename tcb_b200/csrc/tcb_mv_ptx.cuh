@@ -125,6 +125,22 @@ __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t phase, int *err
   return false;
 }
 
+// Bring this CTA's share of [p, p + bytes) into L2 (bulk prefetches of at
+// most 64 KB; a hint: no completion, no shared memory).  Used to stream the
+// weights of the next kernel of a chain while this one runs.
+__device__ __forceinline__ void prefetch_slice_l2(const void *p, size_t bytes) {
+  if (!p || bytes < 16) return;
+  const size_t per = ((bytes + gridDim.x - 1) / gridDim.x + 15) & ~(size_t)15;
+  const size_t b0 = per * blockIdx.x;
+  const size_t b1 = b0 + per < bytes ? b0 + per : bytes;
+  const char *base = static_cast<const char *>(p);
+  for (size_t o = b0; o + 16 <= b1; o += 65536) {
+    const size_t n = (b1 - o < 65536 ? b1 - o : 65536) & ~(size_t)15;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(base + o)), "r"((uint32_t)n)
+                 : "memory");
+  }
+}
+
 // poll with a back-off of ns nanoseconds (bounded: about 2^24 polls)
 __device__ __forceinline__ bool spin_bar_ns(uint64_t *bar, uint32_t phase, int *err, unsigned ns) {
   for (uint32_t i = 0; i < (1u << 24); i++) {

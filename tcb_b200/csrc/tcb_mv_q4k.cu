@@ -66,7 +66,7 @@ constexpr int kBoxBytes = kRows * kPitch;   // one stage
 constexpr int kSlots = 4;                   // tile partial slots in flight
 constexpr int kPF = 4;                      // boxes prefetched into L2 ahead of the stages
 constexpr int kFrag = 512, kScl = 64;       // per block: B fragments, lane scales
-constexpr int kBarOff = 0, kFlagOff = 256, kPartOff = 512;
+constexpr int kBarOff = 0, kFlagOff = 256, kNormOff = 288, kPartOff = 512;
 constexpr int kPartBytes = kSlots * kC * kRows * 4;
 constexpr int kXOff = kPartOff + kPartBytes;
 
@@ -80,7 +80,11 @@ struct Params {
   int accumulate;
   int tiles, nch, S;
   int *err;
-  int soff;  // stage offset in shared memory
+  int soff;         // stage offset in shared memory
+  const float *nw;  // RMSNorm weight fused into the prologue (nullptr: none)
+  float eps;
+  const void *pf;   // weights of the next kernel of a chain, prefetched into L2 (or nullptr)
+  size_t pf_bytes;
 };
 
 // x region: [nb][kFrag] B fragments ([set s][round pair rp][column n][16
@@ -144,19 +148,37 @@ __device__ __forceinline__ void load8(const void *x, int e, int xdt, bool vec, f
 // sigma = 1/id, not exact, so it is the hardware reciprocal.  Returns false
 // if a sub-block sum is not finite (a NaN or Inf in x, or a sum that
 // overflows, which only sends the call down the exact fp32 path).
-__device__ bool prep_warp(const Params &a, uint8_t *xr, int own, int lane) {
+__device__ bool prep_warp(const Params &a, uint8_t *xr, int own, int lane, float &ss) {
   constexpr float MAGIC = 12582912.0f;
   constexpr int NB = 4;  // blocks in flight per lane
   uint8_t *frag = xr;
   float *scl = reinterpret_cast<float *>(xr + a.nb * kFrag);
   const bool vec = (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
   bool fin = true;
+  ss = 0.f;
   for (int base = own; base < a.nb; base += kC * NB) {
     float xv[NB][8];
 #pragma unroll
     for (int j = 0; j < NB; j++) {
       const int bg = base + kC * j;
       if (bg < a.nb) load8(a.x, bg * 256 + 8 * lane, a.xdt, vec, xv[j]);
+    }
+    if (a.nw) {
+      // fused RMSNorm: digits of x * w; the 1/rms factor is applied to the
+      // row sums (the product is linear in x)
+#pragma unroll
+      for (int j = 0; j < NB; j++) {
+        const int bg = base + kC * j;
+        if (bg >= a.nb) break;
+        const float4 w0 = *reinterpret_cast<const float4 *>(a.nw + bg * 256 + 8 * lane);
+        const float4 w1 = *reinterpret_cast<const float4 *>(a.nw + bg * 256 + 8 * lane + 4);
+        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          ss = fmaf(xv[j][i], xv[j][i], ss);
+          xv[j][i] = __fmul_rn(xv[j][i], wv[i]);
+        }
+      }
     }
 #pragma unroll
     for (int j = 0; j < NB; j++) {
@@ -206,6 +228,8 @@ __device__ bool prep_warp(const Params &a, uint8_t *xr, int own, int lane) {
       }
     }
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
   return __all_sync(0xFFFFFFFFu, fin);
 }
 
@@ -329,6 +353,7 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq4k(const __grid_constant_
         if (it >= a.S && !spin_bar_ns(&empty[buf], (uint32_t)(((it / a.S) & 1) ^ 1), a.err, 64)) return;
         mbar_expect_tx(&full[buf], (uint32_t)kBoxBytes);
         tma_load_2d(stages + buf * kBoxBytes, &tmap, bx(it), by(it), &full[buf]);
+        if (it == (nstages < a.S ? nstages : a.S) - 1) prefetch_slice_l2(a.pf, a.pf_bytes);
         if (it == a.S - 1 || (it >= a.S && it + kPF < nstages)) {
           for (int p = (it == a.S - 1 ? a.S : it + kPF); p < nstages && p <= it + kPF; p++)
             tma_prefetch_2d(&tmap, bx(p), by(p));
@@ -343,7 +368,9 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq4k(const __grid_constant_
   pdl_wait();
   if (warp < kC) {
     if (warp == 0) reinterpret_cast<uint4 *>(xr + a.nb * (kFrag + kScl))[lane] = make_uint4(0u, 0u, 0u, 0u);
-    if (!prep_warp(a, xr, (warp + (int)blockIdx.x) & (kBlk - 1), lane) && lane == 0) *flag = 1;
+    float ss;
+    if (!prep_warp(a, xr, (warp + (int)blockIdx.x) & (kBlk - 1), lane, ss) && lane == 0) *flag = 1;
+    if (lane == 0) reinterpret_cast<float *>(sm + kNormOff)[warp] = ss;
   }
   asm volatile("bar.sync 1, %0;" ::"n"(32 * (kC + 1)) : "memory");
   const bool slow = *flag != 0;
@@ -352,6 +379,14 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq4k(const __grid_constant_
     // sum the eight partials of each row in block order (block j of a
     // stage is owned by warp (j - blockIdx) mod 8)
     const int rot = (int)blockIdx.x & (kBlk - 1);
+    float rms = 1.f;
+    if (a.nw) {
+      // the warps' sums of squares in warp order: sqrt(mean(x^2) + eps)
+      const float *nss = reinterpret_cast<const float *>(sm + kNormOff);
+      float tot = 0.f;
+      for (int w2 = 0; w2 < kC; w2++) tot += nss[w2];
+      rms = sqrtf(__fdiv_rn(tot, (float)a.K) + a.eps);
+    }
     for (int ti = 0; ti < my_tiles; ti++) {
       const int row = ((int)blockIdx.x + ti * (int)gridDim.x) * kRows + lane;
       const bool mine = row < a.N;
@@ -362,6 +397,7 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq4k(const __grid_constant_
       float v = 0.f;
 #pragma unroll
       for (int j = 0; j < kC; j++) v += pt[((j - rot) & (kBlk - 1)) * kRows];
+      if (a.nw) v = __fdiv_rn(v, rms);
       __syncwarp();
       if (lane == 0) mbar_arrive(&tfree[slot]);
       if (mine) store_out_old(a.c, row, a.cdt, v, a.accumulate != 0, cold);
@@ -434,6 +470,15 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq4k(const __grid_constant_
     }
     const int widx = warp == kEpi ? kC : warp;  // 0..kC
     const long rowBytes = (long)a.nb * 144;
+    if (a.nw) {
+      // rms(x) of an x with a NaN or Inf has a NaN in every row's inputs
+      for (int ti = 0; ti < my_tiles; ti++) {
+        const int r0 = ((int)blockIdx.x + ti * (int)gridDim.x) * kRows;
+        for (int n = r0 + widx * 32 + lane; n < r0 + kRows && n < a.N; n += (kC + 1) * 32)
+          store_out(a.c, n, a.cdt, __int_as_float(0x7FC00000), a.accumulate != 0);
+      }
+      return;
+    }
     for (int ti = 0; ti < my_tiles; ti++) {
       const int r0 = ((int)blockIdx.x + ti * (int)gridDim.x) * kRows;
       for (int n = r0 + widx; n < r0 + kRows && n < a.N; n += kC + 1) {
@@ -500,7 +545,8 @@ MvPlan q4k_plan(int N, int K, const void *w, int sms) {
 }
 
 cudaError_t q4k_launch(const MvPlan &pl, int N, int K, const void *w, const void *x, int xdt, void *c, int cdt,
-                       int accumulate, int *err, cudaStream_t s) {
+                       int accumulate, int *err, cudaStream_t s, const float *nw, float eps, const void *pf,
+                       size_t pf_bytes) {
   using namespace mvk;
   Params a{};
   a.w = static_cast<const uint8_t *>(w);
@@ -517,6 +563,10 @@ cudaError_t q4k_launch(const MvPlan &pl, int N, int K, const void *w, const void
   a.S = pl.stages;
   a.err = err;
   a.soff = pl.soff;
+  a.nw = nw;
+  a.eps = eps;
+  a.pf = pf;
+  a.pf_bytes = pf_bytes;
   CUtensorMap tm;
   memcpy(&tm, pl.tmap, sizeof tm);
   cudaError_t e = cudaFuncSetAttribute(k_mvq4k, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem);
