@@ -1,6 +1,6 @@
 """Benchmark of the B200 quantized matvec path (one JSON line on rank 0).
 
-Workload (BASELINE config 1): Q4_K weight 11008 x 4096 in GGUF blocks,
+Workload (BASELINE config 2): Q4_K weight 11008 x 4096 in GGUF blocks,
 f32 activations x[1, 4096] ~ N(0, 1), batch 1, float path
 (c = x . dequant(W)^T).  Synthetic seeded blocks with the benchmark's value
 distributions (tcb_b200/synth.py); no model files exist on the box.
@@ -11,7 +11,9 @@ weight from HBM.  The ring sweep is captured once in a CUDA graph and
 replayed.  `value` is the algorithmic bytes (weight blocks + x + y) of all
 ranks / the max over ranks of the device time.  `e2e` repeats the metric
 through the public C ABI with host buffers: every step copies x from
-pinned host memory, runs tcb_qgemm and copies y back.
+pinned host memory, runs tcb_qgemm and copies y back.  `decode` adds the
+metric's second half: 8B-shape Q4_K_M greedy decode tokens/s at batch 1
+through the tcb_llama engine.
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
     torchrun --nproc-per-node N bench.py --gpus N   (one process per GPU)
@@ -135,6 +137,57 @@ def cpu_baseline(seconds: float = 12.0) -> dict:
                                       f"in {dt:.1f} s"}
 
 
+def decode_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
+    """8B-shape Q4_K_M greedy decode at batch 1: a
+    512-token random prompt fed through the decode step, then 256 greedy
+    tokens, every step one replay of the captured CUDA graph (token, position
+    and prompt stay on the device).  Random-init synthetic weights (fp16 block
+    scales sized for order-one activations, tcb_b200/llama.py)."""
+    import torch
+
+    from tcb_b200 import llama
+
+    cfg = llama.LLAMA3_8B
+    model = llama.device_model(cfg, seed=7 + rank)
+    eng = llama.Llama(ctx, model)
+    prompt = np.random.default_rng(11 + rank).integers(0, cfg.vocab, 512)
+    stream = torch.cuda.Stream()
+    eng.start(prompt, stream)
+    eng.capture(stream)
+    eng.start(prompt, stream)
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        eng.step(511, stream)
+        e1.record(stream)
+        eng.step(256, stream)
+        e2.record(stream)
+    e2.synchronize()
+    t = torch.tensor([e1.elapsed_time(e2)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    toks = eng.tokens(768, stream)
+    bpt = llama.weight_bytes_per_token(cfg)
+    kv = 2 * cfg.n_layers * cfg.n_kv_heads * cfg.head_dim * 2 * (512 + 128)  # fp16 K/V read per token (mean position)
+    per_tok_s = ms / 1e3 / 256
+    eng.close()
+    del model
+    return {
+        "model": "llama3-8b-shape q4_k_m (random init, synthetic)", "prompt_tokens": 512, "generated_tokens": 256,
+        "tokens_per_s": round(256 * world / (ms / 1e3), 2), "ms_per_token": round(ms / 256, 4),
+        "prefill_token_by_token_ms": round(e0.elapsed_time(e1), 2),
+        "bytes_per_token": bpt + kv, "weight_bytes_per_token": bpt,
+        "roofline": {"bound": "hbm", "achieved": round((bpt + kv) / per_tok_s / 1e9, 2), "peak": peak_gbs,
+                     "unit": "GB/s", "frac": round((bpt + kv) / per_tok_s / 1e9 / peak_gbs, 4),
+                     "ceiling_tokens_per_s": round(peak_gbs * 1e9 / (bpt + kv), 1)},
+        "gpu_launches_per_token": 1 + 6 * cfg.n_layers + 4, "last_tokens": [int(v) for v in toks[-4:]],
+        "timing": "CUDA events around 256 graph replays on the engine's stream",
+    }
+
+
 def dist_init():
     if "RANK" not in os.environ:
         return 0, 1, 0
@@ -166,6 +219,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the 8B-shape decode measurement")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -269,6 +323,8 @@ def main():
 
         dist.all_reduce(et, op=dist.ReduceOp.MAX)
     e2e_value = per_launch_bytes * e2e_steps * world / (float(et.item()) / 1e3) / 1e9
+    del g
+    decode = None if args.no_decode else decode_bench(ctx, rank, world, peaks["hbm_gbs"])
 
     if rank == 0:
         line = {
@@ -287,10 +343,11 @@ def main():
             "gpu_launches": launches,
             "clocks": clk.summary(),
         }
+        if decode is not None:
+            line["decode"] = decode
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
-    del g
     if world > 1:
         import torch.distributed as dist
 

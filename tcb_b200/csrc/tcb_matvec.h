@@ -10,7 +10,7 @@ namespace tcb {
 // shape is not taken by it (the caller then runs the portable kernel)
 struct MvPlan {
   bool ok;
-  int kind;                    // 0: generic kernel (16-row tiles), 1: Q4_K float kernel (32-row tiles)
+  int kind;                    // 0: generic kernel, 1: Q4_K float kernel
   int tiles, cbc, nch;         // tiles, blocks per staged chunk, chunks per row
   int stages, pitch;           // TMA stages, bytes per staged row
   int xoff, toff, soff, smem;  // shared-memory layout
