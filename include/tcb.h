@@ -145,6 +145,13 @@ typedef struct tcb_llama_config {
   int max_ctx;        /* KV-cache positions (prompt + generated) */
   float eps;          /* RMSNorm epsilon */
   float rope_theta;   /* rotary frequency base */
+  /* tensor parallelism (0 or 1: none).  Rank r holds query heads
+   * [r H/tp, (r+1) H/tp) with their KV heads, gate/up rows [r ffn/tp, ...)
+   * of each half, the matching K-columns of o and down, and vocabulary rows
+   * [r vocab/tp, ...) of the head; the embedding table, the norms and the
+   * residual are replicated.  One all-reduce follows o and down, and an
+   * all-gather of the local greedy candidates picks the token. */
+  int tp_size, tp_rank;
 } tcb_llama_config;
 
 typedef struct tcb_llama_weights {
@@ -176,8 +183,14 @@ int tcb_llama_step(tcb_llama *m, void *stream);
  * caller's stream from then on. */
 int tcb_llama_capture(tcb_llama *m, void *stream);
 /* Device pointers of the token history (int64 [max_ctx]) and the logits of
- * the last step (float [vocab]). */
+ * the last step (float [vocab], this rank's vocabulary rows). */
 int tcb_llama_buffers(tcb_llama *m, int64_t **tokens, float **logits);
+/* Tensor parallelism over NCCL (libnccl.so.2, loaded at run time; the copy
+ * the process has already loaded is reused).  Rank 0 makes an id, every
+ * rank passes the same 128 bytes to tcb_llama_tp_init (before the first
+ * step or capture), with its device current. */
+int tcb_nccl_unique_id(unsigned char *id128);
+int tcb_llama_tp_init(tcb_llama *m, const unsigned char *id128);
 
 /* Size of the device array that tcb_qgemm_act8_static works in. */
 #define TCB_STATIC_SCRATCH_BYTES (4u << 20)

@@ -25,6 +25,7 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <dlfcn.h>
 #include <stdio.h>
 
 #include <utility>
@@ -351,6 +352,58 @@ __global__ void k_next_token(const float *pm, const int *pi, int nb, int *pos, i
   mv::pdl_launch_dependents();
 }
 
+// Tensor parallelism: this rank's greedy candidate (first maximum of its
+// vocabulary rows, as a global index), for the all-gather.
+__global__ void k_local_best(const float *pm, const int *pi, int nb, int off, int2 *cand) {
+  mv::pdl_wait();
+  const int lane = threadIdx.x;
+  float best = -INFINITY;
+  int bi = 0x7FFFFFFF;
+  for (int b = lane; b < nb; b += 32) {
+    const float v = pm[b];
+    const int i = pi[b];
+    if (i != 0x7FFFFFFF && (bi == 0x7FFFFFFF || v > best || (v == best && i < bi))) {
+      best = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+    const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+    if (oi != 0x7FFFFFFF && (bi == 0x7FFFFFFF || ob > best || (ob == best && oi < bi))) {
+      best = ob;
+      bi = oi;
+    }
+  }
+  if (lane == 0) *cand = make_int2(__float_as_int(best), bi == 0x7FFFFFFF ? bi : bi + off);
+  mv::pdl_launch_dependents();
+}
+
+// the next token from the ranks' candidates (rank order = vocabulary order,
+// so ties still go to the lowest index)
+__global__ void k_pick_tp(const int2 *cand, int n, int *pos, int64_t *tok, int64_t *hist, const int64_t *prompt,
+                          const int *nprompt, int max_ctx) {
+  mv::pdl_wait();
+  if (threadIdx.x != 0) return;
+  float best = -INFINITY;
+  int bi = 0x7FFFFFFF;
+  for (int r = 0; r < n; r++) {
+    const float v = __int_as_float(cand[r].x);
+    const int i = cand[r].y;
+    if (i != 0x7FFFFFFF && (bi == 0x7FFFFFFF || v > best || (v == best && i < bi))) {
+      best = v;
+      bi = i;
+    }
+  }
+  const int p = *pos;
+  const int64_t next = (p + 1 < *nprompt) ? prompt[p + 1] : (int64_t)(bi == 0x7FFFFFFF ? 0 : bi);
+  if (p + 1 < max_ctx) hist[p + 1] = next;
+  *tok = next;
+  *pos = p + 1;
+  mv::pdl_launch_dependents();
+}
+
 template <typename... Exp, typename... Act>
 cudaError_t launch(void (*k)(Exp...), dim3 grid, dim3 block, cudaStream_t s, Act &&...args) {
   cudaLaunchConfig_t cfg = {};
@@ -367,6 +420,50 @@ cudaError_t launch(void (*k)(Exp...), dim3 grid, dim3 block, cudaStream_t s, Act
 
 }  // namespace ll
 }  // namespace tcb
+
+// ----------------------------------------------------------------- NCCL
+
+namespace {
+
+// NCCL, loaded at run time (no link dependency): the copy a process has
+// already loaded (e.g. by its framework) is reused, else libnccl.so.2 from
+// the loader's path.  Types restated from nccl.h: an opaque communicator, a
+// 128-byte id passed by value, int enums (float32 = 7, int32 = 2, sum = 0).
+struct NcclId {
+  char internal[128];
+};
+struct Nccl {
+  void *h = nullptr;
+  int (*get_id)(NcclId *) = nullptr;
+  int (*init_rank)(void **, int, NcclId, int) = nullptr;
+  int (*all_reduce)(const void *, void *, size_t, int, int, void *, cudaStream_t) = nullptr;
+  int (*all_gather)(const void *, void *, size_t, int, void *, cudaStream_t) = nullptr;
+  int (*destroy)(void *) = nullptr;
+  const char *(*err)(int) = nullptr;
+};
+constexpr int kNcclInt32 = 2, kNcclFloat32 = 7, kNcclSum = 0;
+
+const Nccl *nccl() {
+  static Nccl n = [] {
+    Nccl r;
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return r;
+    r.get_id = reinterpret_cast<int (*)(NcclId *)>(dlsym(h, "ncclGetUniqueId"));
+    r.init_rank = reinterpret_cast<int (*)(void **, int, NcclId, int)>(dlsym(h, "ncclCommInitRank"));
+    r.all_reduce =
+        reinterpret_cast<int (*)(const void *, void *, size_t, int, int, void *, cudaStream_t)>(dlsym(h, "ncclAllReduce"));
+    r.all_gather =
+        reinterpret_cast<int (*)(const void *, void *, size_t, int, void *, cudaStream_t)>(dlsym(h, "ncclAllGather"));
+    r.destroy = reinterpret_cast<int (*)(void *)>(dlsym(h, "ncclCommDestroy"));
+    r.err = reinterpret_cast<const char *(*)(int)>(dlsym(h, "ncclGetErrorString"));
+    if (r.get_id && r.init_rank && r.all_reduce && r.all_gather && r.destroy && r.err) r.h = h;
+    return r;
+  }();
+  return n.h ? &n : nullptr;
+}
+
+}  // namespace
 
 // ----------------------------------------------------------------- engine
 
@@ -405,12 +502,24 @@ struct tcb_llama {
   cudaGraphExec_t exec = nullptr;
   cudaStream_t cap = nullptr;  // capture stream (the caller's may be the legacy default stream)
   std::vector<void *> allocs;
+  // tensor parallelism: cfg holds this rank's local dimensions
+  int tp = 1, tr = 0, vocab_all = 0, vocab_off = 0;
+  void *comm = nullptr;  // ncclComm_t
+  int2 *cand = nullptr;  // greedy candidates [tp]
+  int nccl_rc = 0;       // last NCCL error
 };
 
 namespace {
 
 int fail(tcb_llama *m, cudaError_t e) {
-  if (m && m->ctx) snprintf(m->ctx->err, sizeof m->ctx->err, "%s", cudaGetErrorString(e));
+  if (m && m->ctx) {
+    if (m->nccl_rc && nccl())
+      snprintf(m->ctx->err, sizeof m->ctx->err, "NCCL: %s", nccl()->err(m->nccl_rc));
+    else if (e == cudaErrorNotReady && m->tp > 1 && !m->comm)
+      snprintf(m->ctx->err, sizeof m->ctx->err, "tensor parallelism: tcb_llama_tp_init was not called");
+    else
+      snprintf(m->ctx->err, sizeof m->ctx->err, "%s", cudaGetErrorString(e));
+  }
   return TCB_ERR_CUDA;
 }
 
@@ -457,6 +566,15 @@ cudaError_t norm_matvec(tcb_llama *m, const Mat &mt, const float *nw, float *y, 
   return e == cudaSuccess ? matvec(m, mt, m->h, y, 0, s) : e;
 }
 
+// x <- sum over ranks (in place), tensor parallelism only
+cudaError_t all_reduce_x(tcb_llama *m, cudaStream_t s) {
+  if (m->tp == 1) return cudaSuccess;
+  const Nccl *nc = nccl();
+  if (!nc || !m->comm) return cudaErrorNotReady;
+  m->nccl_rc = nc->all_reduce(m->x, m->x, (size_t)m->cfg.d_model, kNcclFloat32, kNcclSum, m->comm, s);
+  return m->nccl_rc ? cudaErrorUnknown : cudaSuccess;
+}
+
 cudaError_t issue_step(tcb_llama *m, cudaStream_t s) {
   using namespace tcb::ll;
   const tcb_llama_config &c = m->cfg;
@@ -483,18 +601,31 @@ cudaError_t issue_step(tcb_llama *m, cudaStream_t s) {
     default: e = cudaErrorInvalidValue;
     }
     if (e != cudaSuccess) break;
-    if ((e = matvec(m, m->o[l], m->att, m->x, 1, s)) != cudaSuccess) break;
+    // rank 0 adds its partial to the residual, the others write theirs; the
+    // all-reduce then leaves x + sum of partials on every rank
+    if ((e = matvec(m, m->o[l], m->att, m->x, m->tr == 0, s)) != cudaSuccess) break;
+    if ((e = all_reduce_x(m, s)) != cudaSuccess) break;
     if ((e = norm_matvec(m, m->gu[l], m->ffn_norm[l], m->gub, s)) != cudaSuccess) break;
     if ((e = launch(k_swiglu, dim3((F + 255) / 256), dim3(256), s, m->gub, m->a, F)) != cudaSuccess) break;
-    e = matvec(m, m->down[l], m->a, m->x, 1, s);
+    if ((e = matvec(m, m->down[l], m->a, m->x, m->tr == 0, s)) != cudaSuccess) break;
+    e = all_reduce_x(m, s);
   }
   if (e != cudaSuccess) return e;
   if ((e = launch(k_rmsnorm, dim3(1), dim3(1024), s, m->x, m->final_norm, m->h, D, c.eps)) != cudaSuccess) return e;
   if ((e = matvec(m, m->head, m->h, m->logits, 0, s)) != cudaSuccess) return e;
   if ((e = launch(k_argmax_part, dim3(kArgBlocks), dim3(256), s, m->logits, c.vocab, m->am_v, m->am_i)) != cudaSuccess)
     return e;
-  return launch(k_next_token, dim3(1), dim3(32), s, m->am_v, m->am_i, kArgBlocks, m->pos, m->tok, m->hist, m->prompt,
-                m->nprompt, c.max_ctx);
+  if (m->tp == 1)
+    return launch(k_next_token, dim3(1), dim3(32), s, m->am_v, m->am_i, kArgBlocks, m->pos, m->tok, m->hist,
+                  m->prompt, m->nprompt, c.max_ctx);
+  if ((e = launch(k_local_best, dim3(1), dim3(32), s, m->am_v, m->am_i, kArgBlocks, m->vocab_off, m->cand + m->tr)) !=
+      cudaSuccess)
+    return e;
+  const Nccl *nc = nccl();
+  if (!nc || !m->comm) return cudaErrorNotReady;
+  if ((m->nccl_rc = nc->all_gather(m->cand + m->tr, m->cand, 2, kNcclInt32, m->comm, s)) != 0) return cudaErrorUnknown;
+  return launch(k_pick_tp, dim3(1), dim3(32), s, m->cand, m->tp, m->pos, m->tok, m->hist, m->prompt, m->nprompt,
+                c.max_ctx);
 }
 
 }  // namespace
@@ -504,11 +635,20 @@ extern "C" {
 int tcb_llama_create(tcb_ctx *ctx, const tcb_llama_config *cfg, const tcb_llama_weights *w, tcb_llama **out) {
   if (!ctx || !cfg || !w || !out) return TCB_ERR_NULL;
   *out = nullptr;
-  const tcb_llama_config &c = *cfg;
-  if (c.n_layers < 1 || c.d_model < 1 || c.n_heads < 1 || c.n_kv_heads < 1 || c.head_dim != tcb::ll::kHd ||
-      c.n_heads % c.n_kv_heads || c.ffn_dim < 1 || c.vocab < 1 || c.max_ctx < 2 || !(c.eps > 0.f) ||
-      !(c.rope_theta > 0.f))
+  const tcb_llama_config &cg = *cfg;
+  const int tp = cg.tp_size > 1 ? cg.tp_size : 1, tr = tp > 1 ? cg.tp_rank : 0;
+  if (cg.n_layers < 1 || cg.d_model < 1 || cg.n_heads < 1 || cg.n_kv_heads < 1 || cg.head_dim != tcb::ll::kHd ||
+      cg.n_heads % cg.n_kv_heads || cg.ffn_dim < 1 || cg.vocab < 1 || cg.max_ctx < 2 || !(cg.eps > 0.f) ||
+      !(cg.rope_theta > 0.f) || tr < 0 || tr >= tp || cg.n_heads % tp || cg.n_kv_heads % tp || cg.ffn_dim % tp ||
+      cg.vocab % tp)
     return TCB_ERR_SHAPE;
+  // this rank's dimensions
+  tcb_llama_config lc = cg;
+  lc.n_heads /= tp;
+  lc.n_kv_heads /= tp;
+  lc.ffn_dim /= tp;
+  lc.vocab /= tp;
+  const tcb_llama_config &c = lc;
   const int G = c.n_heads / c.n_kv_heads;
   if (G != 1 && G != 2 && G != 4 && G != 8) return TCB_ERR_UNSUPPORTED;
   if (!w->tok_emb || !w->final_norm || !w->head || !w->attn_norm || !w->ffn_norm || !w->qkv || !w->o ||
@@ -527,6 +667,10 @@ int tcb_llama_create(tcb_ctx *ctx, const tcb_llama_config *cfg, const tcb_llama_
   tcb_llama *m = new tcb_llama();
   m->ctx = ctx;
   m->cfg = c;
+  m->tp = tp;
+  m->tr = tr;
+  m->vocab_all = cg.vocab;
+  m->vocab_off = tr * c.vocab;
   m->tok_emb = w->tok_emb;
   m->tok_emb_type = w->tok_emb_type;
   m->final_norm = w->final_norm;
@@ -577,7 +721,7 @@ int tcb_llama_create(tcb_ctx *ctx, const tcb_llama_config *cfg, const tcb_llama_
       (e = alloc(m, &m->vc, cache)) != cudaSuccess || (e = alloc(m, &m->pos, 1)) != cudaSuccess ||
       (e = alloc(m, &m->nprompt, 1)) != cudaSuccess || (e = alloc(m, &m->tok, 1)) != cudaSuccess ||
       (e = alloc(m, &m->hist, c.max_ctx)) != cudaSuccess || (e = alloc(m, &m->prompt, c.max_ctx)) != cudaSuccess ||
-      (e = alloc(m, &m->acount, KVH)) != cudaSuccess) {
+      (e = alloc(m, &m->acount, KVH)) != cudaSuccess || (e = alloc(m, &m->cand, tp)) != cudaSuccess) {
     tcb_llama_destroy(m);
     return e == cudaErrorMemoryAllocation ? TCB_ERR_NOMEM : TCB_ERR_CUDA;
   }
@@ -610,6 +754,7 @@ int tcb_llama_destroy(tcb_llama *m) {
   if (m->graph) cudaGraphDestroy(m->graph);
   if (!m->allocs.empty()) cudaDeviceSynchronize();
   if (m->cap) cudaStreamDestroy(m->cap);
+  if (m->comm) nccl()->destroy(m->comm);
   for (void *p : m->allocs) cudaFree(p);
   delete m;
   return TCB_OK;
@@ -619,7 +764,7 @@ int tcb_llama_start(tcb_llama *m, const int64_t *prompt, int n, void *stream) {
   if (!m || !prompt) return TCB_ERR_NULL;
   if (n < 1 || n > m->cfg.max_ctx) return TCB_ERR_SHAPE;
   for (int i = 0; i < n; i++)
-    if (prompt[i] < 0 || prompt[i] >= m->cfg.vocab) return TCB_ERR_BOUNDS;
+    if (prompt[i] < 0 || prompt[i] >= m->vocab_all) return TCB_ERR_BOUNDS;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int zero = 0;
   cudaError_t e;
@@ -675,6 +820,34 @@ int tcb_llama_capture(tcb_llama *m, void *stream) {
   if ((e = cudaGraphInstantiate(&m->exec, g, 0)) != cudaSuccess) {
     m->exec = nullptr;
     return fail(m, e);
+  }
+  return TCB_OK;
+}
+
+int tcb_nccl_unique_id(unsigned char *id128) {
+  if (!id128) return TCB_ERR_NULL;
+  const Nccl *nc = nccl();
+  if (!nc) return TCB_ERR_UNSUPPORTED;
+  NcclId id;
+  if (nc->get_id(&id) != 0) return TCB_ERR_CUDA;
+  memcpy(id128, id.internal, sizeof id.internal);
+  return TCB_OK;
+}
+
+int tcb_llama_tp_init(tcb_llama *m, const unsigned char *id128) {
+  if (!m || !id128) return TCB_ERR_NULL;
+  if (m->tp == 1) return TCB_OK;
+  const Nccl *nc = nccl();
+  if (!nc) return TCB_ERR_UNSUPPORTED;
+  if (m->comm) return TCB_OK;
+  if (cudaSetDevice(m->ctx->dev) != cudaSuccess) return TCB_ERR_CUDA;
+  NcclId id;
+  memcpy(id.internal, id128, sizeof id.internal);
+  const int rc = nc->init_rank(&m->comm, m->tp, id, m->tr);
+  if (rc != 0) {
+    snprintf(m->ctx->err, sizeof m->ctx->err, "NCCL: %s", nc->err(rc));
+    m->comm = nullptr;
+    return TCB_ERR_CUDA;
   }
   return TCB_OK;
 }

@@ -38,6 +38,7 @@ class LlamaConfig:
 
 
 LLAMA3_8B = LlamaConfig(32, 4096, 32, 8, 128, 14336, 128256, 768)
+LLAMA3_70B = LlamaConfig(80, 8192, 64, 8, 128, 28672, 128256, 1024 + 128 + 1)
 TYPES = {"tok_emb": Q4_K, "qkv": Q4_K, "o": Q6_K, "gate_up": Q4_K, "down": Q6_K, "head": Q6_K}
 # Standard deviation of the fp16 block scales of a random-init decoder.  The
 # matvec benchmark's |N(0, 0.01)| scales give weights of standard deviation
@@ -68,6 +69,49 @@ def weight_bytes_per_token(cfg: LlamaConfig) -> int:
     return tot
 
 
+def local_shapes(cfg: LlamaConfig, tp: int) -> dict:
+    """(rows, K) of every tensor kind held by one of tp ranks."""
+    H, KVH, hd, D, F = cfg.n_heads // tp, cfg.n_kv_heads // tp, cfg.head_dim, cfg.d_model, cfg.ffn_dim // tp
+    return {"tok_emb": (cfg.vocab, D), "qkv": ((H + 2 * KVH) * hd, D), "o": (D, H * hd),
+            "gate_up": (2 * F, D), "down": (D, F), "head": (cfg.vocab // tp, D)}
+
+
+def _rows(a: np.ndarray, kind: str, K: int, r0: int, r1: int) -> np.ndarray:
+    """rows [r0, r1) of a block store with K columns"""
+    e, b = BLOCK[TYPES[kind]]
+    rb = K // e * b
+    return a[r0 * rb:r1 * rb]
+
+
+def _cols(a: np.ndarray, kind: str, N: int, K: int, k0: int, k1: int) -> np.ndarray:
+    """columns [k0, k1) (block aligned) of a block store of N rows"""
+    e, b = BLOCK[TYPES[kind]]
+    return a.reshape(N, K // e, b)[:, k0 // e:k1 // e].reshape(-1)
+
+
+def shard(cfg: LlamaConfig, model: dict, tp: int, r: int) -> dict:
+    """Rank r's part of a host model for tensor parallelism over tp ranks:
+    column-parallel qkv (its query heads and their KV heads) and gate/up
+    (its rows of each half), row-parallel (K-split) o and down,
+    vocabulary-parallel head; embedding and norms replicated."""
+    if tp == 1:
+        return model
+    H, KVH, hd, D, F, V = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.d_model, cfg.ffn_dim, cfg.vocab
+    h, kv, f, v = H // tp, KVH // tp, F // tp, V // tp
+    out = {"cfg": cfg, "tok_emb": model["tok_emb"], "final_norm": model["final_norm"],
+           "attn_norm": model["attn_norm"], "ffn_norm": model["ffn_norm"],
+           "head": _rows(model["head"], "head", D, r * v, (r + 1) * v)}
+    out["qkv"] = [np.concatenate([_rows(w, "qkv", D, r * h * hd, (r + 1) * h * hd),
+                                  _rows(w, "qkv", D, (H + r * kv) * hd, (H + (r + 1) * kv) * hd),
+                                  _rows(w, "qkv", D, (H + KVH + r * kv) * hd, (H + KVH + (r + 1) * kv) * hd)])
+                  for w in model["qkv"]]
+    out["o"] = [_cols(w, "o", D, H * hd, r * h * hd, (r + 1) * h * hd) for w in model["o"]]
+    out["gate_up"] = [np.concatenate([_rows(w, "gate_up", D, r * f, (r + 1) * f),
+                                      _rows(w, "gate_up", D, F + r * f, F + (r + 1) * f)]) for w in model["gate_up"]]
+    out["down"] = [_cols(w, "down", D, F, r * f, (r + 1) * f) for w in model["down"]]
+    return out
+
+
 def host_model(cfg: LlamaConfig, seed: int) -> dict:
     """Seeded model as numpy arrays (small configurations: parity tests)."""
     sh = shapes(cfg)
@@ -84,7 +128,7 @@ def host_model(cfg: LlamaConfig, seed: int) -> dict:
     return m
 
 
-def device_model(cfg: LlamaConfig, seed: int, host: dict | None = None) -> dict:
+def device_model(cfg: LlamaConfig, seed: int, host: dict | None = None, tp: tuple = (1, 0)) -> dict:
     """The model on cuda:0: uploads `host` if given, else generates the
     blocks on the GPU (fp16 block scales |N(0, D_STD)|, every other byte
     uniform, as host_model)."""
@@ -94,15 +138,16 @@ def device_model(cfg: LlamaConfig, seed: int, host: dict | None = None) -> dict:
         return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
     if host is not None:
+        host = shard(cfg, host, *tp)
         d = {"cfg": cfg}
         for k, v in host.items():
             if k == "cfg":
                 continue
             d[k] = [up(x) for x in v] if isinstance(v, list) else up(v)
         return d
-    sh = shapes(cfg)
+    sh = local_shapes(cfg, tp[0])
     gen = torch.Generator(device="cuda")
-    gen.manual_seed(seed)
+    gen.manual_seed(seed * 64 + tp[1])
 
     def blocks(kind):
         wt = TYPES[kind]
@@ -131,7 +176,7 @@ class _Cfg(ctypes.Structure):
     _fields_ = [("n_layers", ctypes.c_int), ("d_model", ctypes.c_int), ("n_heads", ctypes.c_int),
                 ("n_kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int), ("ffn_dim", ctypes.c_int),
                 ("vocab", ctypes.c_int), ("max_ctx", ctypes.c_int), ("eps", ctypes.c_float),
-                ("rope_theta", ctypes.c_float)]
+                ("rope_theta", ctypes.c_float), ("tp_size", ctypes.c_int), ("tp_rank", ctypes.c_int)]
 
 
 _PP = ctypes.POINTER(ctypes.c_void_p)
@@ -155,6 +200,8 @@ def _bind():
     L.tcb_llama_step.argtypes = [P, P]
     L.tcb_llama_capture.argtypes = [P, P]
     L.tcb_llama_buffers.argtypes = [P, ctypes.POINTER(P), ctypes.POINTER(P)]
+    L.tcb_nccl_unique_id.argtypes = [P]
+    L.tcb_llama_tp_init.argtypes = [P, P]
     L._llama_bound = True
     return L
 
@@ -162,12 +209,13 @@ def _bind():
 class Llama:
     """A decoder engine over a device model (keeps the model alive)."""
 
-    def __init__(self, ctx, model: dict):
+    def __init__(self, ctx, model: dict, tp: tuple = (1, 0)):
+        """model: this rank's tensors (device_model(..., tp=tp)); tp = (size, rank)."""
         L = _bind()
         cfg = model["cfg"]
-        self.cfg, self.model, self._L = cfg, model, L
+        self.cfg, self.model, self._L, self.tp = cfg, model, L, tp
         c = _Cfg(cfg.n_layers, cfg.d_model, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn_dim, cfg.vocab,
-                 cfg.max_ctx, cfg.eps, cfg.rope_theta)
+                 cfg.max_ctx, cfg.eps, cfg.rope_theta, tp[0], tp[1])
 
         def arr(ts):
             return (ctypes.c_void_p * len(ts))(*[t.data_ptr() for t in ts])
@@ -218,8 +266,14 @@ class Llama:
         return self._download(self._buffers()[0], np.empty(n, np.int64), stream)
 
     def logits(self, stream=None) -> np.ndarray:
-        """The logits of the last step."""
-        return self._download(self._buffers()[1], np.empty(self.cfg.vocab, np.float32), stream)
+        """The logits of the last step (this rank's vocabulary rows)."""
+        n = self.cfg.vocab // self.tp[0]
+        return self._download(self._buffers()[1], np.empty(n, np.float32), stream)
+
+    def tp_init(self, nccl_id: bytes):
+        """Join the tensor-parallel group (every rank, the same 128-byte id)."""
+        buf = ctypes.create_string_buffer(bytes(nccl_id), 128)
+        self._check(self._L.tcb_llama_tp_init(self._h, buf), "tp_init")
 
     def close(self):
         if getattr(self, "_h", None):
@@ -231,3 +285,23 @@ class Llama:
             self.close()
         except Exception:
             pass
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh NCCL id (rank 0 makes it, every rank passes it to tp_init)."""
+    L = _bind()
+    buf = ctypes.create_string_buffer(128)
+    rc = L.tcb_nccl_unique_id(buf)
+    if rc != 0:
+        raise TcbError(rc, "tcb_nccl_unique_id")
+    return buf.raw
+
+
+def share_id(make, rank: int) -> bytes:
+    """Rank 0's make() result on every rank of the default torch.distributed
+    group (any backend)."""
+    import torch.distributed as dist
+
+    obj = [make() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    return obj[0]
