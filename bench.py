@@ -188,6 +188,54 @@ def decode_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
     }
 
 
+def decode_tp_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
+    """70B-shape Q4_K_M greedy decode at batch 1, tensor-parallel over the
+    world's GPUs (QKV/gate/up column-parallel, o/down
+    row-parallel with an NCCL all-reduce each, vocabulary-parallel head):
+    a 1024-token random prompt through the decode step, then 128 greedy
+    tokens, every step one replay of the captured graph.  Batch 16 is not
+    provided (the engine is batch 1)."""
+    import torch
+    import torch.distributed as dist
+
+    from tcb_b200 import llama
+
+    cfg = llama.LLAMA3_70B
+    model = llama.device_model(cfg, seed=9, tp=(world, rank))
+    eng = llama.Llama(ctx, model, tp=(world, rank))
+    eng.tp_init(llama.share_id(llama.nccl_unique_id, rank))
+    prompt = np.random.default_rng(13).integers(0, cfg.vocab, 1024)
+    stream = torch.cuda.Stream()
+    eng.start(prompt, stream)
+    eng.capture(stream)
+    eng.start(prompt, stream)
+    e1, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        eng.step(1023, stream)
+        e1.record(stream)
+        eng.step(128, stream)
+        e2.record(stream)
+    e2.synchronize()
+    t = torch.tensor([e1.elapsed_time(e2)], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    toks = eng.tokens(1152, stream)
+    eng.close()
+    del model
+    bpt = llama.weight_bytes_per_token(cfg)
+    per_gpu = bpt / world
+    return {
+        "model": "llama3-70b-shape q4_k_m (random init, synthetic)", "tensor_parallel": world,
+        "prompt_tokens": 1024, "generated_tokens": 128, "tokens_per_s": round(128 / (ms / 1e3), 2),
+        "ms_per_token": round(ms / 128, 4), "weight_bytes_per_token": bpt, "weight_bytes_per_gpu_per_token": per_gpu,
+        "roofline": {"bound": "hbm", "achieved_per_gpu": round(per_gpu / (ms / 1e3 / 128) / 1e9, 2),
+                     "peak": peak_gbs, "unit": "GB/s", "frac": round(per_gpu / (ms / 1e3 / 128) / 1e9 / peak_gbs, 4),
+                     "ceiling_tokens_per_s": round(peak_gbs * 1e9 / per_gpu, 1)},
+        "collectives_per_token": 2 * cfg.n_layers + 1, "last_tokens": [int(v) for v in toks[-4:]],
+        "timing": "CUDA events around 128 graph replays, max over ranks",
+    }
+
+
 def dist_init():
     if "RANK" not in os.environ:
         return 0, 1, 0
@@ -324,7 +372,10 @@ def main():
         dist.all_reduce(et, op=dist.ReduceOp.MAX)
     e2e_value = per_launch_bytes * e2e_steps * world / (float(et.item()) / 1e3) / 1e9
     del g
-    decode = None if args.no_decode else decode_bench(ctx, rank, world, peaks["hbm_gbs"])
+    decode = None
+    if not args.no_decode:
+        decode = (decode_bench(ctx, rank, world, peaks["hbm_gbs"]) if world == 1
+                  else decode_tp_bench(ctx, rank, world, peaks["hbm_gbs"]))
 
     if rank == 0:
         line = {
