@@ -15,7 +15,9 @@
 //    row pitch is 16 mod 128 and the lane reads below are conflict-free),
 //    issued by a producer warp; rows past N and bytes past the row end are
 //    zero-filled by the copy engine.  Compute warp w (of 8) takes block w of
-//    every stage for both 16-row halves of the tile.
+//    every stage for both 16-row slices of the tile, sharing the x
+//    fragments (measured faster than 16-row tiles, although those balance
+//    the CTAs better).
 //  * x is split per 32-element sub-block into two int8 digits,
 //    x ~= sigma * (h + l/254), sigma = amax/127 (relative error of the x
 //    representation below 1/(2*127*254) of the sub-block maximum).  Each
@@ -59,6 +61,7 @@ constexpr int kProd = kC;                   // producer warp
 constexpr int kEpi = kC + 1;                // epilogue warp
 constexpr int kWarps = kC + 2;
 constexpr int kRows = 32;                   // rows per tile (one box)
+constexpr int kHalves = kRows / 16;         // 16-row MMA slices per tile
 constexpr int kBlk = 8;                     // Q4_K blocks per box
 constexpr int kBox8 = 146;                  // box width, 8-byte elements (8 * 18 + 2)
 constexpr int kPitch = kBox8 * 8;           // staged row pitch (1168 = 16 mod 128)
@@ -282,12 +285,12 @@ __device__ __forceinline__ void epi16(const uint4 (&hd)[2], const float4 sg, con
   }
 }
 
-// A warp's tile partials (rows g, g+8, g+16, g+24, each summed over the four
-// lanes of its group) into slot ti % kSlots for the epilogue warp.
-__device__ __forceinline__ bool tile_partial(int ti, float (&acc)[4], float *part, uint64_t *tdone, uint64_t *tfree,
-                                             int warp, int lane, int *err) {
+// A warp's tile partials (rows g, g+8 of each 16-row slice, each summed over
+// the four lanes of its group) into slot ti % kSlots for the epilogue warp.
+__device__ __forceinline__ bool tile_partial(int ti, float (&acc)[2 * kHalves], float *part, uint64_t *tdone,
+                                             uint64_t *tfree, int warp, int lane, int *err) {
 #pragma unroll
-  for (int i = 0; i < 4; i++) {
+  for (int i = 0; i < 2 * kHalves; i++) {
     acc[i] += __shfl_xor_sync(0xFFFFFFFFu, acc[i], 1);
     acc[i] += __shfl_xor_sync(0xFFFFFFFFu, acc[i], 2);
   }
@@ -297,15 +300,13 @@ __device__ __forceinline__ bool tile_partial(int ti, float (&acc)[4], float *par
   if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) return false;
   float *pt = part + (slot * kC + warp) * kRows + (lane >> 2);
   if ((lane & 3) == 0) {
-    pt[0] = acc[0];
-    pt[8] = acc[1];
-    pt[16] = acc[2];
-    pt[24] = acc[3];
+#pragma unroll
+    for (int i = 0; i < 2 * kHalves; i++) pt[8 * i] = acc[i];
   }
   __syncwarp();
   if (lane == 0) mbar_arrive(&tdone[slot]);
 #pragma unroll
-  for (int i = 0; i < 4; i++) acc[i] = 0.f;
+  for (int i = 0; i < 2 * kHalves; i++) acc[i] = 0.f;
   return true;
 }
 
@@ -316,7 +317,7 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq4k(const __grid_constant_
   uint64_t *tdone = full + 16;                                 // [slots] tile partials ready
   uint64_t *tfree = full + 24;                                 // [slots] tile partials summed
   int *flag = reinterpret_cast<int *>(sm + kFlagOff);
-  float *part = reinterpret_cast<float *>(sm + kPartOff);      // [slots][kC][32]
+  float *part = reinterpret_cast<float *>(sm + kPartOff);      // [slots][kC][kRows]
   uint8_t *xr = sm + kXOff;
   uint8_t *stages = sm + a.soff;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -389,11 +390,11 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq4k(const __grid_constant_
     }
     for (int ti = 0; ti < my_tiles; ti++) {
       const int row = ((int)blockIdx.x + ti * (int)gridDim.x) * kRows + lane;
-      const bool mine = row < a.N;
+      const bool mine = lane < kRows && row < a.N;
       const float cold = (a.accumulate && mine) ? load_out(a.c, row, a.cdt) : 0.f;
       const int slot = ti % kSlots;
       if (!spin_bar_ns(&tdone[slot], (uint32_t)((ti / kSlots) & 1), a.err, 128)) return;
-      const float *pt = part + slot * kC * kRows + lane;
+      const float *pt = part + slot * kC * kRows + (lane < kRows ? lane : 0);
       float v = 0.f;
 #pragma unroll
       for (int j = 0; j < kC; j++) v += pt[((j - rot) & (kBlk - 1)) * kRows];
@@ -415,7 +416,7 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq4k(const __grid_constant_
     const int g = lane >> 2;
     const int own = (warp + (int)blockIdx.x) & (kBlk - 1);
     const int last_ch = own < a.nb ? (a.nb - 1 - own) / kBlk : -1;  // the warp's last chunk of a tile
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    float acc[2 * kHalves] = {};
     int it = 0;
     for (int ti = 0; ti < my_tiles; ti++) {
       for (int ch = 0; ch < a.nch; ch++, it++) {
@@ -424,18 +425,18 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq4k(const __grid_constant_
         if (lane == 0) ok = wait_bar(&full[buf], (uint32_t)((it / a.S) & 1), a.err);
         if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) return;
         const bool has = ch <= last_ch;
-        int D[2][2][4];
-        uint4 hd[2][2];
+        int D[kHalves][2][4];
+        uint4 hd[kHalves][2];
         float4 sg = make_float4(0.f, 0.f, 0.f, 0.f);
         if (has) {
           const int bg = ch * kBlk + own;
           const uint8_t *r0 = stages + buf * kBoxBytes + g * kPitch + own * 144;
           uint4 B[2][2];
           bfrag(Q.xb + bg * Q.xs, B);
-          mma16(r0, B, Q, D[0]);
-          mma16(r0 + 16 * kPitch, B, Q, D[1]);
 #pragma unroll
-          for (int h = 0; h < 2; h++)
+          for (int h = 0; h < kHalves; h++) mma16(r0 + 16 * h * kPitch, B, Q, D[h]);
+#pragma unroll
+          for (int h = 0; h < kHalves; h++)
 #pragma unroll
             for (int r = 0; r < 2; r++)
               hd[h][r] = *reinterpret_cast<const uint4 *>(r0 + (16 * h + 8 * r) * kPitch);
@@ -444,8 +445,8 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq4k(const __grid_constant_
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[buf]);
         if (has) {
-          epi16(hd[0], sg, Q, D[0], acc[0], acc[1]);
-          epi16(hd[1], sg, Q, D[1], acc[2], acc[3]);
+#pragma unroll
+          for (int h = 0; h < kHalves; h++) epi16(hd[h], sg, Q, D[h], acc[2 * h], acc[2 * h + 1]);
         }
         if ((ch == last_ch || (last_ch < 0 && ch == a.nch - 1)) &&
             !tile_partial(ti, acc, part, tdone, tfree, warp, lane, a.err))
@@ -511,7 +512,8 @@ MvPlan q4k_plan(int N, int K, const void *w, int sms) {
   const int base = (kXOff + x_bytes(nb) + 127) & ~127;
   int S, per_sm;
   if (base + 2 * kBoxBytes <= kSmemTwo) {
-    S = 2;
+    S = (kSmemTwo - base) / kBoxBytes;
+    if (S > 6) S = 6;
     per_sm = 2;
   } else {
     S = (kSmemOne - base) / kBoxBytes;
