@@ -12,6 +12,7 @@
 #include "tcb_common.cuh"
 #include "tcb_launch.h"
 #include "tcb_ctx.h"
+#include "tcb_gemm_tc.h"
 #include "tcb_matvec.h"
 
 
@@ -65,8 +66,25 @@ int run_matvec(tcb_ctx *ctx, int wtype, int act8, int M, int N, int K, const voi
   *taken = false;
   tcb::MvPlan pl = tcb::matvec_plan(wtype, act8, M, N, K, w, ctx->sms);
   if (!pl.ok) return TCB_OK;
+  if (pl.split_bytes > ctx->sk_cap) {
+    // grow the split-K scratch (after the device has finished with the old one)
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (pl.split_bytes > ctx->sk_cap) {
+      if (ctx->sk) {
+        TCB_CU(ctx, cudaDeviceSynchronize());
+        cudaFree(ctx->sk);
+        ctx->sk = nullptr;
+        ctx->sk_cap = 0;
+      }
+      const size_t cap = pl.split_bytes + (pl.split_bytes >> 1);
+      TCB_CU(ctx, cudaMalloc(&ctx->sk, cap));
+      TCB_CU(ctx, cudaMemset(ctx->sk, 0, cap));
+      ctx->sk_cap = cap;
+    }
+  }
   *taken = true;
-  cudaError_t e = tcb::matvec_launch(pl, wtype, act8, N, K, w, x, xdt, c, cdt, accumulate, ctx->derr, s);
+  cudaError_t e =
+      tcb::matvec_launch(pl, wtype, act8, N, K, w, x, xdt, c, cdt, accumulate, ctx->derr, s, nullptr, 0, ctx->sk);
   return e == cudaSuccess ? TCB_OK : cuda_fail(ctx, e);
 }
 
@@ -157,7 +175,7 @@ int tcb_ctx_destroy(tcb_ctx *ctx) {
   if (!ctx) return TCB_OK;
   int rc = TCB_OK;
   if (cudaSetDevice(ctx->dev) != cudaSuccess) rc = TCB_ERR_CUDA;
-  for (void *p : {ctx->ws, (void *)ctx->derr})
+  for (void *p : {ctx->ws, (void *)ctx->derr, ctx->sk})
     if (p && cudaFree(p) != cudaSuccess) rc = TCB_ERR_CUDA;
   delete ctx;
   return rc;
@@ -174,6 +192,12 @@ int tcb_qgemm(tcb_ctx *ctx, int wtype, int M, int N, int K, const void *w, const
   bool taken = false;
   rc = run_matvec(ctx, wtype, 0, M, N, K, w, x, xdtype, c, cdtype, accumulate, s, &taken);
   if (taken || rc != TCB_OK) return rc;
+  if (tcb::tc_eligible(wtype, M, N, K, w)) {
+    if ((rc = ensure_ws(ctx, tcb::tc_workspace_bytes(M, N, K))) != TCB_OK) return rc;
+    cudaError_t e = tcb::launch_qgemm_tc(wtype, w, M, N, K, x, xdtype, ldx, c, cdtype, ldc, accumulate, ctx->ws,
+                                         ctx->derr, s);
+    return e == cudaSuccess ? TCB_OK : cuda_fail(ctx, e);
+  }
   cudaError_t e = tcb::launch_qgemm_simt(wtype, w, M, N, K, x, xdtype, ldx, c, cdtype, ldc, accumulate, ctx->sms, s);
   if (e != cudaSuccess) return cuda_fail(ctx, e);
   return TCB_OK;

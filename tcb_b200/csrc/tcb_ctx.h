@@ -11,6 +11,8 @@ struct tcb_ctx {
   void *ws = nullptr;  // scratch owned by the context, grown on demand
   size_t ws_cap = 0;
   int *derr = nullptr;  // device error word (bounded waits that gave up)
+  void *sk = nullptr;   // split-K scratch of the matvec kernels (zeroed; kernels leave it zeroed)
+  size_t sk_cap = 0;
   std::mutex mu;
   char err[256] = {0};
 };

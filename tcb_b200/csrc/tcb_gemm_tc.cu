@@ -1,0 +1,518 @@
+// tcb_gemm_tc.cu - the many-row float product (prefill: M >= kTcMinM rows
+// of activations) on the fifth-generation tensor cores.
+//
+// C (+)= X · dequant(W)ᵀ for Q4_K weights W [N, K] (TR's Backend.Gemm quant
+// branch, gpu/backend_quant.go:43-65; CPU semantics quantGemm,
+// tensor/cpu_quant.go:47-147: the product of X with the opened weights).
+//
+// Two launches:
+//  1. k_tc_prep: each activation row x[m] is scaled by a power of two
+//     (row max brought into [2^14, 2^15)) and rounded once to fp16, stored
+//     K-contiguous in workspace with the fixed 8-periodic order below; each
+//     weight row n gets a power-of-two multiplier from its blocks' scales
+//     (the largest magnitude a row can dequantise to is brought under 2^15),
+//     so no dequantised fp16 weight overflows and small rows keep precision.
+//  2. k_qgemm_tc: a CTA owns a 128 x 256 tile of C (rows of X x rows of W)
+//     and runs a warp-specialised pipeline:
+//       warp 0        TMA loads of fp16 X tiles (128 x 64, 128-byte swizzle)
+//       warp 10       TMA loads of raw Q4_K superblocks (256 rows x 144 B)
+//       warps 2..9    dequantise one 64-element K step of 256 weight rows
+//                     into fp16 in the UMMA K-major 128-byte-swizzled
+//                     layout (one row per thread, packed half2 math), then
+//                     read the accumulator out of tensor memory
+//       warp 1        allocates 256 tensor-memory columns and issues
+//                     tcgen05.mma (M 128, N 256, K 16, f16 x f16 -> f32) from
+//                     one thread; tcgen05.commit frees the operand stages
+//     The epilogue divides out the two power-of-two multipliers (exact) and
+//     writes C with TR's one-rounding rule (accumulate: round(old + v)).
+//
+// Numerics: the weights are computed as fma(q, d·sc, -dmin·m) in fp16 with
+// d·sc and dmin·m rounded once each, the activations are rounded once to
+// fp16 (exact for bf16/f16 inputs), and the products accumulate in f32:
+// about 2e-4 relative L2 against TR's f32 path.
+//
+// The K order inside every aligned group of 8 elements is (0 2 1 3 4 6 5 7):
+// the order in which two 32-bit words of packed nibbles unpack into half2
+// pairs with one mask each.  X is written in the same order, so the dot
+// products are unchanged.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/tcb.h"
+#include "tcb_common.cuh"
+#include "tcb_gemm_tc.h"
+#include "tcb_mv_ptx.cuh"
+
+namespace tcb {
+namespace tc {
+
+using mv::mbar_arrive;
+using mv::mbar_expect_tx;
+using mv::mbar_init;
+using mv::mbar_test_wait;
+using mv::sa;
+using mv::tma_load_2d;
+
+constexpr int kBM = 128, kBN = 256, kBK = 64;
+constexpr int kSA = 4, kSB = 2, kSR = 2;
+constexpr int kABytes = kBM * kBK * 2;  // 16384
+constexpr int kBBytes = kBN * kBK * 2;  // 32768
+constexpr int kRawPitch = 144;          // one Q4_K superblock per row
+constexpr int kRawBytes = kBN * kRawPitch;
+constexpr int kOffB = kSA * kABytes;
+constexpr int kOffR = kOffB + kSB * kBBytes;
+constexpr int kOffBar = kOffR + kSR * kRawBytes;
+constexpr int kNumBars = 2 * kSA + 2 * kSB + 2 * kSR + 1;
+constexpr int kOffSlot = kOffBar + 8 * kNumBars;
+constexpr int kSmem = kOffSlot + 16 + 1024;  // + alignment slack
+constexpr int kWarpA = 0, kWarpMma = 1, kWarpDq = 2, kDqWarps = 8, kWarpRaw = 10;
+constexpr int kThreads = 11 * 32;
+constexpr uint32_t kTmemCols = 256;
+static_assert(kDqWarps * 32 == kBN, "one dequantising thread per weight row");
+
+// tcgen05 instruction descriptor: D f32, A f16, B f16, both K-major, N, M
+constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(kBN >> 3) << 17) |
+                            ((uint32_t)(kBM >> 4) << 24);
+
+// ----------------------------------------------------------------- PTX
+
+// shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (SBO), descriptor version 1
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+__device__ __forceinline__ void tmem_alloc(uint32_t slot, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "r"(cols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void mma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(kIdesc), "r"(acc)
+      : "memory");
+}
+// arrive on bar once every tcgen05 operation this thread issued has completed
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(sa(bar))
+               : "memory");
+}
+// 32 lanes x 32 consecutive 32-bit columns of tensor memory
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%"
+      "19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Bounded poll of a barrier phase by one thread.  Gives up (false) when
+// another role has aborted or after 2^26 polls, recording a timeout.
+__device__ __forceinline__ bool poll(uint64_t *bar, uint32_t ph, volatile int *ab, int *err, unsigned ns) {
+  for (uint32_t i = 0; i < (1u << 26); i++) {
+    if (mbar_test_wait(bar, ph)) return true;
+    if (*ab) return false;
+    if (ns) __nanosleep(ns);
+  }
+  *ab = 1;
+  atomicExch(err, TCB_ERR_TIMEOUT);
+  return false;
+}
+// The same for a whole warp: lane 0 polls, __syncwarp orders the other
+// lanes' accesses after the phase it observed.
+__device__ __forceinline__ bool warp_poll(uint64_t *bar, uint32_t ph, volatile int *ab, int *err, unsigned ns) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = poll(bar, ph, ab, err, ns);
+  __syncwarp();
+  return __shfl_sync(0xFFFFFFFFu, ok, 0) != 0;
+}
+// the same without the abort exit (draining copies still in flight)
+__device__ __forceinline__ void drain(uint64_t *bar, uint32_t ph, int *err) {
+  for (uint32_t i = 0; i < (1u << 22); i++) {
+    if (mbar_test_wait(bar, ph)) return;
+    __nanosleep(64);
+  }
+  atomicExch(err, TCB_ERR_TIMEOUT);
+}
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+__device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+
+// 1024 + q for the two 4-bit fields of u under mask (lanes 0-15 / 16-31)
+__device__ __forceinline__ __half2 nib2(uint32_t u, uint32_t mask) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(u), "r"(mask), "r"(0x64006400u));  // (u & mask) | magic
+  return bits_h2(r);
+}
+
+// ----------------------------------------------------------------- kernels
+
+// k_tc_prep: blocks [0, M) scale and convert activation rows; the rest scan
+// weight rows (one warp per row).
+__global__ void __launch_bounds__(256) k_tc_prep(const void *x, int xdt, long ldx, int M, int K, __half *xh,
+                                                 float *ix, const uint8_t *w, int N, int nsb, float *mw,
+                                                 float *iw) {
+  __shared__ float red[8];
+  __shared__ int bad_s;
+  if ((int)blockIdx.x < M) {
+    const int m = blockIdx.x;
+    const char *row = static_cast<const char *>(x) + (size_t)m * ldx * (xdt == TCB_F32 ? 4 : 2);
+    float amax = 0.f;
+    int bad = 0;
+    if (threadIdx.x == 0) bad_s = 0;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+      const float v = fabsf(load_act(row, k, xdt));
+      bad |= !(v <= 3.402823466e38f);
+      amax = fmaxf(amax, v);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    if (bad) bad_s = 1;
+    __syncthreads();
+    float a = red[0];
+    for (int i = 1; i < 8; i++) a = fmaxf(a, red[i]);
+    int e = 0;
+    if (!bad_s && a > 0.f) e = min(max(ilogbf(a) - 14, -100), 100);
+    const float mul = ldexpf(1.f, -e);
+    if (threadIdx.x == 0) ix[m] = ldexpf(1.f, e);
+    // 8 outputs per thread in the K order (0 2 1 3 4 6 5 7)
+    uint4 *dst = reinterpret_cast<uint4 *>(xh + (size_t)m * K);
+    for (int g = threadIdx.x; g < K / 8; g += blockDim.x) {
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 8; i++) v[i] = __fmul_rn(load_act(row, 8 * g + i, xdt), mul);
+      uint4 o;
+      o.x = h2_bits(__floats2half2_rn(v[0], v[2]));
+      o.y = h2_bits(__floats2half2_rn(v[1], v[3]));
+      o.z = h2_bits(__floats2half2_rn(v[4], v[6]));
+      o.w = h2_bits(__floats2half2_rn(v[5], v[7]));
+      dst[g] = o;
+    }
+    return;
+  }
+  // weight row n: the largest |d·sc·q - dmin·m| any of its blocks can give is
+  // below 945|d| + 63|dmin|
+  const int n = ((int)blockIdx.x - M) * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (n >= N) return;
+  const uint8_t *r = w + (size_t)n * nsb * kRawPitch;
+  float bound = 0.f;
+  int bad = 0;
+  for (int b = lane; b < nsb; b += 32) {
+    const uint32_t dm = *reinterpret_cast<const uint32_t *>(r + (size_t)b * kRawPitch);
+    const float d = fabsf(__half2float(__ushort_as_half((unsigned short)(dm & 0xFFFFu))));
+    const float dn = fabsf(__half2float(__ushort_as_half((unsigned short)(dm >> 16))));
+    const float bb = fmaf(945.f, d, 63.f * dn);
+    bad |= !(bb <= 3.402823466e38f);
+    bound = fmaxf(bound, bb);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) bound = fmaxf(bound, __shfl_xor_sync(0xFFFFFFFFu, bound, o));
+  bad = __any_sync(0xFFFFFFFFu, bad);
+  int e = 0;
+  if (!bad && bound > 0.f) e = min(max(ilogbf(bound) - 14, -100), 100);
+  if (lane == 0) {
+    mw[n] = ldexpf(1.f, -e);
+    iw[n] = ldexpf(1.f, e);
+  }
+}
+
+struct TcArgs {
+  CUtensorMap ta;  // fp16 X [M][K], box 64 x 128, 128-byte swizzle
+  CUtensorMap tw;  // weight bytes [N][nsb * 144], box 144 x 256
+  const float *mw, *iw, *ix;
+  void *c;
+  long ldc;
+  int cdt, accumulate, M, N, nsb;
+  int *err;
+};
+
+__global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc(const __grid_constant__ TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint8_t *sA = sm, *sB = sm + kOffB, *sR = sm + kOffR;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kOffBar);
+  uint64_t *aF = bars, *aE = bars + kSA, *bF = bars + 2 * kSA, *bE = bF + kSB, *rF = bE + kSB, *rE = rF + kSR,
+           *accF = rE + kSR;
+  uint32_t *slot = reinterpret_cast<uint32_t *>(sm + kOffSlot);
+  volatile int *ab = reinterpret_cast<volatile int *>(sm + kOffSlot + 4);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tn = blockIdx.x, tm = blockIdx.y;
+  const int nks = a.nsb * 4;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kSA; i++) {
+      mbar_init(aF + i, 1);
+      mbar_init(aE + i, 1);
+    }
+    for (int i = 0; i < kSB; i++) {
+      mbar_init(bF + i, kDqWarps);
+      mbar_init(bE + i, 1);
+    }
+    for (int i = 0; i < kSR; i++) {
+      mbar_init(rF + i, 1);
+      mbar_init(rE + i, kDqWarps);
+    }
+    mbar_init(accF, 1);
+    *ab = 0;
+    mv::fence_barrier_init();
+  }
+  if (warp == kWarpMma) {
+    tmem_alloc(sa(slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *slot;
+  mv::pdl_wait();
+
+  if (warp == kWarpA) {
+    if (lane == 0) {
+      int ks = 0;
+      for (; ks < nks; ks++) {
+        const int s = ks % kSA;
+        if (!poll(aE + s, ((ks / kSA) & 1) ^ 1, ab, a.err, 0)) break;
+        mbar_expect_tx(aF + s, kABytes);
+        tma_load_2d(sA + s * kABytes, &a.ta, ks * kBK, tm * kBM, aF + s);
+      }
+      for (int j = ks - kSA > 0 ? ks - kSA : 0; j < ks; j++) drain(aF + j % kSA, (j / kSA) & 1, a.err);
+    }
+  } else if (warp == kWarpRaw) {
+    if (lane == 0) {
+      int sb = 0;
+      for (; sb < a.nsb; sb++) {
+        const int r = sb % kSR;
+        if (!poll(rE + r, ((sb / kSR) & 1) ^ 1, ab, a.err, 0)) break;
+        mbar_expect_tx(rF + r, kRawBytes);
+        tma_load_2d(sR + r * kRawBytes, &a.tw, sb * kRawPitch, tn * kBN, rF + r);
+      }
+      for (int j = sb - kSR > 0 ? sb - kSR : 0; j < sb; j++) drain(rF + j % kSR, (j / kSR) & 1, a.err);
+    }
+  } else if (warp == kWarpMma) {
+    if (lane == 0) {
+      const uint32_t a0 = sa(sA), b0 = sa(sB);
+      for (int ks = 0; ks < nks; ks++) {
+        const int s = ks % kSA, t = ks % kSB;
+        if (!poll(aF + s, (ks / kSA) & 1, ab, a.err, 0)) break;
+        if (!poll(bF + t, (ks / kSB) & 1, ab, a.err, 0)) break;
+        tc_fence_after();
+        const uint64_t da = sw128_desc(a0 + s * kABytes), db = sw128_desc(b0 + t * kBBytes);
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; kk++) mma_f16(tmem, da + 2 * kk, db + 2 * kk, (ks | kk) != 0);
+        mma_commit(aE + s);
+        mma_commit(bE + t);
+      }
+      mma_commit(accF);
+    }
+  } else {
+    // ---- dequantise: thread = weight row of the tile
+    const int row = threadIdx.x - kWarpDq * 32;
+    const int n = tn * kBN + row;
+    const float mwr = n < a.N ? a.mw[n] : 0.f;
+    const uint32_t sw = (uint32_t)(row & 7);
+    bool ok = true;
+    for (int sb = 0; sb < a.nsb && ok; sb++) {
+      const int r = sb % kSR;
+      if (!warp_poll(rF + r, (sb / kSR) & 1, ab, a.err, 32)) {
+        ok = false;
+        break;
+      }
+      const uint8_t *blk = sR + r * kRawBytes + row * kRawPitch;
+      const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
+      const float dd = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFFu))), mwr);
+      const float dm = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(hdr.x >> 16))), mwr);
+      const uint8_t sc12[12] = {
+          (uint8_t)hdr.y,         (uint8_t)(hdr.y >> 8), (uint8_t)(hdr.y >> 16), (uint8_t)(hdr.y >> 24),
+          (uint8_t)hdr.z,         (uint8_t)(hdr.z >> 8), (uint8_t)(hdr.z >> 16), (uint8_t)(hdr.z >> 24),
+          (uint8_t)hdr.w,         (uint8_t)(hdr.w >> 8), (uint8_t)(hdr.w >> 16), (uint8_t)(hdr.w >> 24)};
+#pragma unroll
+      for (int g = 0; g < 4; g++) {
+        const int ks = sb * 4 + g, t = ks % kSB;
+        if (!warp_poll(bE + t, ((ks / kSB) & 1) ^ 1, ab, a.err, 32)) {
+          ok = false;
+          break;
+        }
+        uint32_t s0, m0, s1, m1;
+        q4k_scale(2 * g, sc12, s0, m0);
+        q4k_scale(2 * g + 1, sc12, s1, m1);
+        const __half2 dlo = __float2half2_rn(__fmul_rn(dd, (float)s0));
+        const __half2 nlo = __float2half2_rn(-__fmul_rn(dm, (float)m0));
+        const __half2 dhi = __float2half2_rn(__fmul_rn(dd, (float)s1 * 0.0625f));
+        const __half2 nhi = __float2half2_rn(-__fmul_rn(dm, (float)m1));
+        const __half2 magic = bits_h2(0x64006400u);
+        const uint4 *qs = reinterpret_cast<const uint4 *>(blk + 16 + 32 * g);
+        uint8_t *dst = sB + t * kBBytes + row * 128;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+          const uint4 q = qs[h];
+          const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+          for (int p = 0; p < 2; p++) {  // 8 bytes -> chunk c (low nibbles) and c + 4 (high)
+            const int c = 2 * h + p;
+            const uint32_t w0 = wd[2 * p], w1 = wd[2 * p + 1], u0 = w0 >> 8, u1 = w1 >> 8;
+            uint4 lo, hi;
+            lo.x = h2_bits(__hfma2(__hsub2(nib2(w0, 0x000F000Fu), magic), dlo, nlo));
+            lo.y = h2_bits(__hfma2(__hsub2(nib2(u0, 0x000F000Fu), magic), dlo, nlo));
+            lo.z = h2_bits(__hfma2(__hsub2(nib2(w1, 0x000F000Fu), magic), dlo, nlo));
+            lo.w = h2_bits(__hfma2(__hsub2(nib2(u1, 0x000F000Fu), magic), dlo, nlo));
+            hi.x = h2_bits(__hfma2(__hsub2(nib2(w0, 0x00F000F0u), magic), dhi, nhi));
+            hi.y = h2_bits(__hfma2(__hsub2(nib2(u0, 0x00F000F0u), magic), dhi, nhi));
+            hi.z = h2_bits(__hfma2(__hsub2(nib2(w1, 0x00F000F0u), magic), dhi, nhi));
+            hi.w = h2_bits(__hfma2(__hsub2(nib2(u1, 0x00F000F0u), magic), dhi, nhi));
+            *reinterpret_cast<uint4 *>(dst + (((uint32_t)c ^ sw) << 4)) = lo;
+            *reinterpret_cast<uint4 *>(dst + (((uint32_t)(c + 4) ^ sw) << 4)) = hi;
+          }
+        }
+        mv::fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bF + t);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(rE + r);
+    }
+    (void)ok;
+    // ---- epilogue: lanes 32q.. of tensor memory = rows of X, half h of the columns
+    // all MMAs done (the MMA thread always commits accF, also after an abort)
+    int done = 0;
+    if (lane == 0) {
+      for (uint32_t i = 0; i < (1u << 24) && !done; i++) {
+        done = mbar_test_wait(accF, 0);
+        if (!done) __nanosleep(64);
+      }
+      if (!done) {
+        *ab = 1;
+        atomicExch(a.err, TCB_ERR_TIMEOUT);
+      }
+    }
+    __syncwarp();
+    done = __shfl_sync(0xFFFFFFFFu, done, 0);
+    tc_fence_after();
+    const int q = warp & 3, h = (warp - kWarpDq) >> 2;
+    const int m = tm * kBM + q * 32 + lane;
+    const bool live = done && !*ab && m < a.M;
+    const float sx = live ? a.ix[m] : 0.f;
+#pragma unroll 1
+    for (int j = 0; j < 4; j++) {
+      const int col = h * 128 + j * 32;
+      uint32_t v[32];
+      tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)col, v);
+      if (live) {
+        const long base = (long)m * a.ldc;
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+          const int nn = tn * kBN + col + i;
+          if (nn < a.N) store_out(a.c, base + nn, a.cdt, __fmul_rn(__fmul_rn(__uint_as_float(v[i]), sx), a.iw[nn]),
+                                  a.accumulate != 0);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWarpMma) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace tc
+
+// ----------------------------------------------------------------- host
+
+bool tc_eligible(int wtype, int M, int N, int K, const void *w) {
+  return wtype == TCB_Q4_K && M >= kTcMinM && N > 0 && K >= 256 && K % 256 == 0 &&
+         (reinterpret_cast<uintptr_t>(w) & 15) == 0 && tensor_map_encoder() != nullptr;
+}
+
+size_t tc_workspace_bytes(int M, int N, int K) {
+  const size_t xh = ((size_t)M * K * 2 + 255) & ~(size_t)255;
+  return xh + (((size_t)M * 4 + 255) & ~(size_t)255) + 2 * (((size_t)N * 4 + 255) & ~(size_t)255);
+}
+
+cudaError_t launch_qgemm_tc(int wtype, const void *w, int M, int N, int K, const void *x, int xdt, long ldx, void *c,
+                            int cdt, long ldc, int accumulate, void *ws, int *err, cudaStream_t s) {
+  (void)wtype;
+  using namespace tc;
+  const int nsb = K / 256;
+  uint8_t *p = static_cast<uint8_t *>(ws);
+  __half *xh = reinterpret_cast<__half *>(p);
+  p += ((size_t)M * K * 2 + 255) & ~(size_t)255;
+  float *ix = reinterpret_cast<float *>(p);
+  p += ((size_t)M * 4 + 255) & ~(size_t)255;
+  float *mw = reinterpret_cast<float *>(p);
+  p += ((size_t)N * 4 + 255) & ~(size_t)255;
+  float *iw = reinterpret_cast<float *>(p);
+
+  TcArgs a{};
+  auto enc = tensor_map_encoder();
+  if (!enc) return cudaErrorNotSupported;
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+    cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    cuuint32_t box[2] = {kBK, kBM}, es[2] = {1, 1};
+    if (enc(&a.ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xh, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  {
+    const size_t rb = (size_t)nsb * kRawPitch;
+    cuuint64_t dims[2] = {(cuuint64_t)rb, (cuuint64_t)N};
+    cuuint64_t strides[1] = {(cuuint64_t)rb};
+    cuuint32_t box[2] = {kRawPitch, kBN}, es[2] = {1, 1};
+    if (enc(&a.tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(w), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  a.mw = mw;
+  a.iw = iw;
+  a.ix = ix;
+  a.c = c;
+  a.ldc = ldc;
+  a.cdt = cdt;
+  a.accumulate = accumulate;
+  a.M = M;
+  a.N = N;
+  a.nsb = nsb;
+  a.err = err;
+
+  k_tc_prep<<<M + (N + 7) / 8, 256, 0, s>>>(x, xdt, ldx, M, K, xh, ix, static_cast<const uint8_t *>(w), N, nsb, mw,
+                                             iw);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+
+  static bool attr = [] {
+    return cudaFuncSetAttribute(k_qgemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) == cudaSuccess;
+  }();
+  if (!attr) return cudaErrorInvalidConfiguration;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((N + kBN - 1) / kBN, (M + kBM - 1) / kBM);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_qgemm_tc, a);
+}
+
+}  // namespace tcb

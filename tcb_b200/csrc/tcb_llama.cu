@@ -506,6 +506,7 @@ struct tcb_llama {
   int tp = 1, tr = 0, vocab_all = 0, vocab_off = 0;
   void *comm = nullptr;  // ncclComm_t
   int2 *cand = nullptr;  // greedy candidates [tp]
+  void *sk = nullptr;    // split-K scratch shared by the step's matvecs (they run one after another)
   int nccl_rc = 0;       // last NCCL error
 };
 
@@ -550,7 +551,7 @@ Mat make_mat(const void *w, int type, int N, int K, int sms) {
 cudaError_t matvec(tcb_llama *m, const Mat &mt, const float *x, float *y, int accumulate, cudaStream_t s) {
   if (mt.plan.ok)
     return tcb::matvec_launch(mt.plan, mt.type, 0, mt.N, mt.K, mt.w, x, TCB_F32, y, TCB_F32, accumulate,
-                              m->ctx->derr, s, mt.pf, mt.pf_bytes);
+                              m->ctx->derr, s, mt.pf, mt.pf_bytes, m->sk);
   return tcb::launch_qgemm_simt(mt.type, mt.w, 1, mt.N, mt.K, x, TCB_F32, mt.K, y, TCB_F32, mt.N, accumulate,
                                 m->ctx->sms, s);
 }
@@ -606,8 +607,16 @@ cudaError_t issue_step(tcb_llama *m, cudaStream_t s) {
     if ((e = matvec(m, m->o[l], m->att, m->x, m->tr == 0, s)) != cudaSuccess) break;
     if ((e = all_reduce_x(m, s)) != cudaSuccess) break;
     if ((e = norm_matvec(m, m->gu[l], m->ffn_norm[l], m->gub, s)) != cudaSuccess) break;
-    if ((e = launch(k_swiglu, dim3((F + 255) / 256), dim3(256), s, m->gub, m->a, F)) != cudaSuccess) break;
-    if ((e = matvec(m, m->down[l], m->a, m->x, m->tr == 0, s)) != cudaSuccess) break;
+    if (m->down[l].plan.ok && m->down[l].plan.kind == 2) {
+      // SwiGLU fused into the Q6_K matvec's prologue
+      const Mat &dm = m->down[l];
+      e = tcb::q6k_launch(dm.plan, dm.N, dm.K, dm.w, m->gub, TCB_F32, m->x, TCB_F32, m->tr == 0, m->ctx->derr, s, 1,
+                          dm.pf, dm.pf_bytes, m->sk);
+    } else {
+      if ((e = launch(k_swiglu, dim3((F + 255) / 256), dim3(256), s, m->gub, m->a, F)) != cudaSuccess) break;
+      e = matvec(m, m->down[l], m->a, m->x, m->tr == 0, s);
+    }
+    if (e != cudaSuccess) break;
     e = all_reduce_x(m, s);
   }
   if (e != cudaSuccess) return e;
@@ -706,6 +715,10 @@ int tcb_llama_create(tcb_ctx *ctx, const tcb_llama_config *cfg, const tcb_llama_
       chain[i]->pf_bytes = nx->bytes() < kPrefetchMax ? nx->bytes() : kPrefetchMax;
     }
   }
+  size_t sk_bytes = m->head.plan.split_bytes;
+  for (int l = 0; l < c.n_layers; l++)
+    for (const Mat *mt : {&m->qkv[l], &m->o[l], &m->gu[l], &m->down[l]})
+      sk_bytes = mt->plan.split_bytes > sk_bytes ? mt->plan.split_bytes : sk_bytes;
   m->nch_max = (c.max_ctx + tcb::ll::kChunk - 1) / tcb::ll::kChunk;
   const size_t cache = (size_t)c.n_layers * KVH * c.max_ctx * hd;
   const int qkvn = (H + 2 * KVH) * hd;
@@ -721,7 +734,8 @@ int tcb_llama_create(tcb_ctx *ctx, const tcb_llama_config *cfg, const tcb_llama_
       (e = alloc(m, &m->vc, cache)) != cudaSuccess || (e = alloc(m, &m->pos, 1)) != cudaSuccess ||
       (e = alloc(m, &m->nprompt, 1)) != cudaSuccess || (e = alloc(m, &m->tok, 1)) != cudaSuccess ||
       (e = alloc(m, &m->hist, c.max_ctx)) != cudaSuccess || (e = alloc(m, &m->prompt, c.max_ctx)) != cudaSuccess ||
-      (e = alloc(m, &m->acount, KVH)) != cudaSuccess || (e = alloc(m, &m->cand, tp)) != cudaSuccess) {
+      (e = alloc(m, &m->acount, KVH)) != cudaSuccess || (e = alloc(m, &m->cand, tp)) != cudaSuccess ||
+      (e = alloc(m, reinterpret_cast<char **>(&m->sk), sk_bytes + 256)) != cudaSuccess) {
     tcb_llama_destroy(m);
     return e == cudaErrorMemoryAllocation ? TCB_ERR_NOMEM : TCB_ERR_CUDA;
   }
@@ -740,7 +754,8 @@ int tcb_llama_create(tcb_ctx *ctx, const tcb_llama_config *cfg, const tcb_llama_
   if ((e = cudaMemcpy(m->cosT, ct.data(), ct.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
       (e = cudaMemcpy(m->sinT, st.data(), st.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
       (e = cudaMemset(m->kc, 0, cache * 2)) != cudaSuccess || (e = cudaMemset(m->vc, 0, cache * 2)) != cudaSuccess ||
-      (e = cudaMemset(m->acount, 0, KVH * sizeof(unsigned))) != cudaSuccess) {
+      (e = cudaMemset(m->acount, 0, KVH * sizeof(unsigned))) != cudaSuccess ||
+      (e = cudaMemset(m->sk, 0, sk_bytes + 256)) != cudaSuccess) {
     tcb_llama_destroy(m);
     return TCB_ERR_CUDA;
   }

@@ -10,13 +10,18 @@ namespace tcb {
 // shape is not taken by it (the caller then runs the portable kernel)
 struct MvPlan {
   bool ok;
-  int kind;                    // 0: generic kernel, 1: Q4_K float kernel
+  int kind;                    // 0: generic kernel, 1: Q4_K float kernel, 2: Q6_K float kernel
   int tiles, cbc, nch;         // tiles, blocks per staged chunk, chunks per row
   int stages, pitch;           // TMA stages, bytes per staged row
   int xoff, toff, soff, smem;  // shared-memory layout
   int grid;
+  int ksplit, cpk;             // K splits and chunks per split (kind 2); 1 when not split
+  size_t split_bytes;          // device scratch a launch needs (zeroed once; launches leave it zeroed), 0 if none
   alignas(64) unsigned char tmap[128];  // TMA descriptor of the weight (CUtensorMap)
 };
+
+// smallest N that takes the Q6_K float kernel (kind 2)
+constexpr int kQ6kMinRows = 32768;
 
 MvPlan matvec_plan(int wtype, int act8, int M, int N, int K, const void *w, int sms);
 
@@ -28,10 +33,19 @@ cudaError_t q4k_launch(const MvPlan &pl, int N, int K, const void *w, const void
                        int accumulate, int *err, cudaStream_t s, const float *nw = nullptr, float eps = 0.f,
                        const void *pf = nullptr, size_t pf_bytes = 0);
 
+// Q6_K float path (kind 2).  With gated, x holds [G | U] (2K elements) and
+// the input is silu(G) * U (a SwiGLU gate fused into the prologue).
+// Small N with large K is split along K (plan.ksplit > 1): the launch then
+// needs plan.split_bytes of scratch that starts zeroed (and is left zeroed).
+MvPlan q6k_plan(int N, int K, const void *w, int sms);
+cudaError_t q6k_launch(const MvPlan &pl, int N, int K, const void *w, const void *x, int xdt, void *c, int cdt,
+                       int accumulate, int *err, cudaStream_t s, int gated = 0, const void *pf = nullptr,
+                       size_t pf_bytes = 0, void *scratch = nullptr);
+
 // pf / pf_bytes: the weights of the next kernel of a chain, streamed into L2
 // by this launch's producers (a hint; nullptr for none)
 cudaError_t matvec_launch(const MvPlan &pl, int wtype, int act8, int N, int K, const void *w, const void *x, int xdt,
                           void *c, int cdt, int accumulate, int *err, cudaStream_t s, const void *pf = nullptr,
-                          size_t pf_bytes = 0);
+                          size_t pf_bytes = 0, void *scratch = nullptr);
 
 }  // namespace tcb

@@ -524,6 +524,8 @@ MvPlan q4k_plan(int N, int K, const void *w, int sms) {
   pl.tiles = (N + kRows - 1) / kRows;
   pl.nch = (nb + kBlk - 1) / kBlk;
   pl.cbc = kBlk;
+  pl.ksplit = 1;
+  pl.cpk = pl.nch;
   pl.stages = S;
   pl.pitch = kPitch;
   pl.xoff = kXOff;

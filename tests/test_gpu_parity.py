@@ -402,6 +402,21 @@ def test_fast_path_non_finite_x(ctx, oracle, fmt):
             assert np.array_equal(got[fin], want[fin])
 
 
+@pytest.mark.parametrize("NK", [(32768, 2560), (40000, 4096)])
+def test_q6k_wide_kernel(ctx, oracle, NK):
+    """Products of at least 32768 rows take the k-slot Q6_K kernel (a full
+    and a ragged last tile, several staged chunks per row)."""
+    N, K = NK
+    raw = synth.weight(T.Q6_K, N, K, seed=N)
+    x = synth.activations(1, K, seed=K)
+    c = torch.zeros((1, N), dtype=torch.float32, device="cuda")
+    ctx.qgemm(T.Q6_K, dev(raw), dev(x), c, accumulate=True)
+    want = oracle.qgemm_float(T.Q6_K, x, raw, N)
+    got = host(c)
+    assert rel_l2(got, want) <= REL_L2
+    assert np.max(np.abs(got - want)) <= 1e-5 * np.sqrt(K) * max(1.0, np.abs(want).max())
+
+
 def test_fast_path_mlp_shapes_16bit(ctx, oracle):
     """bf16 x and bf16/f16 c on the batch-1 kernel (one rounding of f32)."""
     N, K = 4096, 4096
