@@ -159,6 +159,26 @@ __device__ __forceinline__ __half2 nib2(uint32_t u, uint32_t mask) {
   return bits_h2(r);
 }
 
+// 8 code bytes (w0 = bytes 0-3, w1 = bytes 4-7 of an 8-byte group) of a
+// 64-element K step -> chunk c (their low nibbles) and chunk c + 4 (high
+// nibbles) of a 128-byte swizzled row: fma(q, d·sc, -dmin·m) per half2
+__device__ __forceinline__ void dq8(uint32_t w0, uint32_t w1, __half2 dlo, __half2 nlo, __half2 dhi, __half2 nhi,
+                                    uint8_t *row, int c, uint32_t sw) {
+  const __half2 magic = bits_h2(0x64006400u);
+  const uint32_t u0 = w0 >> 8, u1 = w1 >> 8;
+  uint4 lo, hi;
+  lo.x = h2_bits(__hfma2(__hsub2(nib2(w0, 0x000F000Fu), magic), dlo, nlo));
+  lo.y = h2_bits(__hfma2(__hsub2(nib2(u0, 0x000F000Fu), magic), dlo, nlo));
+  lo.z = h2_bits(__hfma2(__hsub2(nib2(w1, 0x000F000Fu), magic), dlo, nlo));
+  lo.w = h2_bits(__hfma2(__hsub2(nib2(u1, 0x000F000Fu), magic), dlo, nlo));
+  hi.x = h2_bits(__hfma2(__hsub2(nib2(w0, 0x00F000F0u), magic), dhi, nhi));
+  hi.y = h2_bits(__hfma2(__hsub2(nib2(u0, 0x00F000F0u), magic), dhi, nhi));
+  hi.z = h2_bits(__hfma2(__hsub2(nib2(w1, 0x00F000F0u), magic), dhi, nhi));
+  hi.w = h2_bits(__hfma2(__hsub2(nib2(u1, 0x00F000F0u), magic), dhi, nhi));
+  *reinterpret_cast<uint4 *>(row + (((uint32_t)c ^ sw) << 4)) = lo;
+  *reinterpret_cast<uint4 *>(row + (((uint32_t)(c + 4) ^ sw) << 4)) = hi;
+}
+
 // ----------------------------------------------------------------- kernels
 
 // k_tc_prep: blocks [0, M) scale and convert activation rows; the rest scan
@@ -355,29 +375,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc(const __grid_constant_
         const __half2 nlo = __float2half2_rn(-__fmul_rn(dm, (float)m0));
         const __half2 dhi = __float2half2_rn(__fmul_rn(dd, (float)s1 * 0.0625f));
         const __half2 nhi = __float2half2_rn(-__fmul_rn(dm, (float)m1));
-        const __half2 magic = bits_h2(0x64006400u);
         const uint4 *qs = reinterpret_cast<const uint4 *>(blk + 16 + 32 * g);
         uint8_t *dst = sB + t * kBBytes + row * 128;
 #pragma unroll
         for (int h = 0; h < 2; h++) {
           const uint4 q = qs[h];
-          const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-          for (int p = 0; p < 2; p++) {  // 8 bytes -> chunk c (low nibbles) and c + 4 (high)
-            const int c = 2 * h + p;
-            const uint32_t w0 = wd[2 * p], w1 = wd[2 * p + 1], u0 = w0 >> 8, u1 = w1 >> 8;
-            uint4 lo, hi;
-            lo.x = h2_bits(__hfma2(__hsub2(nib2(w0, 0x000F000Fu), magic), dlo, nlo));
-            lo.y = h2_bits(__hfma2(__hsub2(nib2(u0, 0x000F000Fu), magic), dlo, nlo));
-            lo.z = h2_bits(__hfma2(__hsub2(nib2(w1, 0x000F000Fu), magic), dlo, nlo));
-            lo.w = h2_bits(__hfma2(__hsub2(nib2(u1, 0x000F000Fu), magic), dlo, nlo));
-            hi.x = h2_bits(__hfma2(__hsub2(nib2(w0, 0x00F000F0u), magic), dhi, nhi));
-            hi.y = h2_bits(__hfma2(__hsub2(nib2(u0, 0x00F000F0u), magic), dhi, nhi));
-            hi.z = h2_bits(__hfma2(__hsub2(nib2(w1, 0x00F000F0u), magic), dhi, nhi));
-            hi.w = h2_bits(__hfma2(__hsub2(nib2(u1, 0x00F000F0u), magic), dhi, nhi));
-            *reinterpret_cast<uint4 *>(dst + (((uint32_t)c ^ sw) << 4)) = lo;
-            *reinterpret_cast<uint4 *>(dst + (((uint32_t)(c + 4) ^ sw) << 4)) = hi;
-          }
+          dq8(q.x, q.y, dlo, nlo, dhi, nhi, dst, 2 * h, sw);
+          dq8(q.z, q.w, dlo, nlo, dhi, nhi, dst, 2 * h + 1, sw);
         }
         mv::fence_proxy_async();
         __syncwarp();
@@ -431,6 +435,395 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc(const __grid_constant_
   }
 }
 
+// ----------------------------------------------------------------- 2-CTA kernel
+//
+// k_qgemm_tc2: a cluster of two CTAs (one per SM) owns a 256 x 256 tile of C
+// and the pair walks the tiles persistently.  CTA r of the pair holds
+// activation rows 128r.. and weight rows 128r.. of the tile; the leader
+// (r = 0) issues tcgen05.mma.cta_group::2 (M 256, N 256, K 16), which reads
+// both CTAs' operand stages and leaves rows 128r.. of the accumulator in CTA
+// r's tensor memory.  Each SM therefore dequantises 128 weight rows per 256
+// rows of X (half the work per flop of the one-CTA tile) and reads half the B
+// operand from shared memory.
+//   warp 0        TMA of the CTA's 128 x 64 fp16 activation tile (both
+//                 CTAs complete_tx on the leader's full barrier)
+//   warp 1        tensor-memory allocation (512 columns: two accumulators);
+//                 in the leader, the MMA issue
+//   warp 2        TMA of raw superblocks (128 weight rows x 144 B)
+//   warps 3..10   dequantise (two threads per weight row, 16 bytes of codes
+//                 each) into the swizzled fp16 stage, arrive on the leader
+//   warps 11..14  epilogue: tensor memory -> C while the next tile runs in
+//                 the other accumulator
+namespace tc2 {
+
+constexpr int kRows = 128;  // activation rows and weight rows per CTA
+constexpr int kBK = 64;
+constexpr int kS = 4;   // operand stages (A and B share the empty barrier)
+constexpr int kSR = 3;  // raw superblock stages
+constexpr int kABytes = kRows * kBK * 2;
+constexpr int kBBytes = kRows * kBK * 2;
+constexpr int kRawBytes = kRows * kRawPitch;
+constexpr int kOffB = kS * kABytes;
+constexpr int kOffR = kOffB + kS * kBBytes;
+constexpr int kOffBar = kOffR + kSR * kRawBytes;
+// aF[kS] bF[kS] E[kS] rF[kSR] rE[kSR] accF[2] accE[2]
+constexpr int kNumBars = 3 * kS + 2 * kSR + 4;
+constexpr int kOffSlot = kOffBar + 8 * kNumBars;
+constexpr int kSmem = kOffSlot + 16 + 1024;
+constexpr int kWarpA = 0, kWarpMma = 1, kWarpRaw = 2, kWarpDq = 3, kDqWarps = 8, kWarpEp = 11, kEpWarps = 4;
+constexpr int kThreads = 15 * 32;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(256 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+static_assert(kDqWarps * 32 == 2 * kRows, "two dequantising threads per weight row");
+static_assert(kSmem <= 232448, "shared memory");
+
+__device__ __forceinline__ uint32_t cta_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// the same shared-memory location in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t mapa(uint32_t a, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void arrive_cluster(uint32_t addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
+}
+__device__ __forceinline__ bool test_wait_cl(uint64_t *bar, uint32_t ph) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(sa(bar)), "r"(ph)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_alloc2(uint32_t slot, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "r"(cols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish2() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc2(uint32_t taddr, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+__device__ __forceinline__ void mma2(uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(kIdesc), "r"(acc)
+      : "memory");
+}
+// arrive on the barrier at cluster address addr once this thread's MMAs are done
+__device__ __forceinline__ void commit2(uint32_t addr) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(addr) : "memory");
+}
+// TMA into this CTA's shared memory, completing on a barrier of either CTA of the pair
+__device__ __forceinline__ void tma_pair(void *dst, const CUtensorMap *tm, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(sa(dst)),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+template <bool CL>
+__device__ __forceinline__ bool poll2(uint64_t *bar, uint32_t ph, volatile int *ab, int *err, unsigned ns) {
+  for (uint32_t i = 0; i < (1u << 26); i++) {
+    if (CL ? test_wait_cl(bar, ph) : mbar_test_wait(bar, ph)) return true;
+    if (*ab) return false;
+    if (ns) __nanosleep(ns);
+  }
+  *ab = 1;
+  atomicExch(err, TCB_ERR_TIMEOUT);
+  return false;
+}
+template <bool CL>
+__device__ __forceinline__ bool warp_poll2(uint64_t *bar, uint32_t ph, volatile int *ab, int *err, unsigned ns) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = poll2<CL>(bar, ph, ab, err, ns);
+  __syncwarp();
+  return __shfl_sync(0xFFFFFFFFu, ok, 0) != 0;
+}
+template <bool CL>
+__device__ __forceinline__ void drain2(uint64_t *bar, uint32_t ph, int *err) {
+  for (uint32_t i = 0; i < (1u << 22); i++) {
+    if (CL ? test_wait_cl(bar, ph) : mbar_test_wait(bar, ph)) return;
+    __nanosleep(64);
+  }
+  atomicExch(err, TCB_ERR_TIMEOUT);
+}
+
+// 32 outputs of row m starting at column n0 (all < N when full)
+__device__ __forceinline__ void store32(const TcArgs &a, long m, int n0, const uint32_t (&v)[32], float sx,
+                                        bool full) {
+  float r[32];
+#pragma unroll
+  for (int i = 0; i < 32; i++) r[i] = __fmul_rn(__uint_as_float(v[i]), sx);
+  const long base = m * a.ldc + n0;
+  const size_t es = a.cdt == TCB_F32 ? 4 : 2;
+  const bool vec = full && ((reinterpret_cast<uintptr_t>(a.c) + (size_t)base * es) & 15) == 0;
+  if (vec) {
+    const float4 *iw4 = reinterpret_cast<const float4 *>(a.iw + n0);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const float4 f = iw4[i];
+      r[4 * i] = __fmul_rn(r[4 * i], f.x);
+      r[4 * i + 1] = __fmul_rn(r[4 * i + 1], f.y);
+      r[4 * i + 2] = __fmul_rn(r[4 * i + 2], f.z);
+      r[4 * i + 3] = __fmul_rn(r[4 * i + 3], f.w);
+    }
+    if (a.cdt == TCB_F32) {
+      float4 *p = reinterpret_cast<float4 *>(static_cast<float *>(a.c) + base);
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        float4 o = make_float4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+        if (a.accumulate) {
+          const float4 old = p[i];
+          o.x = __fadd_rn(old.x, o.x);
+          o.y = __fadd_rn(old.y, o.y);
+          o.z = __fadd_rn(old.z, o.z);
+          o.w = __fadd_rn(old.w, o.w);
+        }
+        p[i] = o;
+      }
+    } else {
+      uint4 *p = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.c) + base);
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        uint4 old = make_uint4(0, 0, 0, 0);
+        if (a.accumulate) old = p[i];
+        const uint32_t ow[4] = {old.x, old.y, old.z, old.w};
+        uint32_t pk[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          uint32_t hh[2];
+#pragma unroll
+          for (int k = 0; k < 2; k++) {
+            float v = r[8 * i + 2 * j + k];
+            const uint16_t o = (uint16_t)(ow[j] >> (16 * k));
+            if (a.accumulate) v = __fadd_rn(a.cdt == TCB_BF16 ? bf16_to_f32(o) : half_exact(o), v);
+            hh[k] = a.cdt == TCB_BF16 ? f32_to_bf16(v) : f32_to_f16(v);
+          }
+          pk[j] = hh[0] | (hh[1] << 16);
+        }
+        p[i] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+    }
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 32; i++)
+    if (n0 + i < a.N) store_out(a.c, base + i, a.cdt, __fmul_rn(r[i], a.iw[n0 + i]), a.accumulate != 0);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant__ TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint8_t *sA = sm, *sB = sm + kOffB, *sR = sm + kOffR;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kOffBar);
+  uint64_t *aF = bars, *bF = bars + kS, *E = bars + 2 * kS, *rF = bars + 3 * kS, *rE = rF + kSR, *accF = rE + kSR,
+           *accE = accF + 2;
+  uint32_t *slot = reinterpret_cast<uint32_t *>(sm + kOffSlot);
+  volatile int *ab = reinterpret_cast<volatile int *>(sm + kOffSlot + 4);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cta_rank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int tiles_n = (a.N + 255) >> 8, tiles = ((a.M + 255) >> 8) * tiles_n;
+  const int nks = a.nsb * 4;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kS; i++) {
+      mbar_init(aF + i, 1);
+      mbar_init(bF + i, 2 * kDqWarps);
+      mbar_init(E + i, 1);
+    }
+    for (int i = 0; i < kSR; i++) {
+      mbar_init(rF + i, 1);
+      mbar_init(rE + i, kDqWarps);
+    }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(accF + i, 1);
+      mbar_init(accE + i, 2 * kEpWarps);
+    }
+    *ab = 0;
+    mv::fence_barrier_init();
+  }
+  if (warp == kWarpMma) {
+    tmem_alloc2(sa(slot), kTmemCols);
+    tmem_relinquish2();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = *slot;
+  mv::pdl_wait();
+
+  if (warp == kWarpA) {
+    if (lane == 0) {
+      const uint32_t laF = mapa(sa(aF), 0);
+      int g = 0;
+      bool ok = true;
+      for (int tile = pair; tile < tiles && ok; tile += npairs) {
+        const int tm = tile / tiles_n;
+        for (int ks = 0; ks < nks; ks++, g++) {
+          const int s = g % kS;
+          if (!poll2<true>(E + s, ((g / kS) & 1) ^ 1, ab, a.err, 0)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_expect_tx(aF + s, 2 * kABytes);
+          tma_pair(sA + s * kABytes, &a.ta, ks * kBK, tm * 256 + (int)rank * kRows, laF + 8 * s);
+        }
+      }
+      // loads still in flight complete before the MMA frees their stage
+      for (int j = g - kS > 0 ? g - kS : 0; j < g; j++) drain2<true>(E + j % kS, (j / kS) & 1, a.err);
+    }
+  } else if (warp == kWarpRaw) {
+    if (lane == 0) {
+      int gr = 0;
+      bool ok = true;
+      for (int tile = pair; tile < tiles && ok; tile += npairs) {
+        const int tn = tile % tiles_n;
+        for (int sb = 0; sb < a.nsb; sb++, gr++) {
+          const int r = gr % kSR;
+          if (!poll2<false>(rE + r, ((gr / kSR) & 1) ^ 1, ab, a.err, 0)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(rF + r, kRawBytes);
+          tma_load_2d(sR + r * kRawBytes, &a.tw, sb * kRawPitch, tn * 256 + (int)rank * kRows, rF + r);
+        }
+      }
+      for (int j = gr - kSR > 0 ? gr - kSR : 0; j < gr; j++) drain2<false>(rF + j % kSR, (j / kSR) & 1, a.err);
+    }
+  } else if (warp == kWarpMma) {
+    if (leader && lane == 0) {
+      const uint32_t a0 = sa(sA), b0 = sa(sB);
+      const uint32_t eOwn = mapa(sa(E), 0), ePeer = mapa(sa(E), 1);
+      const uint32_t fOwn = mapa(sa(accF), 0), fPeer = mapa(sa(accF), 1);
+      int g = 0, it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < tiles && ok; tile += npairs, it++) {
+        const int buf = it & 1;
+        if (!poll2<true>(accE + buf, ((it >> 1) & 1) ^ 1, ab, a.err, 0)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(buf * 256);
+        for (int ks = 0; ks < nks; ks++, g++) {
+          const int s = g % kS;
+          if (!poll2<true>(aF + s, (g / kS) & 1, ab, a.err, 0) || !poll2<true>(bF + s, (g / kS) & 1, ab, a.err, 0)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = sw128_desc(a0 + s * kABytes), db = sw128_desc(b0 + s * kBBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; kk++) mma2(d, da + 2 * kk, db + 2 * kk, (ks | kk) != 0);
+          commit2(eOwn + 8 * s);
+          commit2(ePeer + 8 * s);
+        }
+        commit2(fOwn + 8 * buf);
+        commit2(fPeer + 8 * buf);
+      }
+    }
+  } else if (warp < kWarpEp) {
+    // ---- dequantise: two threads per weight row, 16 code bytes each
+    const int tid = threadIdx.x - kWarpDq * 32, row = tid >> 1, hf = tid & 1;
+    const uint32_t sw = (uint32_t)(row & 7);
+    const uint32_t lbF = mapa(sa(bF), 0);
+    int g = 0, gr = 0;
+    bool ok = true;
+    for (int tile = pair; tile < tiles && ok; tile += npairs) {
+      const int n = (tile % tiles_n) * 256 + (int)rank * kRows + row;
+      const float mwr = n < a.N ? a.mw[n] : 0.f;
+      for (int sb = 0; sb < a.nsb && ok; sb++, gr++) {
+        const int r = gr % kSR;
+        if (!warp_poll2<false>(rF + r, (gr / kSR) & 1, ab, a.err, 32)) {
+          ok = false;
+          break;
+        }
+        const uint8_t *blk = sR + r * kRawBytes + row * kRawPitch;
+        const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
+        const float dd = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFFu))), mwr);
+        const float dm = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(hdr.x >> 16))), mwr);
+        const uint8_t sc12[12] = {
+            (uint8_t)hdr.y, (uint8_t)(hdr.y >> 8), (uint8_t)(hdr.y >> 16), (uint8_t)(hdr.y >> 24),
+            (uint8_t)hdr.z, (uint8_t)(hdr.z >> 8), (uint8_t)(hdr.z >> 16), (uint8_t)(hdr.z >> 24),
+            (uint8_t)hdr.w, (uint8_t)(hdr.w >> 8), (uint8_t)(hdr.w >> 16), (uint8_t)(hdr.w >> 24)};
+#pragma unroll
+        for (int g4 = 0; g4 < 4; g4++) {
+          const int s = g % kS;
+          if (!warp_poll2<true>(E + s, ((g / kS) & 1) ^ 1, ab, a.err, 32)) {
+            ok = false;
+            break;
+          }
+          uint32_t s0, m0, s1, m1;
+          q4k_scale(2 * g4, sc12, s0, m0);
+          q4k_scale(2 * g4 + 1, sc12, s1, m1);
+          const __half2 dlo = __float2half2_rn(__fmul_rn(dd, (float)s0));
+          const __half2 nlo = __float2half2_rn(-__fmul_rn(dm, (float)m0));
+          const __half2 dhi = __float2half2_rn(__fmul_rn(dd, (float)s1 * 0.0625f));
+          const __half2 nhi = __float2half2_rn(-__fmul_rn(dm, (float)m1));
+          const uint4 q = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * g4 + 16 * hf);
+          uint8_t *dst = sB + s * kBBytes + row * 128;
+          dq8(q.x, q.y, dlo, nlo, dhi, nhi, dst, 2 * hf, sw);
+          dq8(q.z, q.w, dlo, nlo, dhi, nhi, dst, 2 * hf + 1, sw);
+          mv::fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) arrive_cluster(lbF + 8 * s);
+          g++;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(rE + r);
+      }
+    }
+  } else {
+    // ---- epilogue: TMEM lanes 32q.. are rows 128 rank + 32q.. of the tile
+    const int q = warp & 3;
+    const uint32_t laE = mapa(sa(accE), 0);
+    int it = 0;
+    for (int tile = pair; tile < tiles; tile += npairs, it++) {
+      const int buf = it & 1;
+      if (!warp_poll2<true>(accF + buf, (it >> 1) & 1, ab, a.err, 64)) break;
+      tc_fence_after();
+      const int tm = tile / tiles_n, tn = tile % tiles_n;
+      const long m = (long)tm * 256 + rank * kRows + q * 32 + lane;
+      const bool live = m < a.M;
+      const float sx = live ? a.ix[m] : 0.f;
+#pragma unroll 1
+      for (int j = 0; j < 8; j++) {
+        uint32_t v[32];
+        tmem_ld32(tmem + (uint32_t)(buf * 256 + j * 32) + ((uint32_t)(q * 32) << 16), v);
+        if (j == 7) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) arrive_cluster(laE + 8 * buf);
+        }
+        const int n0 = tn * 256 + j * 32;
+        if (live && n0 < a.N) store32(a, m, n0, v, sx, n0 + 32 <= a.N);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncwarp();
+  __syncthreads();
+  cluster_sync();
+  if (warp == kWarpMma) {
+    tc_fence_after();
+    tmem_dealloc2(tmem, kTmemCols);
+  }
+}
+
+}  // namespace tc2
+
 }  // namespace tc
 
 // ----------------------------------------------------------------- host
@@ -471,11 +864,12 @@ cudaError_t launch_qgemm_tc(int wtype, const void *w, int M, int N, int K, const
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
+  const bool pair = M > kBM;  // the 2-CTA kernel once X has more than one 128-row tile
   {
     const size_t rb = (size_t)nsb * kRawPitch;
     cuuint64_t dims[2] = {(cuuint64_t)rb, (cuuint64_t)N};
     cuuint64_t strides[1] = {(cuuint64_t)rb};
-    cuuint32_t box[2] = {kRawPitch, kBN}, es[2] = {1, 1};
+    cuuint32_t box[2] = {kRawPitch, pair ? (cuuint32_t)tc2::kRows : (cuuint32_t)kBN}, es[2] = {1, 1};
     if (enc(&a.tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(w), dims, strides, box, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
@@ -498,19 +892,52 @@ cudaError_t launch_qgemm_tc(int wtype, const void *w, int M, int N, int K, const
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
 
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.stream = s;
+  if (pair) {
+    // persistent pairs: as many clusters as fit at once, at most one per tile
+    static int max_clusters = [] {
+      if (cudaFuncSetAttribute(tc2::k_qgemm_tc2, cudaFuncAttributeMaxDynamicSharedMemorySize, tc2::kSmem) !=
+          cudaSuccess)
+        return 0;
+      cudaLaunchConfig_t q{};
+      cudaLaunchAttribute ca[1];
+      ca[0].id = cudaLaunchAttributeClusterDimension;
+      ca[0].val.clusterDim.x = 2;
+      ca[0].val.clusterDim.y = 1;
+      ca[0].val.clusterDim.z = 1;
+      q.gridDim = dim3(2 * 148);
+      q.blockDim = dim3(tc2::kThreads);
+      q.dynamicSmemBytes = tc2::kSmem;
+      q.attrs = ca;
+      q.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, tc2::k_qgemm_tc2, &q) != cudaSuccess) n = 0;
+      return n;
+    }();
+    if (max_clusters <= 0) return cudaErrorInvalidConfiguration;
+    const int tiles = ((M + 255) / 256) * ((N + 255) / 256);
+    cfg.gridDim = dim3(2 * (tiles < max_clusters ? tiles : max_clusters));
+    cfg.blockDim = dim3(tc2::kThreads);
+    cfg.dynamicSmemBytes = tc2::kSmem;
+    at[1].id = cudaLaunchAttributeClusterDimension;
+    at[1].val.clusterDim.x = 2;
+    at[1].val.clusterDim.y = 1;
+    at[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, tc2::k_qgemm_tc2, a);
+  }
   static bool attr = [] {
     return cudaFuncSetAttribute(k_qgemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) == cudaSuccess;
   }();
   if (!attr) return cudaErrorInvalidConfiguration;
-  cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((N + kBN - 1) / kBN, (M + kBM - 1) / kBM);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = kSmem;
-  cfg.stream = s;
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = at;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, k_qgemm_tc, a);
 }
