@@ -450,8 +450,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc(const __grid_constant_
 //   warp 1        tensor-memory allocation (512 columns: two accumulators);
 //                 in the leader, the MMA issue
 //   warp 2        TMA of raw superblocks (128 weight rows x 144 B)
-//   warps 3..10   dequantise (two threads per weight row, 16 bytes of codes
-//                 each) into the swizzled fp16 stage, arrive on the leader
+//   warps 3..10   dequantise into the swizzled fp16 stage, arrive on the
+//                 leader: two groups of 4 warps take alternate K steps (one
+//                 thread per weight row), so two steps are in flight
 //   warps 11..14  epilogue: tensor memory -> C while the next tile runs in
 //                 the other accumulator
 namespace tc2 {
@@ -474,7 +475,7 @@ constexpr int kWarpA = 0, kWarpMma = 1, kWarpRaw = 2, kWarpDq = 3, kDqWarps = 8,
 constexpr int kThreads = 15 * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(256 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
-static_assert(kDqWarps * 32 == 2 * kRows, "two dequantising threads per weight row");
+static_assert(kDqWarps * 32 == 2 * kRows, "two groups of one dequantising thread per weight row");
 static_assert(kSmem <= 232448, "shared memory");
 
 __device__ __forceinline__ uint32_t cta_rank() {
@@ -642,7 +643,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
   if (threadIdx.x == 0) {
     for (int i = 0; i < kS; i++) {
       mbar_init(aF + i, 1);
-      mbar_init(bF + i, 2 * kDqWarps);
+      mbar_init(bF + i, kDqWarps);  // 4 warps of one group in each CTA
       mbar_init(E + i, 1);
     }
     for (int i = 0; i < kSR; i++) {
@@ -735,11 +736,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
       }
     }
   } else if (warp < kWarpEp) {
-    // ---- dequantise: two threads per weight row, 16 code bytes each
-    const int tid = threadIdx.x - kWarpDq * 32, row = tid >> 1, hf = tid & 1;
+    // ---- dequantise: two groups of 4 warps take alternate K steps of each
+    // superblock (two steps in flight); one thread per weight row
+    const int tid = threadIdx.x - kWarpDq * 32, grp = tid >> 7, row = tid & (kRows - 1);
     const uint32_t sw = (uint32_t)(row & 7);
     const uint32_t lbF = mapa(sa(bF), 0);
-    int g = 0, gr = 0;
+    int gr = 0;
     bool ok = true;
     for (int tile = pair; tile < tiles && ok; tile += npairs) {
       const int n = (tile % tiles_n) * 256 + (int)rank * kRows + row;
@@ -759,8 +761,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
             (uint8_t)hdr.z, (uint8_t)(hdr.z >> 8), (uint8_t)(hdr.z >> 16), (uint8_t)(hdr.z >> 24),
             (uint8_t)hdr.w, (uint8_t)(hdr.w >> 8), (uint8_t)(hdr.w >> 16), (uint8_t)(hdr.w >> 24)};
 #pragma unroll
-        for (int g4 = 0; g4 < 4; g4++) {
-          const int s = g % kS;
+        for (int h2 = 0; h2 < 2; h2++) {
+          const int g4 = grp + 2 * h2;  // K step within the superblock
+          const int g = gr * 4 + g4, s = g % kS;
           if (!warp_poll2<true>(E + s, ((g / kS) & 1) ^ 1, ab, a.err, 32)) {
             ok = false;
             break;
@@ -772,14 +775,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
           const __half2 nlo = __float2half2_rn(-__fmul_rn(dm, (float)m0));
           const __half2 dhi = __float2half2_rn(__fmul_rn(dd, (float)s1 * 0.0625f));
           const __half2 nhi = __float2half2_rn(-__fmul_rn(dm, (float)m1));
-          const uint4 q = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * g4 + 16 * hf);
+          const uint4 *qs = reinterpret_cast<const uint4 *>(blk + 16 + 32 * g4);
+          const uint4 q0 = qs[0], q1 = qs[1];
           uint8_t *dst = sB + s * kBBytes + row * 128;
-          dq8(q.x, q.y, dlo, nlo, dhi, nhi, dst, 2 * hf, sw);
-          dq8(q.z, q.w, dlo, nlo, dhi, nhi, dst, 2 * hf + 1, sw);
+          dq8(q0.x, q0.y, dlo, nlo, dhi, nhi, dst, 0, sw);
+          dq8(q0.z, q0.w, dlo, nlo, dhi, nhi, dst, 1, sw);
+          dq8(q1.x, q1.y, dlo, nlo, dhi, nhi, dst, 2, sw);
+          dq8(q1.z, q1.w, dlo, nlo, dhi, nhi, dst, 3, sw);
           mv::fence_proxy_async();
           __syncwarp();
           if (lane == 0) arrive_cluster(lbF + 8 * s);
-          g++;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(rE + r);
