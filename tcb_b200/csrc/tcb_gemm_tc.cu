@@ -159,6 +159,21 @@ __device__ __forceinline__ __half2 nib2(uint32_t u, uint32_t mask) {
   return bits_h2(r);
 }
 
+// Q4_K 6-bit scale and min of sub-block j (0..7, a runtime index) from the
+// three words y, z, w of the 12 packed scale bytes (TR tensor/quant.go:158-163)
+__device__ __forceinline__ void q4k_scale_words(int j, uint32_t y, uint32_t z, uint32_t w, uint32_t &sc,
+                                                uint32_t &m) {
+  const uint32_t sh = 8u * (uint32_t)(j & 3);
+  const uint32_t by = (y >> sh) & 0xFFu, bz = (z >> sh) & 0xFFu, bw = (w >> sh) & 0xFFu;
+  if (j < 4) {
+    sc = by & 63u;
+    m = bz & 63u;
+  } else {
+    sc = (bw & 15u) | ((by >> 6) << 4);
+    m = (bw >> 4) | ((bz >> 6) << 4);
+  }
+}
+
 // 8 code bytes (w0 = bytes 0-3, w1 = bytes 4-7 of an 8-byte group) of a
 // 64-element K step -> chunk c (their low nibbles) and chunk c + 4 (high
 // nibbles) of a 128-byte swizzled row: fma(q, d·sc, -dmin·m) per half2
@@ -451,16 +466,26 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc(const __grid_constant_
 //                 in the leader, the MMA issue
 //   warp 2        TMA of raw superblocks (128 weight rows x 144 B)
 //   warps 3..10   dequantise into the swizzled fp16 stage, arrive on the
-//                 leader: two groups of 4 warps take alternate K steps (one
-//                 thread per weight row), so two steps are in flight
+//                 leader: kGroups groups of warps take interleaved K steps
+//                 of each superblock, so kGroups steps are in flight
 //   warps 11..14  epilogue: tensor memory -> C while the next tile runs in
 //                 the other accumulator
 namespace tc2 {
 
 constexpr int kRows = 128;  // activation rows and weight rows per CTA
 constexpr int kBK = 64;
-constexpr int kS = 4;   // operand stages (A and B share the empty barrier)
-constexpr int kSR = 3;  // raw superblock stages
+#ifndef TCB_TC2_STAGES
+#define TCB_TC2_STAGES 5
+#endif
+#ifndef TCB_TC2_RAW_STAGES
+#define TCB_TC2_RAW_STAGES 2
+#endif
+#ifndef TCB_TC2_DQ_SLEEP
+#define TCB_TC2_DQ_SLEEP 0
+#endif
+constexpr int kS = TCB_TC2_STAGES;       // operand stages (A and B share the empty barrier)
+constexpr int kSR = TCB_TC2_RAW_STAGES;  // raw superblock stages
+constexpr unsigned kDqSleep = TCB_TC2_DQ_SLEEP;  // back-off of the dequantising warps' polls (ns)
 constexpr int kABytes = kRows * kBK * 2;
 constexpr int kBBytes = kRows * kBK * 2;
 constexpr int kRawBytes = kRows * kRawPitch;
@@ -475,7 +500,13 @@ constexpr int kWarpA = 0, kWarpMma = 1, kWarpRaw = 2, kWarpDq = 3, kDqWarps = 8,
 constexpr int kThreads = 15 * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(256 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
-static_assert(kDqWarps * 32 == 2 * kRows, "two groups of one dequantising thread per weight row");
+#ifndef TCB_TC2_GROUPS
+#define TCB_TC2_GROUPS 4
+#endif
+constexpr int kGroups = TCB_TC2_GROUPS;     // dequantising groups (K steps in flight)
+constexpr int kGT = kDqWarps * 32 / kGroups;  // threads per group
+constexpr int kRPT = kRows / kGT;             // weight rows per thread
+static_assert((kGroups == 2 || kGroups == 4) && kRPT * kGT == kRows, "dequantising groups");
 static_assert(kSmem <= 232448, "shared memory");
 
 __device__ __forceinline__ uint32_t cta_rank() {
@@ -643,7 +674,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
   if (threadIdx.x == 0) {
     for (int i = 0; i < kS; i++) {
       mbar_init(aF + i, 1);
-      mbar_init(bF + i, kDqWarps);  // 4 warps of one group in each CTA
+      mbar_init(bF + i, 2 * (kDqWarps / kGroups));  // one group's warps in each CTA
       mbar_init(E + i, 1);
     }
     for (int i = 0; i < kSR; i++) {
@@ -736,52 +767,60 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
       }
     }
   } else if (warp < kWarpEp) {
-    // ---- dequantise: two groups of 4 warps take alternate K steps of each
-    // superblock (two steps in flight); one thread per weight row
-    const int tid = threadIdx.x - kWarpDq * 32, grp = tid >> 7, row = tid & (kRows - 1);
-    const uint32_t sw = (uint32_t)(row & 7);
+    // ---- dequantise: kGroups groups of warps take interleaved K steps of
+    // each superblock (kGroups steps in flight); a thread owns kRPT rows
+    const int tid = threadIdx.x - kWarpDq * 32, grp = tid / kGT, t = tid % kGT;
     const uint32_t lbF = mapa(sa(bF), 0);
     int gr = 0;
     bool ok = true;
     for (int tile = pair; tile < tiles && ok; tile += npairs) {
-      const int n = (tile % tiles_n) * 256 + (int)rank * kRows + row;
-      const float mwr = n < a.N ? a.mw[n] : 0.f;
+      float mwr[kRPT];
+#pragma unroll
+      for (int i = 0; i < kRPT; i++) {
+        const int n = (tile % tiles_n) * 256 + (int)rank * kRows + t + i * kGT;
+        mwr[i] = n < a.N ? a.mw[n] : 0.f;
+      }
       for (int sb = 0; sb < a.nsb && ok; sb++, gr++) {
         const int r = gr % kSR;
-        if (!warp_poll2<false>(rF + r, (gr / kSR) & 1, ab, a.err, 32)) {
+        if (!warp_poll2<false>(rF + r, (gr / kSR) & 1, ab, a.err, kDqSleep)) {
           ok = false;
           break;
         }
-        const uint8_t *blk = sR + r * kRawBytes + row * kRawPitch;
-        const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
-        const float dd = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFFu))), mwr);
-        const float dm = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(hdr.x >> 16))), mwr);
-        const uint8_t sc12[12] = {
-            (uint8_t)hdr.y, (uint8_t)(hdr.y >> 8), (uint8_t)(hdr.y >> 16), (uint8_t)(hdr.y >> 24),
-            (uint8_t)hdr.z, (uint8_t)(hdr.z >> 8), (uint8_t)(hdr.z >> 16), (uint8_t)(hdr.z >> 24),
-            (uint8_t)hdr.w, (uint8_t)(hdr.w >> 8), (uint8_t)(hdr.w >> 16), (uint8_t)(hdr.w >> 24)};
+        uint4 hdr[kRPT];
+        float dd[kRPT], dm[kRPT];
 #pragma unroll
-        for (int h2 = 0; h2 < 2; h2++) {
-          const int g4 = grp + 2 * h2;  // K step within the superblock
+        for (int i = 0; i < kRPT; i++) {
+          hdr[i] = *reinterpret_cast<const uint4 *>(sR + r * kRawBytes + (t + i * kGT) * kRawPitch);
+          dd[i] = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(hdr[i].x & 0xFFFFu))), mwr[i]);
+          dm[i] = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(hdr[i].x >> 16))), mwr[i]);
+        }
+#pragma unroll
+        for (int h2 = 0; h2 < 4 / kGroups; h2++) {
+          const int g4 = grp + kGroups * h2;  // K step within the superblock
           const int g = gr * 4 + g4, s = g % kS;
-          if (!warp_poll2<true>(E + s, ((g / kS) & 1) ^ 1, ab, a.err, 32)) {
+          if (!warp_poll2<true>(E + s, ((g / kS) & 1) ^ 1, ab, a.err, kDqSleep)) {
             ok = false;
             break;
           }
-          uint32_t s0, m0, s1, m1;
-          q4k_scale(2 * g4, sc12, s0, m0);
-          q4k_scale(2 * g4 + 1, sc12, s1, m1);
-          const __half2 dlo = __float2half2_rn(__fmul_rn(dd, (float)s0));
-          const __half2 nlo = __float2half2_rn(-__fmul_rn(dm, (float)m0));
-          const __half2 dhi = __float2half2_rn(__fmul_rn(dd, (float)s1 * 0.0625f));
-          const __half2 nhi = __float2half2_rn(-__fmul_rn(dm, (float)m1));
-          const uint4 *qs = reinterpret_cast<const uint4 *>(blk + 16 + 32 * g4);
-          const uint4 q0 = qs[0], q1 = qs[1];
-          uint8_t *dst = sB + s * kBBytes + row * 128;
-          dq8(q0.x, q0.y, dlo, nlo, dhi, nhi, dst, 0, sw);
-          dq8(q0.z, q0.w, dlo, nlo, dhi, nhi, dst, 1, sw);
-          dq8(q1.x, q1.y, dlo, nlo, dhi, nhi, dst, 2, sw);
-          dq8(q1.z, q1.w, dlo, nlo, dhi, nhi, dst, 3, sw);
+#pragma unroll
+          for (int i = 0; i < kRPT; i++) {
+            const int row = t + i * kGT;
+            const uint32_t sw = (uint32_t)(row & 7);
+            uint32_t s0, m0, s1, m1;
+            q4k_scale_words(2 * g4, hdr[i].y, hdr[i].z, hdr[i].w, s0, m0);
+            q4k_scale_words(2 * g4 + 1, hdr[i].y, hdr[i].z, hdr[i].w, s1, m1);
+            const __half2 dlo = __float2half2_rn(__fmul_rn(dd[i], (float)s0));
+            const __half2 nlo = __float2half2_rn(-__fmul_rn(dm[i], (float)m0));
+            const __half2 dhi = __float2half2_rn(__fmul_rn(dd[i], (float)s1 * 0.0625f));
+            const __half2 nhi = __float2half2_rn(-__fmul_rn(dm[i], (float)m1));
+            const uint4 *qs = reinterpret_cast<const uint4 *>(sR + r * kRawBytes + row * kRawPitch + 16 + 32 * g4);
+            const uint4 q0 = qs[0], q1 = qs[1];
+            uint8_t *dst = sB + s * kBBytes + row * 128;
+            dq8(q0.x, q0.y, dlo, nlo, dhi, nhi, dst, 0, sw);
+            dq8(q0.z, q0.w, dlo, nlo, dhi, nhi, dst, 1, sw);
+            dq8(q1.x, q1.y, dlo, nlo, dhi, nhi, dst, 2, sw);
+            dq8(q1.z, q1.w, dlo, nlo, dhi, nhi, dst, 3, sw);
+          }
           mv::fence_proxy_async();
           __syncwarp();
           if (lane == 0) arrive_cluster(lbF + 8 * s);
