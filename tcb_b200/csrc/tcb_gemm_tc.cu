@@ -461,7 +461,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc(const __grid_constant_
 // rows of X (half the work per flop of the one-CTA tile) and reads half the B
 // operand from shared memory.
 //   warp 0        TMA of the CTA's 128 x 64 fp16 activation tile (both
-//                 CTAs complete_tx on the leader's full barrier)
+//                 CTAs complete_tx on the leader's full barrier of the stage,
+//                 which the dequantising warps of both CTAs also arrive on)
 //   warp 1        tensor-memory allocation (512 columns: two accumulators);
 //                 in the leader, the MMA issue
 //   warp 2        TMA of raw superblocks (128 weight rows x 144 B)
@@ -492,8 +493,8 @@ constexpr int kRawBytes = kRows * kRawPitch;
 constexpr int kOffB = kS * kABytes;
 constexpr int kOffR = kOffB + kS * kBBytes;
 constexpr int kOffBar = kOffR + kSR * kRawBytes;
-// aF[kS] bF[kS] E[kS] rF[kSR] rE[kSR] accF[2] accE[2]
-constexpr int kNumBars = 3 * kS + 2 * kSR + 4;
+// F[kS] E[kS] rF[kSR] rE[kSR] accF[2] accE[2]
+constexpr int kNumBars = 2 * kS + 2 * kSR + 4;
 constexpr int kOffSlot = kOffBar + 8 * kNumBars;
 constexpr int kSmem = kOffSlot + 16 + 1024;
 constexpr int kWarpA = 0, kWarpMma = 1, kWarpRaw = 2, kWarpDq = 3, kDqWarps = 8, kWarpEp = 11, kEpWarps = 4;
@@ -522,16 +523,6 @@ __device__ __forceinline__ uint32_t mapa(uint32_t a, uint32_t rank) {
 }
 __device__ __forceinline__ void arrive_cluster(uint32_t addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
-}
-__device__ __forceinline__ bool test_wait_cl(uint64_t *bar, uint32_t ph) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(sa(bar)), "r"(ph)
-      : "memory");
-  return ok != 0;
 }
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -565,10 +556,15 @@ __device__ __forceinline__ void tma_pair(void *dst, const CUtensorMap *tm, int x
       : "memory");
 }
 
-template <bool CL>
+// Bounded poll of a barrier phase by one thread (acquire at the default CTA
+// scope, as for every barrier wait of this kernel, including phases that the
+// peer CTA's copies, arrives and the leader's commits complete).  Gives up
+// (false) when another role has aborted or after 2^26 polls (over a second),
+// recording a timeout.  The bound is an iteration count: reading the clock
+// inside the spin measured 8 % slower on the whole product.
 __device__ __forceinline__ bool poll2(uint64_t *bar, uint32_t ph, volatile int *ab, int *err, unsigned ns) {
   for (uint32_t i = 0; i < (1u << 26); i++) {
-    if (CL ? test_wait_cl(bar, ph) : mbar_test_wait(bar, ph)) return true;
+    if (mbar_test_wait(bar, ph)) return true;
     if (*ab) return false;
     if (ns) __nanosleep(ns);
   }
@@ -576,17 +572,16 @@ __device__ __forceinline__ bool poll2(uint64_t *bar, uint32_t ph, volatile int *
   atomicExch(err, TCB_ERR_TIMEOUT);
   return false;
 }
-template <bool CL>
 __device__ __forceinline__ bool warp_poll2(uint64_t *bar, uint32_t ph, volatile int *ab, int *err, unsigned ns) {
   int ok = 0;
-  if ((threadIdx.x & 31) == 0) ok = poll2<CL>(bar, ph, ab, err, ns);
+  if ((threadIdx.x & 31) == 0) ok = poll2(bar, ph, ab, err, ns);
   __syncwarp();
   return __shfl_sync(0xFFFFFFFFu, ok, 0) != 0;
 }
-template <bool CL>
+// the same without the abort exit (draining copies still in flight)
 __device__ __forceinline__ void drain2(uint64_t *bar, uint32_t ph, int *err) {
   for (uint32_t i = 0; i < (1u << 22); i++) {
-    if (CL ? test_wait_cl(bar, ph) : mbar_test_wait(bar, ph)) return;
+    if (mbar_test_wait(bar, ph)) return;
     __nanosleep(64);
   }
   atomicExch(err, TCB_ERR_TIMEOUT);
@@ -660,7 +655,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
   uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint8_t *sA = sm, *sB = sm + kOffB, *sR = sm + kOffR;
   uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kOffBar);
-  uint64_t *aF = bars, *bF = bars + kS, *E = bars + 2 * kS, *rF = bars + 3 * kS, *rE = rF + kSR, *accF = rE + kSR,
+  uint64_t *F = bars, *E = bars + kS, *rF = bars + 2 * kS, *rE = rF + kSR, *accF = rE + kSR,
            *accE = accF + 2;
   uint32_t *slot = reinterpret_cast<uint32_t *>(sm + kOffSlot);
   volatile int *ab = reinterpret_cast<volatile int *>(sm + kOffSlot + 4);
@@ -673,8 +668,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kS; i++) {
-      mbar_init(aF + i, 1);
-      mbar_init(bF + i, 2 * (kDqWarps / kGroups));  // one group's warps in each CTA
+      // full: the leader's expect_tx arrive (both CTAs' activation bytes) and
+      // the arrives of one dequantising group's warps in each CTA
+      mbar_init(F + i, 1 + 2 * (kDqWarps / kGroups));
       mbar_init(E + i, 1);
     }
     for (int i = 0; i < kSR; i++) {
@@ -701,23 +697,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
 
   if (warp == kWarpA) {
     if (lane == 0) {
-      const uint32_t laF = mapa(sa(aF), 0);
+      const uint32_t lF = mapa(sa(F), 0);
       int g = 0;
       bool ok = true;
       for (int tile = pair; tile < tiles && ok; tile += npairs) {
         const int tm = tile / tiles_n;
         for (int ks = 0; ks < nks; ks++, g++) {
           const int s = g % kS;
-          if (!poll2<true>(E + s, ((g / kS) & 1) ^ 1, ab, a.err, 0)) {
+          if (!poll2(E + s, ((g / kS) & 1) ^ 1, ab, a.err, 0)) {
             ok = false;
             break;
           }
-          if (leader) mbar_expect_tx(aF + s, 2 * kABytes);
-          tma_pair(sA + s * kABytes, &a.ta, ks * kBK, tm * 256 + (int)rank * kRows, laF + 8 * s);
+          if (leader) mbar_expect_tx(F + s, 2 * kABytes);
+          tma_pair(sA + s * kABytes, &a.ta, ks * kBK, tm * 256 + (int)rank * kRows, lF + 8 * s);
         }
       }
       // loads still in flight complete before the MMA frees their stage
-      for (int j = g - kS > 0 ? g - kS : 0; j < g; j++) drain2<true>(E + j % kS, (j / kS) & 1, a.err);
+      for (int j = g - kS > 0 ? g - kS : 0; j < g; j++) drain2(E + j % kS, (j / kS) & 1, a.err);
     }
   } else if (warp == kWarpRaw) {
     if (lane == 0) {
@@ -727,7 +723,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
         const int tn = tile % tiles_n;
         for (int sb = 0; sb < a.nsb; sb++, gr++) {
           const int r = gr % kSR;
-          if (!poll2<false>(rE + r, ((gr / kSR) & 1) ^ 1, ab, a.err, 0)) {
+          if (!poll2(rE + r, ((gr / kSR) & 1) ^ 1, ab, a.err, 0)) {
             ok = false;
             break;
           }
@@ -735,32 +731,37 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
           tma_load_2d(sR + r * kRawBytes, &a.tw, sb * kRawPitch, tn * 256 + (int)rank * kRows, rF + r);
         }
       }
-      for (int j = gr - kSR > 0 ? gr - kSR : 0; j < gr; j++) drain2<false>(rF + j % kSR, (j / kSR) & 1, a.err);
+      for (int j = gr - kSR > 0 ? gr - kSR : 0; j < gr; j++) drain2(rF + j % kSR, (j / kSR) & 1, a.err);
     }
   } else if (warp == kWarpMma) {
     if (leader && lane == 0) {
-      const uint32_t a0 = sa(sA), b0 = sa(sB);
+      const uint64_t da0 = sw128_desc(sa(sA)), db0 = sw128_desc(sa(sB));
       const uint32_t eOwn = mapa(sa(E), 0), ePeer = mapa(sa(E), 1);
       const uint32_t fOwn = mapa(sa(accF), 0), fPeer = mapa(sa(accF), 1);
-      int g = 0, it = 0;
+      int it = 0, s = 0;
+      uint32_t ph = 0;
       bool ok = true;
       for (int tile = pair; tile < tiles && ok; tile += npairs, it++) {
         const int buf = it & 1;
-        if (!poll2<true>(accE + buf, ((it >> 1) & 1) ^ 1, ab, a.err, 0)) break;
+        if (!poll2(accE + buf, ((it >> 1) & 1) ^ 1, ab, a.err, 0)) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(buf * 256);
-        for (int ks = 0; ks < nks; ks++, g++) {
-          const int s = g % kS;
-          if (!poll2<true>(aF + s, (g / kS) & 1, ab, a.err, 0) || !poll2<true>(bF + s, (g / kS) & 1, ab, a.err, 0)) {
+        for (int ks = 0; ks < nks; ks++) {
+          if (!poll2(F + s, ph, ab, a.err, 0)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t da = sw128_desc(a0 + s * kABytes), db = sw128_desc(b0 + s * kBBytes);
+          // stage offsets in the descriptors' 16-byte address units
+          const uint64_t da = da0 + (uint64_t)(s * (kABytes >> 4)), db = db0 + (uint64_t)(s * (kBBytes >> 4));
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; kk++) mma2(d, da + 2 * kk, db + 2 * kk, (ks | kk) != 0);
           commit2(eOwn + 8 * s);
           commit2(ePeer + 8 * s);
+          if (++s == kS) {
+            s = 0;
+            ph ^= 1;
+          }
         }
         commit2(fOwn + 8 * buf);
         commit2(fPeer + 8 * buf);
@@ -770,7 +771,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
     // ---- dequantise: kGroups groups of warps take interleaved K steps of
     // each superblock (kGroups steps in flight); a thread owns kRPT rows
     const int tid = threadIdx.x - kWarpDq * 32, grp = tid / kGT, t = tid % kGT;
-    const uint32_t lbF = mapa(sa(bF), 0);
+    const uint32_t lF = mapa(sa(F), 0);
     int gr = 0;
     bool ok = true;
     for (int tile = pair; tile < tiles && ok; tile += npairs) {
@@ -782,7 +783,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
       }
       for (int sb = 0; sb < a.nsb && ok; sb++, gr++) {
         const int r = gr % kSR;
-        if (!warp_poll2<false>(rF + r, (gr / kSR) & 1, ab, a.err, kDqSleep)) {
+        if (!warp_poll2(rF + r, (gr / kSR) & 1, ab, a.err, kDqSleep)) {
           ok = false;
           break;
         }
@@ -798,7 +799,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
         for (int h2 = 0; h2 < 4 / kGroups; h2++) {
           const int g4 = grp + kGroups * h2;  // K step within the superblock
           const int g = gr * 4 + g4, s = g % kS;
-          if (!warp_poll2<true>(E + s, ((g / kS) & 1) ^ 1, ab, a.err, kDqSleep)) {
+          if (!warp_poll2(E + s, ((g / kS) & 1) ^ 1, ab, a.err, kDqSleep)) {
             ok = false;
             break;
           }
@@ -823,7 +824,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
           }
           mv::fence_proxy_async();
           __syncwarp();
-          if (lane == 0) arrive_cluster(lbF + 8 * s);
+          if (lane == 0) arrive_cluster(lF + 8 * s);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(rE + r);
@@ -836,7 +837,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
     int it = 0;
     for (int tile = pair; tile < tiles; tile += npairs, it++) {
       const int buf = it & 1;
-      if (!warp_poll2<true>(accF + buf, (it >> 1) & 1, ab, a.err, 64)) break;
+      if (!warp_poll2(accF + buf, (it >> 1) & 1, ab, a.err, 64)) break;
       tc_fence_after();
       const int tm = tile / tiles_n, tn = tile % tiles_n;
       const long m = (long)tm * 256 + rank * kRows + q * 32 + lane;
