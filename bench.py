@@ -50,8 +50,9 @@ def load_peaks() -> dict:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         d = json.load(open(p))
-        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d.get("bf16_tflops", 1590.0)),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
 def load_traffic(name: str):
@@ -188,6 +189,59 @@ def decode_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
     }
 
 
+def prefill_bench(ctx, rank: int, peaks: dict, cpu: bool) -> dict:
+    """Prefill product: Q4_K weights 14336x4096 and
+    4096x14336 against bf16 activations of M = 2048 rows, f32 output, through
+    the tcgen05 kernel.  Each shape cycles through 4 weight copies (more than
+    the 126 MB L2 together); CUDA events around 20 calls after 3 warm-up
+    calls.  Tensor roofline: 2*M*N*K flops against the measured dense bf16
+    peak (burst figure: the kernel is timed alone)."""
+    import torch
+
+    from tcb_b200 import synth
+
+    M = 2048
+    out = {"model": "q4_k x bf16 prefill products (synthetic)", "M": M, "x_dtype": "bf16", "c_dtype": "f32",
+           "shapes": []}
+    peak = peaks.get("bf16_tflops")
+    stream = torch.cuda.Stream()
+    for N, K in ((14336, 4096), (4096, 14336)):
+        ring = [torch.from_numpy(synth.weight(Q4_K, N, K, seed=31 + i + rank)).cuda() for i in range(4)]
+        x = torch.from_numpy(synth.activations(M, K, seed=33 + rank)).cuda().to(torch.bfloat16)
+        c = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        with torch.cuda.stream(stream):
+            for i in range(3):
+                ctx.qgemm(Q4_K, ring[i % 4], x, c, stream=stream)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            n = 20
+            e0.record(stream)
+            for i in range(n):
+                ctx.qgemm(Q4_K, ring[i % 4], x, c, stream=stream)
+            e1.record(stream)
+            e1.synchronize()
+        ms = e0.elapsed_time(e1) / n
+        tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
+        row = {"N": N, "K": K, "us_per_call": round(ms * 1e3, 1), "tflops": round(tf, 1),
+               "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
+                            "frac": round(tf / peak, 4) if peak else None,
+                            "peak_source": ("measured (burst)" if peaks.get("source") == "measured" else "fallback")}}
+        if cpu and rank == 0:
+            # the oracle's float path on the host cores, on a sample of rows
+            from oracle import oracle as O
+
+            xs = x[:16].float().cpu().numpy()
+            w = ring[0].cpu().numpy()
+            t0 = time.perf_counter()
+            O.qgemm_float(Q4_K, xs, w, N)
+            dt = time.perf_counter() - t0
+            row["cpu_baseline"] = {"value": round(2.0 * 16 * N * K / dt / 1e12, 4), "unit": "TFLOP/s",
+                                   "cores": os.cpu_count(), "kind": "port",
+                                   "sample": f"16 of {M} rows through the oracle's float path"}
+        out["shapes"].append(row)
+        del ring, x, c
+    return out
+
+
 def decode_tp_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
     """70B-shape Q4_K_M greedy decode at batch 1, tensor-parallel over the
     world's GPUs (QKV/gate/up column-parallel, o/down
@@ -268,6 +322,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the 8B-shape decode measurement")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill-product measurement")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -377,6 +432,10 @@ def main():
         decode = (decode_bench(ctx, rank, world, peaks["hbm_gbs"]) if world == 1
                   else decode_tp_bench(ctx, rank, world, peaks["hbm_gbs"]))
 
+    prefill = None
+    if world == 1 and not args.no_prefill:
+        prefill = prefill_bench(ctx, rank, peaks, not args.no_cpu_baseline)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -396,6 +455,8 @@ def main():
         }
         if decode is not None:
             line["decode"] = decode
+        if prefill is not None:
+            line["prefill"] = prefill
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
