@@ -196,6 +196,32 @@ __device__ __forceinline__ void dq8(uint32_t w0, uint32_t w1, __half2 dlo, __hal
 
 // ----------------------------------------------------------------- kernels
 
+// activation elements 8g .. 8g+7 of a row as f32 (16-byte loads when the
+// row is 16-byte aligned)
+__device__ __forceinline__ void load8(const char *row, int g, int xdt, bool vec, float (&v)[8]) {
+  if (vec && xdt == TCB_F32) {
+    const float4 *p = reinterpret_cast<const float4 *>(row) + 2 * g;
+    const float4 a = p[0], b = p[1];
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+  } else if (vec) {
+    const uint4 u = reinterpret_cast<const uint4 *>(row)[g];
+    const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      if (xdt == TCB_BF16) {
+        v[2 * i] = __uint_as_float(wd[i] << 16);
+        v[2 * i + 1] = __uint_as_float(wd[i] & 0xFFFF0000u);
+      } else {
+        v[2 * i] = __half2float(__ushort_as_half((unsigned short)(wd[i] & 0xFFFFu)));
+        v[2 * i + 1] = __half2float(__ushort_as_half((unsigned short)(wd[i] >> 16)));
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = load_act(row, 8 * g + i, xdt);
+  }
+}
+
 // k_tc_prep: blocks [0, M) scale and convert activation rows; the rest scan
 // weight rows (one warp per row).
 __global__ void __launch_bounds__(256) k_tc_prep(const void *x, int xdt, long ldx, int M, int K, __half *xh,
@@ -206,13 +232,19 @@ __global__ void __launch_bounds__(256) k_tc_prep(const void *x, int xdt, long ld
   if ((int)blockIdx.x < M) {
     const int m = blockIdx.x;
     const char *row = static_cast<const char *>(x) + (size_t)m * ldx * (xdt == TCB_F32 ? 4 : 2);
+    const bool vec = (reinterpret_cast<uintptr_t>(row) & 15) == 0;  // 16-byte loads
     float amax = 0.f;
     int bad = 0;
     if (threadIdx.x == 0) bad_s = 0;
-    for (int k = threadIdx.x; k < K; k += blockDim.x) {
-      const float v = fabsf(load_act(row, k, xdt));
-      bad |= !(v <= 3.402823466e38f);
-      amax = fmaxf(amax, v);
+    for (int g = threadIdx.x; g < K / 8; g += blockDim.x) {
+      float v[8];
+      load8(row, g, xdt, vec, v);
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const float av = fabsf(v[i]);
+        bad |= !(av <= 3.402823466e38f);
+        amax = fmaxf(amax, av);
+      }
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
@@ -226,12 +258,14 @@ __global__ void __launch_bounds__(256) k_tc_prep(const void *x, int xdt, long ld
     if (!bad_s && a > 0.f) e = min(max(ilogbf(a) - 14, -100), 100);
     const float mul = ldexpf(1.f, -e);
     if (threadIdx.x == 0) ix[m] = ldexpf(1.f, e);
-    // 8 outputs per thread in the K order (0 2 1 3 4 6 5 7)
+    // 8 outputs per thread in the K order (0 2 1 3 4 6 5 7); the second pass
+    // re-reads the row from L1
     uint4 *dst = reinterpret_cast<uint4 *>(xh + (size_t)m * K);
     for (int g = threadIdx.x; g < K / 8; g += blockDim.x) {
       float v[8];
+      load8(row, g, xdt, vec, v);
 #pragma unroll
-      for (int i = 0; i < 8; i++) v[i] = __fmul_rn(load_act(row, 8 * g + i, xdt), mul);
+      for (int i = 0; i < 8; i++) v[i] = __fmul_rn(v[i], mul);
       uint4 o;
       o.x = h2_bits(__floats2half2_rn(v[0], v[2]));
       o.y = h2_bits(__floats2half2_rn(v[1], v[3]));

@@ -98,6 +98,18 @@ def test_tc_dtypes_strides_accumulate(ctx, oracle):
     assert not host(cw[:, :20]).any() and not host(cw[:, 20 + N:]).any()
 
 
+def test_tc_unaligned_activation_rows(ctx, oracle):
+    """An activation view one element in (rows 4-byte, not 16-byte, aligned)
+    and an odd row stride: the prep kernel's element-wise path."""
+    M, N, K = 96, 256, 512
+    raw = synth.weight(T.Q4_K, N, K, seed=21)
+    xf = synth.activations(M, K + 3, seed=22)
+    xd = dev(xf)[:, 1:1 + K]
+    c = torch.zeros((M, N), dtype=torch.float32, device="cuda")
+    ctx.qgemm(T.Q4_K, dev(raw), xd, c)
+    check(host(c), oracle.qgemm_float(T.Q4_K, xf[:, 1:1 + K], raw, N))
+
+
 def test_tc_row_scales(ctx, oracle):
     """Rows of X and W far from unit scale: the power-of-two row scaling keeps
     fp16 in range (no Inf) and keeps precision for tiny rows."""
