@@ -5,26 +5,22 @@
 // branch, gpu/backend_quant.go:43-65; CPU semantics quantGemm,
 // tensor/cpu_quant.go:47-147: the product of X with the opened weights).
 //
-// Two launches:
+// Launches:
 //  1. k_tc_prep: each activation row x[m] is scaled by a power of two
 //     (row max brought into [2^14, 2^15)) and rounded once to fp16, stored
 //     K-contiguous in workspace with the fixed 8-periodic order below; each
 //     weight row n gets a power-of-two multiplier from its blocks' scales
 //     (the largest magnitude a row can dequantise to is brought under 2^15),
 //     so no dequantised fp16 weight overflows and small rows keep precision.
-//  2. k_qgemm_tc: a CTA owns a 128 x 256 tile of C (rows of X x rows of W)
-//     and runs a warp-specialised pipeline:
-//       warp 0        TMA loads of fp16 X tiles (128 x 64, 128-byte swizzle)
-//       warp 10       TMA loads of raw Q4_K superblocks (256 rows x 144 B)
-//       warps 2..9    dequantise one 64-element K step of 256 weight rows
-//                     into fp16 in the UMMA K-major 128-byte-swizzled
-//                     layout (one row per thread, packed half2 math), then
-//                     read the accumulator out of tensor memory
-//       warp 1        allocates 256 tensor-memory columns and issues
-//                     tcgen05.mma (M 128, N 256, K 16, f16 x f16 -> f32) from
-//                     one thread; tcgen05.commit frees the operand stages
-//     The epilogue divides out the two power-of-two multipliers (exact) and
-//     writes C with TR's one-rounding rule (accumulate: round(old + v)).
+//  2. k_qgemm_tc2: clusters of two CTAs (one per SM) walk 256 x 256 tiles of
+//     C persistently; the leader issues tcgen05.mma.cta_group::2 over both
+//     CTAs' operand stages (warp roles at the kernel).  When the tiles are
+//     fewer than the pairs, a tile's K range is split into whole-superblock
+//     pieces (work units) and the epilogue writes f32 partials instead.
+//  3. k_tc_reduce (split runs only): adds the partials in split order and
+//     writes C.
+// The epilogue divides out the two power-of-two multipliers (exact) and
+// writes C with TR's one-rounding rule (accumulate: round(old + v)).
 //
 // Numerics: the weights are computed as fma(q, d·sc, -dmin·m) in fp16 with
 // d·sc and dmin·m rounded once each, the activations are rounded once to
@@ -55,26 +51,8 @@ using mv::mbar_test_wait;
 using mv::sa;
 using mv::tma_load_2d;
 
-constexpr int kBM = 128, kBN = 256, kBK = 64;
-constexpr int kSA = 4, kSB = 2, kSR = 2;
-constexpr int kABytes = kBM * kBK * 2;  // 16384
-constexpr int kBBytes = kBN * kBK * 2;  // 32768
-constexpr int kRawPitch = 144;          // one Q4_K superblock per row
-constexpr int kRawBytes = kBN * kRawPitch;
-constexpr int kOffB = kSA * kABytes;
-constexpr int kOffR = kOffB + kSB * kBBytes;
-constexpr int kOffBar = kOffR + kSR * kRawBytes;
-constexpr int kNumBars = 2 * kSA + 2 * kSB + 2 * kSR + 1;
-constexpr int kOffSlot = kOffBar + 8 * kNumBars;
-constexpr int kSmem = kOffSlot + 16 + 1024;  // + alignment slack
-constexpr int kWarpA = 0, kWarpMma = 1, kWarpDq = 2, kDqWarps = 8, kWarpRaw = 10;
-constexpr int kThreads = 11 * 32;
-constexpr uint32_t kTmemCols = 256;
-static_assert(kDqWarps * 32 == kBN, "one dequantising thread per weight row");
-
-// tcgen05 instruction descriptor: D f32, A f16, B f16, both K-major, N, M
-constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(kBN >> 3) << 17) |
-                            ((uint32_t)(kBM >> 4) << 24);
+constexpr int kBK = 64;          // K elements per operand stage (one 128-byte swizzle row of fp16)
+constexpr int kRawPitch = 144;  // one Q4_K superblock per staged row
 
 // ----------------------------------------------------------------- PTX
 
@@ -84,29 +62,8 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
   return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
-__device__ __forceinline__ void tmem_alloc(uint32_t slot, uint32_t cols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "r"(cols) : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
-}
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void mma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
-      "l"(a), "l"(b), "r"(kIdesc), "r"(acc)
-      : "memory");
-}
-// arrive on bar once every tcgen05 operation this thread issued has completed
-__device__ __forceinline__ void mma_commit(uint64_t *bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(sa(bar))
-               : "memory");
-}
 // 32 lanes x 32 consecutive 32-bit columns of tensor memory
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
@@ -118,35 +75,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// Bounded poll of a barrier phase by one thread.  Gives up (false) when
-// another role has aborted or after 2^26 polls, recording a timeout.
-__device__ __forceinline__ bool poll(uint64_t *bar, uint32_t ph, volatile int *ab, int *err, unsigned ns) {
-  for (uint32_t i = 0; i < (1u << 26); i++) {
-    if (mbar_test_wait(bar, ph)) return true;
-    if (*ab) return false;
-    if (ns) __nanosleep(ns);
-  }
-  *ab = 1;
-  atomicExch(err, TCB_ERR_TIMEOUT);
-  return false;
-}
-// The same for a whole warp: lane 0 polls, __syncwarp orders the other
-// lanes' accesses after the phase it observed.
-__device__ __forceinline__ bool warp_poll(uint64_t *bar, uint32_t ph, volatile int *ab, int *err, unsigned ns) {
-  int ok = 0;
-  if ((threadIdx.x & 31) == 0) ok = poll(bar, ph, ab, err, ns);
-  __syncwarp();
-  return __shfl_sync(0xFFFFFFFFu, ok, 0) != 0;
-}
-// the same without the abort exit (draining copies still in flight)
-__device__ __forceinline__ void drain(uint64_t *bar, uint32_t ph, int *err) {
-  for (uint32_t i = 0; i < (1u << 22); i++) {
-    if (mbar_test_wait(bar, ph)) return;
-    __nanosleep(64);
-  }
-  atomicExch(err, TCB_ERR_TIMEOUT);
 }
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
@@ -303,186 +231,15 @@ __global__ void __launch_bounds__(256) k_tc_prep(const void *x, int xdt, long ld
 
 struct TcArgs {
   CUtensorMap ta;  // fp16 X [M][K], box 64 x 128, 128-byte swizzle
-  CUtensorMap tw;  // weight bytes [N][nsb * 144], box 144 x 256
+  CUtensorMap tw;  // weight bytes [N][nsb * 144], box 144 x 128
   const float *mw, *iw, *ix;
   void *c;
   long ldc;
   int cdt, accumulate, M, N, nsb;
+  int ksplit, sbper;  // K splits of a tile and superblocks per split
+  float *part;        // [ksplit][M][N] f32 partials when ksplit > 1
   int *err;
 };
-
-__global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc(const __grid_constant__ TcArgs a) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint8_t *sA = sm, *sB = sm + kOffB, *sR = sm + kOffR;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kOffBar);
-  uint64_t *aF = bars, *aE = bars + kSA, *bF = bars + 2 * kSA, *bE = bF + kSB, *rF = bE + kSB, *rE = rF + kSR,
-           *accF = rE + kSR;
-  uint32_t *slot = reinterpret_cast<uint32_t *>(sm + kOffSlot);
-  volatile int *ab = reinterpret_cast<volatile int *>(sm + kOffSlot + 4);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tn = blockIdx.x, tm = blockIdx.y;
-  const int nks = a.nsb * 4;
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < kSA; i++) {
-      mbar_init(aF + i, 1);
-      mbar_init(aE + i, 1);
-    }
-    for (int i = 0; i < kSB; i++) {
-      mbar_init(bF + i, kDqWarps);
-      mbar_init(bE + i, 1);
-    }
-    for (int i = 0; i < kSR; i++) {
-      mbar_init(rF + i, 1);
-      mbar_init(rE + i, kDqWarps);
-    }
-    mbar_init(accF, 1);
-    *ab = 0;
-    mv::fence_barrier_init();
-  }
-  if (warp == kWarpMma) {
-    tmem_alloc(sa(slot), kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *slot;
-  mv::pdl_wait();
-
-  if (warp == kWarpA) {
-    if (lane == 0) {
-      int ks = 0;
-      for (; ks < nks; ks++) {
-        const int s = ks % kSA;
-        if (!poll(aE + s, ((ks / kSA) & 1) ^ 1, ab, a.err, 0)) break;
-        mbar_expect_tx(aF + s, kABytes);
-        tma_load_2d(sA + s * kABytes, &a.ta, ks * kBK, tm * kBM, aF + s);
-      }
-      for (int j = ks - kSA > 0 ? ks - kSA : 0; j < ks; j++) drain(aF + j % kSA, (j / kSA) & 1, a.err);
-    }
-  } else if (warp == kWarpRaw) {
-    if (lane == 0) {
-      int sb = 0;
-      for (; sb < a.nsb; sb++) {
-        const int r = sb % kSR;
-        if (!poll(rE + r, ((sb / kSR) & 1) ^ 1, ab, a.err, 0)) break;
-        mbar_expect_tx(rF + r, kRawBytes);
-        tma_load_2d(sR + r * kRawBytes, &a.tw, sb * kRawPitch, tn * kBN, rF + r);
-      }
-      for (int j = sb - kSR > 0 ? sb - kSR : 0; j < sb; j++) drain(rF + j % kSR, (j / kSR) & 1, a.err);
-    }
-  } else if (warp == kWarpMma) {
-    if (lane == 0) {
-      const uint32_t a0 = sa(sA), b0 = sa(sB);
-      for (int ks = 0; ks < nks; ks++) {
-        const int s = ks % kSA, t = ks % kSB;
-        if (!poll(aF + s, (ks / kSA) & 1, ab, a.err, 0)) break;
-        if (!poll(bF + t, (ks / kSB) & 1, ab, a.err, 0)) break;
-        tc_fence_after();
-        const uint64_t da = sw128_desc(a0 + s * kABytes), db = sw128_desc(b0 + t * kBBytes);
-#pragma unroll
-        for (int kk = 0; kk < kBK / 16; kk++) mma_f16(tmem, da + 2 * kk, db + 2 * kk, (ks | kk) != 0);
-        mma_commit(aE + s);
-        mma_commit(bE + t);
-      }
-      mma_commit(accF);
-    }
-  } else {
-    // ---- dequantise: thread = weight row of the tile
-    const int row = threadIdx.x - kWarpDq * 32;
-    const int n = tn * kBN + row;
-    const float mwr = n < a.N ? a.mw[n] : 0.f;
-    const uint32_t sw = (uint32_t)(row & 7);
-    bool ok = true;
-    for (int sb = 0; sb < a.nsb && ok; sb++) {
-      const int r = sb % kSR;
-      if (!warp_poll(rF + r, (sb / kSR) & 1, ab, a.err, 32)) {
-        ok = false;
-        break;
-      }
-      const uint8_t *blk = sR + r * kRawBytes + row * kRawPitch;
-      const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
-      const float dd = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFFu))), mwr);
-      const float dm = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(hdr.x >> 16))), mwr);
-      const uint8_t sc12[12] = {
-          (uint8_t)hdr.y,         (uint8_t)(hdr.y >> 8), (uint8_t)(hdr.y >> 16), (uint8_t)(hdr.y >> 24),
-          (uint8_t)hdr.z,         (uint8_t)(hdr.z >> 8), (uint8_t)(hdr.z >> 16), (uint8_t)(hdr.z >> 24),
-          (uint8_t)hdr.w,         (uint8_t)(hdr.w >> 8), (uint8_t)(hdr.w >> 16), (uint8_t)(hdr.w >> 24)};
-#pragma unroll
-      for (int g = 0; g < 4; g++) {
-        const int ks = sb * 4 + g, t = ks % kSB;
-        if (!warp_poll(bE + t, ((ks / kSB) & 1) ^ 1, ab, a.err, 32)) {
-          ok = false;
-          break;
-        }
-        uint32_t s0, m0, s1, m1;
-        q4k_scale(2 * g, sc12, s0, m0);
-        q4k_scale(2 * g + 1, sc12, s1, m1);
-        const __half2 dlo = __float2half2_rn(__fmul_rn(dd, (float)s0));
-        const __half2 nlo = __float2half2_rn(-__fmul_rn(dm, (float)m0));
-        const __half2 dhi = __float2half2_rn(__fmul_rn(dd, (float)s1 * 0.0625f));
-        const __half2 nhi = __float2half2_rn(-__fmul_rn(dm, (float)m1));
-        const uint4 *qs = reinterpret_cast<const uint4 *>(blk + 16 + 32 * g);
-        uint8_t *dst = sB + t * kBBytes + row * 128;
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-          const uint4 q = qs[h];
-          dq8(q.x, q.y, dlo, nlo, dhi, nhi, dst, 2 * h, sw);
-          dq8(q.z, q.w, dlo, nlo, dhi, nhi, dst, 2 * h + 1, sw);
-        }
-        mv::fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bF + t);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(rE + r);
-    }
-    (void)ok;
-    // ---- epilogue: lanes 32q.. of tensor memory = rows of X, half h of the columns
-    // all MMAs done (the MMA thread always commits accF, also after an abort)
-    int done = 0;
-    if (lane == 0) {
-      for (uint32_t i = 0; i < (1u << 24) && !done; i++) {
-        done = mbar_test_wait(accF, 0);
-        if (!done) __nanosleep(64);
-      }
-      if (!done) {
-        *ab = 1;
-        atomicExch(a.err, TCB_ERR_TIMEOUT);
-      }
-    }
-    __syncwarp();
-    done = __shfl_sync(0xFFFFFFFFu, done, 0);
-    tc_fence_after();
-    const int q = warp & 3, h = (warp - kWarpDq) >> 2;
-    const int m = tm * kBM + q * 32 + lane;
-    const bool live = done && !*ab && m < a.M;
-    const float sx = live ? a.ix[m] : 0.f;
-#pragma unroll 1
-    for (int j = 0; j < 4; j++) {
-      const int col = h * 128 + j * 32;
-      uint32_t v[32];
-      tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)col, v);
-      if (live) {
-        const long base = (long)m * a.ldc;
-#pragma unroll
-        for (int i = 0; i < 32; i++) {
-          const int nn = tn * kBN + col + i;
-          if (nn < a.N) store_out(a.c, base + nn, a.cdt, __fmul_rn(__fmul_rn(__uint_as_float(v[i]), sx), a.iw[nn]),
-                                  a.accumulate != 0);
-        }
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == kWarpMma) {
-    tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
-  }
-}
 
 // ----------------------------------------------------------------- 2-CTA kernel
 //
@@ -684,6 +441,28 @@ __device__ __forceinline__ void store32(const TcArgs &a, long m, int n0, const u
     if (n0 + i < a.N) store_out(a.c, base + i, a.cdt, __fmul_rn(r[i], a.iw[n0 + i]), a.accumulate != 0);
 }
 
+// 32 scaled f32 partials of row m from column n0 into split `split`'s slice
+__device__ __forceinline__ void store_part(const TcArgs &a, int split, long m, int n0, const uint32_t (&v)[32],
+                                           float sx, bool full) {
+  float *p = a.part + ((size_t)split * a.M + m) * a.N + n0;
+  if (full && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+    const float4 *iw4 = reinterpret_cast<const float4 *>(a.iw + n0);
+    float4 *p4 = reinterpret_cast<float4 *>(p);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const float4 f = iw4[i];
+      p4[i] = make_float4(__fmul_rn(__fmul_rn(__uint_as_float(v[4 * i]), sx), f.x),
+                          __fmul_rn(__fmul_rn(__uint_as_float(v[4 * i + 1]), sx), f.y),
+                          __fmul_rn(__fmul_rn(__uint_as_float(v[4 * i + 2]), sx), f.z),
+                          __fmul_rn(__fmul_rn(__uint_as_float(v[4 * i + 3]), sx), f.w));
+    }
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 32; i++)
+    if (n0 + i < a.N) p[i] = __fmul_rn(__fmul_rn(__uint_as_float(v[i]), sx), a.iw[n0 + i]);
+}
+
 __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant__ TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -698,7 +477,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
   const bool leader = rank == 0;
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int tiles_n = (a.N + 255) >> 8, tiles = ((a.M + 255) >> 8) * tiles_n;
-  const int nks = a.nsb * 4;
+  // work unit u: tile u / ksplit, superblocks [sb0, sb1) of split u % ksplit
+  const int units = tiles * a.ksplit;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kS; i++) {
@@ -734,9 +514,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
       const uint32_t lF = mapa(sa(F), 0);
       int g = 0;
       bool ok = true;
-      for (int tile = pair; tile < tiles && ok; tile += npairs) {
+      for (int u = pair; u < units && ok; u += npairs) {
+        const int tile = u / a.ksplit, sb0 = (u % a.ksplit) * a.sbper, sb1 = min(a.nsb, sb0 + a.sbper);
         const int tm = tile / tiles_n;
-        for (int ks = 0; ks < nks; ks++, g++) {
+        for (int ks = 4 * sb0; ks < 4 * sb1; ks++, g++) {
           const int s = g % kS;
           if (!poll2(E + s, ((g / kS) & 1) ^ 1, ab, a.err, 0)) {
             ok = false;
@@ -753,9 +534,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
     if (lane == 0) {
       int gr = 0;
       bool ok = true;
-      for (int tile = pair; tile < tiles && ok; tile += npairs) {
+      for (int u = pair; u < units && ok; u += npairs) {
+        const int tile = u / a.ksplit, sb0 = (u % a.ksplit) * a.sbper, sb1 = min(a.nsb, sb0 + a.sbper);
         const int tn = tile % tiles_n;
-        for (int sb = 0; sb < a.nsb; sb++, gr++) {
+        for (int sb = sb0; sb < sb1; sb++, gr++) {
           const int r = gr % kSR;
           if (!poll2(rE + r, ((gr / kSR) & 1) ^ 1, ab, a.err, 0)) {
             ok = false;
@@ -775,12 +557,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
       int it = 0, s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int tile = pair; tile < tiles && ok; tile += npairs, it++) {
+      for (int u = pair; u < units && ok; u += npairs, it++) {
+        const int sb0 = (u % a.ksplit) * a.sbper, sb1 = min(a.nsb, sb0 + a.sbper);
         const int buf = it & 1;
         if (!poll2(accE + buf, ((it >> 1) & 1) ^ 1, ab, a.err, 0)) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(buf * 256);
-        for (int ks = 0; ks < nks; ks++) {
+        for (int ks = 4 * sb0; ks < 4 * sb1; ks++) {
           if (!poll2(F + s, ph, ab, a.err, 0)) {
             ok = false;
             break;
@@ -789,7 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
           // stage offsets in the descriptors' 16-byte address units
           const uint64_t da = da0 + (uint64_t)(s * (kABytes >> 4)), db = db0 + (uint64_t)(s * (kBBytes >> 4));
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; kk++) mma2(d, da + 2 * kk, db + 2 * kk, (ks | kk) != 0);
+          for (int kk = 0; kk < kBK / 16; kk++) mma2(d, da + 2 * kk, db + 2 * kk, (ks != 4 * sb0) || kk != 0);
           commit2(eOwn + 8 * s);
           commit2(ePeer + 8 * s);
           if (++s == kS) {
@@ -808,14 +591,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
     const uint32_t lF = mapa(sa(F), 0);
     int gr = 0;
     bool ok = true;
-    for (int tile = pair; tile < tiles && ok; tile += npairs) {
+    for (int u = pair; u < units && ok; u += npairs) {
+      const int tile = u / a.ksplit, sb0 = (u % a.ksplit) * a.sbper, sb1 = min(a.nsb, sb0 + a.sbper);
       float mwr[kRPT];
 #pragma unroll
       for (int i = 0; i < kRPT; i++) {
         const int n = (tile % tiles_n) * 256 + (int)rank * kRows + t + i * kGT;
         mwr[i] = n < a.N ? a.mw[n] : 0.f;
       }
-      for (int sb = 0; sb < a.nsb && ok; sb++, gr++) {
+      for (int sb = sb0; sb < sb1 && ok; sb++, gr++) {
         const int r = gr % kSR;
         if (!warp_poll2(rF + r, (gr / kSR) & 1, ab, a.err, kDqSleep)) {
           ok = false;
@@ -869,7 +653,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
     const int q = warp & 3;
     const uint32_t laE = mapa(sa(accE), 0);
     int it = 0;
-    for (int tile = pair; tile < tiles; tile += npairs, it++) {
+    for (int u = pair; u < units; u += npairs, it++) {
+      const int tile = u / a.ksplit, split = u % a.ksplit;
       const int buf = it & 1;
       if (!warp_poll2(accF + buf, (it >> 1) & 1, ab, a.err, 64)) break;
       tc_fence_after();
@@ -887,7 +672,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
           if (lane == 0) arrive_cluster(laE + 8 * buf);
         }
         const int n0 = tn * 256 + j * 32;
-        if (live && n0 < a.N) store32(a, m, n0, v, sx, n0 + 32 <= a.N);
+        if (!live || n0 >= a.N) continue;
+        if (a.ksplit == 1) store32(a, m, n0, v, sx, n0 + 32 <= a.N);
+        else store_part(a, split, m, n0, v, sx, n0 + 32 <= a.N);
       }
     }
   }
@@ -901,35 +688,102 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
   }
 }
 
+// C (+)= the sum of the K splits' partials, added in split order (deterministic)
+__global__ void __launch_bounds__(256) k_tc_reduce(const float *part, int ksplit, int M, int N, void *c, int cdt,
+                                                   long ldc, int accumulate) {
+  const size_t total = (size_t)M * N, slice = total;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    float v = part[i];
+    for (int k = 1; k < ksplit; k++) v = __fadd_rn(v, part[k * slice + i]);
+    const long m = (long)(i / N), n = (long)(i % N);
+    store_out(c, m * ldc + n, cdt, v, accumulate != 0);
+  }
+}
+
 }  // namespace tc2
 
 }  // namespace tc
 
 // ----------------------------------------------------------------- host
 
+namespace {
+
+// clusters of the 2-CTA kernel that fit on the device at once (0 if the
+// kernel cannot be configured)
+int max_pairs() {
+  static int n = [] {
+    if (cudaFuncSetAttribute(tc::tc2::k_qgemm_tc2, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::tc2::kSmem) !=
+        cudaSuccess)
+      return 0;
+    cudaLaunchConfig_t q{};
+    cudaLaunchAttribute ca[1];
+    ca[0].id = cudaLaunchAttributeClusterDimension;
+    ca[0].val.clusterDim.x = 2;
+    ca[0].val.clusterDim.y = 1;
+    ca[0].val.clusterDim.z = 1;
+    q.gridDim = dim3(2 * 148);
+    q.blockDim = dim3(tc::tc2::kThreads);
+    q.dynamicSmemBytes = tc::tc2::kSmem;
+    q.attrs = ca;
+    q.numAttrs = 1;
+    int r = 0;
+    if (cudaOccupancyMaxActiveClusters(&r, tc::tc2::k_qgemm_tc2, &q) != cudaSuccess) r = 0;
+    return r;
+  }();
+  return n;
+}
+
+struct TcPlan {
+  int tiles, ksplit, sbper, pairs;
+  size_t xh, ix, w, part;  // workspace pieces (bytes, 256-aligned)
+};
+
+size_t up256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+// K splits when the 256 x 256 tiles do not give every pair one: as many
+// splits (whole superblocks each) as keep one round of work units
+TcPlan tc_plan(int M, int N, int K) {
+  TcPlan p{};
+  const int nsb = K / 256;
+  p.pairs = max_pairs();
+  p.tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  int ks = p.pairs > p.tiles ? p.pairs / p.tiles : 1;
+  if (ks > nsb) ks = nsb;
+  if (ks < 1) ks = 1;
+  p.sbper = (nsb + ks - 1) / ks;
+  p.ksplit = (nsb + p.sbper - 1) / p.sbper;
+  p.xh = up256((size_t)M * K * 2);
+  p.ix = up256((size_t)M * 4);
+  p.w = up256((size_t)N * 4);
+  p.part = p.ksplit > 1 ? up256((size_t)p.ksplit * M * N * 4) : 0;
+  return p;
+}
+
+}  // namespace
+
 bool tc_eligible(int wtype, int M, int N, int K, const void *w) {
   return wtype == TCB_Q4_K && M >= kTcMinM && N > 0 && K >= 256 && K % 256 == 0 &&
-         (reinterpret_cast<uintptr_t>(w) & 15) == 0 && tensor_map_encoder() != nullptr;
+         (reinterpret_cast<uintptr_t>(w) & 15) == 0 && tensor_map_encoder() != nullptr && max_pairs() > 0;
 }
 
 size_t tc_workspace_bytes(int M, int N, int K) {
-  const size_t xh = ((size_t)M * K * 2 + 255) & ~(size_t)255;
-  return xh + (((size_t)M * 4 + 255) & ~(size_t)255) + 2 * (((size_t)N * 4 + 255) & ~(size_t)255);
+  const TcPlan p = tc_plan(M, N, K);
+  return p.xh + p.ix + 2 * p.w + p.part;
 }
 
 cudaError_t launch_qgemm_tc(int wtype, const void *w, int M, int N, int K, const void *x, int xdt, long ldx, void *c,
                             int cdt, long ldc, int accumulate, void *ws, int *err, cudaStream_t s) {
   (void)wtype;
   using namespace tc;
+  const TcPlan pl = tc_plan(M, N, K);
+  if (pl.pairs <= 0) return cudaErrorInvalidConfiguration;
   const int nsb = K / 256;
   uint8_t *p = static_cast<uint8_t *>(ws);
   __half *xh = reinterpret_cast<__half *>(p);
-  p += ((size_t)M * K * 2 + 255) & ~(size_t)255;
-  float *ix = reinterpret_cast<float *>(p);
-  p += ((size_t)M * 4 + 255) & ~(size_t)255;
-  float *mw = reinterpret_cast<float *>(p);
-  p += ((size_t)N * 4 + 255) & ~(size_t)255;
-  float *iw = reinterpret_cast<float *>(p);
+  float *ix = reinterpret_cast<float *>(p + pl.xh);
+  float *mw = reinterpret_cast<float *>(p + pl.xh + pl.ix);
+  float *iw = reinterpret_cast<float *>(p + pl.xh + pl.ix + pl.w);
+  float *part = pl.ksplit > 1 ? reinterpret_cast<float *>(p + pl.xh + pl.ix + 2 * pl.w) : nullptr;
 
   TcArgs a{};
   auto enc = tensor_map_encoder();
@@ -937,18 +791,17 @@ cudaError_t launch_qgemm_tc(int wtype, const void *w, int M, int N, int K, const
   {
     cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
     cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-    cuuint32_t box[2] = {kBK, kBM}, es[2] = {1, 1};
+    cuuint32_t box[2] = {kBK, (cuuint32_t)tc2::kRows}, es[2] = {1, 1};
     if (enc(&a.ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xh, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
-  const bool pair = M > kBM;  // the 2-CTA kernel once X has more than one 128-row tile
   {
     const size_t rb = (size_t)nsb * kRawPitch;
     cuuint64_t dims[2] = {(cuuint64_t)rb, (cuuint64_t)N};
     cuuint64_t strides[1] = {(cuuint64_t)rb};
-    cuuint32_t box[2] = {kRawPitch, pair ? (cuuint32_t)tc2::kRows : (cuuint32_t)kBN}, es[2] = {1, 1};
+    cuuint32_t box[2] = {kRawPitch, (cuuint32_t)tc2::kRows}, es[2] = {1, 1};
     if (enc(&a.tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(w), dims, strides, box, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
@@ -964,6 +817,9 @@ cudaError_t launch_qgemm_tc(int wtype, const void *w, int M, int N, int K, const
   a.M = M;
   a.N = N;
   a.nsb = nsb;
+  a.ksplit = pl.ksplit;
+  a.sbper = pl.sbper;
+  a.part = part;
   a.err = err;
 
   k_tc_prep<<<M + (N + 7) / 8, 256, 0, s>>>(x, xdt, ldx, M, K, xh, ix, static_cast<const uint8_t *>(w), N, nsb, mw,
@@ -971,54 +827,27 @@ cudaError_t launch_qgemm_tc(int wtype, const void *w, int M, int N, int K, const
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
 
+  // persistent pairs: as many clusters as fit at once, at most one per work unit
+  const int units = pl.tiles * pl.ksplit;
   cudaLaunchConfig_t cfg{};
   cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = 1;
+  at[1].id = cudaLaunchAttributeClusterDimension;
+  at[1].val.clusterDim.x = 2;
+  at[1].val.clusterDim.y = 1;
+  at[1].val.clusterDim.z = 1;
   cfg.attrs = at;
+  cfg.numAttrs = 2;
   cfg.stream = s;
-  if (pair) {
-    // persistent pairs: as many clusters as fit at once, at most one per tile
-    static int max_clusters = [] {
-      if (cudaFuncSetAttribute(tc2::k_qgemm_tc2, cudaFuncAttributeMaxDynamicSharedMemorySize, tc2::kSmem) !=
-          cudaSuccess)
-        return 0;
-      cudaLaunchConfig_t q{};
-      cudaLaunchAttribute ca[1];
-      ca[0].id = cudaLaunchAttributeClusterDimension;
-      ca[0].val.clusterDim.x = 2;
-      ca[0].val.clusterDim.y = 1;
-      ca[0].val.clusterDim.z = 1;
-      q.gridDim = dim3(2 * 148);
-      q.blockDim = dim3(tc2::kThreads);
-      q.dynamicSmemBytes = tc2::kSmem;
-      q.attrs = ca;
-      q.numAttrs = 1;
-      int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, tc2::k_qgemm_tc2, &q) != cudaSuccess) n = 0;
-      return n;
-    }();
-    if (max_clusters <= 0) return cudaErrorInvalidConfiguration;
-    const int tiles = ((M + 255) / 256) * ((N + 255) / 256);
-    cfg.gridDim = dim3(2 * (tiles < max_clusters ? tiles : max_clusters));
-    cfg.blockDim = dim3(tc2::kThreads);
-    cfg.dynamicSmemBytes = tc2::kSmem;
-    at[1].id = cudaLaunchAttributeClusterDimension;
-    at[1].val.clusterDim.x = 2;
-    at[1].val.clusterDim.y = 1;
-    at[1].val.clusterDim.z = 1;
-    cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, tc2::k_qgemm_tc2, a);
-  }
-  static bool attr = [] {
-    return cudaFuncSetAttribute(k_qgemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) == cudaSuccess;
-  }();
-  if (!attr) return cudaErrorInvalidConfiguration;
-  cfg.gridDim = dim3((N + kBN - 1) / kBN, (M + kBM - 1) / kBM);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = kSmem;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_qgemm_tc, a);
+  cfg.gridDim = dim3(2 * (units < pl.pairs ? units : pl.pairs));
+  cfg.blockDim = dim3(tc2::kThreads);
+  cfg.dynamicSmemBytes = tc2::kSmem;
+  if ((e = cudaLaunchKernelEx(&cfg, tc2::k_qgemm_tc2, a)) != cudaSuccess || pl.ksplit == 1) return e;
+  const size_t total = (size_t)M * N;
+  const int blocks = (int)((total + 255) / 256 < 148 * 8 ? (total + 255) / 256 : 148 * 8);
+  tc2::k_tc_reduce<<<blocks, 256, 0, s>>>(part, pl.ksplit, M, N, c, cdt, ldc, accumulate);
+  return cudaGetLastError();
 }
 
 }  // namespace tcb
