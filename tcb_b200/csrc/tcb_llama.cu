@@ -43,6 +43,7 @@ namespace ll {
 
 constexpr int kHd = 128;        // head dimension supported by the attention kernel
 constexpr int kChunk = 64;      // positions per attention CTA
+constexpr int kMaxChunks = 256; // chunks a merge holds in shared memory (max_ctx <= 16384)
 constexpr int kArgBlocks = 148;
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -99,6 +100,9 @@ __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cos
   __shared__ float wo[8][G][kHd];
   __shared__ int last;
   mv::pdl_wait();
+  // the next kernel (the o projection) may launch now: its weight stream does
+  // not depend on this one, and it waits for this grid before reading `out`
+  mv::pdl_launch_dependents();
   const int p = *pos, n = p + 1, kh = blockIdx.x, c = blockIdx.y, t0 = c * kChunk;
   if (t0 >= n) return;
   const int tid = threadIdx.x;
@@ -247,22 +251,52 @@ __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cos
   __syncthreads();
   if (!last) return;
   __threadfence();
+  // merge: every chunk's (max, sum) into shared memory at once (the per-warp
+  // output buffer is free again), one warp per query head forms the chunk
+  // weights exp(m_c - M) and L, then each thread sums its output element over
+  // the chunks in chunk order with the loads issued ahead
+  float *cw = &wo[0][0][0], *cl = cw + G * nch;  // [G][nch] each
+  for (int i = tid; i < G * nch; i += blockDim.x) {
+    const int g = i / nch, cc = i % nch;
+    const float *pc = part + ((size_t)(kh * G + g) * nch_max + cc) * (2 + kHd);
+    cw[i] = __ldcg(pc);
+    cl[i] = __ldcg(pc + 1);
+  }
+  __syncthreads();
+  {
+    const int w = tid >> 5, lane = tid & 31;
+    if (w < G) {
+      float M = -INFINITY;
+      for (int cc = lane; cc < nch; cc += 32) M = fmaxf(M, cw[w * nch + cc]);
+      M = warp_max(M);
+      __syncwarp();
+      for (int cc = lane; cc < nch; cc += 32) cw[w * nch + cc] = __expf(cw[w * nch + cc] - M);
+      __syncwarp();
+      if (lane == 0) {
+        float L = 0.f;
+        for (int cc = 0; cc < nch; cc++) L = fmaf(cl[w * nch + cc], cw[w * nch + cc], L);
+        gl[w] = L;
+      }
+    }
+  }
+  __syncthreads();
   for (int i = tid; i < G * kHd; i += blockDim.x) {
     const int g = i / kHd, d = i % kHd;
-    const float *ph = part + (size_t)(kh * G + g) * nch_max * (2 + kHd);
-    float M = -INFINITY;
-    for (int cc = 0; cc < nch; cc++) M = fmaxf(M, __ldcg(ph + (size_t)cc * (2 + kHd)));
-    float L = 0.f, O = 0.f;
-    for (int cc = 0; cc < nch; cc++) {
-      const float *pc = ph + (size_t)cc * (2 + kHd);
-      const float f = __expf(__ldcg(pc) - M);
-      L = fmaf(__ldcg(pc + 1), f, L);
-      O = fmaf(__ldcg(pc + 2 + d), f, O);
+    const float *ph = part + (size_t)(kh * G + g) * nch_max * (2 + kHd) + 2 + d;
+    float O = 0.f;
+    int cc = 0;
+    for (; cc + 4 <= nch; cc += 4) {
+      const float o0 = __ldcg(ph + (size_t)cc * (2 + kHd)), o1 = __ldcg(ph + (size_t)(cc + 1) * (2 + kHd));
+      const float o2 = __ldcg(ph + (size_t)(cc + 2) * (2 + kHd)), o3 = __ldcg(ph + (size_t)(cc + 3) * (2 + kHd));
+      O = fmaf(o0, cw[g * nch + cc], O);
+      O = fmaf(o1, cw[g * nch + cc + 1], O);
+      O = fmaf(o2, cw[g * nch + cc + 2], O);
+      O = fmaf(o3, cw[g * nch + cc + 3], O);
     }
-    out[(size_t)(kh * G + g) * kHd + d] = __fdiv_rn(O, L);
+    for (; cc < nch; cc++) O = fmaf(__ldcg(ph + (size_t)cc * (2 + kHd)), cw[g * nch + cc], O);
+    out[(size_t)(kh * G + g) * kHd + d] = __fdiv_rn(O, gl[g]);
   }
   if (tid == 0) count[kh] = 0u;
-  mv::pdl_launch_dependents();
 }
 
 // a = silu(g) * u over the merged [G | U] rows
@@ -647,7 +681,8 @@ int tcb_llama_create(tcb_ctx *ctx, const tcb_llama_config *cfg, const tcb_llama_
   const tcb_llama_config &cg = *cfg;
   const int tp = cg.tp_size > 1 ? cg.tp_size : 1, tr = tp > 1 ? cg.tp_rank : 0;
   if (cg.n_layers < 1 || cg.d_model < 1 || cg.n_heads < 1 || cg.n_kv_heads < 1 || cg.head_dim != tcb::ll::kHd ||
-      cg.n_heads % cg.n_kv_heads || cg.ffn_dim < 1 || cg.vocab < 1 || cg.max_ctx < 2 || !(cg.eps > 0.f) ||
+      cg.n_heads % cg.n_kv_heads || cg.ffn_dim < 1 || cg.vocab < 1 || cg.max_ctx < 2 ||
+      cg.max_ctx > tcb::ll::kChunk * tcb::ll::kMaxChunks || !(cg.eps > 0.f) ||
       !(cg.rope_theta > 0.f) || tr < 0 || tr >= tp || cg.n_heads % tp || cg.n_kv_heads % tp || cg.ffn_dim % tp ||
       cg.vocab % tp)
     return TCB_ERR_SHAPE;
