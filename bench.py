@@ -285,7 +285,7 @@ def decode_tp_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
         "roofline": {"bound": "hbm", "achieved_per_gpu": round(per_gpu / (ms / 1e3 / 128) / 1e9, 2),
                      "peak": peak_gbs, "unit": "GB/s", "frac": round(per_gpu / (ms / 1e3 / 128) / 1e9 / peak_gbs, 4),
                      "ceiling_tokens_per_s": round(peak_gbs * 1e9 / per_gpu, 1)},
-        "collectives_per_token": 2 * cfg.n_layers + 1, "last_tokens": [int(v) for v in toks[-4:]],
+        "allreduce": "peer memory (NVLink)" if getattr(eng, "peer_active", False) else "nccl", "collectives_per_token": 2 * cfg.n_layers + 1, "last_tokens": [int(v) for v in toks[-4:]],
         "timing": "CUDA events around 128 graph replays, max over ranks",
     }
 

@@ -191,6 +191,15 @@ int tcb_llama_buffers(tcb_llama *m, int64_t **tokens, float **logits);
  * step or capture), with its device current. */
 int tcb_nccl_unique_id(unsigned char *id128);
 int tcb_llama_tp_init(tcb_llama *m, const unsigned char *id128);
+/* All-reduce of the residual over NVLink peer memory in place of NCCL's
+ * (the step's collective after o and after down, TR's row-parallel
+ * sublayers, layers.tr 348-389): each rank makes its exchange buffer and
+ * exports a 64-byte CUDA IPC handle of it, the caller gathers all ranks'
+ * handles in rank order (tp_size * 64 bytes) and passes them to
+ * tcb_llama_peer_init, before the first step or capture.  Without it the
+ * step uses NCCL.  The greedy pick's all-gather stays on NCCL. */
+int tcb_llama_peer_handle(tcb_llama *m, unsigned char *handle64);
+int tcb_llama_peer_init(tcb_llama *m, const unsigned char *handles);
 
 /* Size of the device array that tcb_qgemm_act8_static works in. */
 #define TCB_STATIC_SCRATCH_BYTES (4u << 20)

@@ -299,6 +299,92 @@ __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cos
   if (tid == 0) count[kh] = 0u;
 }
 
+// ---- all-reduce of the residual over peer memory (tensor parallelism)
+//
+// Every rank's exchange buffer (cudaMalloc'd, mapped into the other ranks by
+// CUDA IPC) holds flags [2][tp][kArBlocks] and slots [2][tp][D].  Call e (a
+// per-rank counter that all ranks advance alike) uses parity e & 1.  Block b
+// of rank r stores its slice of r's partial into slot [par][r] of every rank
+// (peer stores over NVLink), raises flag [par][r][b] = e on every rank, waits
+// until its own buffer holds flag e from all ranks for block b, and adds the
+// ranks' slices in rank order to the residual: x += ((y_0 + y_1) + ...) --
+// the same operations on every rank, so the ranks keep identical residuals.
+// A slot parity is written again only two calls later, when every rank has
+// finished the call in between and therefore read the old contents.  Waits
+// are bounded (about a second); a timeout records TCB_ERR_TIMEOUT.
+constexpr int kArBlocks = 16, kArThreads = 128, kMaxTp = 8;
+struct PeerBufs {
+  float *slot[kMaxTp];      // rank r's slots [2][tp][D] (this process's mapping)
+  unsigned *flag[kMaxTp];   // rank r's flags [2][tp][kArBlocks]
+};
+
+__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(kArThreads) k_peer_ar(const __grid_constant__ PeerBufs pb, const float *yp, float *x, int D, int tp,
+                                                       int rank, unsigned *epoch, unsigned *done, int *err) {
+  mv::pdl_wait();
+  mv::pdl_launch_dependents();
+  const unsigned e = *reinterpret_cast<volatile unsigned *>(epoch) + 1u;
+  const int par = (int)(e & 1u), b = blockIdx.x, nb = gridDim.x;
+  const int per = ((D + nb - 1) / nb + 3) & ~3;
+  const int i0 = b * per, i1 = min(D, i0 + per);
+  for (int r = 0; r < tp; r++) {
+    float *dst = pb.slot[r] + ((size_t)par * tp + rank) * D;
+    for (int i = i0 + 4 * threadIdx.x; i < i1; i += 4 * blockDim.x)
+      *reinterpret_cast<float4 *>(dst + i) = *reinterpret_cast<const float4 *>(yp + i);
+  }
+  __threadfence_system();
+  __syncthreads();
+  if ((int)threadIdx.x < tp) st_release_sys(pb.flag[threadIdx.x] + ((size_t)par * tp + rank) * nb + b, e);
+  if ((int)threadIdx.x < tp) {
+    const unsigned *f = pb.flag[rank] + ((size_t)par * tp + threadIdx.x) * nb + b;
+    bool ok = false;
+    for (uint32_t it = 0; it < (1u << 22); it++) {
+      if (ld_acquire_sys(f) == e) {
+        ok = true;
+        break;
+      }
+      __nanosleep(32);
+    }
+    if (!ok) atomicExch(err, TCB_ERR_TIMEOUT);
+  }
+  __syncthreads();
+  const float *mine = pb.slot[rank] + (size_t)par * tp * D;
+  for (int i = i0 + 4 * threadIdx.x; i < i1; i += 4 * blockDim.x) {
+    float4 acc = __ldcg(reinterpret_cast<const float4 *>(mine + i));
+    for (int r = 1; r < tp; r++) {
+      const float4 v = __ldcg(reinterpret_cast<const float4 *>(mine + (size_t)r * D + i));
+      acc.x = __fadd_rn(acc.x, v.x);
+      acc.y = __fadd_rn(acc.y, v.y);
+      acc.z = __fadd_rn(acc.z, v.z);
+      acc.w = __fadd_rn(acc.w, v.w);
+    }
+    float4 xv = *reinterpret_cast<float4 *>(x + i);
+    xv.x = __fadd_rn(xv.x, acc.x);
+    xv.y = __fadd_rn(xv.y, acc.y);
+    xv.z = __fadd_rn(xv.z, acc.z);
+    xv.w = __fadd_rn(xv.w, acc.w);
+    *reinterpret_cast<float4 *>(x + i) = xv;
+  }
+  // the last block to finish advances the counter (every block has read it)
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(done, 1u) == (unsigned)nb - 1u) {
+      *done = 0u;
+      *reinterpret_cast<volatile unsigned *>(epoch) = e;
+      __threadfence();
+    }
+  }
+}
+
 // a = silu(g) * u over the merged [G | U] rows
 __global__ void k_swiglu(const float *gu, float *a, int F) {
   mv::pdl_wait();
@@ -542,6 +628,14 @@ struct tcb_llama {
   int2 *cand = nullptr;  // greedy candidates [tp]
   void *sk = nullptr;    // split-K scratch shared by the step's matvecs (they run one after another)
   int nccl_rc = 0;       // last NCCL error
+  // peer-memory all-reduce (tcb_llama_peer_init); NCCL's when not set up
+  char *xbuf = nullptr;              // this rank's exchange buffer (flags, then slots)
+  size_t xbuf_bytes = 0;
+  tcb::ll::PeerBufs pb{};
+  std::vector<void *> opened;        // peers' buffers opened through CUDA IPC
+  bool peer = false;
+  float *yp = nullptr;               // this rank's partial of o / down
+  unsigned *ar_epoch = nullptr, *ar_done = nullptr;
 };
 
 namespace {
@@ -601,9 +695,14 @@ cudaError_t norm_matvec(tcb_llama *m, const Mat &mt, const float *nw, float *y, 
   return e == cudaSuccess ? matvec(m, mt, m->h, y, 0, s) : e;
 }
 
-// x <- sum over ranks (in place), tensor parallelism only
+// x <- sum over ranks (in place), tensor parallelism only.  With the peer
+// all-reduce every rank's partial is in yp and x holds the residual.
 cudaError_t all_reduce_x(tcb_llama *m, cudaStream_t s) {
   if (m->tp == 1) return cudaSuccess;
+  if (m->peer)
+    return tcb::ll::launch(tcb::ll::k_peer_ar, dim3(tcb::ll::kArBlocks), dim3(tcb::ll::kArThreads), s, m->pb,
+                           (const float *)m->yp, m->x, m->cfg.d_model, m->tp, m->tr, m->ar_epoch, m->ar_done,
+                           m->ctx->derr);
   const Nccl *nc = nccl();
   if (!nc || !m->comm) return cudaErrorNotReady;
   m->nccl_rc = nc->all_reduce(m->x, m->x, (size_t)m->cfg.d_model, kNcclFloat32, kNcclSum, m->comm, s);
@@ -638,17 +737,22 @@ cudaError_t issue_step(tcb_llama *m, cudaStream_t s) {
     if (e != cudaSuccess) break;
     // rank 0 adds its partial to the residual, the others write theirs; the
     // all-reduce then leaves x + sum of partials on every rank
-    if ((e = matvec(m, m->o[l], m->att, m->x, m->tr == 0, s)) != cudaSuccess) break;
+    // NCCL: rank 0 adds its partial to the residual, the others write theirs,
+    // and the in-place all-reduce sums x.  Peer: every rank writes its partial
+    // to yp and the all-reduce adds the ranks' partials to x.
+    float *dst = m->peer ? m->yp : m->x;
+    const int acc = m->peer ? 0 : m->tr == 0;
+    if ((e = matvec(m, m->o[l], m->att, dst, acc, s)) != cudaSuccess) break;
     if ((e = all_reduce_x(m, s)) != cudaSuccess) break;
     if ((e = norm_matvec(m, m->gu[l], m->ffn_norm[l], m->gub, s)) != cudaSuccess) break;
     if (m->down[l].plan.ok && m->down[l].plan.kind == 2) {
       // SwiGLU fused into the Q6_K matvec's prologue
       const Mat &dm = m->down[l];
-      e = tcb::q6k_launch(dm.plan, dm.N, dm.K, dm.w, m->gub, TCB_F32, m->x, TCB_F32, m->tr == 0, m->ctx->derr, s, 1,
+      e = tcb::q6k_launch(dm.plan, dm.N, dm.K, dm.w, m->gub, TCB_F32, dst, TCB_F32, acc, m->ctx->derr, s, 1,
                           dm.pf, dm.pf_bytes, m->sk);
     } else {
       if ((e = launch(k_swiglu, dim3((F + 255) / 256), dim3(256), s, m->gub, m->a, F)) != cudaSuccess) break;
-      e = matvec(m, m->down[l], m->a, m->x, m->tr == 0, s);
+      e = matvec(m, m->down[l], m->a, dst, acc, s);
     }
     if (e != cudaSuccess) break;
     e = all_reduce_x(m, s);
@@ -805,6 +909,7 @@ int tcb_llama_destroy(tcb_llama *m) {
   if (!m->allocs.empty()) cudaDeviceSynchronize();
   if (m->cap) cudaStreamDestroy(m->cap);
   if (m->comm) nccl()->destroy(m->comm);
+  for (void *p : m->opened) cudaIpcCloseMemHandle(p);
   for (void *p : m->allocs) cudaFree(p);
   delete m;
   return TCB_OK;
@@ -899,6 +1004,59 @@ int tcb_llama_tp_init(tcb_llama *m, const unsigned char *id128) {
     m->comm = nullptr;
     return TCB_ERR_CUDA;
   }
+  return TCB_OK;
+}
+
+int tcb_llama_peer_handle(tcb_llama *m, unsigned char *handle64) {
+  if (!m || !handle64) return TCB_ERR_NULL;
+  memset(handle64, 0, 64);
+  if (m->tp == 1) return TCB_OK;
+  if (m->tp > tcb::ll::kMaxTp || m->cfg.d_model % 4) return TCB_ERR_UNSUPPORTED;
+  cudaError_t e = cudaSetDevice(m->ctx->dev);
+  if (e == cudaSuccess && !m->xbuf) {
+    const size_t flags = ((size_t)2 * m->tp * tcb::ll::kArBlocks * 4 + 255) & ~(size_t)255;
+    m->xbuf_bytes = flags + (size_t)2 * m->tp * m->cfg.d_model * 4;
+    if ((e = alloc(m, &m->xbuf, m->xbuf_bytes)) == cudaSuccess && (e = cudaMemset(m->xbuf, 0, m->xbuf_bytes)) == cudaSuccess &&
+        (e = alloc(m, &m->yp, (size_t)m->cfg.d_model)) == cudaSuccess && (e = alloc(m, &m->ar_epoch, 2)) == cudaSuccess)
+      e = cudaMemset(m->ar_epoch, 0, 2 * sizeof(unsigned));
+    m->ar_done = m->ar_epoch + 1;
+  }
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, m->xbuf);
+  if (e != cudaSuccess) return fail(m, e);
+  memcpy(handle64, &h, 64);
+  return TCB_OK;
+}
+
+int tcb_llama_peer_init(tcb_llama *m, const unsigned char *handles) {
+  if (!m || !handles) return TCB_ERR_NULL;
+  if (m->tp == 1) return TCB_OK;
+  if (!m->xbuf) {  // tcb_llama_peer_handle makes the buffer first
+    snprintf(m->ctx->err, sizeof m->ctx->err, "tcb_llama_peer_init before tcb_llama_peer_handle");
+    return TCB_ERR_UNSUPPORTED;
+  }
+  if (m->peer) return TCB_OK;
+  cudaError_t e = cudaSetDevice(m->ctx->dev);
+  const size_t flags = ((size_t)2 * m->tp * tcb::ll::kArBlocks * 4 + 255) & ~(size_t)255;
+  for (int r = 0; r < m->tp && e == cudaSuccess; r++) {
+    char *base = m->xbuf;
+    if (r != m->tr) {
+      cudaIpcMemHandle_t h;
+      memcpy(&h, handles + 64 * r, 64);
+      void *p = nullptr;
+      if ((e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess)) != cudaSuccess) break;
+      m->opened.push_back(p);
+      base = static_cast<char *>(p);
+    }
+    m->pb.flag[r] = reinterpret_cast<unsigned *>(base);
+    m->pb.slot[r] = reinterpret_cast<float *>(base + flags);
+  }
+  if (e != cudaSuccess) {
+    for (void *p : m->opened) cudaIpcCloseMemHandle(p);
+    m->opened.clear();
+    return fail(m, e);
+  }
+  m->peer = true;
   return TCB_OK;
 }
 

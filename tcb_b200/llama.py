@@ -202,6 +202,8 @@ def _bind():
     L.tcb_llama_buffers.argtypes = [P, ctypes.POINTER(P), ctypes.POINTER(P)]
     L.tcb_nccl_unique_id.argtypes = [P]
     L.tcb_llama_tp_init.argtypes = [P, P]
+    L.tcb_llama_peer_handle.argtypes = [P, P]
+    L.tcb_llama_peer_init.argtypes = [P, P]
     L._llama_bound = True
     return L
 
@@ -270,10 +272,30 @@ class Llama:
         n = self.cfg.vocab // self.tp[0]
         return self._download(self._buffers()[1], np.empty(n, np.float32), stream)
 
-    def tp_init(self, nccl_id: bytes):
-        """Join the tensor-parallel group (every rank, the same 128-byte id)."""
+    def tp_init(self, nccl_id: bytes, peer: bool = True):
+        """Join the tensor-parallel group (every rank, the same 128-byte id).
+        With peer=True the residual all-reduce runs over NVLink peer memory:
+        the ranks' CUDA IPC handles are gathered in rank order over the
+        default torch.distributed group (every rank must call this).  If the
+        peers cannot be mapped the step keeps NCCL's all-reduce
+        (self.peer_active says which)."""
         buf = ctypes.create_string_buffer(bytes(nccl_id), 128)
         self._check(self._L.tcb_llama_tp_init(self._h, buf), "tp_init")
+        self.peer_active = False
+        if not peer or self.tp[0] == 1:
+            return
+        h = ctypes.create_string_buffer(64)
+        ok = self._L.tcb_llama_peer_handle(self._h, h) == 0
+        handles = gather_bytes(h.raw if ok else b"", self.tp[0])
+        if ok and all(len(x) == 64 for x in handles):
+            hb = ctypes.create_string_buffer(b"".join(handles), 64 * len(handles))
+            ok = self._L.tcb_llama_peer_init(self._h, hb) == 0
+        else:
+            ok = False
+        # every rank takes the same path: peer only if all ranks mapped their peers
+        self.peer_active = all(gather_bytes(b"1" if ok else b"0", self.tp[0])[i] == b"1" for i in range(self.tp[0]))
+        if ok and not self.peer_active:
+            raise RuntimeError("peer all-reduce set up on some ranks only")
 
     def close(self):
         if getattr(self, "_h", None):
@@ -295,6 +317,16 @@ def nccl_unique_id() -> bytes:
     if rc != 0:
         raise TcbError(rc, "tcb_nccl_unique_id")
     return buf.raw
+
+
+def gather_bytes(b: bytes, world: int) -> list:
+    """Every rank's bytes, in rank order, on every rank of the default
+    torch.distributed group (any backend)."""
+    import torch.distributed as dist
+
+    out = [None] * world
+    dist.all_gather_object(out, bytes(b))
+    return out
 
 
 def share_id(make, rank: int) -> bytes:

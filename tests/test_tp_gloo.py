@@ -1,5 +1,6 @@
-"""The id exchange of the tensor-parallel decoder (llama.share_id) on two
-gloo ranks on the CPU: rank 0's bytes reach every rank."""
+"""The exchanges of the tensor-parallel decoder on two gloo ranks on the
+CPU: rank 0's NCCL id reaches every rank (llama.share_id), and every rank's
+64-byte peer handle reaches every rank in rank order (llama.gather_bytes)."""
 import os
 import socket
 
@@ -23,7 +24,8 @@ def _worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     got = llama.share_id(lambda: bytes(range(128)), rank)
-    q.put((rank, got))
+    handles = llama.gather_bytes(bytes([rank]) * 64, world)
+    q.put((rank, (got, handles)))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -39,4 +41,5 @@ def test_share_id_two_ranks():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    assert res[0] == res[1] == bytes(range(128))
+    assert res[0][0] == res[1][0] == bytes(range(128))
+    assert res[0][1] == res[1][1] == [bytes([0]) * 64, bytes([1]) * 64]
