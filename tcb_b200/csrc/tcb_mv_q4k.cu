@@ -67,7 +67,6 @@ constexpr int kBox8 = 146;                  // box width, 8-byte elements (8 * 1
 constexpr int kPitch = kBox8 * 8;           // staged row pitch (1168 = 16 mod 128)
 constexpr int kBoxBytes = kRows * kPitch;   // one stage
 constexpr int kSlots = 4;                   // tile partial slots in flight
-constexpr int kPF = 4;                      // boxes prefetched into L2 ahead of the stages
 constexpr int kFrag = 512, kScl = 64;       // per block: B fragments, lane scales
 constexpr int kBarOff = 0, kFlagOff = 256, kNormOff = 288, kPartOff = 512;
 constexpr int kPartBytes = kSlots * kC * kRows * 4;
@@ -344,9 +343,9 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq4k(const __grid_constant_
     // before the previous kernel of the stream has finished
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
-      // box it: tile blockIdx.x + (it / nch) * grid, chunk it % nch.  Boxes
-      // beyond the shared-memory stages are first brought into L2, kPF
-      // ahead, so a refill is an L2 read.
+      // box it: tile blockIdx.x + (it / nch) * grid, chunk it % nch.  (An L2
+      // prefetch of the boxes beyond the stages measured slower: 6-19 % on
+      // 25-66 MB products.)
       auto bx = [&](int it) { return (it % a.nch) * kBlk * 18; };
       auto by = [&](int it) { return ((int)blockIdx.x + (it / a.nch) * (int)gridDim.x) * kRows; };
       for (int it = 0; it < nstages; it++) {
@@ -355,10 +354,6 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq4k(const __grid_constant_
         mbar_expect_tx(&full[buf], (uint32_t)kBoxBytes);
         tma_load_2d(stages + buf * kBoxBytes, &tmap, bx(it), by(it), &full[buf]);
         if (it == (nstages < a.S ? nstages : a.S) - 1) prefetch_slice_l2(a.pf, a.pf_bytes);
-        if (it == a.S - 1 || (it >= a.S && it + kPF < nstages)) {
-          for (int p = (it == a.S - 1 ? a.S : it + kPF); p < nstages && p <= it + kPF; p++)
-            tma_prefetch_2d(&tmap, bx(p), by(p));
-        }
       }
     }
     return;
@@ -511,7 +506,9 @@ MvPlan q4k_plan(int N, int K, const void *w, int sms) {
   if (!enc) return pl;
   const int base = (kXOff + x_bytes(nb) + 127) & ~127;
   int S, per_sm;
-  if (base + 2 * kBoxBytes <= kSmemTwo) {
+  // two CTAs per SM when the tiles outnumber the SMs; otherwise one CTA per
+  // SM streams its (long) rows through the deeper pipeline one CTA affords
+  if (base + 2 * kBoxBytes <= kSmemTwo && (N + kRows - 1) / kRows > sms) {
     S = (kSmemTwo - base) / kBoxBytes;
     if (S > 6) S = 6;
     per_sm = 2;

@@ -50,7 +50,6 @@ constexpr int kBox8 = 210;                  // box width, 8-byte elements (8 blo
 constexpr int kPitch = kBox8 * 8;           // staged row pitch (1680 = 16 mod 128)
 constexpr int kBoxBytes = kRows * kPitch;   // one stage
 constexpr int kSlots = 4;                   // tile partial slots in flight
-constexpr int kPF = 4;                      // boxes prefetched into L2 ahead of the stages
 constexpr int kFrag = 512, kScl = 128;      // per block: B fragments, lane scales
 constexpr int kBarOff = 0, kFlagOff = 256, kPartOff = 512;
 constexpr int kPartBytes = kSlots * kC * kRows * 4;
@@ -370,10 +369,6 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq6k(const __grid_constant_
         mbar_expect_tx(&full[buf], (uint32_t)kBoxBytes);
         tma_load_2d(stages + buf * kBoxBytes, &tmap, bx(it), by(it), &full[buf]);
         if (it == (nstages < a.S ? nstages : a.S) - 1) prefetch_slice_l2(a.pf, a.pf_bytes);
-        if (it == a.S - 1 || (it >= a.S && it + kPF < nstages)) {
-          for (int p = (it == a.S - 1 ? a.S : it + kPF); p < nstages && p <= it + kPF; p++)
-            tma_prefetch_2d(&tmap, bx(p), by(p));
-        }
       }
     }
     return;
