@@ -150,13 +150,13 @@ __device__ __forceinline__ void load8(const void *x, int e, int xdt, bool vec, f
 // sigma = 1/id, not exact, so it is the hardware reciprocal.  Returns false
 // if a sub-block sum is not finite (a NaN or Inf in x, or a sum that
 // overflows, which only sends the call down the exact fp32 path).
-__device__ bool prep_warp(const Params &a, uint8_t *xr, int own, int lane, float &ss) {
+__device__ bool prep_warp(const Params &a, uint8_t *xr, int own, int lane, float &ss, uint64_t *xgo) {
   constexpr float MAGIC = 12582912.0f;
   constexpr int NB = 4;  // blocks in flight per lane
   uint8_t *frag = xr;
   float *scl = reinterpret_cast<float *>(xr + a.nb * kFrag);
   const bool vec = (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
-  bool fin = true;
+  bool fin = true, told = false;
   ss = 0.f;
   for (int base = own; base < a.nb; base += kC * NB) {
     float xv[NB][8];
@@ -164,6 +164,13 @@ __device__ bool prep_warp(const Params &a, uint8_t *xr, int own, int lane, float
     for (int j = 0; j < NB; j++) {
       const int bg = base + kC * j;
       if (bg < a.nb) load8(a.x, bg * 256 + 8 * lane, a.xdt, vec, xv[j]);
+    }
+    if (!told) {
+      // the first x loads are out: the producer may issue the rest of the
+      // weight stream behind them
+      __syncwarp();
+      if (lane == 0) mbar_arrive(xgo);
+      told = true;
     }
     if (a.nw) {
       // fused RMSNorm: digits of x * w; the 1/rms factor is applied to the
@@ -232,6 +239,10 @@ __device__ bool prep_warp(const Params &a, uint8_t *xr, int own, int lane, float
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+  if (!told) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(xgo);
+  }
   return __all_sync(0xFFFFFFFFu, fin);
 }
 
@@ -315,6 +326,7 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq4k(const __grid_constant_
   uint64_t *empty = full + 8;                                  // [S]     compute -> producer
   uint64_t *tdone = full + 16;                                 // [slots] tile partials ready
   uint64_t *tfree = full + 24;                                 // [slots] tile partials summed
+  uint64_t *xgo = full + 20;                                   // compute warps -> producer: x loads issued
   int *flag = reinterpret_cast<int *>(sm + kFlagOff);
   float *part = reinterpret_cast<float *>(sm + kPartOff);      // [slots][kC][kRows]
   uint8_t *xr = sm + kXOff;
@@ -333,6 +345,7 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq4k(const __grid_constant_
       mbar_init(&tdone[s], kC);
       mbar_init(&tfree[s], 1);
     }
+    mbar_init(xgo, kC);
     fence_barrier_init();
   }
   __syncthreads();
@@ -350,6 +363,10 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq4k(const __grid_constant_
       auto by = [&](int it) { return ((int)blockIdx.x + (it / a.nch) * (int)gridDim.x) * kRows; };
       for (int it = 0; it < nstages; it++) {
         const int buf = it % a.S;
+        // one box goes out before the previous kernel has finished; the rest
+        // queue behind this CTA's x loads (issued right after the dependency
+        // wait), so x does not wait for the whole weight stream
+        if (it == 1 && !spin_bar_ns(xgo, 0u, a.err, 32)) return;
         if (it >= a.S && !spin_bar_ns(&empty[buf], (uint32_t)(((it / a.S) & 1) ^ 1), a.err, 64)) return;
         mbar_expect_tx(&full[buf], (uint32_t)kBoxBytes);
         tma_load_2d(stages + buf * kBoxBytes, &tmap, bx(it), by(it), &full[buf]);
@@ -365,7 +382,7 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq4k(const __grid_constant_
   if (warp < kC) {
     if (warp == 0) reinterpret_cast<uint4 *>(xr + a.nb * (kFrag + kScl))[lane] = make_uint4(0u, 0u, 0u, 0u);
     float ss;
-    if (!prep_warp(a, xr, (warp + (int)blockIdx.x) & (kBlk - 1), lane, ss) && lane == 0) *flag = 1;
+    if (!prep_warp(a, xr, (warp + (int)blockIdx.x) & (kBlk - 1), lane, ss, xgo) && lane == 0) *flag = 1;
     if (lane == 0) reinterpret_cast<float *>(sm + kNormOff)[warp] = ss;
   }
   asm volatile("bar.sync 1, %0;" ::"n"(32 * (kC + 1)) : "memory");
