@@ -120,13 +120,14 @@ __device__ __forceinline__ void load8(const void *x, int e, int xdt, bool vec, f
 // x is not finite.
 // Blocks [b0, b0 + nbl) of x (this CTA's K split), stored at local block
 // index bg - b0.
-__device__ bool prep_warp(const Params &a, uint8_t *xr, int own, int lane, int b0, int nbl, int nbl_cap) {
+__device__ bool prep_warp(const Params &a, uint8_t *xr, int own, int lane, int b0, int nbl, int nbl_cap,
+                          uint64_t *xgo) {
   constexpr float MAGIC = 12582912.0f;
   constexpr int NB = 4;
   uint8_t *frag = xr;
   float *scl = reinterpret_cast<float *>(xr + nbl_cap * kFrag);
   const bool vec = (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (a.K & 3) == 0;
-  bool fin = true;
+  bool fin = true, told = false;
   for (int base = own; base < nbl; base += kC * NB) {
     float xv[NB][8];
 #pragma unroll
@@ -144,6 +145,13 @@ __device__ bool prep_warp(const Params &a, uint8_t *xr, int own, int lane, int b
           }
         }
       }
+    }
+    if (!told) {
+      // the first x loads are back: the producer may issue the rest of the
+      // weight stream behind them
+      __syncwarp();
+      if (lane == 0) mbar_arrive(xgo);
+      told = true;
     }
 #pragma unroll
     for (int j = 0; j < NB; j++) {
@@ -196,6 +204,10 @@ __device__ bool prep_warp(const Params &a, uint8_t *xr, int own, int lane, int b
       if ((lane & 3) == 0) sl[st] = sigma * (1.0f / 254.0f);
       if ((lane & 1) == 0) sl[2 + 2 * st + ((lane >> 1) & 1)] = -32.0f * fmaf(fh, 254.0f, fl);
     }
+  }
+  if (!told) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(xgo);
   }
   return __all_sync(0xFFFFFFFFu, fin);
 }
@@ -330,6 +342,7 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq6k(const __grid_constant_
   uint64_t *empty = full + 8;
   uint64_t *tdone = full + 16;
   uint64_t *tfree = full + 24;
+  uint64_t *xgo = full + 20;  // compute warps -> producer: first x loads done
   int *flag = reinterpret_cast<int *>(sm + kFlagOff);
   float *part = reinterpret_cast<float *>(sm + kPartOff);  // [slots][kC][16]
   uint8_t *xr = sm + kXOff;
@@ -353,6 +366,7 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq6k(const __grid_constant_
       mbar_init(&tdone[st], kC);
       mbar_init(&tfree[st], 1);
     }
+    mbar_init(xgo, kC);
     fence_barrier_init();
   }
   __syncthreads();
@@ -365,6 +379,8 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq6k(const __grid_constant_
       auto by = [&](int it) { return tile_of(it / nchl) * kRows; };
       for (int it = 0; it < nstages; it++) {
         const int buf = it % a.S;
+        // one box before the dependency wait; the rest queue behind x
+        if (it == 1 && !spin_bar_ns(xgo, 0u, a.err, 32)) return;
         if (it >= a.S && !spin_bar_ns(&empty[buf], (uint32_t)(((it / a.S) & 1) ^ 1), a.err, 64)) return;
         mbar_expect_tx(&full[buf], (uint32_t)kBoxBytes);
         tma_load_2d(stages + buf * kBoxBytes, &tmap, bx(it), by(it), &full[buf]);
@@ -377,7 +393,7 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq6k(const __grid_constant_
   pdl_wait();
   if (warp < kC) {
     if (warp == 0) reinterpret_cast<uint4 *>(xr + nbl_cap * (kFrag + kScl))[lane] = make_uint4(0u, 0u, 0u, 0u);
-    if (!prep_warp(a, xr, (warp + (int)blockIdx.x) & (kBlk - 1), lane, b0, nbl, nbl_cap) && lane == 0) *flag = 1;
+    if (!prep_warp(a, xr, (warp + (int)blockIdx.x) & (kBlk - 1), lane, b0, nbl, nbl_cap, xgo) && lane == 0) *flag = 1;
   }
   asm volatile("bar.sync 1, %0;" ::"n"(32 * (kC + 1)) : "memory");
   const bool slow = *flag != 0;
