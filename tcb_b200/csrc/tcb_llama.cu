@@ -93,7 +93,7 @@ __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cos
                                               __half *kc, __half *vc, float *part, unsigned *count, float *out, int H,
                                               int KVH, int max_ctx, int nch_max, float scale) {
   constexpr int half = kHd / 2;
-  __shared__ float qs[G][kHd];
+  __shared__ __align__(16) float qs[G][kHd];
   __shared__ float knew[kHd], vnew[kHd];
   __shared__ float sc[G][kChunk];
   __shared__ float gm[G], gl[G];
@@ -170,10 +170,18 @@ __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cos
           }
         }
       }
+      // 16-byte q loads (a broadcast among the lanes of one sk) and the G
+      // heads' chains interleaved
 #pragma unroll
-      for (int g = 0; g < G; g++)
+      for (int i4 = 0; i4 < 8; i4++)
 #pragma unroll
-        for (int i = 0; i < 32; i++) s[g] = fmaf(qs[g][32 * sk + i], kv[i], s[g]);
+        for (int g = 0; g < G; g++) {
+          const float4 q4 = *reinterpret_cast<const float4 *>(&qs[g][32 * sk + 4 * i4]);
+          s[g] = fmaf(q4.x, kv[4 * i4], s[g]);
+          s[g] = fmaf(q4.y, kv[4 * i4 + 1], s[g]);
+          s[g] = fmaf(q4.z, kv[4 * i4 + 2], s[g]);
+          s[g] = fmaf(q4.w, kv[4 * i4 + 3], s[g]);
+        }
     }
 #pragma unroll
     for (int g = 0; g < G; g++) {
