@@ -193,7 +193,7 @@ int tcb_qgemm(tcb_ctx *ctx, int wtype, int M, int N, int K, const void *w, const
   rc = run_matvec(ctx, wtype, 0, M, N, K, w, x, xdtype, c, cdtype, accumulate, s, &taken);
   if (taken || rc != TCB_OK) return rc;
   if (tcb::tc_eligible(wtype, M, N, K, w)) {
-    if ((rc = ensure_ws(ctx, tcb::tc_workspace_bytes(M, N, K))) != TCB_OK) return rc;
+    if ((rc = ensure_ws(ctx, tcb::tc_workspace_bytes(wtype, M, N, K))) != TCB_OK) return rc;
     cudaError_t e = tcb::launch_qgemm_tc(wtype, w, M, N, K, x, xdtype, ldx, c, cdtype, ldc, accumulate, ctx->ws,
                                          ctx->derr, s);
     return e == cudaSuccess ? TCB_OK : cuda_fail(ctx, e);

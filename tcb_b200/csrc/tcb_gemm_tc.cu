@@ -1,9 +1,12 @@
 // tcb_gemm_tc.cu - the many-row float product (prefill: M >= kTcMinM rows
 // of activations) on the fifth-generation tensor cores.
 //
-// C (+)= X · dequant(W)ᵀ for Q4_K weights W [N, K] (TR's Backend.Gemm quant
-// branch, gpu/backend_quant.go:43-65; CPU semantics quantGemm,
-// tensor/cpu_quant.go:47-147: the product of X with the opened weights).
+// C (+)= X · dequant(W)ᵀ for weights W [N, K] in GGUF blocks (TR's
+// Backend.Gemm quant branch, gpu/backend_quant.go:43-65; CPU semantics
+// quantGemm, tensor/cpu_quant.go:47-147: the product of X with the opened
+// weights).  Q4_K superblocks are dequantised inside the kernel; Q6_K, Q8_0
+// and Q4_0 rows are first dequantised exactly (k_tc_wdeq) to row-scaled fp16
+// in workspace, and the kernel loads them by TMA like X.
 //
 // Launches:
 //  1. k_tc_prep: each activation row x[m] is scaled by a power of two
@@ -38,6 +41,7 @@
 
 #include "../../include/tcb.h"
 #include "tcb_common.cuh"
+#include "tcb_dequant.cuh"
 #include "tcb_gemm_tc.h"
 #include "tcb_mv_ptx.cuh"
 
@@ -154,7 +158,7 @@ __device__ __forceinline__ void load8(const char *row, int g, int xdt, bool vec,
 // weight rows (one warp per row).
 __global__ void __launch_bounds__(256) k_tc_prep(const void *x, int xdt, long ldx, int M, int K, __half *xh,
                                                  float *ix, const uint8_t *w, int N, int nsb, float *mw,
-                                                 float *iw) {
+                                                 float *iw, int perm) {
   __shared__ float red[8];
   __shared__ int bad_s;
   if ((int)blockIdx.x < M) {
@@ -195,10 +199,17 @@ __global__ void __launch_bounds__(256) k_tc_prep(const void *x, int xdt, long ld
 #pragma unroll
       for (int i = 0; i < 8; i++) v[i] = __fmul_rn(v[i], mul);
       uint4 o;
-      o.x = h2_bits(__floats2half2_rn(v[0], v[2]));
-      o.y = h2_bits(__floats2half2_rn(v[1], v[3]));
-      o.z = h2_bits(__floats2half2_rn(v[4], v[6]));
-      o.w = h2_bits(__floats2half2_rn(v[5], v[7]));
+      if (perm) {
+        o.x = h2_bits(__floats2half2_rn(v[0], v[2]));
+        o.y = h2_bits(__floats2half2_rn(v[1], v[3]));
+        o.z = h2_bits(__floats2half2_rn(v[4], v[6]));
+        o.w = h2_bits(__floats2half2_rn(v[5], v[7]));
+      } else {
+        o.x = h2_bits(__floats2half2_rn(v[0], v[1]));
+        o.y = h2_bits(__floats2half2_rn(v[2], v[3]));
+        o.z = h2_bits(__floats2half2_rn(v[4], v[5]));
+        o.w = h2_bits(__floats2half2_rn(v[6], v[7]));
+      }
       dst[g] = o;
     }
     return;
@@ -226,6 +237,91 @@ __global__ void __launch_bounds__(256) k_tc_prep(const void *x, int xdt, long ld
   if (lane == 0) {
     mw[n] = ldexpf(1.f, -e);
     iw[n] = ldexpf(1.f, e);
+  }
+}
+
+// elements j .. j+7 (j a multiple of 8) of the block at b, with TR's
+// dequant operations; the 8 share their block scales
+template <int W>
+__device__ __forceinline__ void dequant8(const uint8_t *b, int j, float (&v)[8]) {
+  if constexpr (W == TCB_Q6_K) {
+    const int n = j >> 7, c = (j >> 5) & 3, l = j & 31;
+    const float ds = mulx(half_exact(ld_u16(b + 208)), (float)(int8_t)b[192 + 8 * n + (l >> 4) + 2 * c]);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const uint32_t low = (b[64 * n + l + i + 32 * (c & 1)] >> (4 * (c >> 1))) & 0xFu;
+      const uint32_t high = (b[128 + 32 * n + l + i] >> (2 * c)) & 3u;
+      v[i] = mulx(ds, (float)((int)(low | (high << 4)) - 32));
+    }
+  } else if constexpr (W == TCB_Q8_0) {
+    const float d = half_exact(ld_u16(b));
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = mulx((float)(int8_t)b[2 + j + i], d);
+  } else {
+    const float d = half_exact(ld_u16(b));
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const uint32_t q = b[2 + ((j + i) & 15)];
+      v[i] = mulx((float)((int)(((j + i) < 16 ? q : q >> 4) & 0xFu) - 8), d);
+    }
+  }
+}
+
+// k_tc_wdeq: the weights of the other block types for the tensor-core
+// kernel: row n dequantised exactly (TR's dequant), scaled by a power of two
+// that brings the row's largest magnitude into [2^14, 2^15) and rounded once
+// to fp16 (natural K order); iw[n] holds the inverse factor.  One pass: a
+// thread keeps its 8-element groups (at most kWdeqGroups) in registers.
+constexpr int kWdeqGroups = 8;  // K <= 8 * 8 * 256 = 16384
+template <int W>
+__global__ void __launch_bounds__(256) k_tc_wdeq(const uint8_t *w, int N, int K, __half *wh, float *iw) {
+  __shared__ float red[8];
+  __shared__ int bad_s;
+  constexpr int E = Fmt<W>::E, B = Fmt<W>::B;
+  const int n = blockIdx.x;
+  const uint8_t *row = w + (size_t)n * (K / E) * B;
+  float v[kWdeqGroups][8];
+  float amax = 0.f;
+  int bad = 0;
+  if (threadIdx.x == 0) bad_s = 0;
+#pragma unroll
+  for (int gi = 0; gi < kWdeqGroups; gi++) {
+    const int k = 8 * (threadIdx.x + gi * blockDim.x);
+    if (k < K) {
+      dequant8<W>(row + (size_t)(k / E) * B, k % E, v[gi]);
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const float a = fabsf(v[gi][i]);
+        bad |= !(a <= 3.402823466e38f);
+        amax = fmaxf(amax, a);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  if (bad) bad_s = 1;
+  __syncthreads();
+  float a = red[0];
+  for (int i = 1; i < 8; i++) a = fmaxf(a, red[i]);
+  int e = 0;
+  if (!bad_s && a > 0.f) e = min(max(ilogbf(a) - 14, -100), 100);
+  const float mul = ldexpf(1.f, -e);
+  if (threadIdx.x == 0) iw[n] = ldexpf(1.f, e);
+  uint4 *dst = reinterpret_cast<uint4 *>(wh + (size_t)n * K);
+#pragma unroll
+  for (int gi = 0; gi < kWdeqGroups; gi++) {
+    const int g = threadIdx.x + gi * blockDim.x;
+    if (8 * g < K) {
+      float *x = v[gi];
+      uint4 o;
+      o.x = h2_bits(__floats2half2_rn(__fmul_rn(x[0], mul), __fmul_rn(x[1], mul)));
+      o.y = h2_bits(__floats2half2_rn(__fmul_rn(x[2], mul), __fmul_rn(x[3], mul)));
+      o.z = h2_bits(__floats2half2_rn(__fmul_rn(x[4], mul), __fmul_rn(x[5], mul)));
+      o.w = h2_bits(__floats2half2_rn(__fmul_rn(x[6], mul), __fmul_rn(x[7], mul)));
+      dst[g] = o;
+    }
   }
 }
 
@@ -463,6 +559,9 @@ __device__ __forceinline__ void store_part(const TcArgs &a, int split, long m, i
     if (n0 + i < a.N) p[i] = __fmul_rn(__fmul_rn(__uint_as_float(v[i]), sx), a.iw[n0 + i]);
 }
 
+// DQ: Q4_K superblocks dequantised in the kernel; otherwise B is fp16
+// weights (a.tw over them) loaded by TMA like A
+template <bool DQ>
 __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant__ TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -484,7 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
     for (int i = 0; i < kS; i++) {
       // full: the leader's expect_tx arrive (both CTAs' activation bytes) and
       // the arrives of one dequantising group's warps in each CTA
-      mbar_init(F + i, 1 + 2 * (kDqWarps / kGroups));
+      mbar_init(F + i, 1 + (DQ ? 2 * (kDqWarps / kGroups) : 0));
       mbar_init(E + i, 1);
     }
     for (int i = 0; i < kSR; i++) {
@@ -523,7 +622,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
             ok = false;
             break;
           }
-          if (leader) mbar_expect_tx(F + s, 2 * kABytes);
+          if (leader) mbar_expect_tx(F + s, 2 * kABytes + (DQ ? 0 : 2 * kBBytes));
           tma_pair(sA + s * kABytes, &a.ta, ks * kBK, tm * 256 + (int)rank * kRows, lF + 8 * s);
         }
       }
@@ -532,22 +631,42 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
     }
   } else if (warp == kWarpRaw) {
     if (lane == 0) {
-      int gr = 0;
-      bool ok = true;
-      for (int u = pair; u < units && ok; u += npairs) {
-        const int tile = u / a.ksplit, sb0 = (u % a.ksplit) * a.sbper, sb1 = min(a.nsb, sb0 + a.sbper);
-        const int tn = tile % tiles_n;
-        for (int sb = sb0; sb < sb1; sb++, gr++) {
-          const int r = gr % kSR;
-          if (!poll2(rE + r, ((gr / kSR) & 1) ^ 1, ab, a.err, 0)) {
-            ok = false;
-            break;
+      if constexpr (DQ) {
+        int gr = 0;
+        bool ok = true;
+        for (int u = pair; u < units && ok; u += npairs) {
+          const int tile = u / a.ksplit, sb0 = (u % a.ksplit) * a.sbper, sb1 = min(a.nsb, sb0 + a.sbper);
+          const int tn = tile % tiles_n;
+          for (int sb = sb0; sb < sb1; sb++, gr++) {
+            const int r = gr % kSR;
+            if (!poll2(rE + r, ((gr / kSR) & 1) ^ 1, ab, a.err, 0)) {
+              ok = false;
+              break;
+            }
+            mbar_expect_tx(rF + r, kRawBytes);
+            tma_load_2d(sR + r * kRawBytes, &a.tw, sb * kRawPitch, tn * 256 + (int)rank * kRows, rF + r);
           }
-          mbar_expect_tx(rF + r, kRawBytes);
-          tma_load_2d(sR + r * kRawBytes, &a.tw, sb * kRawPitch, tn * 256 + (int)rank * kRows, rF + r);
         }
+        for (int j = gr - kSR > 0 ? gr - kSR : 0; j < gr; j++) drain2(rF + j % kSR, (j / kSR) & 1, a.err);
+      } else {
+        // fp16 weight tiles of this CTA's 128 rows, on the leader's full barrier
+        const uint32_t lF = mapa(sa(F), 0);
+        int g = 0;
+        bool ok = true;
+        for (int u = pair; u < units && ok; u += npairs) {
+          const int tile = u / a.ksplit, sb0 = (u % a.ksplit) * a.sbper, sb1 = min(a.nsb, sb0 + a.sbper);
+          const int tn = tile % tiles_n;
+          for (int ks = 4 * sb0; ks < 4 * sb1; ks++, g++) {
+            const int s = g % kS;
+            if (!poll2(E + s, ((g / kS) & 1) ^ 1, ab, a.err, 0)) {
+              ok = false;
+              break;
+            }
+            tma_pair(sB + s * kBBytes, &a.tw, ks * kBK, tn * 256 + (int)rank * kRows, lF + 8 * s);
+          }
+        }
+        for (int j = g - kS > 0 ? g - kS : 0; j < g; j++) drain2(E + j % kS, (j / kS) & 1, a.err);
       }
-      for (int j = gr - kSR > 0 ? gr - kSR : 0; j < gr; j++) drain2(rF + j % kSR, (j / kSR) & 1, a.err);
     }
   } else if (warp == kWarpMma) {
     if (leader && lane == 0) {
@@ -585,6 +704,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
       }
     }
   } else if (warp < kWarpEp) {
+    if constexpr (!DQ) {
+      // B arrives by TMA: nothing to dequantise
+    } else {
     // ---- dequantise: kGroups groups of warps take interleaved K steps of
     // each superblock (kGroups steps in flight); a thread owns kRPT rows
     const int tid = threadIdx.x - kWarpDq * 32, grp = tid / kGT, t = tid % kGT;
@@ -647,6 +769,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm_tc2(const __grid_constant
         __syncwarp();
         if (lane == 0) mbar_arrive(rE + r);
       }
+    }
     }
   } else {
     // ---- epilogue: TMEM lanes 32q.. are rows 128 rank + 32q.. of the tile
@@ -712,8 +835,10 @@ namespace {
 // kernel cannot be configured)
 int max_pairs() {
   static int n = [] {
-    if (cudaFuncSetAttribute(tc::tc2::k_qgemm_tc2, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::tc2::kSmem) !=
-        cudaSuccess)
+    if (cudaFuncSetAttribute(tc::tc2::k_qgemm_tc2<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             tc::tc2::kSmem) != cudaSuccess ||
+        cudaFuncSetAttribute(tc::tc2::k_qgemm_tc2<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             tc::tc2::kSmem) != cudaSuccess)
       return 0;
     cudaLaunchConfig_t q{};
     cudaLaunchAttribute ca[1];
@@ -727,7 +852,7 @@ int max_pairs() {
     q.attrs = ca;
     q.numAttrs = 1;
     int r = 0;
-    if (cudaOccupancyMaxActiveClusters(&r, tc::tc2::k_qgemm_tc2, &q) != cudaSuccess) r = 0;
+    if (cudaOccupancyMaxActiveClusters(&r, tc::tc2::k_qgemm_tc2<true>, &q) != cudaSuccess) r = 0;
     return r;
   }();
   return n;
@@ -735,14 +860,14 @@ int max_pairs() {
 
 struct TcPlan {
   int tiles, ksplit, sbper, pairs;
-  size_t xh, ix, w, part;  // workspace pieces (bytes, 256-aligned)
+  size_t xh, ix, w, part, wh;  // workspace pieces (bytes, 256-aligned)
 };
 
 size_t up256(size_t b) { return (b + 255) & ~(size_t)255; }
 
 // K splits when the 256 x 256 tiles do not give every pair one: as many
 // splits (whole superblocks each) as keep one round of work units
-TcPlan tc_plan(int M, int N, int K) {
+TcPlan tc_plan(int wtype, int M, int N, int K) {
   TcPlan p{};
   const int nsb = K / 256;
   p.pairs = max_pairs();
@@ -756,26 +881,30 @@ TcPlan tc_plan(int M, int N, int K) {
   p.ix = up256((size_t)M * 4);
   p.w = up256((size_t)N * 4);
   p.part = p.ksplit > 1 ? up256((size_t)p.ksplit * M * N * 4) : 0;
+  p.wh = wtype == TCB_Q4_K ? 0 : up256((size_t)N * K * 2);  // fp16 weights of the other types
   return p;
 }
 
 }  // namespace
 
 bool tc_eligible(int wtype, int M, int N, int K, const void *w) {
-  return wtype == TCB_Q4_K && M >= kTcMinM && N > 0 && K >= 256 && K % 256 == 0 &&
-         (reinterpret_cast<uintptr_t>(w) & 15) == 0 && tensor_map_encoder() != nullptr && max_pairs() > 0;
+  const bool typ = (wtype == TCB_Q4_K && (reinterpret_cast<uintptr_t>(w) & 15) == 0) || wtype == TCB_Q6_K ||
+                   wtype == TCB_Q8_0 || wtype == TCB_Q4_0;
+  return typ && M >= kTcMinM && N > 0 && K >= 256 && K % 256 == 0 &&
+         (wtype == TCB_Q4_K || K <= 8 * tc::kWdeqGroups * 256) && tensor_map_encoder() != nullptr &&
+         max_pairs() > 0;
 }
 
-size_t tc_workspace_bytes(int M, int N, int K) {
-  const TcPlan p = tc_plan(M, N, K);
-  return p.xh + p.ix + 2 * p.w + p.part;
+size_t tc_workspace_bytes(int wtype, int M, int N, int K) {
+  const TcPlan p = tc_plan(wtype, M, N, K);
+  return p.xh + p.ix + 2 * p.w + p.part + p.wh;
 }
 
 cudaError_t launch_qgemm_tc(int wtype, const void *w, int M, int N, int K, const void *x, int xdt, long ldx, void *c,
                             int cdt, long ldc, int accumulate, void *ws, int *err, cudaStream_t s) {
-  (void)wtype;
   using namespace tc;
-  const TcPlan pl = tc_plan(M, N, K);
+  const TcPlan pl = tc_plan(wtype, M, N, K);
+  const bool dq = wtype == TCB_Q4_K;
   if (pl.pairs <= 0) return cudaErrorInvalidConfiguration;
   const int nsb = K / 256;
   uint8_t *p = static_cast<uint8_t *>(ws);
@@ -784,6 +913,7 @@ cudaError_t launch_qgemm_tc(int wtype, const void *w, int M, int N, int K, const
   float *mw = reinterpret_cast<float *>(p + pl.xh + pl.ix);
   float *iw = reinterpret_cast<float *>(p + pl.xh + pl.ix + pl.w);
   float *part = pl.ksplit > 1 ? reinterpret_cast<float *>(p + pl.xh + pl.ix + 2 * pl.w) : nullptr;
+  __half *wh = dq ? nullptr : reinterpret_cast<__half *>(p + pl.xh + pl.ix + 2 * pl.w + pl.part);
 
   TcArgs a{};
   auto enc = tensor_map_encoder();
@@ -797,13 +927,21 @@ cudaError_t launch_qgemm_tc(int wtype, const void *w, int M, int N, int K, const
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
-  {
+  if (dq) {
     const size_t rb = (size_t)nsb * kRawPitch;
     cuuint64_t dims[2] = {(cuuint64_t)rb, (cuuint64_t)N};
     cuuint64_t strides[1] = {(cuuint64_t)rb};
     cuuint32_t box[2] = {kRawPitch, (cuuint32_t)tc2::kRows}, es[2] = {1, 1};
     if (enc(&a.tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(w), dims, strides, box, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  } else {
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)N};
+    cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    cuuint32_t box[2] = {kBK, (cuuint32_t)tc2::kRows}, es[2] = {1, 1};
+    if (enc(&a.tw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, wh, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
@@ -822,8 +960,17 @@ cudaError_t launch_qgemm_tc(int wtype, const void *w, int M, int N, int K, const
   a.part = part;
   a.err = err;
 
-  k_tc_prep<<<M + (N + 7) / 8, 256, 0, s>>>(x, xdt, ldx, M, K, xh, ix, static_cast<const uint8_t *>(w), N, nsb, mw,
-                                             iw);
+  const uint8_t *wb = static_cast<const uint8_t *>(w);
+  if (dq) {
+    k_tc_prep<<<M + (N + 7) / 8, 256, 0, s>>>(x, xdt, ldx, M, K, xh, ix, wb, N, nsb, mw, iw, 1);
+  } else {
+    switch (wtype) {
+    case TCB_Q6_K: k_tc_wdeq<TCB_Q6_K><<<N, 256, 0, s>>>(wb, N, K, wh, iw); break;
+    case TCB_Q8_0: k_tc_wdeq<TCB_Q8_0><<<N, 256, 0, s>>>(wb, N, K, wh, iw); break;
+    default: k_tc_wdeq<TCB_Q4_0><<<N, 256, 0, s>>>(wb, N, K, wh, iw); break;
+    }
+    k_tc_prep<<<M, 256, 0, s>>>(x, xdt, ldx, M, K, xh, ix, nullptr, N, nsb, mw, iw, 0);
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
 
@@ -843,7 +990,8 @@ cudaError_t launch_qgemm_tc(int wtype, const void *w, int M, int N, int K, const
   cfg.gridDim = dim3(2 * (units < pl.pairs ? units : pl.pairs));
   cfg.blockDim = dim3(tc2::kThreads);
   cfg.dynamicSmemBytes = tc2::kSmem;
-  if ((e = cudaLaunchKernelEx(&cfg, tc2::k_qgemm_tc2, a)) != cudaSuccess || pl.ksplit == 1) return e;
+  e = dq ? cudaLaunchKernelEx(&cfg, tc2::k_qgemm_tc2<true>, a) : cudaLaunchKernelEx(&cfg, tc2::k_qgemm_tc2<false>, a);
+  if (e != cudaSuccess || pl.ksplit == 1) return e;
   const size_t total = (size_t)M * N;
   const int blocks = (int)((total + 255) / 256 < 148 * 8 ? (total + 255) / 256 : 148 * 8);
   tc2::k_tc_reduce<<<blocks, 256, 0, s>>>(part, pl.ksplit, M, N, c, cdt, ldc, accumulate);

@@ -179,3 +179,55 @@ def test_tc_prefill_config(ctx, oracle, NK):
     xs = xd[torch.from_numpy(rows).cuda()].float().cpu().numpy()
     got = host(c)[rows]
     check(got, oracle.qgemm_float(T.Q4_K, xs, raw, N))
+
+
+# ---------------------------------------------------------------- other block types
+# Q6_K, Q8_0, Q4_0 at M >= 64: the weights are dequantised exactly (TR's
+# dequant) to row-scaled fp16 in workspace, then the same 2-CTA kernel runs
+# with B loaded by TMA.
+
+OTHER = [T.Q6_K, T.Q8_0, T.Q4_0]
+
+
+@pytest.mark.parametrize("fmt", OTHER)
+@pytest.mark.parametrize("MNK", [(64, 256, 256), (200, 300, 512), (130, 2000, 2304), (256, 1024, 4096)])
+def test_tc_other_types(ctx, oracle, fmt, MNK):
+    M, N, K = MNK
+    raw = synth.weight(fmt, N, K, seed=M + N + fmt)
+    x = synth.activations(M, K, seed=K + 1)
+    c = torch.zeros((M, N), dtype=torch.float32, device="cuda")
+    ctx.qgemm(fmt, dev(raw), dev(x), c)
+    check(host(c), oracle.qgemm_float(fmt, x, raw, N))
+
+
+@pytest.mark.parametrize("fmt", OTHER)
+def test_tc_other_types_lcg_and_16bit(ctx, oracle, fmt):
+    """TR's LCG blocks (small pinned scale exponents), bf16 activations, a
+    bf16 output accumulated onto."""
+    M, N, K = 96, 272, 768
+    e, size = T.BLOCK[fmt]
+    raw = oracle.random_quant(fmt, 55 + fmt, N * K // e).reshape(-1, size)
+    for b in {T.Q8_0: [1], T.Q4_0: [1], T.Q6_K: [209]}[fmt]:
+        raw[:, b] = 0x1C | (raw[:, b] & 0x83)
+    raw = raw.reshape(-1)
+    xd = dev(np.random.default_rng(fmt).standard_normal((M, K), dtype=np.float32)).to(torch.bfloat16)
+    base = np.random.default_rng(2).standard_normal((M, N), dtype=np.float32)
+    cd = dev(base).to(torch.bfloat16)
+    old = host(cd)
+    ctx.qgemm(fmt, dev(raw), xd, cd, accumulate=True)
+    want = oracle.qgemm_float(fmt, xd.float().cpu().numpy(), raw, N, c=old)
+    assert rel_l2(host(cd), want) <= 1e-2
+
+
+def test_tc_q6k_down_projection(ctx, oracle):
+    """The 8B decoder's down projection (Q6_K 4096 x 14336) at M = 2048,
+    24 sampled rows against the oracle."""
+    N, K, M = 4096, 14336, 2048
+    raw = synth.weight(T.Q6_K, N, K, seed=3)
+    xd = dev(synth.activations(M, K, seed=4)).to(torch.bfloat16)
+    c = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    ctx.qgemm(T.Q6_K, dev(raw), xd, c)
+    rows = np.random.default_rng(5).choice(M, 24, replace=False)
+    rows[:2] = [0, M - 1]
+    xs = xd[torch.from_numpy(rows).cuda()].float().cpu().numpy()
+    check(host(c)[rows], oracle.qgemm_float(T.Q6_K, xs, raw, N))
