@@ -51,8 +51,8 @@ def load_peaks() -> dict:
     if os.path.exists(p):
         d = json.load(open(p))
         return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d.get("bf16_tflops", 1590.0)),
-                "source": "measured"}
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", 1400.0)), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
 def load_traffic(name: str):
@@ -140,10 +140,12 @@ def cpu_baseline(seconds: float = 12.0) -> dict:
 
 def decode_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
     """8B-shape Q4_K_M greedy decode at batch 1: a
-    512-token random prompt fed through the decode step, then 256 greedy
-    tokens, every step one replay of the captured CUDA graph (token, position
-    and prompt stay on the device).  Random-init synthetic weights (fp16 block
-    scales sized for order-one activations, tcb_b200/llama.py)."""
+    512-token random prompt fed by the prompt pass (tcb_llama_prefill: 511
+    rows through the tensor-core products, the last token by the first step),
+    then 256 greedy tokens, every step one replay of the captured CUDA graph
+    (token, position and prompt stay on the device).  Random-init synthetic
+    weights (fp16 block scales sized for order-one activations,
+    tcb_b200/llama.py)."""
     import torch
 
     from tcb_b200 import llama
@@ -156,10 +158,12 @@ def decode_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
     eng.start(prompt, stream)
     eng.capture(stream)
     eng.start(prompt, stream)
+    eng.prefill(stream)  # warm-up of the prompt pass (workspace, kernel attributes)
+    eng.start(prompt, stream)
     e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
     with torch.cuda.stream(stream):
         e0.record(stream)
-        eng.step(511, stream)
+        eng.prefill(stream)
         e1.record(stream)
         eng.step(256, stream)
         e2.record(stream)
@@ -179,7 +183,7 @@ def decode_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
     return {
         "model": "llama3-8b-shape q4_k_m (random init, synthetic)", "prompt_tokens": 512, "generated_tokens": 256,
         "tokens_per_s": round(256 * world / (ms / 1e3), 2), "ms_per_token": round(ms / 256, 4),
-        "prefill_token_by_token_ms": round(e0.elapsed_time(e1), 2),
+        "prompt_pass_ms": round(e0.elapsed_time(e1), 2),
         "bytes_per_token": bpt + kv, "weight_bytes_per_token": bpt,
         "roofline": {"bound": "hbm", "achieved": round((bpt + kv) / per_tok_s / 1e9, 2), "peak": peak_gbs,
                      "unit": "GB/s", "frac": round((bpt + kv) / per_tok_s / 1e9 / peak_gbs, 4),
@@ -187,6 +191,64 @@ def decode_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
         "gpu_launches_per_token": 1 + 6 * cfg.n_layers + 4, "last_tokens": [int(v) for v in toks[-4:]],
         "timing": "CUDA events around 256 graph replays on the engine's stream",
     }
+
+
+def model_prefill_bench(ctx, peaks: dict) -> dict:
+    """8B-shape model prefill (second part): 2048-token
+    random prompts at batch 4, each fed by the prompt pass (2047 rows through
+    the tensor-core products and the causal flash-attention kernel) plus the
+    first decode step (the last prompt token and the first greedy token), so
+    the time is the time to first token.  The engine holds one sequence, so
+    the batch of 4 runs as 4 sequences back to back; CUDA events around each
+    after one warm-up sequence.  Tensor roofline: the products' 2*rows*N*K
+    flops plus the causal attention's 4*hd per (query head, query, key)
+    pair, against the measured sustained dense bf16 peak (a pass of about a
+    hundred milliseconds)."""
+    import dataclasses
+
+    import torch
+
+    from tcb_b200 import llama
+
+    T_, B = 2048, 4
+    cfg = dataclasses.replace(llama.LLAMA3_8B, max_ctx=T_ + 1)
+    model = llama.device_model(cfg, seed=7)
+    eng = llama.Llama(ctx, model)
+    stream = torch.cuda.Stream()
+    rng = np.random.default_rng(17)
+    prompts = [rng.integers(0, cfg.vocab, T_) for _ in range(B + 1)]
+    ms = []
+    for i, p in enumerate(prompts):
+        eng.start(p, stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            eng.prefill(stream)
+            eng.step(1, stream)
+            e1.record(stream)
+        e1.synchronize()
+        if i:
+            ms.append(e0.elapsed_time(e1))
+    toks = eng.tokens(T_ + 1, stream)
+    eng.close()
+    del model
+    D, H, KVH, hd, F, L = cfg.d_model, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn_dim, cfg.n_layers
+    rows = T_ - 1
+    per_row = 2 * ((H + 2 * KVH) * hd * D + D * H * hd + 2 * F * D + D * F)
+    attn = 4 * hd * H * (rows * (rows + 1) // 2)
+    flops = L * (rows * per_row + attn)
+    total = sum(ms)
+    peak = peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops")
+    tf = flops * B / (total / 1e3) / 1e12
+    return {"model": "llama3-8b-shape q4_k_m (random init, synthetic)", "prompt_tokens": T_, "batch": B,
+            "batch_mode": "sequences back to back (one KV cache per engine)",
+            "tokens_per_s": round(T_ * B / (total / 1e3), 1), "ms_per_sequence": [round(v, 2) for v in ms],
+            "time_to_first_token_ms": round(total / B, 2),
+            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(tf / peak, 4) if peak else None,
+                         "flops_per_sequence": flops,
+                         "peak_source": ("measured (sustained)" if peaks.get("source") == "measured" else "fallback")},
+            "first_token": int(toks[-1])}
 
 
 def prefill_bench(ctx, rank: int, peaks: dict, cpu: bool) -> dict:
@@ -432,9 +494,10 @@ def main():
         decode = (decode_bench(ctx, rank, world, peaks["hbm_gbs"]) if world == 1
                   else decode_tp_bench(ctx, rank, world, peaks["hbm_gbs"]))
 
-    prefill = None
+    prefill = model_prefill = None
     if world == 1 and not args.no_prefill:
         prefill = prefill_bench(ctx, rank, peaks, not args.no_cpu_baseline)
+        model_prefill = model_prefill_bench(ctx, peaks)
 
     if rank == 0:
         line = {
@@ -457,6 +520,8 @@ def main():
             line["decode"] = decode
         if prefill is not None:
             line["prefill"] = prefill
+        if model_prefill is not None:
+            line["model_prefill"] = model_prefill
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)

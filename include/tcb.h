@@ -173,6 +173,17 @@ int tcb_llama_destroy(tcb_llama *m);
  * device and sets position 0 with prompt[0] as the current token.  Steps
  * 0..n-2 then feed the prompt; later steps feed their own greedy token. */
 int tcb_llama_start(tcb_llama *m, const int64_t *prompt, int n, void *stream);
+/* Feed prompt[0..n-2] (n given to tcb_llama_start, which must come directly
+ * before) through the model as row batches of up to 2048 positions: the
+ * quantized products on the tensor cores (tcb_qgemm), causal attention over
+ * the cache, the K/V of every position appended.  Leaves the engine where
+ * n-1 prompt steps would have left it (position n-1, current token
+ * prompt[n-1]); the next tcb_llama_step feeds the last prompt token and
+ * takes the first greedy token.  TR's generate runs the whole prompt
+ * through the model in one call the same way (lib/layers.tr 735-740).
+ * Tensor parallelism sums the residual rows with NCCL.  Returns
+ * TCB_ERR_UNSUPPORTED when a step has already run since the start. */
+int tcb_llama_prefill(tcb_llama *m, void *stream);
 /* One step: embed the current token, run every layer at the current
  * position (appending its K/V), score the vocabulary, take the greedy
  * token (first maximum), store it at tokens[pos + 1], advance.  Replays the

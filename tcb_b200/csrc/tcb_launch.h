@@ -2,6 +2,7 @@
 // (internal to libtcb; the public boundary is include/tcb.h).
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -36,5 +37,10 @@ cudaError_t launch_act8_quantize(int blk, int M, int K, const void *x, int xdt, 
 cudaError_t launch_act8_dot(int wtype, const void *w, int M, int N, int K, const Act8Scratch &sc, const void *x,
                             int xdt, long ldx, void *c, int cdt, long ldc, int accumulate, int sms,
                             cudaStream_t s);
+
+// causal grouped-query attention of M prompt rows (positions p0 ..) over one
+// layer's fp16 cache [KVH][max_ctx][128] (tcb_attn_prefill.cu)
+cudaError_t launch_attn_prefill(const float *q, long ldq, const __half *kc, const __half *vc, float *out, long ldo,
+                                int p0, int M, int H, int KVH, int max_ctx, cudaStream_t s);
 
 }  // namespace tcb

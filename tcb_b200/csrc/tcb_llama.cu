@@ -23,6 +23,7 @@
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <dlfcn.h>
@@ -45,6 +46,7 @@ constexpr int kHd = 128;        // head dimension supported by the attention ker
 constexpr int kChunk = 64;      // positions per attention CTA
 constexpr int kMaxChunks = 256; // chunks a merge holds in shared memory (max_ctx <= 16384)
 constexpr int kArgBlocks = 148;
+constexpr int kPrefillRows = 2048;  // prompt rows per pass of tcb_llama_prefill
 
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
@@ -57,9 +59,11 @@ __device__ __forceinline__ float warp_add(float v) {
   return v;
 }
 
-// out = x / sqrt(mean(x^2) + eps) * w   (one CTA)
+// out = x / sqrt(mean(x^2) + eps) * w   (one CTA per row)
 __global__ void k_rmsnorm(const float *x, const float *w, float *out, int D, float eps) {
   __shared__ float red[32];
+  x += (size_t)blockIdx.x * D;
+  out += (size_t)blockIdx.x * D;
   mv::pdl_wait();
   float ss = 0.f;
   for (int i = threadIdx.x; i < D; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
@@ -404,6 +408,58 @@ __global__ void k_swiglu(const float *gu, float *a, int F) {
   }
 }
 
+// ---- prompt rows (tcb_llama_prefill)
+
+// Row r of the chunk (position p0 + r): rotate its query and key heads with
+// the decode step's arithmetic, query heads in place, and store the rotated
+// key and the value heads into the fp16 cache.  One CTA per row.
+__global__ void k_rope_rows(float *qkv, const float *cosT, const float *sinT, int p0, __half *kc, __half *vc, int H,
+                            int KVH, int max_ctx) {
+  constexpr int half = kHd / 2;
+  const int r = blockIdx.x, p = p0 + r;
+  float *row = qkv + (size_t)r * (H + 2 * KVH) * kHd;
+  const float *cs = cosT + (size_t)p * half, *sn = sinT + (size_t)p * half;
+  for (int i = threadIdx.x; i < (H + KVH) * half; i += blockDim.x) {
+    const int hh = i / half, j = i % half;
+    float *v = row + (size_t)hh * kHd;
+    const float a = v[j], b = v[j + half];
+    const float ra = __fsub_rn(__fmul_rn(a, cs[j]), __fmul_rn(b, sn[j]));
+    const float rb = __fadd_rn(__fmul_rn(a, sn[j]), __fmul_rn(b, cs[j]));
+    if (hh < H) {
+      v[j] = ra;
+      v[j + half] = rb;
+    } else {
+      __half *kd = kc + ((size_t)(hh - H) * max_ctx + p) * kHd;
+      kd[j] = __float2half_rn(ra);
+      kd[j + half] = __float2half_rn(rb);
+    }
+  }
+  for (int i = threadIdx.x; i < KVH * kHd; i += blockDim.x) {
+    const int kh = i / kHd, d = i % kHd;
+    vc[((size_t)kh * max_ctx + p) * kHd + d] = __float2half_rn(row[(size_t)(H + KVH + kh) * kHd + d]);
+  }
+}
+
+// a[r][i] = silu(g) * u over rows of merged [G | U] (k_swiglu per row)
+__global__ void k_swiglu_rows(const float *gu, float *a, int F, long n) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const long r = i / F;
+    const int c = (int)(i - r * F);
+    const float g = gu[r * 2 * F + c], u = gu[r * 2 * F + F + c];
+    a[i] = __fmul_rn(__fmul_rn(g, __frcp_rn(__fadd_rn(1.0f, expf(-g)))), u);
+  }
+}
+
+// the state n-1 prompt steps leave: history = prompt[0..n-1], position n-1,
+// current token prompt[n-1]
+__global__ void k_prefill_done(const int64_t *prompt, int n, int *pos, int64_t *tok, int64_t *hist) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) hist[i] = prompt[i];
+  if (threadIdx.x == 0) {
+    *pos = n - 1;
+    *tok = prompt[n - 1];
+  }
+}
+
 // (max, first index) per CTA
 __global__ void k_argmax_part(const float *v, int n, float *pm, int *pi) {
   __shared__ float sm_v[32];
@@ -644,6 +700,10 @@ struct tcb_llama {
   bool peer = false;
   float *yp = nullptr;               // this rank's partial of o / down
   unsigned *ar_epoch = nullptr, *ar_done = nullptr;
+  // prompt pass (tcb_llama_prefill): row buffers of pf_rows rows, made on first use
+  int host_n = 0;                    // prompt length given to tcb_llama_start
+  int pf_rows = 0;
+  float *px = nullptr, *ph = nullptr, *pqkv = nullptr, *patt = nullptr, *pgu = nullptr, *pa = nullptr;
 };
 
 namespace {
@@ -941,6 +1001,84 @@ int tcb_llama_start(tcb_llama *m, const int64_t *prompt, int n, void *stream) {
       (e = cudaMemcpy(m->pos, &zero, 4, cudaMemcpyHostToDevice)) != cudaSuccess)
     return fail(m, e);
   m->host_pos = 0;
+  m->host_n = n;
+  return TCB_OK;
+}
+
+int tcb_llama_prefill(tcb_llama *m, void *stream) {
+  using namespace tcb::ll;
+  if (!m) return TCB_ERR_NULL;
+  const int n = m->host_n;
+  if (n < 1 || m->host_pos != 0) return TCB_ERR_UNSUPPORTED;
+  if (n == 1) return TCB_OK;
+  const tcb_llama_config &c = m->cfg;
+  const int H = c.n_heads, KVH = c.n_kv_heads, hd = c.head_dim, D = c.d_model, F = c.ffn_dim;
+  const int qkvn = (H + 2 * KVH) * hd;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaSetDevice(m->ctx->dev);
+  if (e != cudaSuccess) return fail(m, e);
+  if (m->tp > 1 && (!nccl() || !m->comm)) return fail(m, cudaErrorNotReady);
+  if (!m->pf_rows) {
+    // TCB_PREFILL_ROWS overrides the rows per pass (tests use it to cover
+    // prompts that take several passes)
+    const char *ev = getenv("TCB_PREFILL_ROWS");
+    int rows = ev && atoi(ev) > 0 ? atoi(ev) : kPrefillRows;
+    if (rows > c.max_ctx - 1) rows = c.max_ctx - 1;
+    if ((e = alloc(m, &m->px, (size_t)rows * D)) != cudaSuccess || (e = alloc(m, &m->ph, (size_t)rows * D)) != cudaSuccess ||
+        (e = alloc(m, &m->pqkv, (size_t)rows * qkvn)) != cudaSuccess ||
+        (e = alloc(m, &m->patt, (size_t)rows * H * hd)) != cudaSuccess ||
+        (e = alloc(m, &m->pgu, (size_t)rows * 2 * F)) != cudaSuccess || (e = alloc(m, &m->pa, (size_t)rows * F)) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return e == cudaErrorMemoryAllocation ? TCB_ERR_NOMEM : fail(m, e);
+    }
+    m->pf_rows = rows;
+  }
+  const size_t cache_layer = (size_t)KVH * c.max_ctx * hd;
+  // NCCL: rank 0 adds its partial to the residual rows, the others write
+  // theirs, and the in-place all-reduce sums them (as in the decode step)
+  const int acc = m->tr == 0;
+  auto reduce = [&](int M) -> int {
+    if (m->tp == 1) return TCB_OK;
+    m->nccl_rc = nccl()->all_reduce(m->px, m->px, (size_t)M * D, kNcclFloat32, kNcclSum, m->comm, s);
+    return m->nccl_rc ? fail(m, cudaErrorUnknown) : TCB_OK;
+  };
+  int rc = TCB_OK;
+  for (int p0 = 0; p0 < n - 1 && rc == TCB_OK; p0 += m->pf_rows) {
+    const int M = n - 1 - p0 < m->pf_rows ? n - 1 - p0 : m->pf_rows;
+    if ((e = tcb::launch_dequant_rows(m->tok_emb_type, m->tok_emb, M, D, m->prompt + p0, m->px, TCB_F32, m->ctx->sms,
+                                      s)) != cudaSuccess)
+      return fail(m, e);
+    for (int l = 0; l < c.n_layers; l++) {
+      __half *kc = m->kc + l * cache_layer, *vc = m->vc + l * cache_layer;
+      k_rmsnorm<<<M, 1024, 0, s>>>(m->px, m->attn_norm[l], m->ph, D, c.eps);
+      const Mat &q = m->qkv[l], &o = m->o[l], &gu = m->gu[l], &dn = m->down[l];
+      if ((rc = tcb_qgemm(m->ctx, q.type, M, q.N, q.K, q.w, m->ph, TCB_F32, q.K, m->pqkv, TCB_F32, q.N, 0, s)) != TCB_OK)
+        break;
+      k_rope_rows<<<M, 256, 0, s>>>(m->pqkv, m->cosT, m->sinT, p0, kc, vc, H, KVH, c.max_ctx);
+      if ((e = tcb::launch_attn_prefill(m->pqkv, qkvn, kc, vc, m->patt, (long)H * hd, p0, M, H, KVH, c.max_ctx, s)) !=
+          cudaSuccess)
+        return fail(m, e);
+      if ((rc = tcb_qgemm(m->ctx, o.type, M, o.N, o.K, o.w, m->patt, TCB_F32, o.K, m->px, TCB_F32, o.N, acc, s)) !=
+              TCB_OK ||
+          (rc = reduce(M)) != TCB_OK)
+        break;
+      k_rmsnorm<<<M, 1024, 0, s>>>(m->px, m->ffn_norm[l], m->ph, D, c.eps);
+      if ((rc = tcb_qgemm(m->ctx, gu.type, M, gu.N, gu.K, gu.w, m->ph, TCB_F32, gu.K, m->pgu, TCB_F32, gu.N, 0, s)) !=
+          TCB_OK)
+        break;
+      const long na = (long)M * F;
+      k_swiglu_rows<<<(int)((na + 255) / 256 < 4096 ? (na + 255) / 256 : 4096), 256, 0, s>>>(m->pgu, m->pa, F, na);
+      if ((rc = tcb_qgemm(m->ctx, dn.type, M, dn.N, dn.K, dn.w, m->pa, TCB_F32, dn.K, m->px, TCB_F32, dn.N, acc, s)) !=
+              TCB_OK ||
+          (rc = reduce(M)) != TCB_OK)
+        break;
+    }
+    if (rc == TCB_OK && (e = cudaGetLastError()) != cudaSuccess) return fail(m, e);
+  }
+  if (rc != TCB_OK) return rc;
+  k_prefill_done<<<1, 256, 0, s>>>(m->prompt, n, m->pos, m->tok, m->hist);
+  if ((e = cudaGetLastError()) != cudaSuccess) return fail(m, e);
+  m->host_pos = n - 1;
   return TCB_OK;
 }
 

@@ -198,6 +198,7 @@ def _bind():
     L.tcb_llama_destroy.argtypes = [P]
     L.tcb_llama_start.argtypes = [P, P, ctypes.c_int, P]
     L.tcb_llama_step.argtypes = [P, P]
+    L.tcb_llama_prefill.argtypes = [P, P]
     L.tcb_llama_capture.argtypes = [P, P]
     L.tcb_llama_buffers.argtypes = [P, ctypes.POINTER(P), ctypes.POINTER(P)]
     L.tcb_nccl_unique_id.argtypes = [P]
@@ -244,6 +245,12 @@ class Llama:
     def start(self, prompt, stream=None):
         p = np.ascontiguousarray(prompt, dtype=np.int64)
         self._check(self._L.tcb_llama_start(self._h, p.ctypes.data, p.size, _stream(stream)), "start")
+
+    def prefill(self, stream=None):
+        """Feed all but the last prompt token in row batches (directly after
+        start); the next step feeds the last one and takes the first greedy
+        token."""
+        self._check(self._L.tcb_llama_prefill(self._h, _stream(stream)), "prefill")
 
     def step(self, n: int = 1, stream=None):
         s = _stream(stream)

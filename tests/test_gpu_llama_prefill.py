@@ -1,0 +1,115 @@
+"""The prompt pass of the decoder engine (tcb_llama_prefill): all but the last
+prompt token fed as row batches through the tensor-core products and the
+causal flash-attention kernel, then greedy steps.  Checked against the CPU
+reference (oracle/llama_ref.py, TR's GPT step fed one token at a time): the
+logits of the first generated step within the float tolerance, greedy tokens
+equal (a mismatch only where the reference's top-2 margin is a tie at float
+precision), in one pass and in several (row batches that start off the
+64-position tile grid, a last batch small enough for the non-tensor-core
+product), for 2 and 4 query heads per KV head; the captured graph continues
+from a prefilled cache exactly as the eager steps do."""
+import numpy as np
+import pytest
+
+import tcb_b200 as T
+from tcb_b200 import llama
+
+pytestmark = pytest.mark.gpu
+
+CFGS = {
+    "gqa2": llama.LlamaConfig(n_layers=2, d_model=512, n_heads=4, n_kv_heads=2, head_dim=128, ffn_dim=1024,
+                              vocab=2048, max_ctx=512, eps=1e-5, rope_theta=500000.0),
+    "gqa4": llama.LlamaConfig(n_layers=2, d_model=1024, n_heads=8, n_kv_heads=2, head_dim=128, ffn_dim=2048,
+                              vocab=2048, max_ctx=512, eps=1e-5, rope_theta=500000.0),
+}
+NPROMPT = 300
+GEN = 32
+
+
+def rel_l2(a, b):
+    return float(np.linalg.norm(a.astype(np.float64) - b) / np.linalg.norm(b.astype(np.float64)))
+
+
+def check_tokens(got, ref, ref_logits, margins, start):
+    for i in range(start, len(ref)):
+        if got[i] != ref[i]:
+            tol = 1e-3 * float(np.abs(ref_logits[i - 1]).max())
+            assert margins[i - 1] < tol, (i, got[i], ref[i], margins[i - 1], tol)
+            return i
+    return len(ref)
+
+
+@pytest.fixture(scope="module", params=sorted(CFGS))
+def setup(request, oracle):
+    from oracle.llama_ref import Reference
+
+    cfg = CFGS[request.param]
+    host = llama.host_model(cfg, seed=7)
+    prompt = np.random.default_rng(21).integers(0, cfg.vocab, NPROMPT).astype(np.int64)
+    ref_toks, ref_logits, margins = Reference(host).generate(prompt, NPROMPT + GEN - 1)
+    ctx = T.Context(0)
+    dev = llama.device_model(cfg, 7, host)
+    return cfg, ctx, dev, prompt, ref_toks, ref_logits, margins
+
+
+def run_prefill(ctx, dev, prompt, gen):
+    m = llama.Llama(ctx, dev)
+    m.start(prompt)
+    m.prefill()
+    m.step(1)
+    first = m.logits()
+    m.step(gen - 1)
+    toks = m.tokens(len(prompt) + gen)
+    m.close()
+    return first, toks
+
+
+def test_prefill_against_reference(setup):
+    cfg, ctx, dev, prompt, ref_toks, ref_logits, margins = setup
+    first, toks = run_prefill(ctx, dev, prompt, GEN)
+    assert list(toks[:NPROMPT]) == list(prompt)
+    assert rel_l2(first, ref_logits[NPROMPT - 1]) <= 1e-3
+    assert check_tokens(toks, ref_toks, ref_logits, margins, NPROMPT) >= NPROMPT + 8
+
+
+def test_prefill_in_several_passes(setup, monkeypatch):
+    cfg, ctx, dev, prompt, ref_toks, ref_logits, margins = setup
+    # 80-row passes: batches start at positions 80, 160, 240 (off the 64-row
+    # tile grid); the last has 59 rows (below the tensor-core path's minimum)
+    monkeypatch.setenv("TCB_PREFILL_ROWS", "80")
+    first, toks = run_prefill(ctx, dev, prompt, GEN)
+    assert rel_l2(first, ref_logits[NPROMPT - 1]) <= 1e-3
+    assert check_tokens(toks, ref_toks, ref_logits, margins, NPROMPT) >= NPROMPT + 8
+
+
+def test_prefill_then_graph(setup):
+    cfg, ctx, dev, prompt, *_ = setup
+    m = llama.Llama(ctx, dev)
+    m.start(prompt)
+    m.prefill()
+    m.step(GEN)
+    eager = m.tokens(NPROMPT + GEN)
+    m.start(prompt)
+    m.capture()
+    m.start(prompt)
+    m.prefill()
+    m.step(GEN)
+    assert list(m.tokens(NPROMPT + GEN)) == list(eager)
+    m.close()
+
+
+def test_prefill_state(setup):
+    cfg, ctx, dev, prompt, ref_toks, *_ = setup
+    m = llama.Llama(ctx, dev)
+    # a one-token prompt has nothing to prefill
+    m.start(prompt[:1])
+    m.prefill()
+    m.step(1)
+    # after a step the cache already holds this sequence's positions
+    with pytest.raises(T.TcbError):
+        m.prefill()
+    # a new start may prefill again; a short prompt takes the matvec path
+    m.start(prompt[:5])
+    m.prefill()
+    m.step(1)
+    m.close()
