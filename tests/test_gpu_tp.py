@@ -24,26 +24,30 @@ def _port():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp2_matches_reference(oracle):
+@pytest.mark.parametrize("mode", ["steps", "prefill"])
+def test_tp2_matches_reference(oracle, mode):
     from oracle.llama_ref import Reference
     from tcb_b200 import llama
 
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     import tp_worker
 
-    gen = 64
+    gen = 64 if mode == "steps" else 40
+    prompt = tp_worker.PROMPT if mode == "steps" else tp_worker.LONG_PROMPT
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-           "--master-addr=127.0.0.1", f"--master-port={_port()}", os.path.join(ROOT, "tests", "tp_worker.py"), str(gen)]
+           "--master-addr=127.0.0.1", f"--master-port={_port()}", os.path.join(ROOT, "tests", "tp_worker.py"), str(gen),
+           mode]
     out = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env, cwd=ROOT)
     assert out.returncode == 0, out.stderr[-3000:]
     res = json.loads([l for l in out.stdout.splitlines() if l.startswith("{")][-1])
     assert res["same_on_ranks"] and res["eager"] == res["graph"]
     host = llama.host_model(tp_worker.CFG, seed=5)
-    ref, logits, margins = Reference(host).generate(tp_worker.PROMPT, len(tp_worker.PROMPT) + gen - 1)
+    ref, logits, margins = Reference(host).generate(prompt, len(prompt) + gen - 1)
     got = np.array(res["eager"])
-    for i in range(1, len(ref)):
+    assert list(got[:len(prompt)]) == list(prompt)
+    for i in range(len(prompt), len(ref)):
         if got[i] != ref[i]:
             assert margins[i - 1] < 1e-3 * float(np.abs(logits[i - 1]).max()), i
-            assert i >= len(tp_worker.PROMPT) + 16
+            assert i >= len(prompt) + 16
             break

@@ -1,6 +1,8 @@
 """One rank of the tensor-parallel decoder check (run with torchrun by
 tests/test_gpu_tp.py): the small decoder sharded over the ranks, greedy
-tokens eager and from the captured graph; rank 0 prints them as JSON."""
+tokens eager and from the captured graph; with "prefill" a longer prompt fed
+by the prompt pass (residual rows summed over the ranks).  Rank 0 prints the
+tokens as JSON."""
 import json
 import os
 import sys
@@ -16,6 +18,7 @@ from tcb_b200 import llama  # noqa: E402
 CFG = llama.LlamaConfig(n_layers=2, d_model=512, n_heads=4, n_kv_heads=2, head_dim=128, ffn_dim=1024,
                         vocab=2048, max_ctx=160, eps=1e-5, rope_theta=500000.0)
 PROMPT = np.array([17, 901, 5, 1333, 42, 2047, 0, 777], np.int64)
+LONG_PROMPT = np.random.default_rng(23).integers(0, CFG.vocab, 100).astype(np.int64)
 
 
 def main():
@@ -28,14 +31,24 @@ def main():
     dev = llama.device_model(CFG, 5, host, tp=(world, rank))
     m = llama.Llama(ctx, dev, tp=(world, rank))
     m.tp_init(llama.share_id(llama.nccl_unique_id, rank))
-    n = len(PROMPT) + int(sys.argv[1] if len(sys.argv) > 1 else 64)
-    m.start(PROMPT)
-    m.step(n - 1)
+    gen = int(sys.argv[1] if len(sys.argv) > 1 else 64)
+    pre = len(sys.argv) > 2 and sys.argv[2] == "prefill"
+    prompt = LONG_PROMPT if pre else PROMPT
+    n = len(prompt) + gen
+
+    def feed():
+        m.start(prompt)
+        if pre:
+            m.prefill()
+            m.step(gen)
+        else:
+            m.step(n - 1)
+
+    feed()
     eager = m.tokens(n)
-    m.start(PROMPT)
+    m.start(prompt)
     m.capture()
-    m.start(PROMPT)
-    m.step(n - 1)
+    feed()
     graph = m.tokens(n)
     all_tok = [None] * world
     dist.all_gather_object(all_tok, eager.tolist())
