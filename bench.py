@@ -390,6 +390,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the 8B-shape decode measurement")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill-product measurement")
+    ap.add_argument("--only-model-prefill", action="store_true",
+                    help="run only the 8B model prefill and print its object (for profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -409,6 +411,9 @@ def main():
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if args.only_model_prefill:
+        print(json.dumps({"model_prefill": model_prefill_bench(T.Context(local), load_peaks())}), flush=True)
+        return
     N, K = WORKLOAD["N"], WORKLOAD["K"]
     wbytes = N * K // 256 * 144
     ring = max(4, -(-512 * 2 ** 20 // wbytes))  # >= 512 MiB of distinct weights

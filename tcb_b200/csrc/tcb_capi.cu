@@ -108,6 +108,18 @@ int check_gemm_args(int wtype, int M, int N, int K, const void *w, const void *x
     return TCB_ERR_ALIGN;
   return TCB_OK;
 }
+
+int qgemm_tc_prologue(tcb_ctx *ctx, int wtype, int M, int N, int K, const void *w, const float *x, long ldx, float *c,
+                      long ldc, int accumulate, const TcPrologue &pro, cudaStream_t s) {
+  if (!ctx) return TCB_ERR_NULL;
+  if (M <= 0 || N <= 0 || !tc_eligible(wtype, M, N, K, w) || !tc_prologue_ok(pro, K, x, ldx) || ldc < N)
+    return TCB_ERR_UNSUPPORTED;
+  int rc = bind(ctx);
+  if (rc != TCB_OK || (rc = ensure_ws(ctx, tc_workspace_bytes(wtype, M, N, K))) != TCB_OK) return rc;
+  cudaError_t e = launch_qgemm_tc(wtype, w, M, N, K, x, TCB_F32, ldx, c, TCB_F32, ldc, accumulate, ctx->ws, ctx->derr,
+                                  s, &pro);
+  return e == cudaSuccess ? TCB_OK : cuda_fail(ctx, e);
+}
 }  // namespace tcb
 
 namespace {

@@ -269,57 +269,179 @@ __device__ __forceinline__ void dequant8(const uint8_t *b, int j, float (&v)[8])
 
 // k_tc_wdeq: the weights of the other block types for the tensor-core
 // kernel: row n dequantised exactly (TR's dequant), scaled by a power of two
-// that brings the row's largest magnitude into [2^14, 2^15) and rounded once
-// to fp16 (natural K order); iw[n] holds the inverse factor.  One pass: a
-// thread keeps its 8-element groups (at most kWdeqGroups) in registers.
-constexpr int kWdeqGroups = 8;  // K <= 8 * 8 * 256 = 16384
+// and rounded once to fp16 (natural K order); iw[n] holds the inverse
+// factor.  The factor brings the row's bound -- the largest magnitude its
+// blocks' scales allow: 32|d|max|sc| (Q6_K), 128|d| (Q8_0), 8|d| (Q4_0) --
+// into [2^14, 2^15), so no value overflows and the normal fp16 values keep
+// their full precision; a non-finite scale leaves the row unscaled.  The
+// row's blocks are first copied into shared memory with 16-byte loads (the
+// whole row in flight at once) and dequantised from there in one pass; little
+// register and shared-memory use per CTA keeps many rows in flight per SM.
+constexpr int kWdeqMaxK = 16384;  // rows of at most this many elements
+template <int W>
+__device__ __forceinline__ float block_bound(const uint8_t *b) {
+  if constexpr (W == TCB_Q6_K) {
+    int sm = 0;
+#pragma unroll
+    for (int i = 0; i < 16; i++) sm = max(sm, abs((int)(int8_t)b[192 + i]));
+    return fabsf(half_exact(ld_u16(b + 208))) * (float)(32 * sm);
+  } else if constexpr (W == TCB_Q8_0) {
+    return fabsf(half_exact(ld_u16(b))) * 128.f;
+  } else {
+    return fabsf(half_exact(ld_u16(b))) * 8.f;
+  }
+}
+
 template <int W>
 __global__ void __launch_bounds__(256) k_tc_wdeq(const uint8_t *w, int N, int K, __half *wh, float *iw) {
+  extern __shared__ __align__(16) uint8_t raw[];
   __shared__ float red[8];
-  __shared__ int bad_s;
   constexpr int E = Fmt<W>::E, B = Fmt<W>::B;
-  const int n = blockIdx.x;
-  const uint8_t *row = w + (size_t)n * (K / E) * B;
-  float v[kWdeqGroups][8];
-  float amax = 0.f;
+  const int n = blockIdx.x, tid = threadIdx.x;
+  const int nb = K / E;
+  const size_t rb = (size_t)nb * B;
+  const uint8_t *row = w + (size_t)n * rb;
+  if (((reinterpret_cast<uintptr_t>(row) | rb) & 15) == 0) {
+    for (int i = tid; i < (int)(rb / 16); i += blockDim.x)
+      reinterpret_cast<uint4 *>(raw)[i] = __ldcs(reinterpret_cast<const uint4 *>(row) + i);
+  } else if (((reinterpret_cast<uintptr_t>(row) | rb) & 1) == 0) {
+    for (int i = tid; i < (int)(rb / 2); i += blockDim.x)
+      reinterpret_cast<uint16_t *>(raw)[i] = __ldcs(reinterpret_cast<const unsigned short *>(row) + i);
+  } else {
+    for (int i = tid; i < (int)rb; i += blockDim.x) raw[i] = row[i];
+  }
+  __syncthreads();
+  float bound = 0.f;
   int bad = 0;
-  if (threadIdx.x == 0) bad_s = 0;
-#pragma unroll
-  for (int gi = 0; gi < kWdeqGroups; gi++) {
-    const int k = 8 * (threadIdx.x + gi * blockDim.x);
-    if (k < K) {
-      dequant8<W>(row + (size_t)(k / E) * B, k % E, v[gi]);
-#pragma unroll
-      for (int i = 0; i < 8; i++) {
-        const float a = fabsf(v[gi][i]);
-        bad |= !(a <= 3.402823466e38f);
-        amax = fmaxf(amax, a);
-      }
-    }
+  for (int b = tid; b < nb; b += blockDim.x) {
+    const float v = block_bound<W>(raw + (size_t)b * B);
+    bad |= !(v <= 3.402823466e38f);
+    bound = fmaxf(bound, v);
   }
 #pragma unroll
-  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
-  __syncthreads();
-  if (bad) bad_s = 1;
-  __syncthreads();
+  for (int o = 16; o; o >>= 1) bound = fmaxf(bound, __shfl_xor_sync(0xFFFFFFFFu, bound, o));
+  if ((tid & 31) == 0) red[tid >> 5] = bound;
+  const int any_bad = __syncthreads_or(bad);
   float a = red[0];
   for (int i = 1; i < 8; i++) a = fmaxf(a, red[i]);
   int e = 0;
-  if (!bad_s && a > 0.f) e = min(max(ilogbf(a) - 14, -100), 100);
+  if (!any_bad && a > 0.f) e = min(max(ilogbf(a) - 14, -100), 100);
   const float mul = ldexpf(1.f, -e);
-  if (threadIdx.x == 0) iw[n] = ldexpf(1.f, e);
+  if (tid == 0) iw[n] = ldexpf(1.f, e);
   uint4 *dst = reinterpret_cast<uint4 *>(wh + (size_t)n * K);
+  for (int g = tid; 8 * g < K; g += blockDim.x) {
+    float x[8];
+    dequant8<W>(raw + (size_t)(8 * g / E) * B, (8 * g) % E, x);
+    uint4 o;
+    o.x = h2_bits(__floats2half2_rn(__fmul_rn(x[0], mul), __fmul_rn(x[1], mul)));
+    o.y = h2_bits(__floats2half2_rn(__fmul_rn(x[2], mul), __fmul_rn(x[3], mul)));
+    o.z = h2_bits(__floats2half2_rn(__fmul_rn(x[4], mul), __fmul_rn(x[5], mul)));
+    o.w = h2_bits(__floats2half2_rn(__fmul_rn(x[6], mul), __fmul_rn(x[7], mul)));
+    __stcs(dst + g, o);
+  }
+}
+
+// k_tc_prep_pro: activation rows with a prologue applied before the scaling
+// of k_tc_prep (same power-of-two rule, same K order):
+//   kTcProRms:    x / sqrt(mean(x^2) + eps) * nw  (RMSNorm, TR lib/layers.tr 68-79)
+//   kTcProSwiglu: silu(g) * u over merged rows [G | U] of 2K elements
+//                 (TR's merged SwiGLU, lib/layers.tr 224-230)
+// One CTA per row; a thread keeps its NG groups of 8 values in registers, so
+// the row is read from memory once.  f32 rows only.
+template <int NG>
+__global__ void __launch_bounds__(256) k_tc_prep_pro(const float *x, long ldx, int K, int pro, const float *nw,
+                                                     float eps, __half *xh, float *ix, int perm) {
+  __shared__ float red[8], red2[8];
+  const int m = blockIdx.x, tid = threadIdx.x;
+  const float *row = x + (size_t)m * ldx;
+  float v[NG][8];
 #pragma unroll
-  for (int gi = 0; gi < kWdeqGroups; gi++) {
-    const int g = threadIdx.x + gi * blockDim.x;
+  for (int gi = 0; gi < NG; gi++) {
+    const int g = tid + gi * 256;
     if (8 * g < K) {
-      float *x = v[gi];
+      const float4 a = __ldcs(reinterpret_cast<const float4 *>(row) + 2 * g);
+      const float4 b = __ldcs(reinterpret_cast<const float4 *>(row) + 2 * g + 1);
+      v[gi][0] = a.x, v[gi][1] = a.y, v[gi][2] = a.z, v[gi][3] = a.w;
+      v[gi][4] = b.x, v[gi][5] = b.y, v[gi][6] = b.z, v[gi][7] = b.w;
+      if (pro == kTcProSwiglu) {
+        const float4 c = __ldcs(reinterpret_cast<const float4 *>(row + K) + 2 * g);
+        const float4 d = __ldcs(reinterpret_cast<const float4 *>(row + K) + 2 * g + 1);
+        const float u[8] = {c.x, c.y, c.z, c.w, d.x, d.y, d.z, d.w};
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          const float gg = v[gi][i];
+          v[gi][i] = __fmul_rn(__fmul_rn(gg, __frcp_rn(__fadd_rn(1.0f, expf(-gg)))), u[i]);
+        }
+      }
+    }
+  }
+  if (pro == kTcProRms) {
+    float ss = 0.f;
+#pragma unroll
+    for (int gi = 0; gi < NG; gi++)
+      if (8 * (tid + gi * 256) < K)
+#pragma unroll
+        for (int i = 0; i < 8; i++) ss = fmaf(v[gi][i], v[gi][i], ss);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    if ((tid & 31) == 0) red2[tid >> 5] = ss;
+    __syncthreads();
+    float t = 0.f;
+    for (int i = 0; i < 8; i++) t += red2[i];
+    const float rs = sqrtf(__fdiv_rn(t, (float)K) + eps);
+#pragma unroll
+    for (int gi = 0; gi < NG; gi++) {
+      const int g = tid + gi * 256;
+      if (8 * g < K) {
+        const float4 a = __ldg(reinterpret_cast<const float4 *>(nw) + 2 * g);
+        const float4 b = __ldg(reinterpret_cast<const float4 *>(nw) + 2 * g + 1);
+        const float ww[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[gi][i] = __fmul_rn(__fdiv_rn(v[gi][i], rs), ww[i]);
+      }
+    }
+  }
+  float amax = 0.f;
+  int bad = 0;
+#pragma unroll
+  for (int gi = 0; gi < NG; gi++)
+    if (8 * (tid + gi * 256) < K)
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const float av = fabsf(v[gi][i]);
+        bad |= !(av <= 3.402823466e38f);
+        amax = fmaxf(amax, av);
+      }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+  if ((tid & 31) == 0) red[tid >> 5] = amax;
+  const int any_bad = __syncthreads_or(bad);
+  float a = red[0];
+  for (int i = 1; i < 8; i++) a = fmaxf(a, red[i]);
+  int e = 0;
+  if (!any_bad && a > 0.f) e = min(max(ilogbf(a) - 14, -100), 100);
+  const float mul = ldexpf(1.f, -e);
+  if (tid == 0) ix[m] = ldexpf(1.f, e);
+  uint4 *dst = reinterpret_cast<uint4 *>(xh + (size_t)m * K);
+#pragma unroll
+  for (int gi = 0; gi < NG; gi++) {
+    const int g = tid + gi * 256;
+    if (8 * g < K) {
+      float *q = v[gi];
+#pragma unroll
+      for (int i = 0; i < 8; i++) q[i] = __fmul_rn(q[i], mul);
       uint4 o;
-      o.x = h2_bits(__floats2half2_rn(__fmul_rn(x[0], mul), __fmul_rn(x[1], mul)));
-      o.y = h2_bits(__floats2half2_rn(__fmul_rn(x[2], mul), __fmul_rn(x[3], mul)));
-      o.z = h2_bits(__floats2half2_rn(__fmul_rn(x[4], mul), __fmul_rn(x[5], mul)));
-      o.w = h2_bits(__floats2half2_rn(__fmul_rn(x[6], mul), __fmul_rn(x[7], mul)));
+      if (perm) {
+        o.x = h2_bits(__floats2half2_rn(q[0], q[2]));
+        o.y = h2_bits(__floats2half2_rn(q[1], q[3]));
+        o.z = h2_bits(__floats2half2_rn(q[4], q[6]));
+        o.w = h2_bits(__floats2half2_rn(q[5], q[7]));
+      } else {
+        o.x = h2_bits(__floats2half2_rn(q[0], q[1]));
+        o.y = h2_bits(__floats2half2_rn(q[2], q[3]));
+        o.z = h2_bits(__floats2half2_rn(q[4], q[5]));
+        o.w = h2_bits(__floats2half2_rn(q[6], q[7]));
+      }
       dst[g] = o;
     }
   }
@@ -891,7 +1013,7 @@ bool tc_eligible(int wtype, int M, int N, int K, const void *w) {
   const bool typ = (wtype == TCB_Q4_K && (reinterpret_cast<uintptr_t>(w) & 15) == 0) || wtype == TCB_Q6_K ||
                    wtype == TCB_Q8_0 || wtype == TCB_Q4_0;
   return typ && M >= kTcMinM && N > 0 && K >= 256 && K % 256 == 0 &&
-         (wtype == TCB_Q4_K || K <= 8 * tc::kWdeqGroups * 256) && tensor_map_encoder() != nullptr &&
+         (wtype == TCB_Q4_K || K <= tc::kWdeqMaxK) && tensor_map_encoder() != nullptr &&
          max_pairs() > 0;
 }
 
@@ -900,8 +1022,16 @@ size_t tc_workspace_bytes(int wtype, int M, int N, int K) {
   return p.xh + p.ix + 2 * p.w + p.part + p.wh;
 }
 
+bool tc_prologue_ok(const TcPrologue &pro, int K, const void *x, long ldx) {
+  if (pro.kind == kTcProNone) return true;
+  if (K > tc::kWdeqMaxK || ldx % 4 || (reinterpret_cast<uintptr_t>(x) & 15)) return false;
+  if (pro.kind == kTcProRms) return pro.w && (reinterpret_cast<uintptr_t>(pro.w) & 15) == 0 && ldx >= K;
+  return pro.kind == kTcProSwiglu && ldx >= 2L * K;
+}
+
 cudaError_t launch_qgemm_tc(int wtype, const void *w, int M, int N, int K, const void *x, int xdt, long ldx, void *c,
-                            int cdt, long ldc, int accumulate, void *ws, int *err, cudaStream_t s) {
+                            int cdt, long ldc, int accumulate, void *ws, int *err, cudaStream_t s,
+                            const TcPrologue *pro) {
   using namespace tc;
   const TcPlan pl = tc_plan(wtype, M, N, K);
   const bool dq = wtype == TCB_Q4_K;
@@ -961,15 +1091,31 @@ cudaError_t launch_qgemm_tc(int wtype, const void *w, int M, int N, int K, const
   a.err = err;
 
   const uint8_t *wb = static_cast<const uint8_t *>(w);
+  const bool fused = pro && pro->kind != kTcProNone;
+  if (fused && (xdt != TCB_F32 || !tc_prologue_ok(*pro, K, x, ldx))) return cudaErrorInvalidValue;
   if (dq) {
-    k_tc_prep<<<M + (N + 7) / 8, 256, 0, s>>>(x, xdt, ldx, M, K, xh, ix, wb, N, nsb, mw, iw, 1);
+    // activation rows (unless the prologue kernel converts them) and the
+    // weight rows' multipliers
+    k_tc_prep<<<(fused ? 0 : M) + (N + 7) / 8, 256, 0, s>>>(x, xdt, ldx, fused ? 0 : M, K, xh, ix, wb, N, nsb, mw,
+                                                             iw, 1);
   } else {
+    const size_t rb = (size_t)nsb * 256 / block_elems(wtype) * block_bytes(wtype);
     switch (wtype) {
-    case TCB_Q6_K: k_tc_wdeq<TCB_Q6_K><<<N, 256, 0, s>>>(wb, N, K, wh, iw); break;
-    case TCB_Q8_0: k_tc_wdeq<TCB_Q8_0><<<N, 256, 0, s>>>(wb, N, K, wh, iw); break;
-    default: k_tc_wdeq<TCB_Q4_0><<<N, 256, 0, s>>>(wb, N, K, wh, iw); break;
+    case TCB_Q6_K: k_tc_wdeq<TCB_Q6_K><<<N, 256, rb, s>>>(wb, N, K, wh, iw); break;
+    case TCB_Q8_0: k_tc_wdeq<TCB_Q8_0><<<N, 256, rb, s>>>(wb, N, K, wh, iw); break;
+    default: k_tc_wdeq<TCB_Q4_0><<<N, 256, rb, s>>>(wb, N, K, wh, iw); break;
     }
-    k_tc_prep<<<M, 256, 0, s>>>(x, xdt, ldx, M, K, xh, ix, nullptr, N, nsb, mw, iw, 0);
+    if (!fused) k_tc_prep<<<M, 256, 0, s>>>(x, xdt, ldx, M, K, xh, ix, nullptr, N, nsb, mw, iw, 0);
+  }
+  if (fused) {
+    const float *xf = static_cast<const float *>(x);
+    const int ng = (K / 8 + 255) / 256, perm = dq ? 1 : 0;
+    if (ng <= 2)
+      k_tc_prep_pro<2><<<M, 256, 0, s>>>(xf, ldx, K, pro->kind, pro->w, pro->eps, xh, ix, perm);
+    else if (ng <= 4)
+      k_tc_prep_pro<4><<<M, 256, 0, s>>>(xf, ldx, K, pro->kind, pro->w, pro->eps, xh, ix, perm);
+    else
+      k_tc_prep_pro<8><<<M, 256, 0, s>>>(xf, ldx, K, pro->kind, pro->w, pro->eps, xh, ix, perm);
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;

@@ -35,6 +35,7 @@
 #include "../../include/tcb.h"
 #include "tcb_common.cuh"
 #include "tcb_ctx.h"
+#include "tcb_gemm_tc.h"
 #include "tcb_launch.h"
 #include "tcb_matvec.h"
 #include "tcb_mv_ptx.cuh"
@@ -1005,6 +1006,23 @@ int tcb_llama_start(tcb_llama *m, const int64_t *prompt, int n, void *stream) {
   return TCB_OK;
 }
 
+namespace {
+// rows out = W · rms(px) for the prompt pass: the RMSNorm in the tensor-core
+// product's activation prologue when that path takes the shape, else a pass
+// of its own into ph
+int norm_gemm(tcb_llama *m, const Mat &mt, const float *nw, int M, float *out, cudaStream_t s) {
+  const tcb_llama_config &c = m->cfg;
+  tcb::TcPrologue pro;
+  pro.kind = tcb::kTcProRms;
+  pro.w = nw;
+  pro.eps = c.eps;
+  int rc = tcb::qgemm_tc_prologue(m->ctx, mt.type, M, mt.N, mt.K, mt.w, m->px, c.d_model, out, mt.N, 0, pro, s);
+  if (rc != TCB_ERR_UNSUPPORTED) return rc;
+  tcb::ll::k_rmsnorm<<<M, 1024, 0, s>>>(m->px, nw, m->ph, c.d_model, c.eps);
+  return tcb_qgemm(m->ctx, mt.type, M, mt.N, mt.K, mt.w, m->ph, TCB_F32, mt.K, out, TCB_F32, mt.N, 0, s);
+}
+}  // namespace
+
 int tcb_llama_prefill(tcb_llama *m, void *stream) {
   using namespace tcb::ll;
   if (!m) return TCB_ERR_NULL;
@@ -1050,10 +1068,8 @@ int tcb_llama_prefill(tcb_llama *m, void *stream) {
       return fail(m, e);
     for (int l = 0; l < c.n_layers; l++) {
       __half *kc = m->kc + l * cache_layer, *vc = m->vc + l * cache_layer;
-      k_rmsnorm<<<M, 1024, 0, s>>>(m->px, m->attn_norm[l], m->ph, D, c.eps);
       const Mat &q = m->qkv[l], &o = m->o[l], &gu = m->gu[l], &dn = m->down[l];
-      if ((rc = tcb_qgemm(m->ctx, q.type, M, q.N, q.K, q.w, m->ph, TCB_F32, q.K, m->pqkv, TCB_F32, q.N, 0, s)) != TCB_OK)
-        break;
+      if ((rc = norm_gemm(m, q, m->attn_norm[l], M, m->pqkv, s)) != TCB_OK) break;
       k_rope_rows<<<M, 256, 0, s>>>(m->pqkv, m->cosT, m->sinT, p0, kc, vc, H, KVH, c.max_ctx);
       if ((e = tcb::launch_attn_prefill(m->pqkv, qkvn, kc, vc, m->patt, (long)H * hd, p0, M, H, KVH, c.max_ctx, s)) !=
           cudaSuccess)
@@ -1062,16 +1078,17 @@ int tcb_llama_prefill(tcb_llama *m, void *stream) {
               TCB_OK ||
           (rc = reduce(M)) != TCB_OK)
         break;
-      k_rmsnorm<<<M, 1024, 0, s>>>(m->px, m->ffn_norm[l], m->ph, D, c.eps);
-      if ((rc = tcb_qgemm(m->ctx, gu.type, M, gu.N, gu.K, gu.w, m->ph, TCB_F32, gu.K, m->pgu, TCB_F32, gu.N, 0, s)) !=
-          TCB_OK)
-        break;
-      const long na = (long)M * F;
-      k_swiglu_rows<<<(int)((na + 255) / 256 < 4096 ? (na + 255) / 256 : 4096), 256, 0, s>>>(m->pgu, m->pa, F, na);
-      if ((rc = tcb_qgemm(m->ctx, dn.type, M, dn.N, dn.K, dn.w, m->pa, TCB_F32, dn.K, m->px, TCB_F32, dn.N, acc, s)) !=
-              TCB_OK ||
-          (rc = reduce(M)) != TCB_OK)
-        break;
+      if ((rc = norm_gemm(m, gu, m->ffn_norm[l], M, m->pgu, s)) != TCB_OK) break;
+      // SwiGLU in the down product's activation prologue, else a pass of its own
+      tcb::TcPrologue sw;
+      sw.kind = tcb::kTcProSwiglu;
+      rc = tcb::qgemm_tc_prologue(m->ctx, dn.type, M, dn.N, dn.K, dn.w, m->pgu, 2L * F, m->px, dn.N, acc, sw, s);
+      if (rc == TCB_ERR_UNSUPPORTED) {
+        const long na = (long)M * F;
+        k_swiglu_rows<<<(int)((na + 255) / 256 < 4096 ? (na + 255) / 256 : 4096), 256, 0, s>>>(m->pgu, m->pa, F, na);
+        rc = tcb_qgemm(m->ctx, dn.type, M, dn.N, dn.K, dn.w, m->pa, TCB_F32, dn.K, m->px, TCB_F32, dn.N, acc, s);
+      }
+      if (rc != TCB_OK || (rc = reduce(M)) != TCB_OK) break;
     }
     if (rc == TCB_OK && (e = cudaGetLastError()) != cudaSuccess) return fail(m, e);
   }
