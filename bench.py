@@ -193,7 +193,7 @@ def decode_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
     }
 
 
-def model_prefill_bench(ctx, peaks: dict) -> dict:
+def model_prefill_bench(ctx, peaks: dict, layers: int = 0) -> dict:
     """8B-shape model prefill (second part): 2048-token
     random prompts at batch 4, each fed by the prompt pass (2047 rows through
     the tensor-core products and the causal flash-attention kernel) plus the
@@ -212,6 +212,8 @@ def model_prefill_bench(ctx, peaks: dict) -> dict:
 
     T_, B = 2048, 4
     cfg = dataclasses.replace(llama.LLAMA3_8B, max_ctx=T_ + 1)
+    if layers:  # profiling: the same layer shapes, fewer layers
+        cfg = dataclasses.replace(cfg, n_layers=layers)
     model = llama.device_model(cfg, seed=7)
     eng = llama.Llama(ctx, model)
     stream = torch.cuda.Stream()
@@ -392,6 +394,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill-product measurement")
     ap.add_argument("--only-model-prefill", action="store_true",
                     help="run only the 8B model prefill and print its object (for profiling)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="with --only-model-prefill: this many layers instead of 32 (small profiling case)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -412,7 +416,8 @@ def main():
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     if args.only_model_prefill:
-        print(json.dumps({"model_prefill": model_prefill_bench(T.Context(local), load_peaks())}), flush=True)
+        print(json.dumps({"model_prefill": model_prefill_bench(T.Context(local), load_peaks(), args.layers)}),
+              flush=True)
         return
     N, K = WORKLOAD["N"], WORKLOAD["K"]
     wbytes = N * K // 256 * 144

@@ -9,9 +9,12 @@
 // own.
 //
 // CTA = (64 query rows, one query head), four warps of 16 rows.  The rotated
-// query rows (f32) are rounded to fp16 once into shared memory and held as
-// mma fragments; 64-position K and V tiles stream from the cache through a
-// two-deep cp.async ring (positions past the needed range are zero-filled).
+// query rows (f32) are rounded to fp16 once into shared memory (read back
+// per K step); 64-position K and V tiles stream from the cache by cp.async
+// into one buffer each, K(t+1) loading while the warps form P V(t) and
+// V(t+1) while they form S(t+1) (positions past the needed range are
+// zero-filled).  51 KB of shared memory and at most 168 registers per
+// thread let three CTAs share an SM.
 // Per tile a warp forms S = Q K^T with m16n8k16 fp16 MMAs (f32
 // accumulators), applies the causal mask, keeps the running row maximum and
 // sum in the log2 domain (scores scaled by log2(e)/sqrt(hd)), rescales its
@@ -34,7 +37,8 @@ constexpr int kBq = 64;          // query rows per CTA
 constexpr int kBk = 64;          // cached positions per tile
 constexpr int kLd = kHd + 8;     // shared-memory row stride in halves (272 B: ldmatrix rows fall in distinct banks)
 constexpr int kThreads = 128;
-constexpr size_t kSmem = (size_t)(kBq + 4 * kBk) * kLd * sizeof(__half);
+constexpr int kMinCtas = 3;      // CTAs per SM the register budget is sized for
+constexpr size_t kSmem = (size_t)(kBq + 2 * kBk) * kLd * sizeof(__half);
 
 struct Args {
   const float *q;        // rotated query rows: row r, head h at q + r*ldq + h*kHd
@@ -75,11 +79,11 @@ __device__ __forceinline__ void cp_wait() {
 }
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 
-__global__ void __launch_bounds__(kThreads) k_attn_prefill(const __grid_constant__ Args a) {
+__global__ void __launch_bounds__(kThreads, kMinCtas) k_attn_prefill(const __grid_constant__ Args a) {
   extern __shared__ __align__(128) unsigned char smem[];
   __half *qs = reinterpret_cast<__half *>(smem);  // [kBq][kLd]
-  __half *ks = qs + kBq * kLd;                    // [2][kBk][kLd]
-  __half *vs = ks + 2 * kBk * kLd;                // [2][kBk][kLd]
+  __half *ks = qs + kBq * kLd;                    // [kBk][kLd]
+  __half *vs = ks + kBk * kLd;                    // [kBk][kLd]
   const int nqb = (a.M + kBq - 1) / kBq;
   const int qb = nqb - 1 - (int)blockIdx.x;
   const int h = blockIdx.y, kh = h / (a.H / a.KVH);
@@ -89,18 +93,18 @@ __global__ void __launch_bounds__(kThreads) k_attn_prefill(const __grid_constant
   const int ntiles = (kv_end + kBk - 1) / kBk;
   const __half *kb = a.kc + (size_t)kh * a.max_ctx * kHd, *vb = a.vc + (size_t)kh * a.max_ctx * kHd;
 
-  auto load_tile = [&](int t, int buf) {
+  // one 64-position tile of K or V into its buffer (one commit group)
+  auto load_tile = [&](const __half *src, __half *dst, int t) {
     const int j0 = t * kBk;
     for (int i = tid; i < kBk * (kHd / 8); i += kThreads) {
       const int r = i / (kHd / 8), c = (i % (kHd / 8)) * 8, j = j0 + r;
       const bool ok = j < kv_end;
-      const size_t off = (size_t)(ok ? j : 0) * kHd + c;
-      cp16(su32(ks + (buf * kBk + r) * kLd + c), kb + off, ok ? 16 : 0);
-      cp16(su32(vs + (buf * kBk + r) * kLd + c), vb + off, ok ? 16 : 0);
+      cp16(su32(dst + r * kLd + c), src + (size_t)(ok ? j : 0) * kHd + c, ok ? 16 : 0);
     }
     cp_commit();
   };
-  load_tile(0, 0);
+  load_tile(kb, ks, 0);
+  load_tile(vb, vs, 0);
   for (int i = tid; i < kBq * (kHd / 4); i += kThreads) {
     const int r = i / (kHd / 4), c = (i % (kHd / 4)) * 4;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -109,14 +113,6 @@ __global__ void __launch_bounds__(kThreads) k_attn_prefill(const __grid_constant
     d[0] = __floats2half2_rn(v.x, v.y);
     d[1] = __floats2half2_rn(v.z, v.w);
   }
-  __syncthreads();
-  uint32_t qf[kHd / 16][4];
-#pragma unroll
-  for (int kk = 0; kk < kHd / 16; kk++) {
-    const int mi = lane >> 3;
-    const int row = warp * 16 + (mi & 1) * 8 + (lane & 7), col = kk * 16 + (mi >> 1) * 8;
-    ldsm4(su32(qs + row * kLd + col), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
-  }
   float o[kHd / 8][4];
 #pragma unroll
   for (int d = 0; d < kHd / 8; d++) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.f;
@@ -124,31 +120,39 @@ __global__ void __launch_bounds__(kThreads) k_attn_prefill(const __grid_constant
   const int g = lane >> 2, tq = lane & 3;
   const int pos0 = a.p0 + r0 + warp * 16 + g, pos1 = pos0 + 8;  // this thread's two rows
   const int wlast = a.p0 + r0 + warp * 16 + 15;                 // the warp's last position
+  // the warp's Q rows in shared memory, read per K step (ldmatrix x4 address)
+  const uint32_t qa = su32(qs + (warp * 16 + ((lane >> 3) & 1) * 8 + (lane & 7)) * kLd + (lane >> 4) * 8);
 
+  // K(t) and V(t) alternate in their buffers: K(t+1) streams while the warps
+  // form P V(t), V(t+1) while they form S(t+1)
   for (int t = 0; t < ntiles; t++) {
-    if (t + 1 < ntiles) {
-      load_tile(t + 1, (t + 1) & 1);
-      cp_wait<1>();
-    } else {
-      cp_wait<0>();
-    }
+    const int j0 = t * kBk;
+    const bool act = j0 <= wlast;
+    cp_wait<1>();  // K(t) has landed (V(t) may still be in flight)
     __syncthreads();
-    const int buf = t & 1, j0 = t * kBk;
-    if (j0 <= wlast) {
-      const __half *kt = ks + buf * kBk * kLd, *vt = vs + buf * kBk * kLd;
-      float s[kBk / 8][4];
+    float s[kBk / 8][4];
+    if (act) {
 #pragma unroll
       for (int n = 0; n < kBk / 8; n++) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
 #pragma unroll
-      for (int kk = 0; kk < kHd / 16; kk++)
+      for (int kk = 0; kk < kHd / 16; kk++) {
+        uint32_t qf[4];
+        ldsm4(qa + kk * 32, qf[0], qf[1], qf[2], qf[3]);
 #pragma unroll
         for (int np = 0; np < kBk / 16; np++) {
           const int row = np * 16 + ((lane >> 4) & 1) * 8 + (lane & 7), col = kk * 16 + ((lane >> 3) & 1) * 8;
           uint32_t b0, b1, b2, b3;
-          ldsm4(su32(kt + row * kLd + col), b0, b1, b2, b3);
-          mma(s[2 * np], qf[kk], b0, b1);
-          mma(s[2 * np + 1], qf[kk], b2, b3);
+          ldsm4(su32(ks + row * kLd + col), b0, b1, b2, b3);
+          mma(s[2 * np], qf, b0, b1);
+          mma(s[2 * np + 1], qf, b2, b3);
         }
+      }
+    }
+    __syncthreads();  // every warp is done with K(t)
+    if (t + 1 < ntiles) load_tile(kb, ks, t + 1);
+    else cp_commit();  // an empty group keeps the wait counts uniform
+    uint32_t pa[kBk / 16][4];
+    if (act) {
       float x0 = -INFINITY, x1 = -INFINITY;
 #pragma unroll
       for (int n = 0; n < kBk / 8; n++)
@@ -181,7 +185,6 @@ __global__ void __launch_bounds__(kThreads) k_attn_prefill(const __grid_constant
         o[d][2] *= c1;
         o[d][3] *= c1;
       }
-      uint32_t pa[kBk / 16][4];
 #pragma unroll
       for (int n = 0; n < kBk / 8; n++) {
         const __half2 p0 = __floats2half2_rn(exp2f(s[n][0] - n0), exp2f(s[n][1] - n0));
@@ -192,19 +195,26 @@ __global__ void __launch_bounds__(kThreads) k_attn_prefill(const __grid_constant
         pa[n >> 1][(n & 1) * 2] = h2u(p0);
         pa[n >> 1][(n & 1) * 2 + 1] = h2u(p1);
       }
+    }
+    cp_wait<1>();  // V(t) has landed (K(t+1) may still be in flight)
+    __syncthreads();
+    if (act) {
 #pragma unroll
       for (int kq = 0; kq < kBk / 16; kq++)
 #pragma unroll
         for (int dp = 0; dp < kHd / 16; dp++) {
           const int row = kq * 16 + ((lane >> 3) & 1) * 8 + (lane & 7), col = dp * 16 + ((lane >> 4) & 1) * 8;
           uint32_t b0, b1, b2, b3;
-          ldsm4t(su32(vt + row * kLd + col), b0, b1, b2, b3);
+          ldsm4t(su32(vs + row * kLd + col), b0, b1, b2, b3);
           mma(o[2 * dp], pa[kq], b0, b1);
           mma(o[2 * dp + 1], pa[kq], b2, b3);
         }
     }
-    __syncthreads();
+    __syncthreads();  // every warp is done with V(t)
+    if (t + 1 < ntiles) load_tile(vb, vs, t + 1);
+    else cp_commit();
   }
+  cp_wait<0>();
   l0 += __shfl_xor_sync(0xFFFFFFFFu, l0, 1);
   l0 += __shfl_xor_sync(0xFFFFFFFFu, l0, 2);
   l1 += __shfl_xor_sync(0xFFFFFFFFu, l1, 1);
