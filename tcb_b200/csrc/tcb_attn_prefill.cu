@@ -21,7 +21,9 @@
 // output accumulators, and adds P V with P rounded to fp16 straight from the
 // score registers.  The row sum adds the rounded P, so the output is an
 // exact weighted mean of the V rows under the weights used.  Query blocks
-// are issued longest first.
+// are issued longest first across all heads (grid x = head, y = block from
+// the end); the mask is applied only on tiles that reach past a warp's first
+// row, and the output is rescaled only when a row maximum changes.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <math.h>
@@ -85,8 +87,8 @@ __global__ void __launch_bounds__(kThreads, kMinCtas) k_attn_prefill(const __gri
   __half *ks = qs + kBq * kLd;                    // [kBk][kLd]
   __half *vs = ks + kBk * kLd;                    // [kBk][kLd]
   const int nqb = (a.M + kBq - 1) / kBq;
-  const int qb = nqb - 1 - (int)blockIdx.x;
-  const int h = blockIdx.y, kh = h / (a.H / a.KVH);
+  const int qb = nqb - 1 - (int)blockIdx.y;  // the longest query blocks of every head first
+  const int h = blockIdx.x, kh = h / (a.H / a.KVH);
   const int r0 = qb * kBq, rows = min(kBq, a.M - r0);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int kv_end = a.p0 + r0 + rows;  // cached positions [0, kv_end) are read
@@ -109,9 +111,10 @@ __global__ void __launch_bounds__(kThreads, kMinCtas) k_attn_prefill(const __gri
     const int r = i / (kHd / 4), c = (i % (kHd / 4)) * 4;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     if (r < rows) v = *reinterpret_cast<const float4 *>(a.q + (size_t)(r0 + r) * a.ldq + (size_t)h * kHd + c);
+    // the score scale log2(e)/sqrt(hd) rides on q
     __half2 *d = reinterpret_cast<__half2 *>(qs + r * kLd + c);
-    d[0] = __floats2half2_rn(v.x, v.y);
-    d[1] = __floats2half2_rn(v.z, v.w);
+    d[0] = __floats2half2_rn(v.x * a.scale_log2, v.y * a.scale_log2);
+    d[1] = __floats2half2_rn(v.z * a.scale_log2, v.w * a.scale_log2);
   }
   float o[kHd / 8][4];
 #pragma unroll
@@ -154,18 +157,21 @@ __global__ void __launch_bounds__(kThreads, kMinCtas) k_attn_prefill(const __gri
     uint32_t pa[kBk / 16][4];
     if (act) {
       float x0 = -INFINITY, x1 = -INFINITY;
+      if (j0 + kBk - 1 > wlast - 15) {  // the tile reaches past the warp's first row: causal mask
 #pragma unroll
-      for (int n = 0; n < kBk / 8; n++)
+        for (int n = 0; n < kBk / 8; n++)
 #pragma unroll
-        for (int e = 0; e < 2; e++) {
-          const int key = j0 + n * 8 + 2 * tq + e;
-          const float v0 = key > pos0 ? -INFINITY : s[n][e] * a.scale_log2;
-          const float v1 = key > pos1 ? -INFINITY : s[n][2 + e] * a.scale_log2;
-          s[n][e] = v0;
-          s[n][2 + e] = v1;
-          x0 = fmaxf(x0, v0);
-          x1 = fmaxf(x1, v1);
-        }
+          for (int e = 0; e < 2; e++) {
+            const int key = j0 + n * 8 + 2 * tq + e;
+            if (key > pos0) s[n][e] = -INFINITY;
+            if (key > pos1) s[n][2 + e] = -INFINITY;
+          }
+      }
+#pragma unroll
+      for (int n = 0; n < kBk / 8; n++) {
+        x0 = fmaxf(x0, fmaxf(s[n][0], s[n][1]));
+        x1 = fmaxf(x1, fmaxf(s[n][2], s[n][3]));
+      }
       x0 = fmaxf(x0, __shfl_xor_sync(0xFFFFFFFFu, x0, 1));
       x0 = fmaxf(x0, __shfl_xor_sync(0xFFFFFFFFu, x0, 2));
       x1 = fmaxf(x1, __shfl_xor_sync(0xFFFFFFFFu, x1, 1));
@@ -173,18 +179,21 @@ __global__ void __launch_bounds__(kThreads, kMinCtas) k_attn_prefill(const __gri
       // tile 0 holds position 0, which every row sees: the maxima are finite
       // from the first tile on
       const float n0 = fmaxf(m0, x0), n1 = fmaxf(m1, x1);
-      const float c0 = exp2f(m0 - n0), c1 = exp2f(m1 - n1);
+      // rescale only when some row of the warp has a new maximum
+      if (__any_sync(0xFFFFFFFFu, n0 != m0 || n1 != m1)) {
+        const float c0 = exp2f(m0 - n0), c1 = exp2f(m1 - n1);
+        l0 *= c0;
+        l1 *= c1;
+#pragma unroll
+        for (int d = 0; d < kHd / 8; d++) {
+          o[d][0] *= c0;
+          o[d][1] *= c0;
+          o[d][2] *= c1;
+          o[d][3] *= c1;
+        }
+      }
       m0 = n0;
       m1 = n1;
-      l0 *= c0;
-      l1 *= c1;
-#pragma unroll
-      for (int d = 0; d < kHd / 8; d++) {
-        o[d][0] *= c0;
-        o[d][1] *= c0;
-        o[d][2] *= c1;
-        o[d][3] *= c1;
-      }
 #pragma unroll
       for (int n = 0; n < kBk / 8; n++) {
         const __half2 p0 = __floats2half2_rn(exp2f(s[n][0] - n0), exp2f(s[n][1] - n0));
@@ -243,7 +252,7 @@ cudaError_t launch_attn_prefill(const float *q, long ldq, const __half *kc, cons
   }();
   if (!attr) return cudaErrorInvalidDeviceFunction;
   pf::Args a{q, ldq, kc, vc, out, ldo, p0, M, H, KVH, max_ctx, (float)(1.4426950408889634 / sqrt((double)pf::kHd))};
-  const dim3 grid((M + pf::kBq - 1) / pf::kBq, H);
+  const dim3 grid(H, (M + pf::kBq - 1) / pf::kBq);
   pf::k_attn_prefill<<<grid, pf::kThreads, pf::kSmem, s>>>(a);
   return cudaGetLastError();
 }
