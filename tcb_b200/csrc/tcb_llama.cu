@@ -83,10 +83,10 @@ __global__ void k_rmsnorm(const float *x, const float *w, float *out, int D, flo
 }
 
 // One layer's attention at position *pos: CTA (KV head blockIdx.x, chunk
-// blockIdx.y of kChunk positions), 256 threads.  Every K and V byte of the
-// chunk is requested right after the dependency wait (K: thread = (position
+// blockIdx.y of kChunk positions), 256 threads.  Every cached K and V byte of
+// the chunk is requested before the dependency wait (K: thread = (position
 // t/4, 32 dimensions (t%4)*32); V: thread = (dimensions (t%32)*4, positions
-// t/32 + 8j)), so a layer costs one memory round trip.  The CTA rotates the
+// t/32 + 8j)), so the loads overlap the qkv product.  The CTA rotates the
 // query rows of its G query heads; the CTA whose chunk holds pos also
 // rotates the new key, stores it and the new value into the fp16 cache and
 // uses them from shared memory for that position.  Each CTA writes its
@@ -104,10 +104,11 @@ __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cos
   __shared__ float gm[G], gl[G];
   __shared__ float wo[8][G][kHd];
   __shared__ int last;
-  mv::pdl_wait();
-  // the next kernel (the o projection) may launch now: its weight stream does
-  // not depend on this one, and it waits for this grid before reading `out`
-  mv::pdl_launch_dependents();
+  // The position and the cached K/V rows before it were written by earlier
+  // steps (every step starts with a plain launch, after the previous one has
+  // completed) or by the prompt pass: they are read before the dependency
+  // wait, while the qkv product finishes.  Row p is this step's, written
+  // below by the CTA that holds it.
   const int p = *pos, n = p + 1, kh = blockIdx.x, c = blockIdx.y, t0 = c * kChunk;
   if (t0 >= n) return;
   const int tid = threadIdx.x;
@@ -126,6 +127,10 @@ __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cos
     const int t = tv + 8 * j;
     if (t < n && t != p) vr[j] = __ldcg(reinterpret_cast<const uint2 *>(vbase + (size_t)t * kHd + dv));
   }
+  mv::pdl_wait();
+  // the next kernel (the o projection) may launch now: its weight stream does
+  // not depend on this one, and it waits for this grid before reading `out`
+  mv::pdl_launch_dependents();
   const float *cs = cosT + (size_t)p * half, *sn = sinT + (size_t)p * half;
   for (int i = tid; i < G * half; i += blockDim.x) {
     const int g = i / half, j = i % half;
@@ -785,6 +790,9 @@ cudaError_t issue_step(tcb_llama *m, cudaStream_t s) {
   const int G = H / KVH;
   const float scale = 1.0f / sqrtf((float)hd);
   const size_t cache_layer = (size_t)KVH * c.max_ctx * hd;
+  // a plain launch (no programmatic dependency): the step starts after the
+  // previous one has completed, which k_attn relies on when it reads the
+  // cached K/V before its dependency wait
   cudaError_t e = tcb::launch_dequant_rows(m->tok_emb_type, m->tok_emb, 1, D, m->tok, m->x, TCB_F32, m->ctx->sms, s);
   for (int l = 0; l < c.n_layers && e == cudaSuccess; l++) {
     __half *kc = m->kc + l * cache_layer, *vc = m->vc + l * cache_layer;
