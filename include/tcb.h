@@ -184,6 +184,15 @@ int tcb_llama_start(tcb_llama *m, const int64_t *prompt, int n, void *stream);
  * Tensor parallelism sums the residual rows with NCCL.  Returns
  * TCB_ERR_UNSUPPORTED when a step has already run since the start. */
 int tcb_llama_prefill(tcb_llama *m, void *stream);
+/* The prompt pass of several sequences at once (TR's generate over a batch
+ * of prompts): count engines made from the same weights and shapes, each
+ * started with its own prompt (tcb_llama_start), are fed as one set of rows
+ * through the products, with rotary, the cache append and causal attention
+ * per sequence; each engine is then left as tcb_llama_prefill leaves it.
+ * The rows of all sequences go through in one pass (row buffers of the first
+ * engine, sized for them).  TCB_ERR_SHAPE when the engines differ in model,
+ * TCB_ERR_UNSUPPORTED when one has stepped since its start or appears twice. */
+int tcb_llama_prefill_batch(tcb_llama *const *engines, int count, void *stream);
 /* One step: embed the current token, run every layer at the current
  * position (appending its K/V), score the vocabulary, take the greedy
  * token (first maximum), store it at tokens[pos + 1], advance.  Replays the

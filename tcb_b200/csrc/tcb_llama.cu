@@ -1029,82 +1029,174 @@ int norm_gemm(tcb_llama *m, const Mat &mt, const float *nw, int M, float *out, c
   tcb::ll::k_rmsnorm<<<M, 1024, 0, s>>>(m->px, nw, m->ph, c.d_model, c.eps);
   return tcb_qgemm(m->ctx, mt.type, M, mt.N, mt.K, mt.w, m->ph, TCB_F32, mt.K, out, TCB_F32, mt.N, 0, s);
 }
+
+// One pass of the prompt over the rows of several sequences that share the
+// model: sq[i] feeds rows p0 .. p0+rows-1 of engine sq[i].m's prompt.  The
+// products run once over all the rows (m0's row buffers); rotary, the cache
+// append and attention run per sequence on its own cache.
+struct PfSeq {
+  tcb_llama *m;
+  int p0, rows;
+};
+
+int prefill_pass(tcb_llama *m0, const PfSeq *sq, int ns, cudaStream_t s) {
+  using namespace tcb::ll;
+  const tcb_llama_config &c = m0->cfg;
+  const int H = c.n_heads, KVH = c.n_kv_heads, hd = c.head_dim, D = c.d_model, F = c.ffn_dim;
+  const int qkvn = (H + 2 * KVH) * hd;
+  const size_t cache_layer = (size_t)KVH * c.max_ctx * hd;
+  int M = 0;
+  for (int i = 0; i < ns; i++) M += sq[i].rows;
+  // NCCL: rank 0 adds its partial to the residual rows, the others write
+  // theirs, and the in-place all-reduce sums them (as in the decode step)
+  const int acc = m0->tr == 0;
+  auto reduce = [&]() -> int {
+    if (m0->tp == 1) return TCB_OK;
+    m0->nccl_rc = nccl()->all_reduce(m0->px, m0->px, (size_t)M * D, kNcclFloat32, kNcclSum, m0->comm, s);
+    return m0->nccl_rc ? fail(m0, cudaErrorUnknown) : TCB_OK;
+  };
+  cudaError_t e;
+  for (int i = 0, r = 0; i < ns; r += sq[i].rows, i++)
+    if ((e = tcb::launch_dequant_rows(m0->tok_emb_type, m0->tok_emb, sq[i].rows, D, sq[i].m->prompt + sq[i].p0,
+                                      m0->px + (size_t)r * D, TCB_F32, m0->ctx->sms, s)) != cudaSuccess)
+      return fail(m0, e);
+  int rc = TCB_OK;
+  for (int l = 0; l < c.n_layers && rc == TCB_OK; l++) {
+    const Mat &q = m0->qkv[l], &o = m0->o[l], &gu = m0->gu[l], &dn = m0->down[l];
+    if ((rc = norm_gemm(m0, q, m0->attn_norm[l], M, m0->pqkv, s)) != TCB_OK) break;
+    for (int i = 0, r = 0; i < ns; r += sq[i].rows, i++) {
+      const tcb_llama *m = sq[i].m;
+      __half *kc = m->kc + l * cache_layer, *vc = m->vc + l * cache_layer;
+      float *qr = m0->pqkv + (size_t)r * qkvn;
+      k_rope_rows<<<sq[i].rows, 256, 0, s>>>(qr, m->cosT, m->sinT, sq[i].p0, kc, vc, H, KVH, c.max_ctx);
+      if ((e = tcb::launch_attn_prefill(qr, qkvn, kc, vc, m0->patt + (size_t)r * H * hd, (long)H * hd, sq[i].p0,
+                                        sq[i].rows, H, KVH, c.max_ctx, s)) != cudaSuccess)
+        return fail(m0, e);
+    }
+    if ((rc = tcb_qgemm(m0->ctx, o.type, M, o.N, o.K, o.w, m0->patt, TCB_F32, o.K, m0->px, TCB_F32, o.N, acc, s)) !=
+            TCB_OK ||
+        (rc = reduce()) != TCB_OK)
+      break;
+    if ((rc = norm_gemm(m0, gu, m0->ffn_norm[l], M, m0->pgu, s)) != TCB_OK) break;
+    // SwiGLU in the down product's activation prologue, else a pass of its own
+    tcb::TcPrologue sw;
+    sw.kind = tcb::kTcProSwiglu;
+    rc = tcb::qgemm_tc_prologue(m0->ctx, dn.type, M, dn.N, dn.K, dn.w, m0->pgu, 2L * F, m0->px, dn.N, acc, sw, s);
+    if (rc == TCB_ERR_UNSUPPORTED) {
+      const long na = (long)M * F;
+      k_swiglu_rows<<<(int)((na + 255) / 256 < 4096 ? (na + 255) / 256 : 4096), 256, 0, s>>>(m0->pgu, m0->pa, F, na);
+      rc = tcb_qgemm(m0->ctx, dn.type, M, dn.N, dn.K, dn.w, m0->pa, TCB_F32, dn.K, m0->px, TCB_F32, dn.N, acc, s);
+    }
+    if (rc == TCB_OK) rc = reduce();
+  }
+  if (rc == TCB_OK && (e = cudaGetLastError()) != cudaSuccess) return fail(m0, e);
+  return rc;
+}
+
+// row buffers of the prompt pass for at least `rows` rows (grown once the
+// stream has drained)
+int pf_alloc(tcb_llama *m, int rows, cudaStream_t s) {
+  if (m->pf_rows >= rows) return TCB_OK;
+  const tcb_llama_config &c = m->cfg;
+  const int H = c.n_heads, KVH = c.n_kv_heads, hd = c.head_dim, D = c.d_model, F = c.ffn_dim;
+  const int qkvn = (H + 2 * KVH) * hd;
+  cudaError_t e;
+  if (m->pf_rows) {
+    if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return fail(m, e);
+    for (float *p : {m->px, m->ph, m->pqkv, m->patt, m->pgu, m->pa})
+      for (size_t i = 0; i < m->allocs.size(); i++)
+        if (m->allocs[i] == p) {
+          cudaFree(p);
+          m->allocs.erase(m->allocs.begin() + i);
+          break;
+        }
+    m->pf_rows = 0;
+  }
+  if ((e = alloc(m, &m->px, (size_t)rows * D)) != cudaSuccess || (e = alloc(m, &m->ph, (size_t)rows * D)) != cudaSuccess ||
+      (e = alloc(m, &m->pqkv, (size_t)rows * qkvn)) != cudaSuccess ||
+      (e = alloc(m, &m->patt, (size_t)rows * H * hd)) != cudaSuccess ||
+      (e = alloc(m, &m->pgu, (size_t)rows * 2 * F)) != cudaSuccess || (e = alloc(m, &m->pa, (size_t)rows * F)) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return e == cudaErrorMemoryAllocation ? TCB_ERR_NOMEM : fail(m, e);
+  }
+  m->pf_rows = rows;
+  return TCB_OK;
+}
+
+// the model (weights, shapes, parallelism) of two engines is the same
+bool same_model(const tcb_llama *a, const tcb_llama *b) {
+  const tcb_llama_config &x = a->cfg, &y = b->cfg;
+  if (a->ctx != b->ctx || a->tp != b->tp || a->tr != b->tr || x.n_layers != y.n_layers || x.d_model != y.d_model ||
+      x.n_heads != y.n_heads || x.n_kv_heads != y.n_kv_heads || x.head_dim != y.head_dim || x.ffn_dim != y.ffn_dim ||
+      x.vocab != y.vocab || x.max_ctx != y.max_ctx || x.eps != y.eps || x.rope_theta != y.rope_theta ||
+      a->tok_emb != b->tok_emb || a->tok_emb_type != b->tok_emb_type)
+    return false;
+  for (int l = 0; l < x.n_layers; l++)
+    if (a->attn_norm[l] != b->attn_norm[l] || a->ffn_norm[l] != b->ffn_norm[l] || a->qkv[l].w != b->qkv[l].w ||
+        a->o[l].w != b->o[l].w || a->gu[l].w != b->gu[l].w || a->down[l].w != b->down[l].w)
+      return false;
+  return true;
+}
+
+int finish_prefill(tcb_llama *m, cudaStream_t s) {
+  const int n = m->host_n;
+  tcb::ll::k_prefill_done<<<1, 256, 0, s>>>(m->prompt, n, m->pos, m->tok, m->hist);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(m, e);
+  m->host_pos = n - 1;
+  return TCB_OK;
+}
 }  // namespace
 
 int tcb_llama_prefill(tcb_llama *m, void *stream) {
-  using namespace tcb::ll;
   if (!m) return TCB_ERR_NULL;
   const int n = m->host_n;
   if (n < 1 || m->host_pos != 0) return TCB_ERR_UNSUPPORTED;
   if (n == 1) return TCB_OK;
-  const tcb_llama_config &c = m->cfg;
-  const int H = c.n_heads, KVH = c.n_kv_heads, hd = c.head_dim, D = c.d_model, F = c.ffn_dim;
-  const int qkvn = (H + 2 * KVH) * hd;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaSetDevice(m->ctx->dev);
   if (e != cudaSuccess) return fail(m, e);
   if (m->tp > 1 && (!nccl() || !m->comm)) return fail(m, cudaErrorNotReady);
-  if (!m->pf_rows) {
-    // TCB_PREFILL_ROWS overrides the rows per pass (tests use it to cover
-    // prompts that take several passes)
-    const char *ev = getenv("TCB_PREFILL_ROWS");
-    int rows = ev && atoi(ev) > 0 ? atoi(ev) : kPrefillRows;
-    if (rows > c.max_ctx - 1) rows = c.max_ctx - 1;
-    if ((e = alloc(m, &m->px, (size_t)rows * D)) != cudaSuccess || (e = alloc(m, &m->ph, (size_t)rows * D)) != cudaSuccess ||
-        (e = alloc(m, &m->pqkv, (size_t)rows * qkvn)) != cudaSuccess ||
-        (e = alloc(m, &m->patt, (size_t)rows * H * hd)) != cudaSuccess ||
-        (e = alloc(m, &m->pgu, (size_t)rows * 2 * F)) != cudaSuccess || (e = alloc(m, &m->pa, (size_t)rows * F)) != cudaSuccess) {
-      (void)cudaGetLastError();
-      return e == cudaErrorMemoryAllocation ? TCB_ERR_NOMEM : fail(m, e);
-    }
-    m->pf_rows = rows;
+  // TCB_PREFILL_ROWS overrides the rows per pass (tests use it to cover
+  // prompts that take several passes)
+  const char *ev = getenv("TCB_PREFILL_ROWS");
+  int rows = ev && atoi(ev) > 0 ? atoi(ev) : tcb::ll::kPrefillRows;
+  if (rows > n - 1) rows = n - 1;
+  int rc = m->pf_rows >= rows ? TCB_OK : pf_alloc(m, rows, s);
+  for (int p0 = 0; p0 < n - 1 && rc == TCB_OK; p0 += rows) {
+    const PfSeq one{m, p0, n - 1 - p0 < rows ? n - 1 - p0 : rows};
+    rc = prefill_pass(m, &one, 1, s);
   }
-  const size_t cache_layer = (size_t)KVH * c.max_ctx * hd;
-  // NCCL: rank 0 adds its partial to the residual rows, the others write
-  // theirs, and the in-place all-reduce sums them (as in the decode step)
-  const int acc = m->tr == 0;
-  auto reduce = [&](int M) -> int {
-    if (m->tp == 1) return TCB_OK;
-    m->nccl_rc = nccl()->all_reduce(m->px, m->px, (size_t)M * D, kNcclFloat32, kNcclSum, m->comm, s);
-    return m->nccl_rc ? fail(m, cudaErrorUnknown) : TCB_OK;
-  };
+  return rc == TCB_OK ? finish_prefill(m, s) : rc;
+}
+
+int tcb_llama_prefill_batch(tcb_llama *const *ms, int count, void *stream) {
+  if (!ms || count < 1) return TCB_ERR_NULL;
+  tcb_llama *m0 = ms[0];
+  for (int i = 0; i < count; i++) {
+    if (!ms[i]) return TCB_ERR_NULL;
+    if (ms[i]->host_n < 1 || ms[i]->host_pos != 0) return TCB_ERR_UNSUPPORTED;
+    if (!same_model(m0, ms[i])) return TCB_ERR_SHAPE;
+    for (int j = 0; j < i; j++)
+      if (ms[j] == ms[i]) return TCB_ERR_UNSUPPORTED;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaSetDevice(m0->ctx->dev);
+  if (e != cudaSuccess) return fail(m0, e);
+  if (m0->tp > 1 && (!nccl() || !m0->comm)) return fail(m0, cudaErrorNotReady);
+  std::vector<PfSeq> sq;
+  long total = 0;
+  for (int i = 0; i < count; i++)
+    if (ms[i]->host_n > 1) {
+      sq.push_back(PfSeq{ms[i], 0, ms[i]->host_n - 1});
+      total += ms[i]->host_n - 1;
+    }
+  if (total > 0x7FFFFFFFL / 8) return TCB_ERR_SHAPE;
   int rc = TCB_OK;
-  for (int p0 = 0; p0 < n - 1 && rc == TCB_OK; p0 += m->pf_rows) {
-    const int M = n - 1 - p0 < m->pf_rows ? n - 1 - p0 : m->pf_rows;
-    if ((e = tcb::launch_dequant_rows(m->tok_emb_type, m->tok_emb, M, D, m->prompt + p0, m->px, TCB_F32, m->ctx->sms,
-                                      s)) != cudaSuccess)
-      return fail(m, e);
-    for (int l = 0; l < c.n_layers; l++) {
-      __half *kc = m->kc + l * cache_layer, *vc = m->vc + l * cache_layer;
-      const Mat &q = m->qkv[l], &o = m->o[l], &gu = m->gu[l], &dn = m->down[l];
-      if ((rc = norm_gemm(m, q, m->attn_norm[l], M, m->pqkv, s)) != TCB_OK) break;
-      k_rope_rows<<<M, 256, 0, s>>>(m->pqkv, m->cosT, m->sinT, p0, kc, vc, H, KVH, c.max_ctx);
-      if ((e = tcb::launch_attn_prefill(m->pqkv, qkvn, kc, vc, m->patt, (long)H * hd, p0, M, H, KVH, c.max_ctx, s)) !=
-          cudaSuccess)
-        return fail(m, e);
-      if ((rc = tcb_qgemm(m->ctx, o.type, M, o.N, o.K, o.w, m->patt, TCB_F32, o.K, m->px, TCB_F32, o.N, acc, s)) !=
-              TCB_OK ||
-          (rc = reduce(M)) != TCB_OK)
-        break;
-      if ((rc = norm_gemm(m, gu, m->ffn_norm[l], M, m->pgu, s)) != TCB_OK) break;
-      // SwiGLU in the down product's activation prologue, else a pass of its own
-      tcb::TcPrologue sw;
-      sw.kind = tcb::kTcProSwiglu;
-      rc = tcb::qgemm_tc_prologue(m->ctx, dn.type, M, dn.N, dn.K, dn.w, m->pgu, 2L * F, m->px, dn.N, acc, sw, s);
-      if (rc == TCB_ERR_UNSUPPORTED) {
-        const long na = (long)M * F;
-        k_swiglu_rows<<<(int)((na + 255) / 256 < 4096 ? (na + 255) / 256 : 4096), 256, 0, s>>>(m->pgu, m->pa, F, na);
-        rc = tcb_qgemm(m->ctx, dn.type, M, dn.N, dn.K, dn.w, m->pa, TCB_F32, dn.K, m->px, TCB_F32, dn.N, acc, s);
-      }
-      if (rc != TCB_OK || (rc = reduce(M)) != TCB_OK) break;
-    }
-    if (rc == TCB_OK && (e = cudaGetLastError()) != cudaSuccess) return fail(m, e);
-  }
-  if (rc != TCB_OK) return rc;
-  k_prefill_done<<<1, 256, 0, s>>>(m->prompt, n, m->pos, m->tok, m->hist);
-  if ((e = cudaGetLastError()) != cudaSuccess) return fail(m, e);
-  m->host_pos = n - 1;
-  return TCB_OK;
+  if (total > 0 && (rc = pf_alloc(m0, (int)total, s)) == TCB_OK) rc = prefill_pass(m0, sq.data(), (int)sq.size(), s);
+  for (int i = 0; i < count && rc == TCB_OK; i++)
+    if (ms[i]->host_n > 1) rc = finish_prefill(ms[i], s);
+  return rc;
 }
 
 int tcb_llama_step(tcb_llama *m, void *stream) {

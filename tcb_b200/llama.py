@@ -199,6 +199,7 @@ def _bind():
     L.tcb_llama_start.argtypes = [P, P, ctypes.c_int, P]
     L.tcb_llama_step.argtypes = [P, P]
     L.tcb_llama_prefill.argtypes = [P, P]
+    L.tcb_llama_prefill_batch.argtypes = [P, ctypes.c_int, P]
     L.tcb_llama_capture.argtypes = [P, P]
     L.tcb_llama_buffers.argtypes = [P, ctypes.POINTER(P), ctypes.POINTER(P)]
     L.tcb_nccl_unique_id.argtypes = [P]
@@ -314,6 +315,15 @@ class Llama:
             self.close()
         except Exception:
             pass
+
+
+def prefill_batch(engines: list, stream=None):
+    """The prompt pass of several engines on the same model at once (each
+    started with its own prompt): one set of rows through the products."""
+    if not engines:
+        return
+    arr = (ctypes.c_void_p * len(engines))(*[e._h.value for e in engines])
+    engines[0]._check(engines[0]._L.tcb_llama_prefill_batch(arr, len(engines), _stream(stream)), "prefill_batch")
 
 
 def nccl_unique_id() -> bytes:

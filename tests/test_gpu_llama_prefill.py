@@ -7,7 +7,8 @@ equal (a mismatch only where the reference's top-2 margin is a tie at float
 precision), in one pass and in several (row batches that start off the
 64-position tile grid, a last batch small enough for the non-tensor-core
 product), for 2 and 4 query heads per KV head; the captured graph continues
-from a prefilled cache exactly as the eager steps do."""
+from a prefilled cache exactly as the eager steps do; several engines fed in
+one batched pass (tcb_llama_prefill_batch) give each one's own result."""
 import numpy as np
 import pytest
 
@@ -113,3 +114,37 @@ def test_prefill_state(setup):
     m.prefill()
     m.step(1)
     m.close()
+
+
+def test_prefill_batch(setup):
+    """Several engines on the same model fed in one pass (the products over
+    all their rows at once, attention per sequence): the same first-step
+    logits as each fed alone, the reference's tokens for the full prompt."""
+    cfg, ctx, dev, prompt, ref_toks, ref_logits, margins = setup
+    prompts = [prompt, prompt[:150][::-1].copy(), prompt[40:117].copy(), prompt[:1].copy()]
+    single = []
+    for p in prompts:
+        m = llama.Llama(ctx, dev)
+        m.start(p)
+        m.prefill()
+        m.step(1)
+        single.append(m.logits())
+        m.close()
+    engines = [llama.Llama(ctx, dev) for _ in prompts]
+    for m, p in zip(engines, prompts):
+        m.start(p)
+    llama.prefill_batch(engines)
+    for i, (m, p) in enumerate(zip(engines, prompts)):
+        m.step(1)
+        assert rel_l2(m.logits(), single[i]) <= 1e-4, i
+    engines[0].step(GEN - 1)
+    toks = engines[0].tokens(NPROMPT + GEN)
+    assert check_tokens(toks, ref_toks, ref_logits, margins, NPROMPT) >= NPROMPT + 8
+    # an engine that has stepped, or one given twice, is refused
+    with pytest.raises(T.TcbError):
+        llama.prefill_batch(engines[:2])
+    engines[1].start(prompts[1])
+    with pytest.raises(T.TcbError):
+        llama.prefill_batch([engines[1], engines[1]])
+    for m in engines:
+        m.close()
