@@ -38,7 +38,7 @@ sys.path.insert(0, ROOT)
 METRIC = "Q4_K matvec HBM GB/s (% of peak); 8B-shape Q4_K_M decode tokens/sec @ batch 1"
 WORKLOAD = {"workload": "q4_k_matvec", "wtype": "q4_k", "N": 11008, "K": 4096, "batch": 1,
             "x_dtype": "f32", "path": "float"}
-Q4_K = 12
+Q4_0, Q8_0, Q4_K = 2, 8, 12
 
 
 def algorithmic_bytes(N: int, K: int, M: int = 1) -> int:
@@ -191,6 +191,70 @@ def decode_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
         "gpu_launches_per_token": 1 + 6 * cfg.n_layers + 4, "last_tokens": [int(v) for v in toks[-4:]],
         "timing": "CUDA events around 256 graph replays on the engine's stream",
     }
+
+
+def matvec_table_bench(ctx, rank: int, peak_gbs: float) -> dict:
+    """BASELINE configs 1 and 2 beside the headline shape: Q8_0 4096x4096 at
+    batch 1 (float path and int8-activation path), Q4_0 and Q4_K at
+    11008x4096 and 4096x11008 for batch 1, 4 and 8 (f32 x ~ N(0, 1), f32 y).
+    Each case sweeps a cold ring of at least 512 MiB of distinct weight copies
+    (one code byte per block flipped), captured in a CUDA graph; CUDA events
+    around 20 sweeps after 3 warm-up sweeps.  GB/s = algorithmic bytes
+    (weight blocks + M*K*4 + M*N*4) per call / time."""
+    import torch
+
+    from tcb_b200 import synth
+
+    code_off = {Q8_0: 2, Q4_0: 2, Q4_K: 16}
+    code_len = {Q8_0: 32, Q4_0: 16, Q4_K: 128}
+    blk = {Q8_0: (32, 34), Q4_0: (32, 18), Q4_K: (256, 144)}
+    names = {Q8_0: "q8_0", Q4_0: "q4_0", Q4_K: "q4_k"}
+    cases = [(Q8_0, 4096, 4096, (1,), (False, True))]
+    for wt in (Q4_0, Q4_K):
+        for N, K in ((11008, 4096), (4096, 11008)):
+            cases.append((wt, N, K, (1, 4, 8), (False,)))
+    rows = []
+    stream = torch.cuda.Stream()
+    for wt, N, K, Ms, modes in cases:
+        E, B = blk[wt]
+        wbytes = N * K // E * B
+        ring = max(4, -(-512 * 2 ** 20 // wbytes))
+        base = torch.from_numpy(synth.weight(wt, N, K, seed=41 + rank)).cuda()
+        weights = [base]
+        for i in range(1, ring):
+            w = base.clone()
+            w[code_off[wt] + (i % code_len[wt])::B] ^= 0x11
+            weights.append(w)
+        for M in Ms:
+            x = torch.from_numpy(synth.activations(M, K, seed=43 + rank)).cuda()
+            y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+            for act8 in modes:
+                def sweep():
+                    for w in weights:
+                        ctx.qgemm(wt, w, x, y, stream=stream, act8=act8)
+
+                with torch.cuda.stream(stream):
+                    sweep()
+                    stream.synchronize()
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g, stream=stream):
+                        sweep()
+                    for _ in range(3):
+                        g.replay()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    for _ in range(20):
+                        g.replay()
+                    e1.record(stream)
+                    e1.synchronize()
+                us = e0.elapsed_time(e1) * 1e3 / (20 * ring)
+                gbs = (wbytes + M * K * 4 + M * N * 4) / (us * 1e-6) / 1e9
+                rows.append({"wtype": names[wt], "N": N, "K": K, "M": M, "path": "int8 activations" if act8 else "float",
+                             "us_per_call": round(us, 2), "GB/s": round(gbs, 1), "frac": round(gbs / peak_gbs, 4)})
+                del g
+        del weights, base
+    return {"timing": "CUDA graph of one sweep over a cold weight ring (>= 512 MiB), 20 sweeps",
+            "peak_gbs": peak_gbs, "cases": rows}
 
 
 def model_prefill_bench(ctx, peaks: dict, layers: int = 0) -> dict:
@@ -396,6 +460,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the 8B-shape decode measurement")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill-product measurement")
+    ap.add_argument("--no-configs", action="store_true", help="skip the BASELINE config 1/2 matvec table")
     ap.add_argument("--only-model-prefill", action="store_true",
                     help="run only the 8B model prefill and print its object (for profiling)")
     ap.add_argument("--layers", type=int, default=0,
@@ -513,6 +578,7 @@ def main():
         decode = (decode_bench(ctx, rank, world, peaks["hbm_gbs"]) if world == 1
                   else decode_tp_bench(ctx, rank, world, peaks["hbm_gbs"]))
 
+    table = matvec_table_bench(ctx, rank, peaks["hbm_gbs"]) if world == 1 and not args.no_configs else None
     prefill = model_prefill = None
     if world == 1 and not args.no_prefill:
         prefill = prefill_bench(ctx, rank, peaks, not args.no_cpu_baseline)
@@ -541,6 +607,8 @@ def main():
             line["prefill"] = prefill
         if model_prefill is not None:
             line["model_prefill"] = model_prefill
+        if table is not None:
+            line["matvec_configs"] = table
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)

@@ -61,10 +61,17 @@ int ensure_ws(tcb_ctx *ctx, size_t bytes) {
 
 // the batch-1 tensor-core path: plan, scratch, launch.  *taken = false when
 // the shape goes to the portable kernel instead.
+// The batch-1 kernels take every M below the tensor-core path's minimum, one
+// activation row per launch: each launch streams the weight blocks again
+// (from L2 after the first), which still beats the portable kernel by an
+// order of magnitude at M = 2..8.  A row's result does not depend on the
+// other rows (the int8-activation fold is per row), so this is the same
+// product as one launch over all rows.
 int run_matvec(tcb_ctx *ctx, int wtype, int act8, int M, int N, int K, const void *w, const void *x, int xdt,
-               void *c, int cdt, int accumulate, cudaStream_t s, bool *taken) {
+               long ldx, void *c, int cdt, long ldc, int accumulate, cudaStream_t s, bool *taken) {
   *taken = false;
-  tcb::MvPlan pl = tcb::matvec_plan(wtype, act8, M, N, K, w, ctx->sms);
+  if (M < 1 || M >= tcb::kTcMinM) return TCB_OK;
+  tcb::MvPlan pl = tcb::matvec_plan(wtype, act8, 1, N, K, w, ctx->sms);
   if (!pl.ok) return TCB_OK;
   if (pl.split_bytes > ctx->sk_cap) {
     // grow the split-K scratch (after the device has finished with the old one)
@@ -83,9 +90,14 @@ int run_matvec(tcb_ctx *ctx, int wtype, int act8, int M, int N, int K, const voi
     }
   }
   *taken = true;
-  cudaError_t e =
-      tcb::matvec_launch(pl, wtype, act8, N, K, w, x, xdt, c, cdt, accumulate, ctx->derr, s, nullptr, 0, ctx->sk);
-  return e == cudaSuccess ? TCB_OK : cuda_fail(ctx, e);
+  for (int m = 0; m < M; m++) {
+    const void *xm = static_cast<const char *>(x) + (size_t)m * ldx * elem_size(xdt);
+    void *cm = static_cast<char *>(c) + (size_t)m * ldc * elem_size(cdt);
+    cudaError_t e =
+        tcb::matvec_launch(pl, wtype, act8, N, K, w, xm, xdt, cm, cdt, accumulate, ctx->derr, s, nullptr, 0, ctx->sk);
+    if (e != cudaSuccess) return cuda_fail(ctx, e);
+  }
+  return TCB_OK;
 }
 
 }  // namespace
@@ -202,7 +214,7 @@ int tcb_qgemm(tcb_ctx *ctx, int wtype, int M, int N, int K, const void *w, const
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (K == 0) return empty_sum(ctx, M, N, c, cdtype, ldc, accumulate, s);
   bool taken = false;
-  rc = run_matvec(ctx, wtype, 0, M, N, K, w, x, xdtype, c, cdtype, accumulate, s, &taken);
+  rc = run_matvec(ctx, wtype, 0, M, N, K, w, x, xdtype, ldx, c, cdtype, ldc, accumulate, s, &taken);
   if (taken || rc != TCB_OK) return rc;
   if (tcb::tc_eligible(wtype, M, N, K, w)) {
     if ((rc = ensure_ws(ctx, tcb::tc_workspace_bytes(wtype, M, N, K))) != TCB_OK) return rc;
@@ -224,7 +236,7 @@ int tcb_qgemm_act8(tcb_ctx *ctx, int wtype, int M, int N, int K, const void *w, 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (K == 0) return empty_sum(ctx, M, N, c, cdtype, ldc, accumulate, s);
   bool taken = false;
-  rc = run_matvec(ctx, wtype, 1, M, N, K, w, x, xdtype, c, cdtype, accumulate, s, &taken);
+  rc = run_matvec(ctx, wtype, 1, M, N, K, w, x, xdtype, ldx, c, cdtype, ldc, accumulate, s, &taken);
   if (taken || rc != TCB_OK) return rc;
   const int blk = tcb::block_elems(wtype);
   std::lock_guard<std::mutex> lock(ctx->mu);
