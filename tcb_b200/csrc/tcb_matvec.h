@@ -17,6 +17,7 @@ struct MvPlan {
   int grid;
   int ksplit, cpk;             // K splits and chunks per split (kind 2); 1 when not split
   size_t split_bytes;          // device scratch a launch needs (zeroed once; launches leave it zeroed), 0 if none
+  int rows, xstride;           // kind 1: rows of x a launch takes, bytes between their digit regions
   alignas(64) unsigned char tmap[128];  // TMA descriptor of the weight (CUtensorMap)
 };
 
@@ -28,10 +29,12 @@ MvPlan matvec_plan(int wtype, int act8, int M, int N, int K, const void *w, int 
 // Q4_K float path (kind 1).  With nw, the product is W * rms(x): an
 // RMSNorm (x / sqrt(mean(x^2) + eps) * nw, K elements, f32 x, finite x
 // assumed) is fused into the prologue.
-MvPlan q4k_plan(int N, int K, const void *w, int sms);
+// mr (1, 2, 4, 8): the most rows of x one launch takes; a launch of M <= mr
+// rows (row strides ldx, ldc) streams the weights once for all of them.
+MvPlan q4k_plan(int N, int K, const void *w, int sms, int mr = 1);
 cudaError_t q4k_launch(const MvPlan &pl, int N, int K, const void *w, const void *x, int xdt, void *c, int cdt,
                        int accumulate, int *err, cudaStream_t s, const float *nw = nullptr, float eps = 0.f,
-                       const void *pf = nullptr, size_t pf_bytes = 0);
+                       const void *pf = nullptr, size_t pf_bytes = 0, int M = 1, long ldx = 0, long ldc = 0);
 
 // Q6_K float path (kind 2).  With gated, x holds [G | U] (2K elements) and
 // the input is silu(G) * U (a SwiGLU gate fused into the prologue).

@@ -87,6 +87,9 @@ struct Params {
   float eps;
   const void *pf;   // weights of the next kernel of a chain, prefetched into L2 (or nullptr)
   size_t pf_bytes;
+  int M;            // activation rows of this launch (1 .. MR of the kernel)
+  long ldx, ldc;    // row strides of x and c, elements
+  int xstride;      // bytes between the x regions of consecutive rows
 };
 
 // x region: [nb][kFrag] B fragments ([set s][round pair rp][column n][16
@@ -150,20 +153,20 @@ __device__ __forceinline__ void load8(const void *x, int e, int xdt, bool vec, f
 // sigma = 1/id, not exact, so it is the hardware reciprocal.  Returns false
 // if a sub-block sum is not finite (a NaN or Inf in x, or a sum that
 // overflows, which only sends the call down the exact fp32 path).
-__device__ bool prep_warp(const Params &a, uint8_t *xr, int own, int lane, float &ss, uint64_t *xgo) {
+__device__ bool prep_warp(const Params &a, const void *x, uint8_t *xr, int own, int lane, float &ss, uint64_t *xgo) {
   constexpr float MAGIC = 12582912.0f;
   constexpr int NB = 4;  // blocks in flight per lane
   uint8_t *frag = xr;
   float *scl = reinterpret_cast<float *>(xr + a.nb * kFrag);
-  const bool vec = (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
-  bool fin = true, told = false;
+  const bool vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  bool fin = true, told = xgo == nullptr;
   ss = 0.f;
   for (int base = own; base < a.nb; base += kC * NB) {
     float xv[NB][8];
 #pragma unroll
     for (int j = 0; j < NB; j++) {
       const int bg = base + kC * j;
-      if (bg < a.nb) load8(a.x, bg * 256 + 8 * lane, a.xdt, vec, xv[j]);
+      if (bg < a.nb) load8(x, bg * 256 + 8 * lane, a.xdt, vec, xv[j]);
     }
     if (!told) {
       // the first x loads are out: the producer may issue the rest of the
@@ -297,30 +300,44 @@ __device__ __forceinline__ void epi16(const uint4 (&hd)[2], const float4 sg, con
 
 // A warp's tile partials (rows g, g+8 of each 16-row slice, each summed over
 // the four lanes of its group) into slot ti % kSlots for the epilogue warp.
-__device__ __forceinline__ bool tile_partial(int ti, float (&acc)[2 * kHalves], float *part, uint64_t *tdone,
-                                             uint64_t *tfree, int warp, int lane, int *err) {
+// Partials of activation row m of slot s: part + ((s * MR + m) * kC + warp) * kRows.
+template <int MR>
+__device__ __forceinline__ bool tile_partial(int ti, float (&acc)[MR][2 * kHalves], int M, float *part,
+                                             uint64_t *tdone, uint64_t *tfree, int warp, int lane, int *err) {
 #pragma unroll
-  for (int i = 0; i < 2 * kHalves; i++) {
-    acc[i] += __shfl_xor_sync(0xFFFFFFFFu, acc[i], 1);
-    acc[i] += __shfl_xor_sync(0xFFFFFFFFu, acc[i], 2);
-  }
+  for (int m = 0; m < MR; m++)
+#pragma unroll
+    for (int i = 0; i < 2 * kHalves; i++) {
+      acc[m][i] += __shfl_xor_sync(0xFFFFFFFFu, acc[m][i], 1);
+      acc[m][i] += __shfl_xor_sync(0xFFFFFFFFu, acc[m][i], 2);
+    }
   const int slot = ti % kSlots;
   bool ok = true;
   if (lane == 0) ok = spin_bar(&tfree[slot], (uint32_t)(((ti / kSlots) & 1) ^ 1), err);
   if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) return false;
-  float *pt = part + (slot * kC + warp) * kRows + (lane >> 2);
   if ((lane & 3) == 0) {
 #pragma unroll
-    for (int i = 0; i < 2 * kHalves; i++) pt[8 * i] = acc[i];
+    for (int m = 0; m < MR; m++) {
+      if (m >= M) break;
+      float *pt = part + ((slot * MR + m) * kC + warp) * kRows + (lane >> 2);
+#pragma unroll
+      for (int i = 0; i < 2 * kHalves; i++) pt[8 * i] = acc[m][i];
+    }
   }
   __syncwarp();
   if (lane == 0) mbar_arrive(&tdone[slot]);
 #pragma unroll
-  for (int i = 0; i < 2 * kHalves; i++) acc[i] = 0.f;
+  for (int m = 0; m < MR; m++)
+#pragma unroll
+    for (int i = 0; i < 2 * kHalves; i++) acc[m][i] = 0.f;
   return true;
 }
 
-__global__ void __launch_bounds__(32 * kWarps, 2) k_mvq4k(const __grid_constant__ CUtensorMap tmap, const Params a) {
+// MR: the most activation rows a launch takes (a.M <= MR); one CTA per SM
+// when MR > 1 (more registers for the row accumulators).
+template <int MR>
+__global__ void __launch_bounds__(32 * kWarps, MR == 1 ? 2 : 1) k_mvq4k(const __grid_constant__ CUtensorMap tmap,
+                                                                       const Params a) {
   extern __shared__ __align__(128) uint8_t sm[];
   uint64_t *full = reinterpret_cast<uint64_t *>(sm + kBarOff);  // [S]     copy engine -> compute
   uint64_t *empty = full + 8;                                  // [S]     compute -> producer
@@ -328,10 +345,11 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq4k(const __grid_constant_
   uint64_t *tfree = full + 24;                                 // [slots] tile partials summed
   uint64_t *xgo = full + 20;                                   // compute warps -> producer: x loads issued
   int *flag = reinterpret_cast<int *>(sm + kFlagOff);
-  float *part = reinterpret_cast<float *>(sm + kPartOff);      // [slots][kC][kRows]
-  uint8_t *xr = sm + kXOff;
+  float *part = reinterpret_cast<float *>(sm + kPartOff);      // [slots][MR][kC][kRows]
+  uint8_t *xr = sm + kPartOff + MR * kPartBytes;               // [MR] x regions, a.xstride apart
   uint8_t *stages = sm + a.soff;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int M = MR == 1 ? 1 : a.M;  // rows of x (a compile-time 1 for the batch-1 kernel)
   const int my_tiles = (a.tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
   const int nstages = my_tiles * a.nch;
 
@@ -380,10 +398,17 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq4k(const __grid_constant_
   // kernel of the stream
   pdl_wait();
   if (warp < kC) {
-    if (warp == 0) reinterpret_cast<uint4 *>(xr + a.nb * (kFrag + kScl))[lane] = make_uint4(0u, 0u, 0u, 0u);
-    float ss;
-    if (!prep_warp(a, xr, (warp + (int)blockIdx.x) & (kBlk - 1), lane, ss, xgo) && lane == 0) *flag = 1;
-    if (lane == 0) reinterpret_cast<float *>(sm + kNormOff)[warp] = ss;
+    const size_t xel = a.xdt == TCB_F32 ? 4 : 2;
+    for (int m = 0; m < M; m++) {
+      uint8_t *xm = xr + (size_t)m * a.xstride;
+      if (warp == 0) reinterpret_cast<uint4 *>(xm + a.nb * (kFrag + kScl))[lane] = make_uint4(0u, 0u, 0u, 0u);
+      float ss;
+      const void *xrow = static_cast<const char *>(a.x) + (size_t)m * a.ldx * xel;
+      if (!prep_warp(a, xrow, xm, (warp + (int)blockIdx.x) & (kBlk - 1), lane, ss, m == 0 ? xgo : nullptr) &&
+          lane == 0)
+        *flag = 1;
+      if (m == 0 && lane == 0) reinterpret_cast<float *>(sm + kNormOff)[warp] = ss;
+    }
   }
   asm volatile("bar.sync 1, %0;" ::"n"(32 * (kC + 1)) : "memory");
   const bool slow = *flag != 0;
@@ -403,17 +428,28 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq4k(const __grid_constant_
     for (int ti = 0; ti < my_tiles; ti++) {
       const int row = ((int)blockIdx.x + ti * (int)gridDim.x) * kRows + lane;
       const bool mine = lane < kRows && row < a.N;
-      const float cold = (a.accumulate && mine) ? load_out(a.c, row, a.cdt) : 0.f;
+      float cold[MR], v[MR];
+#pragma unroll
+      for (int m = 0; m < MR; m++)
+        cold[m] = (a.accumulate && mine && m < M) ? load_out(a.c, (long)m * a.ldc + row, a.cdt) : 0.f;
       const int slot = ti % kSlots;
       if (!spin_bar_ns(&tdone[slot], (uint32_t)((ti / kSlots) & 1), a.err, 128)) return;
-      const float *pt = part + slot * kC * kRows + (lane < kRows ? lane : 0);
-      float v = 0.f;
 #pragma unroll
-      for (int j = 0; j < kC; j++) v += pt[((j - rot) & (kBlk - 1)) * kRows];
-      if (a.nw) v = __fdiv_rn(v, rms);
+      for (int m = 0; m < MR; m++) {
+        v[m] = 0.f;
+        if (m >= M) continue;
+        const float *pt = part + (slot * MR + m) * kC * kRows + (lane < kRows ? lane : 0);
+#pragma unroll
+        for (int j = 0; j < kC; j++) v[m] += pt[((j - rot) & (kBlk - 1)) * kRows];
+        if (a.nw) v[m] = __fdiv_rn(v[m], rms);
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&tfree[slot]);
-      if (mine) store_out_old(a.c, row, a.cdt, v, a.accumulate != 0, cold);
+      if (mine) {
+#pragma unroll
+        for (int m = 0; m < MR; m++)
+          if (m < M) store_out_old(a.c, (long)m * a.ldc + row, a.cdt, v[m], a.accumulate != 0, cold[m]);
+      }
     }
     return;
   }
@@ -428,7 +464,7 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq4k(const __grid_constant_
     const int g = lane >> 2;
     const int own = (warp + (int)blockIdx.x) & (kBlk - 1);
     const int last_ch = own < a.nb ? (a.nb - 1 - own) / kBlk : -1;  // the warp's last chunk of a tile
-    float acc[2 * kHalves] = {};
+    float acc[MR][2 * kHalves] = {};
     int it = 0;
     for (int ti = 0; ti < my_tiles; ti++) {
       for (int ch = 0; ch < a.nch; ch++, it++) {
@@ -437,31 +473,40 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq4k(const __grid_constant_
         if (lane == 0) ok = wait_bar(&full[buf], (uint32_t)((it / a.S) & 1), a.err);
         if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) return;
         const bool has = ch <= last_ch;
-        int D[kHalves][2][4];
-        uint4 hd[kHalves][2];
-        float4 sg = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (has) {
-          const int bg = ch * kBlk + own;
-          const uint8_t *r0 = stages + buf * kBoxBytes + g * kPitch + own * 144;
-          uint4 B[2][2];
-          bfrag(Q.xb + bg * Q.xs, B);
+        const int bg = ch * kBlk + own;
+        const uint8_t *r0 = stages + buf * kBoxBytes + g * kPitch + own * 144;
+        // the rows of x one after another on the staged block; the stage is
+        // released once the last row's operands are read
 #pragma unroll
-          for (int h = 0; h < kHalves; h++) mma16(r0 + 16 * h * kPitch, B, Q, D[h]);
+        for (int m = 0; m < MR; m++) {
+          if (m >= M) break;  // uniform
+          int D[kHalves][2][4];
+          uint4 hd[kHalves][2];
+          float4 sg = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (has) {
+            uint4 B[2][2];
+            bfrag(Q.xb + m * a.xstride + bg * Q.xs, B);
 #pragma unroll
-          for (int h = 0; h < kHalves; h++)
+            for (int h = 0; h < kHalves; h++) mma16(r0 + 16 * h * kPitch, B, Q, D[h]);
 #pragma unroll
-            for (int r = 0; r < 2; r++)
-              hd[h][r] = *reinterpret_cast<const uint4 *>(r0 + (16 * h + 8 * r) * kPitch);
-          sg = *reinterpret_cast<const float4 *>(Q.scl + bg * 16);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[buf]);
-        if (has) {
+            for (int h = 0; h < kHalves; h++)
 #pragma unroll
-          for (int h = 0; h < kHalves; h++) epi16(hd[h], sg, Q, D[h], acc[2 * h], acc[2 * h + 1]);
+              for (int r = 0; r < 2; r++)
+                hd[h][r] = *reinterpret_cast<const uint4 *>(r0 + (16 * h + 8 * r) * kPitch);
+            sg = *reinterpret_cast<const float4 *>(reinterpret_cast<const uint8_t *>(Q.scl + bg * 16) +
+                                                    m * a.xstride);
+          }
+          if (m == M - 1) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[buf]);
+          }
+          if (has) {
+#pragma unroll
+            for (int h = 0; h < kHalves; h++) epi16(hd[h], sg, Q, D[h], acc[m][2 * h], acc[m][2 * h + 1]);
+          }
         }
         if ((ch == last_ch || (last_ch < 0 && ch == a.nch - 1)) &&
-            !tile_partial(ti, acc, part, tdone, tfree, warp, lane, a.err))
+            !tile_partial<MR>(ti, acc, M, part, tdone, tfree, warp, lane, a.err))
           return;
       }
     }
@@ -492,14 +537,17 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq4k(const __grid_constant_
       }
       return;
     }
+    const size_t xel = a.xdt == TCB_F32 ? 4 : 2;
     for (int ti = 0; ti < my_tiles; ti++) {
       const int r0 = ((int)blockIdx.x + ti * (int)gridDim.x) * kRows;
-      for (int n = r0 + widx; n < r0 + kRows && n < a.N; n += kC + 1) {
-        float accs[1] = {0.0f};
-        lane_row_float<TCB_Q4_K, 1>(a.w + (long)n * rowBytes, a.K, lane, XGlobal{a.x, 0, a.xdt}, accs);
-        const float v = warp_sum(accs[0]);
-        if (lane == 0) store_out(a.c, n, a.cdt, v, a.accumulate != 0);
-      }
+      for (int n = r0 + widx; n < r0 + kRows && n < a.N; n += kC + 1)
+        for (int m = 0; m < M; m++) {
+          float accs[1] = {0.0f};
+          const void *xrow = static_cast<const char *>(a.x) + (size_t)m * a.ldx * xel;
+          lane_row_float<TCB_Q4_K, 1>(a.w + (long)n * rowBytes, a.K, lane, XGlobal{xrow, 0, a.xdt}, accs);
+          const float v = warp_sum(accs[0]);
+          if (lane == 0) store_out(a.c, (long)m * a.ldc + n, a.cdt, v, a.accumulate != 0);
+        }
     }
   }
 }
@@ -511,21 +559,26 @@ constexpr int kSmemTwo = 113 * 1024;  // per CTA with two CTAs on an SM
 constexpr int kSmemOne = 227 * 1024;
 }  // namespace
 
-// The plan of a Q4_K float-path matvec (M = 1): two CTAs per SM when two
-// stages fit in half an SM's shared memory, else one CTA with more stages.
-MvPlan q4k_plan(int N, int K, const void *w, int sms) {
+// The plan of a Q4_K float-path matvec of up to mr (1, 2, 4 or 8) rows of x
+// per launch: two CTAs per SM when two stages fit in half an SM's shared
+// memory (mr = 1 only), else one CTA with more stages.  Every row of x has
+// its own digit region and tile partials; the plan fails (ok = false) when
+// fewer than two stages fit beside them.
+MvPlan q4k_plan(int N, int K, const void *w, int sms, int mr) {
   using namespace mvk;
   MvPlan pl{};
   const int nb = K / 256;
   const long rowBytes = (long)nb * 144;
   if (K % 256 || nb == 0 || rowBytes % 16 || reinterpret_cast<uintptr_t>(w) % 16) return pl;
+  if (mr != 1 && mr != 2 && mr != 4 && mr != 8) return pl;
   auto enc = tensor_map_encoder();
   if (!enc) return pl;
-  const int base = (kXOff + x_bytes(nb) + 127) & ~127;
+  const int xstride = (x_bytes(nb) + 127) & ~127;
+  const int base = (kPartOff + mr * kPartBytes + mr * xstride + 127) & ~127;
   int S, per_sm;
   // two CTAs per SM when the tiles outnumber the SMs; otherwise one CTA per
   // SM streams its (long) rows through the deeper pipeline one CTA affords
-  if (base + 2 * kBoxBytes <= kSmemTwo && (N + kRows - 1) / kRows > sms) {
+  if (mr == 1 && base + 2 * kBoxBytes <= kSmemTwo && (N + kRows - 1) / kRows > sms) {
     S = (kSmemTwo - base) / kBoxBytes;
     if (S > 6) S = 6;
     per_sm = 2;
@@ -547,6 +600,8 @@ MvPlan q4k_plan(int N, int K, const void *w, int sms) {
   pl.smem = base + S * kBoxBytes;
   pl.grid = pl.tiles < per_sm * sms ? pl.tiles : per_sm * sms;
   pl.kind = 1;
+  pl.rows = mr;
+  pl.xstride = xstride;
   CUtensorMap tm;
   cuuint64_t gdim[2] = {(cuuint64_t)(rowBytes / 8), (cuuint64_t)N};
   cuuint64_t gstride[1] = {(cuuint64_t)rowBytes};
@@ -564,8 +619,9 @@ MvPlan q4k_plan(int N, int K, const void *w, int sms) {
 
 cudaError_t q4k_launch(const MvPlan &pl, int N, int K, const void *w, const void *x, int xdt, void *c, int cdt,
                        int accumulate, int *err, cudaStream_t s, const float *nw, float eps, const void *pf,
-                       size_t pf_bytes) {
+                       size_t pf_bytes, int M, long ldx, long ldc) {
   using namespace mvk;
+  if (M < 1 || M > pl.rows || (M > 1 && nw)) return cudaErrorInvalidValue;
   Params a{};
   a.w = static_cast<const uint8_t *>(w);
   a.N = N;
@@ -585,9 +641,17 @@ cudaError_t q4k_launch(const MvPlan &pl, int N, int K, const void *w, const void
   a.eps = eps;
   a.pf = pf;
   a.pf_bytes = pf_bytes;
+  a.M = M;
+  a.ldx = ldx;
+  a.ldc = ldc;
+  a.xstride = pl.xstride;
   CUtensorMap tm;
   memcpy(&tm, pl.tmap, sizeof tm);
-  cudaError_t e = cudaFuncSetAttribute(k_mvq4k, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem);
+  void (*kern)(const CUtensorMap, const Params) = pl.rows == 8   ? k_mvq4k<8>
+                                                  : pl.rows == 4 ? k_mvq4k<4>
+                                                  : pl.rows == 2 ? k_mvq4k<2>
+                                                                 : k_mvq4k<1>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.grid);
@@ -599,7 +663,7 @@ cudaError_t q4k_launch(const MvPlan &pl, int N, int K, const void *w, const void
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_mvq4k, tm, a);
+  return cudaLaunchKernelEx(&cfg, kern, tm, a);
 }
 
 }  // namespace tcb

@@ -402,6 +402,28 @@ def test_fast_path_non_finite_x(ctx, oracle, fmt):
             assert np.array_equal(got[fin], want[fin])
 
 
+@pytest.mark.parametrize("fmt", FORMATS)
+@pytest.mark.parametrize("M", [3, 8])
+def test_fast_path_non_finite_rows(ctx, oracle, fmt, M):
+    """Several rows of x, one with a NaN/Inf (the Q4_K kernel takes up to 8
+    rows per launch): NaN where TR has NaN and the same values in that row,
+    the other rows within the float tolerance."""
+    e, _ = T.BLOCK[fmt]
+    N, K = 40, 16 * e
+    raw = small_scale(oracle, fmt, 5, N * K // e)
+    for bad in (np.nan, np.inf):
+        x = np.random.default_rng(2).standard_normal((M, K), dtype=np.float32)
+        x[1, K // 3] = bad
+        c = torch.zeros((M, N), dtype=torch.float32, device="cuda")
+        ctx.qgemm(fmt, dev(raw), dev(x), c, accumulate=True)
+        got, want = host(c), oracle.qgemm_float(fmt, x, raw, N)
+        assert np.array_equal(np.isnan(got), np.isnan(want))
+        fin = ~np.isnan(want[1])
+        assert np.array_equal(got[1][fin], want[1][fin])
+        good = [m for m in range(M) if m != 1]
+        assert rel_l2(got[good], want[good]) <= REL_L2
+
+
 @pytest.mark.parametrize("NK", [(32768, 2560), (40000, 4096)])
 def test_q6k_wide_kernel(ctx, oracle, NK):
     """Products of at least 32768 rows take the k-slot Q6_K kernel (a full
