@@ -71,21 +71,21 @@ int run_matvec(tcb_ctx *ctx, int wtype, int act8, int M, int N, int K, const voi
                long ldx, void *c, int cdt, long ldc, int accumulate, cudaStream_t s, bool *taken) {
   *taken = false;
   if (M < 1 || M >= tcb::kTcMinM) return TCB_OK;
-  if (wtype == TCB_Q4_K && !act8 && M > 1) {
-    // the Q4_K kernel takes up to 8 rows per launch, streaming the weights
-    // once for all of them (fewer rows per launch when their digit regions
-    // leave too little shared memory for the stages)
+  if (!act8 && M > 1) {
+    // the float-path kernels take up to 8 rows per launch, streaming the
+    // weights once for all of them (fewer rows per launch when their digit
+    // regions leave too little shared memory for the stages)
     tcb::MvPlan pq{};
     for (int mr = 8; mr >= 2 && !pq.ok; mr /= 2)
-      if (mr <= 2 * M - 1 || mr == 2) pq = tcb::q4k_plan(N, K, w, ctx->sms, mr);
+      if (mr <= 2 * M - 1 || mr == 2) pq = tcb::matvec_plan_rows(wtype, N, K, w, ctx->sms, mr);
     if (pq.ok) {
       *taken = true;
       for (int m0 = 0; m0 < M; m0 += pq.rows) {
         const int rows = M - m0 < pq.rows ? M - m0 : pq.rows;
         const void *xm = static_cast<const char *>(x) + (size_t)m0 * ldx * elem_size(xdt);
         void *cm = static_cast<char *>(c) + (size_t)m0 * ldc * elem_size(cdt);
-        cudaError_t e = tcb::q4k_launch(pq, N, K, w, xm, xdt, cm, cdt, accumulate, ctx->derr, s, nullptr, 0.f,
-                                        nullptr, 0, rows, ldx, ldc);
+        cudaError_t e = tcb::matvec_launch(pq, wtype, 0, N, K, w, xm, xdt, cm, cdt, accumulate, ctx->derr, s, nullptr,
+                                           0, ctx->sk, rows, ldx, ldc);
         if (e != cudaSuccess) return cuda_fail(ctx, e);
       }
       return TCB_OK;

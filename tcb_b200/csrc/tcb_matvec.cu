@@ -81,6 +81,9 @@ struct Params {
   int xoff, toff, soff;   // shared-memory offsets: x region, int8 terms, stages
   const void *pf;         // weights of the next kernel of a chain, prefetched into L2 (or nullptr)
   size_t pf_bytes;
+  int M;                  // rows of x of this launch (float path: 1 .. MR of the kernel)
+  long ldx, ldc;          // row strides of x and c, elements
+  int xstride;            // bytes between the x regions of consecutive rows
 };
 
 // x region layout (float path): NDIG digit planes of K int8, then per group
@@ -565,9 +568,14 @@ constexpr int kWarpsAll = kConsumers + 2;
 constexpr int kPartSlots = 8;             // tile partial slots in flight
 constexpr int kBarBytes = 1024;
 
-template <int W, bool ACT8>
+// MR: the most rows of x a launch takes (float path; 1 on the int8 path).
+// Each row has its own digit region and tile partials; every staged block is
+// multiplied against all the rows before the stage is released.
+template <int W, bool ACT8, int MR>
 __global__ void __launch_bounds__(32 * kWarpsAll, 1) k_mv1(const __grid_constant__ CUtensorMap tmap, const Params a) {
   using P = Pol<W>;
+  static_assert(MR == 1 || !ACT8, "several rows per launch on the float path only");
+  const int M = MR == 1 ? 1 : a.M;  // rows of x (a compile-time 1 for the batch-1 kernel)
   constexpr int pitch = P::BOX8 * 8, box_bytes = 16 * pitch, NBOX = P::NBOX;
   extern __shared__ __align__(128) uint8_t sm[];
   uint64_t *full = reinterpret_cast<uint64_t *>(sm);  // [S]     copy engine -> compute
@@ -577,8 +585,8 @@ __global__ void __launch_bounds__(32 * kWarpsAll, 1) k_mv1(const __grid_constant
   uint64_t *tdone = full + 32;                        // [slots] tile partials ready
   uint64_t *tfree = full + 40;                        // [slots] tile partials summed
   int *flag = reinterpret_cast<int *>(sm + 512);
-  float *part = reinterpret_cast<float *>(sm + kBarBytes);  // [slots][kConsumers][16]
-  uint8_t *xr = sm + a.xoff;
+  float *part = reinterpret_cast<float *>(sm + kBarBytes);  // [slots][MR][kConsumers][16]
+  uint8_t *xr = sm + a.xoff;                                // [MR] x regions, a.xstride apart
   float *terms = reinterpret_cast<float *>(sm + a.toff);  // [S][16][cbc]
   uint8_t *stages = sm + a.soff;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -628,8 +636,16 @@ __global__ void __launch_bounds__(32 * kWarpsAll, 1) k_mv1(const __grid_constant
   // kernel of the stream
   pdl_wait();
   if (warp < kConsumers) {
-    if constexpr (ACT8) prep_act8<W>(a, xr, flag);
-    else prep_float<W>(a, xr, flag);
+    if constexpr (ACT8) {
+      prep_act8<W>(a, xr, flag);
+    } else {
+      const size_t xel = a.xdt == TCB_F32 ? 4 : 2;
+      for (int m = 0; m < M; m++) {
+        Params ar = a;
+        ar.x = static_cast<const char *>(a.x) + (size_t)m * a.ldx * xel;
+        prep_float<W>(ar, xr + (size_t)m * a.xstride, flag);
+      }
+    }
   }
   asm volatile("bar.sync 1, %0;" ::"n"(32 * (kConsumers + 1)) : "memory");
   const bool slow = *flag != 0;
@@ -642,19 +658,35 @@ __global__ void __launch_bounds__(32 * kWarpsAll, 1) k_mv1(const __grid_constant
       const int tile = (int)blockIdx.x + ti * (int)gridDim.x;
       const int row = tile * 16 + lane;
       const bool mine = lane < 16 && row < a.N;
-      const float cold = (a.accumulate && mine) ? load_out(a.c, row, a.cdt) : 0.f;
-      float v = 0.f;
       if constexpr (!ACT8) {
+        float cold[MR], vs[MR];
+#pragma unroll
+        for (int m = 0; m < MR; m++)
+          cold[m] = (a.accumulate && mine && m < M) ? load_out(a.c, (long)m * a.ldc + row, a.cdt) : 0.f;
         const int slot = ti % kPartSlots;
         if (!spin_bar(&tdone[slot], (uint32_t)((ti / kPartSlots) & 1), a.err)) return;
-        const float *pt = part + slot * kConsumers * 16;
-        if (lane < 16)
 #pragma unroll
-          for (int w2 = 0; w2 < kConsumers; w2++) v += pt[w2 * 16 + lane];
+        for (int m = 0; m < MR; m++) {
+          vs[m] = 0.f;
+          if (m >= M) continue;
+          const float *pt = part + (slot * MR + m) * kConsumers * 16;
+          if (lane < 16)
+#pragma unroll
+            for (int w2 = 0; w2 < kConsumers; w2++) vs[m] += pt[w2 * 16 + lane];
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&tfree[slot]);
         it += a.nch;
-      } else {
+        if (mine) {
+#pragma unroll
+          for (int m = 0; m < MR; m++)
+            if (m < M) store_out_old(a.c, (long)m * a.ldc + row, a.cdt, vs[m], a.accumulate != 0, cold[m]);
+        }
+        continue;
+      }
+      const float cold = (a.accumulate && mine) ? load_out(a.c, row, a.cdt) : 0.f;
+      float v = 0.f;
+      {
         for (int ch = 0; ch < a.nch; ch++, it++) {
           const int buf = it % a.S;
           if (!spin_bar(&sdone[buf], (uint32_t)((it / a.S) & 1), a.err)) return;
@@ -678,7 +710,7 @@ __global__ void __launch_bounds__(32 * kWarpsAll, 1) k_mv1(const __grid_constant
     for (int c = 0; c < 8; c++) mk[c] = L.g == c ? 0xFFFFFFFFu : 0u;
     int it = 0;
     for (int ti = 0; ti < my_tiles; ti++) {
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      float acc[MR][4] = {};
       for (int ch = 0; ch < a.nch; ch++, it++) {
         const int buf = it % a.S;
         const uint32_t ph = (uint32_t)((it / a.S) & 1);
@@ -693,9 +725,14 @@ __global__ void __launch_bounds__(32 * kWarpsAll, 1) k_mv1(const __grid_constant
           for (int lb = warp * P::RB; lb < nblk; lb += kConsumers * P::RB) {
             const uint8_t *r0 = st + (lb / P::BPB) * box_bytes + L.g * pitch + (lb % P::BPB) * P::B;
             const uint8_t *r1 = r0 + 8 * pitch;
-            if constexpr (W == TCB_Q4_K) body_q4k<ACT8>(r0, r1, b0 + lb, lb, L, mk, xr, a.K, acc, tb, a.cbc);
-            else if constexpr (W == TCB_Q6_K) body_q6k<ACT8>(r0, r1, b0 + lb, lb, L, mk, xr, a.K, acc, tb, a.cbc);
-            else body_q32<W, ACT8>(r0, r1, b0 + lb, lb, L, mk, xr, a.K, acc, tb, a.cbc);
+#pragma unroll
+            for (int m = 0; m < MR; m++) {
+              if (m >= M) break;  // uniform
+              const uint8_t *xm = xr + (size_t)m * a.xstride;
+              if constexpr (W == TCB_Q4_K) body_q4k<ACT8>(r0, r1, b0 + lb, lb, L, mk, xm, a.K, acc[m], tb, a.cbc);
+              else if constexpr (W == TCB_Q6_K) body_q6k<ACT8>(r0, r1, b0 + lb, lb, L, mk, xm, a.K, acc[m], tb, a.cbc);
+              else body_q32<W, ACT8>(r0, r1, b0 + lb, lb, L, mk, xm, a.K, acc[m], tb, a.cbc);
+            }
           }
         }
         __syncwarp();
@@ -705,19 +742,23 @@ __global__ void __launch_bounds__(32 * kWarpsAll, 1) k_mv1(const __grid_constant
         }
       }
       if (!ACT8 && !slow) {
-        float s0 = acc[0] + acc[1], s1 = acc[2] + acc[3];
-        s0 += __shfl_xor_sync(0xFFFFFFFFu, s0, 1);
-        s1 += __shfl_xor_sync(0xFFFFFFFFu, s1, 1);
-        s0 += __shfl_xor_sync(0xFFFFFFFFu, s0, 2);
-        s1 += __shfl_xor_sync(0xFFFFFFFFu, s1, 2);
         const int slot = ti % kPartSlots;
         bool ok = true;
         if (lane == 0) ok = spin_bar(&tfree[slot], (uint32_t)(((ti / kPartSlots) & 1) ^ 1), a.err);
         if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) return;
-        float *pt = part + slot * kConsumers * 16;
-        if (L.t == 0) {
-          pt[warp * 16 + L.g] = s0;
-          pt[warp * 16 + L.g + 8] = s1;
+#pragma unroll
+        for (int m = 0; m < MR; m++) {
+          if (m >= M) break;
+          float s0 = acc[m][0] + acc[m][1], s1 = acc[m][2] + acc[m][3];
+          s0 += __shfl_xor_sync(0xFFFFFFFFu, s0, 1);
+          s1 += __shfl_xor_sync(0xFFFFFFFFu, s1, 1);
+          s0 += __shfl_xor_sync(0xFFFFFFFFu, s0, 2);
+          s1 += __shfl_xor_sync(0xFFFFFFFFu, s1, 2);
+          float *pt = part + (slot * MR + m) * kConsumers * 16;
+          if (L.t == 0) {
+            pt[warp * 16 + L.g] = s0;
+            pt[warp * 16 + L.g + 8] = s1;
+          }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&tdone[slot]);
@@ -728,12 +769,15 @@ __global__ void __launch_bounds__(32 * kWarpsAll, 1) k_mv1(const __grid_constant
     // NaN/Inf in x: TR's float path (the int8 path also falls back to it,
     // cpu_quant_q8.go:157-163), one warp per row
     const int widx = warp == kEpi ? kConsumers : warp;  // 0..16 over the compute and epilogue warps
-    for (int n = (int)blockIdx.x * (kConsumers + 1) + widx; n < a.N; n += (int)gridDim.x * (kConsumers + 1)) {
-      float accs[1] = {0.0f};
-      lane_row_float<W, 1>(a.w + (long)n * a.rowBytes, a.K, lane, XGlobal{a.x, 0, a.xdt}, accs);
-      const float v = warp_sum(accs[0]);
-      if (lane == 0) store_out(a.c, n, a.cdt, v, a.accumulate != 0);
-    }
+    const size_t xel = a.xdt == TCB_F32 ? 4 : 2;
+    for (int n = (int)blockIdx.x * (kConsumers + 1) + widx; n < a.N; n += (int)gridDim.x * (kConsumers + 1))
+      for (int m = 0; m < M; m++) {
+        float accs[1] = {0.0f};
+        const void *xrow = static_cast<const char *>(a.x) + (size_t)m * a.ldx * xel;
+        lane_row_float<W, 1>(a.w + (long)n * a.rowBytes, a.K, lane, XGlobal{xrow, 0, a.xdt}, accs);
+        const float v = warp_sum(accs[0]);
+        if (lane == 0) store_out(a.c, (long)m * a.ldc + n, a.cdt, v, a.accumulate != 0);
+      }
   }
 }
 
@@ -761,7 +805,9 @@ bool encode_weight_map(CUtensorMap *tm, const void *w, int N, long rowBytes) {
 
 template <int W, bool ACT8>
 cudaError_t plan_launch(const MvPlan &pl, const void *w, int N, int K, const void *x, int xdt, void *c, int cdt,
-                        int accumulate, int *err, cudaStream_t s, const void *pf, size_t pf_bytes) {
+                        int accumulate, int *err, cudaStream_t s, const void *pf, size_t pf_bytes, int M, long ldx,
+                        long ldc) {
+  if (M < 1 || M > pl.rows) return cudaErrorInvalidValue;
   mv::Params a{};
   a.w = static_cast<const uint8_t *>(w);
   a.nb = K / mv::Pol<W>::E;
@@ -783,10 +829,19 @@ cudaError_t plan_launch(const MvPlan &pl, const void *w, int N, int K, const voi
   a.soff = pl.soff;
   a.pf = pf;
   a.pf_bytes = pf_bytes;
+  a.M = M;
+  a.ldx = ldx;
+  a.ldc = ldc;
+  a.xstride = pl.xstride;
   CUtensorMap tm;
   static_assert(sizeof(tm) == sizeof(pl.tmap), "CUtensorMap size");
   memcpy(&tm, pl.tmap, sizeof tm);
-  auto kern = mv::k_mv1<W, ACT8>;
+  void (*kern)(const CUtensorMap, const mv::Params) = mv::k_mv1<W, ACT8, 1>;
+  if constexpr (!ACT8 && W != TCB_Q4_K) {  // Q4_K rows take k_mvq4k
+    if (pl.rows == 8) kern = mv::k_mv1<W, false, 8>;
+    else if (pl.rows == 4) kern = mv::k_mv1<W, false, 4>;
+    else if (pl.rows == 2) kern = mv::k_mv1<W, false, 2>;
+  }
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
@@ -802,10 +857,12 @@ cudaError_t plan_launch(const MvPlan &pl, const void *w, int N, int K, const voi
   return cudaLaunchKernelEx(&cfg, kern, tm, a);
 }
 
+// mr (1, 2, 4, 8; 1 on the int8 path): the most rows of x a launch takes
 template <int W, bool ACT8>
-MvPlan plan_w(int N, int K, const void *w, int sms) {
+MvPlan plan_w(int N, int K, const void *w, int sms, int mr = 1) {
   using P = mv::Pol<W>;
   MvPlan pl{};
+  if (mr != 1 && (ACT8 || (mr != 2 && mr != 4 && mr != 8))) return pl;
   const int nb = K / P::E;
   const long rowBytes = (long)nb * P::B;
   if (rowBytes % 16 || reinterpret_cast<uintptr_t>(w) % 16 || nb == 0) return pl;
@@ -816,8 +873,9 @@ MvPlan plan_w(int N, int K, const void *w, int sms) {
   pl.ksplit = 1;
   pl.cpk = pl.nch;
   pl.pitch = mv::Pol<W>::BOX8 * 8;
-  pl.xoff = mv::kBarBytes + mv::kPartSlots * mv::kConsumers * 16 * 4;
-  pl.toff = pl.xoff + ((mv::x_region_bytes<W, ACT8>(K) + 127) & ~127);
+  pl.xstride = (mv::x_region_bytes<W, ACT8>(K) + 127) & ~127;
+  pl.xoff = mv::kBarBytes + mr * mv::kPartSlots * mv::kConsumers * 16 * 4;
+  pl.toff = pl.xoff + mr * pl.xstride;
   const int tbytes_per_stage = ACT8 ? 16 * pl.cbc * 4 : 0;
   const int stage_bytes = P::NBOX * 16 * pl.pitch;
   int S = (kSmemMax - pl.toff - 128) / (stage_bytes + tbytes_per_stage);
@@ -828,6 +886,7 @@ MvPlan plan_w(int N, int K, const void *w, int sms) {
   pl.smem = pl.soff + S * stage_bytes;
   pl.tiles = (N + 15) / 16;
   pl.grid = pl.tiles < sms ? pl.tiles : sms;
+  pl.rows = mr;
   CUtensorMap tm;
   if (!encode_weight_map<W, ACT8>(&tm, w, N, rowBytes)) return pl;
   memcpy(pl.tmap, &tm, sizeof tm);
@@ -854,14 +913,32 @@ MvPlan matvec_plan(int wtype, int act8, int M, int N, int K, const void *w, int 
   return none;
 }
 
+MvPlan matvec_plan_rows(int wtype, int N, int K, const void *w, int sms, int mr) {
+  MvPlan none{};
+  if (N <= 0 || K <= 0) return none;
+  switch (wtype) {
+  case TCB_Q4_K: return q4k_plan(N, K, w, sms, mr);
+  // Q6_K rows of more than 8192 elements: one row per launch measured faster
+  // (4096x14336: 37 vs 42 us at M = 2, the digit regions crowd out stages)
+  case TCB_Q6_K: return N >= kQ6kMinRows || K > 8192 ? none : plan_w<TCB_Q6_K, false>(N, K, w, sms, mr);
+  case TCB_Q8_0: return plan_w<TCB_Q8_0, false>(N, K, w, sms, mr);
+  case TCB_Q4_0: return plan_w<TCB_Q4_0, false>(N, K, w, sms, mr);
+  }
+  return none;
+}
+
 cudaError_t matvec_launch(const MvPlan &pl, int wtype, int act8, int N, int K, const void *w, const void *x, int xdt,
                           void *c, int cdt, int accumulate, int *err, cudaStream_t s, const void *pf, size_t pf_bytes,
-                          void *scratch) {
-#define TCB_MV(WT)                                                                                    \
-  return act8 ? plan_launch<WT, true>(pl, w, N, K, x, xdt, c, cdt, accumulate, err, s, pf, pf_bytes) \
-              : plan_launch<WT, false>(pl, w, N, K, x, xdt, c, cdt, accumulate, err, s, pf, pf_bytes)
-  if (pl.kind == 1) return q4k_launch(pl, N, K, w, x, xdt, c, cdt, accumulate, err, s, nullptr, 0.f, pf, pf_bytes);
-  if (pl.kind == 2) return q6k_launch(pl, N, K, w, x, xdt, c, cdt, accumulate, err, s, 0, pf, pf_bytes, scratch);
+                          void *scratch, int M, long ldx, long ldc) {
+#define TCB_MV(WT)                                                                                                \
+  return act8 ? plan_launch<WT, true>(pl, w, N, K, x, xdt, c, cdt, accumulate, err, s, pf, pf_bytes, M, ldx, ldc) \
+              : plan_launch<WT, false>(pl, w, N, K, x, xdt, c, cdt, accumulate, err, s, pf, pf_bytes, M, ldx, ldc)
+  if (pl.kind == 1)
+    return q4k_launch(pl, N, K, w, x, xdt, c, cdt, accumulate, err, s, nullptr, 0.f, pf, pf_bytes, M, ldx, ldc);
+  if (pl.kind == 2) {
+    if (M != 1) return cudaErrorInvalidValue;
+    return q6k_launch(pl, N, K, w, x, xdt, c, cdt, accumulate, err, s, 0, pf, pf_bytes, scratch);
+  }
   switch (wtype) {
   case TCB_Q4_K: TCB_MV(TCB_Q4_K);
   case TCB_Q6_K: TCB_MV(TCB_Q6_K);
