@@ -59,18 +59,21 @@ int ensure_ws(tcb_ctx *ctx, size_t bytes) {
   return TCB_OK;
 }
 
-// the batch-1 tensor-core path: plan, scratch, launch.  *taken = false when
-// the shape goes to the portable kernel instead.
-// The batch-1 kernels take every M below the tensor-core path's minimum, one
-// activation row per launch: each launch streams the weight blocks again
-// (from L2 after the first), which still beats the portable kernel by an
-// order of magnitude at M = 2..8.  A row's result does not depend on the
-// other rows (the int8-activation fold is per row), so this is the same
-// product as one launch over all rows.
+// The TMA matvec kernels: plan, scratch, launch; *taken = false when the
+// shape goes to another kernel.  They take the float product below the
+// tensor-core path's minimum M (up to 8 rows of x per launch, the weights
+// streamed once for them) and the int8-activation product at every M (one
+// row per launch).  A row's result does not depend on the other rows (the
+// int8-activation fold is per row), so row groups give the same product as
+// one launch over all rows.
 int run_matvec(tcb_ctx *ctx, int wtype, int act8, int M, int N, int K, const void *w, const void *x, int xdt,
                long ldx, void *c, int cdt, long ldc, int accumulate, cudaStream_t s, bool *taken) {
   *taken = false;
-  if (M < 1 || M >= tcb::kTcMinM) return TCB_OK;
+  // the float path from kTcMinM rows on is the tensor-core product's; the
+  // int8-activation product has no other fast kernel, so every M comes here
+  // (one row per launch: about 12-20 us a row on the prefill shapes, against
+  // about 240 us a row for the portable kernel at 64 rows and more)
+  if (M < 1 || (!act8 && M >= tcb::kTcMinM)) return TCB_OK;
   if (!act8 && M > 1) {
     // the float-path kernels take up to 8 rows per launch, streaming the
     // weights once for all of them (fewer rows per launch when their digit

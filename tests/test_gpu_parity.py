@@ -258,7 +258,7 @@ def bits(a):
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
-@pytest.mark.parametrize("M", [1, 4, 5, 8])
+@pytest.mark.parametrize("M", [1, 4, 5, 8, 17, 70])
 def test_act8_bit_exact(ctx, oracle, fmt, M):
     """The int8-activation product equals TR's CPU kernels bit for bit
     (dotQ4Q8Go / dotQ4KQ8Go / dotQ6KQ8Go; Q8_0 by dotQ4Q8Go's fold)."""
