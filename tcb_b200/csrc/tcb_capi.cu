@@ -61,9 +61,8 @@ int ensure_ws(tcb_ctx *ctx, size_t bytes) {
 
 // The TMA matvec kernels: plan, scratch, launch; *taken = false when the
 // shape goes to another kernel.  They take the float product below the
-// tensor-core path's minimum M (up to 8 rows of x per launch, the weights
-// streamed once for them) and the int8-activation product at every M (one
-// row per launch).  A row's result does not depend on the other rows (the
+// tensor-core path's minimum M and the int8-activation product at every M,
+// up to 8 rows of x per launch with the weights streamed once for them.  A row's result does not depend on the other rows (the
 // int8-activation fold is per row), so row groups give the same product as
 // one launch over all rows.
 int run_matvec(tcb_ctx *ctx, int wtype, int act8, int M, int N, int K, const void *w, const void *x, int xdt,
@@ -71,24 +70,23 @@ int run_matvec(tcb_ctx *ctx, int wtype, int act8, int M, int N, int K, const voi
   *taken = false;
   // the float path from kTcMinM rows on is the tensor-core product's; the
   // int8-activation product has no other fast kernel, so every M comes here
-  // (one row per launch: about 12-20 us a row on the prefill shapes, against
-  // about 240 us a row for the portable kernel at 64 rows and more)
+  // (the portable kernel costs about 240 us a row on the prefill shapes)
   if (M < 1 || (!act8 && M >= tcb::kTcMinM)) return TCB_OK;
-  if (!act8 && M > 1) {
-    // the float-path kernels take up to 8 rows per launch, streaming the
-    // weights once for all of them (fewer rows per launch when their digit
-    // regions leave too little shared memory for the stages)
+  if (M > 1) {
+    // the kernels take up to 8 rows per launch, streaming the weights once
+    // for all of them (fewer rows per launch when their x regions leave too
+    // little shared memory for the stages)
     tcb::MvPlan pq{};
     for (int mr = 8; mr >= 2 && !pq.ok; mr /= 2)
-      if (mr <= 2 * M - 1 || mr == 2) pq = tcb::matvec_plan_rows(wtype, N, K, w, ctx->sms, mr);
+      if (mr <= 2 * M - 1 || mr == 2) pq = tcb::matvec_plan_rows(wtype, act8, N, K, w, ctx->sms, mr);
     if (pq.ok) {
       *taken = true;
       for (int m0 = 0; m0 < M; m0 += pq.rows) {
         const int rows = M - m0 < pq.rows ? M - m0 : pq.rows;
         const void *xm = static_cast<const char *>(x) + (size_t)m0 * ldx * elem_size(xdt);
         void *cm = static_cast<char *>(c) + (size_t)m0 * ldc * elem_size(cdt);
-        cudaError_t e = tcb::matvec_launch(pq, wtype, 0, N, K, w, xm, xdt, cm, cdt, accumulate, ctx->derr, s, nullptr,
-                                           0, ctx->sk, rows, ldx, ldc);
+        cudaError_t e = tcb::matvec_launch(pq, wtype, act8, N, K, w, xm, xdt, cm, cdt, accumulate, ctx->derr, s,
+                                           nullptr, 0, ctx->sk, rows, ldx, ldc);
         if (e != cudaSuccess) return cuda_fail(ctx, e);
       }
       return TCB_OK;

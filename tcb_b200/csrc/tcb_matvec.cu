@@ -568,13 +568,13 @@ constexpr int kWarpsAll = kConsumers + 2;
 constexpr int kPartSlots = 8;             // tile partial slots in flight
 constexpr int kBarBytes = 1024;
 
-// MR: the most rows of x a launch takes (float path; 1 on the int8 path).
-// Each row has its own digit region and tile partials; every staged block is
-// multiplied against all the rows before the stage is released.
+// MR: the most rows of x a launch takes.  Each row has its own x region and
+// tile partials (float path) or block terms (int8 path, [S][MR][16][cbc],
+// each row's folded in block order); every staged block is multiplied
+// against all the rows before the stage is released.
 template <int W, bool ACT8, int MR>
 __global__ void __launch_bounds__(32 * kWarpsAll, 1) k_mv1(const __grid_constant__ CUtensorMap tmap, const Params a) {
   using P = Pol<W>;
-  static_assert(MR == 1 || !ACT8, "several rows per launch on the float path only");
   const int M = MR == 1 ? 1 : a.M;  // rows of x (a compile-time 1 for the batch-1 kernel)
   constexpr int pitch = P::BOX8 * 8, box_bytes = 16 * pitch, NBOX = P::NBOX;
   extern __shared__ __align__(128) uint8_t sm[];
@@ -584,10 +584,11 @@ __global__ void __launch_bounds__(32 * kWarpsAll, 1) k_mv1(const __grid_constant
   uint64_t *sfree = full + 24;                        // [S]     int8 terms folded
   uint64_t *tdone = full + 32;                        // [slots] tile partials ready
   uint64_t *tfree = full + 40;                        // [slots] tile partials summed
-  int *flag = reinterpret_cast<int *>(sm + 512);
+  int *flag = reinterpret_cast<int *>(sm + 512);   // the whole launch takes TR's float path
+  int *rflag = flag + 1;                           // [MR] int8 path, MR > 1: row m is not finite
   float *part = reinterpret_cast<float *>(sm + kBarBytes);  // [slots][MR][kConsumers][16]
   uint8_t *xr = sm + a.xoff;                                // [MR] x regions, a.xstride apart
-  float *terms = reinterpret_cast<float *>(sm + a.toff);  // [S][16][cbc]
+  float *terms = reinterpret_cast<float *>(sm + a.toff);  // [S][MR][16][cbc]
   uint8_t *stages = sm + a.soff;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int stage_bytes = NBOX * box_bytes;
@@ -596,6 +597,7 @@ __global__ void __launch_bounds__(32 * kWarpsAll, 1) k_mv1(const __grid_constant
 
   if (threadIdx.x == 0) {
     *flag = 0;
+    for (int m = 0; m < MR; m++) rflag[m] = 0;
     for (int s = 0; s < a.S; s++) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumers);
@@ -636,15 +638,14 @@ __global__ void __launch_bounds__(32 * kWarpsAll, 1) k_mv1(const __grid_constant
   // kernel of the stream
   pdl_wait();
   if (warp < kConsumers) {
-    if constexpr (ACT8) {
-      prep_act8<W>(a, xr, flag);
-    } else {
-      const size_t xel = a.xdt == TCB_F32 ? 4 : 2;
-      for (int m = 0; m < M; m++) {
-        Params ar = a;
-        ar.x = static_cast<const char *>(a.x) + (size_t)m * a.ldx * xel;
-        prep_float<W>(ar, xr + (size_t)m * a.xstride, flag);
-      }
+    const size_t xel = a.xdt == TCB_F32 ? 4 : 2;
+    for (int m = 0; m < M; m++) {
+      Params ar = a;
+      ar.x = static_cast<const char *>(a.x) + (size_t)m * a.ldx * xel;
+      // int8 path with several rows: a row that is not finite takes TR's
+      // float path alone (in the epilogue); the others stay integer-exact
+      if constexpr (ACT8) prep_act8<W>(ar, xr + (size_t)m * a.xstride, MR == 1 ? flag : rflag + m);
+      else prep_float<W>(ar, xr + (size_t)m * a.xstride, flag);
     }
   }
   asm volatile("bar.sync 1, %0;" ::"n"(32 * (kConsumers + 1)) : "memory");
@@ -684,21 +685,50 @@ __global__ void __launch_bounds__(32 * kWarpsAll, 1) k_mv1(const __grid_constant
         }
         continue;
       }
-      const float cold = (a.accumulate && mine) ? load_out(a.c, row, a.cdt) : 0.f;
-      float v = 0.f;
-      {
-        for (int ch = 0; ch < a.nch; ch++, it++) {
-          const int buf = it % a.S;
-          if (!spin_bar(&sdone[buf], (uint32_t)((it / a.S) & 1), a.err)) return;
-          const int nblk = min(a.nb, (ch + 1) * a.cbc) - ch * a.cbc;
-          const float *tb = terms + buf * 16 * a.cbc;
+      float cold[MR], v[MR];
+#pragma unroll
+      for (int m = 0; m < MR; m++) {
+        cold[m] = (a.accumulate && mine && m < M) ? load_out(a.c, (long)m * a.ldc + row, a.cdt) : 0.f;
+        v[m] = 0.f;
+      }
+      for (int ch = 0; ch < a.nch; ch++, it++) {
+        const int buf = it % a.S;
+        if (!spin_bar(&sdone[buf], (uint32_t)((it / a.S) & 1), a.err)) return;
+        const int nblk = min(a.nb, (ch + 1) * a.cbc) - ch * a.cbc;
+#pragma unroll
+        for (int m = 0; m < MR; m++) {
+          if (m >= M) break;
+          const float *tb = terms + (buf * MR + m) * 16 * a.cbc;
           if (lane < 16)
-            for (int lb = 0; lb < nblk; lb++) v = __fadd_rn(v, tb[lane * a.cbc + lb]);
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&sfree[buf]);
+            for (int lb = 0; lb < nblk; lb++) v[m] = __fadd_rn(v[m], tb[lane * a.cbc + lb]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sfree[buf]);
+      }
+      if constexpr (MR > 1) {
+        // rows of x that are not finite: TR's float path, one output row at
+        // a time over the warp (their int8 terms are discarded)
+        const size_t xel = a.xdt == TCB_F32 ? 4 : 2;
+        for (int m = 0; m < M; m++) {
+          if (!rflag[m]) continue;
+          const void *xrow = static_cast<const char *>(a.x) + (size_t)m * a.ldx * xel;
+          for (int r = 0; r < 16; r++) {
+            const int n = tile * 16 + r;
+            if (n >= a.N) break;
+            float accs[1] = {0.0f};
+            lane_row_float<W, 1>(a.w + (long)n * a.rowBytes, a.K, lane, XGlobal{xrow, 0, a.xdt}, accs);
+            const float f = warp_sum(accs[0]);
+#pragma unroll
+            for (int mm = 0; mm < MR; mm++)
+              if (mm == m && lane == r) v[mm] = f;
+          }
         }
       }
-      if (mine) store_out_old(a.c, row, a.cdt, v, a.accumulate != 0, cold);
+      if (mine) {
+#pragma unroll
+        for (int m = 0; m < MR; m++)
+          if (m < M) store_out_old(a.c, (long)m * a.ldc + row, a.cdt, v[m], a.accumulate != 0, cold[m]);
+      }
     }
     return;
   }
@@ -721,7 +751,6 @@ __global__ void __launch_bounds__(32 * kWarpsAll, 1) k_mv1(const __grid_constant
         if (!slow) {
           const uint8_t *st = stages + buf * stage_bytes;
           const int b0 = ch * a.cbc, nblk = min(a.nb, b0 + a.cbc) - b0;
-          float *tb = terms + buf * 16 * a.cbc;
           for (int lb = warp * P::RB; lb < nblk; lb += kConsumers * P::RB) {
             const uint8_t *r0 = st + (lb / P::BPB) * box_bytes + L.g * pitch + (lb % P::BPB) * P::B;
             const uint8_t *r1 = r0 + 8 * pitch;
@@ -729,6 +758,7 @@ __global__ void __launch_bounds__(32 * kWarpsAll, 1) k_mv1(const __grid_constant
             for (int m = 0; m < MR; m++) {
               if (m >= M) break;  // uniform
               const uint8_t *xm = xr + (size_t)m * a.xstride;
+              float *tb = terms + (buf * MR + m) * 16 * a.cbc;
               if constexpr (W == TCB_Q4_K) body_q4k<ACT8>(r0, r1, b0 + lb, lb, L, mk, xm, a.K, acc[m], tb, a.cbc);
               else if constexpr (W == TCB_Q6_K) body_q6k<ACT8>(r0, r1, b0 + lb, lb, L, mk, xm, a.K, acc[m], tb, a.cbc);
               else body_q32<W, ACT8>(r0, r1, b0 + lb, lb, L, mk, xm, a.K, acc[m], tb, a.cbc);
@@ -837,10 +867,10 @@ cudaError_t plan_launch(const MvPlan &pl, const void *w, int N, int K, const voi
   static_assert(sizeof(tm) == sizeof(pl.tmap), "CUtensorMap size");
   memcpy(&tm, pl.tmap, sizeof tm);
   void (*kern)(const CUtensorMap, const mv::Params) = mv::k_mv1<W, ACT8, 1>;
-  if constexpr (!ACT8 && W != TCB_Q4_K) {  // Q4_K rows take k_mvq4k
-    if (pl.rows == 8) kern = mv::k_mv1<W, false, 8>;
-    else if (pl.rows == 4) kern = mv::k_mv1<W, false, 4>;
-    else if (pl.rows == 2) kern = mv::k_mv1<W, false, 2>;
+  if constexpr (ACT8 || W != TCB_Q4_K) {  // Q4_K float rows take k_mvq4k
+    if (pl.rows == 8) kern = mv::k_mv1<W, ACT8, 8>;
+    else if (pl.rows == 4) kern = mv::k_mv1<W, ACT8, 4>;
+    else if (pl.rows == 2) kern = mv::k_mv1<W, ACT8, 2>;
   }
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem);
   if (e != cudaSuccess) return e;
@@ -862,7 +892,7 @@ template <int W, bool ACT8>
 MvPlan plan_w(int N, int K, const void *w, int sms, int mr = 1) {
   using P = mv::Pol<W>;
   MvPlan pl{};
-  if (mr != 1 && (ACT8 || (mr != 2 && mr != 4 && mr != 8))) return pl;
+  if (mr != 1 && mr != 2 && mr != 4 && mr != 8) return pl;
   const int nb = K / P::E;
   const long rowBytes = (long)nb * P::B;
   if (rowBytes % 16 || reinterpret_cast<uintptr_t>(w) % 16 || nb == 0) return pl;
@@ -876,7 +906,7 @@ MvPlan plan_w(int N, int K, const void *w, int sms, int mr = 1) {
   pl.xstride = (mv::x_region_bytes<W, ACT8>(K) + 127) & ~127;
   pl.xoff = mv::kBarBytes + mr * mv::kPartSlots * mv::kConsumers * 16 * 4;
   pl.toff = pl.xoff + mr * pl.xstride;
-  const int tbytes_per_stage = ACT8 ? 16 * pl.cbc * 4 : 0;
+  const int tbytes_per_stage = ACT8 ? mr * 16 * pl.cbc * 4 : 0;
   const int stage_bytes = P::NBOX * 16 * pl.pitch;
   int S = (kSmemMax - pl.toff - 128) / (stage_bytes + tbytes_per_stage);
   if (S > 6) S = 6;
@@ -913,9 +943,18 @@ MvPlan matvec_plan(int wtype, int act8, int M, int N, int K, const void *w, int 
   return none;
 }
 
-MvPlan matvec_plan_rows(int wtype, int N, int K, const void *w, int sms, int mr) {
+MvPlan matvec_plan_rows(int wtype, int act8, int N, int K, const void *w, int sms, int mr) {
   MvPlan none{};
   if (N <= 0 || K <= 0) return none;
+  if (act8) {
+    switch (wtype) {
+    case TCB_Q4_K: return plan_w<TCB_Q4_K, true>(N, K, w, sms, mr);
+    case TCB_Q6_K: return plan_w<TCB_Q6_K, true>(N, K, w, sms, mr);
+    case TCB_Q8_0: return plan_w<TCB_Q8_0, true>(N, K, w, sms, mr);
+    case TCB_Q4_0: return plan_w<TCB_Q4_0, true>(N, K, w, sms, mr);
+    }
+    return none;
+  }
   switch (wtype) {
   case TCB_Q4_K: return q4k_plan(N, K, w, sms, mr);
   // Q6_K rows of more than 8192 elements: one row per launch measured faster

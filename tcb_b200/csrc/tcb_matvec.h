@@ -25,10 +25,10 @@ struct MvPlan {
 constexpr int kQ6kMinRows = 32768;
 
 MvPlan matvec_plan(int wtype, int act8, int M, int N, int K, const void *w, int sms);
-// float path, up to mr (2, 4, 8) rows of x per launch streaming the weights
-// once (ok = false when the rows' digit regions leave too little shared
-// memory, or for the wide Q6_K kernel)
-MvPlan matvec_plan_rows(int wtype, int N, int K, const void *w, int sms, int mr);
+// up to mr (2, 4, 8) rows of x per launch streaming the weights once, float
+// or int8-activation path (ok = false when the rows' x regions leave too
+// little shared memory, or for the wide Q6_K kernel)
+MvPlan matvec_plan_rows(int wtype, int act8, int N, int K, const void *w, int sms, int mr);
 
 // Q4_K float path (kind 1).  With nw, the product is W * rms(x): an
 // RMSNorm (x / sqrt(mean(x^2) + eps) * nw, K elements, f32 x, finite x

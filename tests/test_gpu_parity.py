@@ -293,11 +293,13 @@ def test_act8_edge_blocks(ctx, oracle, fmt):
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
-def test_act8_keeps_non_finite(ctx, oracle, fmt):
+@pytest.mark.parametrize("kb,M", [(2, 5), (16, 8)])
+def test_act8_keeps_non_finite(ctx, oracle, fmt, kb, M):
     """TestQ8PathKeepsNonFinite: a row with NaN/Inf takes the float path
-    (NaN/Inf where TR has them); the other rows stay bit-exact."""
+    (NaN/Inf where TR has them); the other rows stay bit-exact, also when
+    they share a launch of several rows with it."""
     e, _ = T.BLOCK[fmt]
-    N, K, M = 9, 2 * e, 5
+    N, K = 9, kb * e
     raw = small_scale(oracle, fmt, M + N, N * K // e)
     rng = np.random.default_rng(34)
     for bad in (np.nan, np.inf, -np.inf):
