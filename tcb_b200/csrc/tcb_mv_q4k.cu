@@ -275,6 +275,40 @@ __device__ __forceinline__ void mma16(const uint8_t *r0, const uint4 (&B)[2][2],
   }
 }
 
+// The A (weight code) operands of mma16, loaded and masked once (several
+// rows of x use them): [set][round pair][word], for rows g (0) and g+8 (1).
+struct AFrag {
+  uint32_t a[2][2][2][4];
+};
+__device__ __forceinline__ void load_afrag(const uint8_t *r0, const Lane &Q, AFrag &F) {
+  const uint8_t *r1 = r0 + 8 * kPitch;
+#pragma unroll
+  for (int st = 0; st < 2; st++)
+#pragma unroll
+    for (int rp = 0; rp < 2; rp++) {
+      const uint4 A0 = *reinterpret_cast<const uint4 *>(r0 + Q.woff + 32 * st + 16 * rp);
+      const uint4 A1 = *reinterpret_cast<const uint4 *>(r1 + Q.woff + 32 * st + 16 * rp);
+      F.a[st][rp][0][0] = A0.x & Q.mq, F.a[st][rp][0][1] = A0.y & Q.mq;
+      F.a[st][rp][0][2] = A0.z & Q.mq, F.a[st][rp][0][3] = A0.w & Q.mq;
+      F.a[st][rp][1][0] = A1.x & Q.mq, F.a[st][rp][1][1] = A1.y & Q.mq;
+      F.a[st][rp][1][2] = A1.z & Q.mq, F.a[st][rp][1][3] = A1.w & Q.mq;
+    }
+}
+// mma16 with preloaded A operands (the same MMAs, the same order)
+__device__ __forceinline__ void mma16p(const AFrag &F, const uint4 (&B)[2][2], int (&D)[2][4]) {
+#pragma unroll
+  for (int st = 0; st < 2; st++) {
+    D[st][0] = D[st][1] = D[st][2] = D[st][3] = 0;
+#pragma unroll
+    for (int rp = 0; rp < 2; rp++) {
+      const uint32_t(&a0)[4] = F.a[st][rp][0];
+      const uint32_t(&a1)[4] = F.a[st][rp][1];
+      imma_u8(D[st], a0[0], a1[0], a0[1], a1[1], B[st][rp].x, B[st][rp].y);
+      imma_u8(D[st], a0[2], a1[2], a0[3], a1[3], B[st][rp].z, B[st][rp].w);
+    }
+  }
+}
+
 // scales of sub-blocks c(0, t) and c(0, t) + 2 of rows g, g+8 (headers h0,
 // h1: d, dmin, the 12 scale bytes; get_scale_min_k4, two at a time in
 // 16-bit lanes), applied to the digit sums:
@@ -295,6 +329,40 @@ __device__ __forceinline__ void epi16(const uint4 (&hd)[2], const float4 sg, con
     const float mn = fmaf(lane16_f(m2, 0x7632u), sg.w, lane16_f(m2, 0x7610u) * sg.z);
     float &acc = r ? acc1 : acc0;
     acc = fmaf(-dm, mn, fmaf(d, q, acc));
+  }
+}
+
+// epi16 split for several rows of x: the block scales decoded once
+// (d, dmin, sc and m of the lane's two sub-blocks, rows g and g+8), then
+// applied per row with epi16's operations in epi16's order.
+struct Scl16 {
+  float d[2], dm[2], s0[2], s1[2], n0[2], n1[2];
+};
+__device__ __forceinline__ void decode16(const uint4 (&hd)[2], const Lane &Q, Scl16 &S) {
+#pragma unroll
+  for (int r = 0; r < 2; r++) {
+    const uint4 h = hd[r];
+    S.d[r] = __half2float(__ushort_as_half((unsigned short)(h.x & 0xFFFFu)));
+    S.dm[r] = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
+    const uint32_t ys = h.y >> Q.sh, zs = h.z >> Q.sh, ws = h.w >> Q.sh;
+    const uint32_t sc2 = ((Q.lo ? ys : ws) & Q.mlo) | ((ys >> 2) & Q.mhi);
+    const uint32_t m2 = ((Q.lo ? zs : (ws >> 4)) & Q.mlo) | ((zs >> 2) & Q.mhi);
+    S.s0[r] = lane16_f(sc2, 0x7610u);
+    S.s1[r] = lane16_f(sc2, 0x7632u);
+    S.n0[r] = lane16_f(m2, 0x7610u);
+    S.n1[r] = lane16_f(m2, 0x7632u);
+  }
+}
+__device__ __forceinline__ void apply16(const Scl16 &S, const float4 sg, const int (&D)[2][4], float &acc0,
+                                        float &acc1) {
+#pragma unroll
+  for (int r = 0; r < 2; r++) {
+    const float v0 = (float)(D[0][2 * r] * 254 + D[0][2 * r + 1]);
+    const float v1 = (float)(D[1][2 * r] * 254 + D[1][2 * r + 1]);
+    const float q = fmaf(S.s1[r] * sg.y, v1, (S.s0[r] * sg.x) * v0);
+    const float mn = fmaf(S.n1[r], sg.w, S.n0[r] * sg.z);
+    float &acc = r ? acc1 : acc0;
+    acc = fmaf(-S.dm[r], mn, fmaf(S.d[r], q, acc));
   }
 }
 
@@ -475,8 +543,41 @@ __global__ void __launch_bounds__(32 * kWarps, MR == 1 ? 2 : 1) k_mvq4k(const __
         const bool has = ch <= last_ch;
         const int bg = ch * kBlk + own;
         const uint8_t *r0 = stages + buf * kBoxBytes + g * kPitch + own * 144;
-        // the rows of x one after another on the staged block; the stage is
-        // released once the last row's operands are read
+        if constexpr (MR > 1) {
+          // several rows of x: the block's weight operands and scales are
+          // read and decoded once, the stage released, then every row's
+          // MMAs and scale math run from registers
+          AFrag F[kHalves];
+          Scl16 Sc[kHalves];
+          if (has) {
+#pragma unroll
+            for (int h = 0; h < kHalves; h++) {
+              load_afrag(r0 + 16 * h * kPitch, Q, F[h]);
+              uint4 hd[2];
+#pragma unroll
+              for (int r = 0; r < 2; r++) hd[r] = *reinterpret_cast<const uint4 *>(r0 + (16 * h + 8 * r) * kPitch);
+              decode16(hd, Q, Sc[h]);
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[buf]);
+          if (has) {
+#pragma unroll
+            for (int m = 0; m < MR; m++) {
+              if (m >= M) break;  // uniform
+              uint4 B[2][2];
+              bfrag(Q.xb + m * a.xstride + bg * Q.xs, B);
+              const float4 sg = *reinterpret_cast<const float4 *>(
+                  reinterpret_cast<const uint8_t *>(Q.scl + bg * 16) + m * a.xstride);
+#pragma unroll
+              for (int h = 0; h < kHalves; h++) {
+                int D[2][4];
+                mma16p(F[h], B, D);
+                apply16(Sc[h], sg, D, acc[m][2 * h], acc[m][2 * h + 1]);
+              }
+            }
+          }
+        } else
 #pragma unroll
         for (int m = 0; m < MR; m++) {
           if (m >= M) break;  // uniform
