@@ -235,13 +235,27 @@ __device__ void prep_act8(const Params &a, uint8_t *xr, int *flag) {
   float *d8 = reinterpret_cast<float *>(xr + up(K));
   int16_t *bs = reinterpret_cast<int16_t *>(xr + up(K) + up(nbk * 4));
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = kConsumers;
-  for (int bi = warp; bi < nbk; bi += nw) {
+  // the loads of NB of the warp's blocks go out together (one memory round
+  // trip per NB blocks, not per block); each block is then quantised as before
+  constexpr int NB = PER == 1 ? 8 : 4;
+  for (int b0 = warp; b0 < nbk; b0 += nw * NB) {
+    float vb[NB][PER];
+#pragma unroll
+    for (int j = 0; j < NB; j++) {
+      const int bj = b0 + j * nw;
+#pragma unroll
+      for (int i = 0; i < PER; i++) vb[j][i] = bj < nbk ? load_act(a.x, (long)bj * E + lane * PER + i, a.xdt) : 0.f;
+    }
+#pragma unroll
+  for (int j = 0; j < NB; j++) {
+    const int bi = b0 + j * nw;
+    if (bi >= nbk) break;  // warp-uniform
     float v[PER];
     float amax = 0.0f;
     bool fin = true;
 #pragma unroll
     for (int i = 0; i < PER; i++) {
-      v[i] = load_act(a.x, (long)bi * E + lane * PER + i, a.xdt);
+      v[i] = vb[j][i];
       float t = fabsf(v[i]);
       amax = t > amax ? t : amax;
       fin = fin && (__fsub_rn(v[i], v[i]) == 0.0f);
@@ -271,6 +285,7 @@ __device__ void prep_act8(const Params &a, uint8_t *xr, int *flag) {
       if ((lane & 15) == 0) bs[(bi * E + lane) / 16] = (int16_t)part;
     }
     if (lane == 0) d8[bi] = zero ? 0.0f : __fdiv_rn(amax, 127.0f);
+  }
   }
 }
 
