@@ -170,11 +170,13 @@ def test_qgemm_matches_oracle(ctx, oracle, fmt, M):
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
-def test_qgemm_precisions_and_views(ctx, oracle, fmt):
+@pytest.mark.parametrize("kb,M", [(2, 3), (16, 8)])
+def test_qgemm_precisions_and_views(ctx, oracle, fmt, kb, M):
     """TestQuantGemvShapesAndPrecisions: bf16/f16 x and c, row strides,
-    an offset (unaligned) activation view, a slice of weight rows."""
+    an offset (unaligned) activation view, a slice of weight rows (with 16
+    blocks per row every format's rows go through the multi-row launches)."""
     e, size = T.BLOCK[fmt]
-    N, K, M = 6, 2 * e, 3
+    N, K = 6, kb * e
     raw = small_scale(oracle, fmt, 9, N * K // e)
     rng = np.random.default_rng(9)
     xf = rng.standard_normal((M, K + 1), dtype=np.float32)
