@@ -298,7 +298,8 @@ __device__ void prep_act8(const Params &a, uint8_t *xr, int *flag) {
 // of its own group once and masks them with mk[c] = (g == c ? ~0 : 0).
 // Float path: acc[4] accumulates (row g, column 2t), (g, 2t+1),
 // (g+8, 2t), (g+8, 2t+1).  Int8 path: block terms go to
-// tb[row * cbc + local block].
+// tb[local block * 16 + row] (the epilogue's 16 lanes read a block's rows
+// from consecutive words).
 
 struct Lane {
   int g, t;
@@ -391,7 +392,7 @@ __device__ __forceinline__ void body_q4k(const uint8_t *r0, const uint8_t *r1, i
         ms += __shfl_xor_sync(0xFFFFFFFFu, ms, o);
       }
       const float tt = __fsub_rn(__fmul_rn(dd[r], (float)is), __fmul_rn(dm[r], (float)ms));
-      if (L.t == 0) tb[(L.g + 8 * r) * cbc + lb] = __fmul_rn(tt, d8);
+      if (L.t == 0) tb[lb * 16 + L.g + 8 * r] = __fmul_rn(tt, d8);
     }
   }
 }
@@ -486,7 +487,7 @@ __device__ __forceinline__ void body_q6k(const uint8_t *r0, const uint8_t *r1, i
         ms[r] += __shfl_xor_sync(0xFFFFFFFFu, ms[r], o);
       }
       const float tt = __fmul_rn(dd[r], (float)(is[r] - 32 * ms[r]));
-      if (L.t == 0) tb[(L.g + 8 * r) * cbc + lb] = __fmul_rn(tt, d8);
+      if (L.t == 0) tb[lb * 16 + L.g + 8 * r] = __fmul_rn(tt, d8);
     }
   }
 }
@@ -565,7 +566,7 @@ __device__ __forceinline__ void body_q32(const uint8_t *s0, const uint8_t *s1, i
       const int j = i & 1;
       int isum = D[0][i];
       if (W == TCB_Q4_0) isum -= 8 * ((int)bs[2 * (G0 + j)] + (int)bs[2 * (G0 + j) + 1]);
-      tb[(L.g + 8 * (i >> 1)) * cbc + lb0 + 2 * L.t + j] = __fmul_rn(__fmul_rn(dw[i], d8[G0 + j]), (float)isum);
+      tb[(lb0 + 2 * L.t + j) * 16 + L.g + 8 * (i >> 1)] = __fmul_rn(__fmul_rn(dw[i], d8[G0 + j]), (float)isum);
     }
   }
 }
@@ -584,7 +585,7 @@ constexpr int kPartSlots = 8;             // tile partial slots in flight
 constexpr int kBarBytes = 1024;
 
 // MR: the most rows of x a launch takes.  Each row has its own x region and
-// tile partials (float path) or block terms (int8 path, [S][MR][16][cbc],
+// tile partials (float path) or block terms (int8 path, [S][MR][cbc][16],
 // each row's folded in block order); every staged block is multiplied
 // against all the rows before the stage is released.
 template <int W, bool ACT8, int MR>
@@ -603,7 +604,7 @@ __global__ void __launch_bounds__(32 * kWarpsAll, 1) k_mv1(const __grid_constant
   int *rflag = flag + 1;                           // [MR] int8 path, MR > 1: row m is not finite
   float *part = reinterpret_cast<float *>(sm + kBarBytes);  // [slots][MR][kConsumers][16]
   uint8_t *xr = sm + a.xoff;                                // [MR] x regions, a.xstride apart
-  float *terms = reinterpret_cast<float *>(sm + a.toff);  // [S][MR][16][cbc]
+  float *terms = reinterpret_cast<float *>(sm + a.toff);  // [S][MR][cbc][16]
   uint8_t *stages = sm + a.soff;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int stage_bytes = NBOX * box_bytes;
@@ -715,7 +716,7 @@ __global__ void __launch_bounds__(32 * kWarpsAll, 1) k_mv1(const __grid_constant
           if (m >= M) break;
           const float *tb = terms + (buf * MR + m) * 16 * a.cbc;
           if (lane < 16)
-            for (int lb = 0; lb < nblk; lb++) v[m] = __fadd_rn(v[m], tb[lane * a.cbc + lb]);
+            for (int lb = 0; lb < nblk; lb++) v[m] = __fadd_rn(v[m], tb[lb * 16 + lane]);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sfree[buf]);
