@@ -43,6 +43,20 @@
 namespace tcb {
 namespace ll {
 
+// L2 loads kept in program order with the dependency wait: the asm of
+// __ldcg is not volatile and names no memory, so the compiler may move it
+// past griddepcontrol.wait; these may not be moved across it
+__device__ __forceinline__ uint4 ldcg_v4_ordered(const void *p) {
+  uint4 r;
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint2 ldcg_v2_ordered(const void *p) {
+  uint2 r;
+  asm volatile("ld.global.cg.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+  return r;
+}
+
 constexpr int kHd = 128;        // head dimension supported by the attention kernel
 constexpr int kChunk = 64;      // positions per attention CTA
 constexpr int kMaxChunks = 256; // chunks a merge holds in shared memory (max_ctx <= 16384)
@@ -120,12 +134,12 @@ __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cos
   const bool kok = tk < n && tk != p;
   if (kok) {
 #pragma unroll
-    for (int j = 0; j < 4; j++) kr[j] = __ldcg(reinterpret_cast<const uint4 *>(kbase + (size_t)tk * kHd + 32 * sk) + j);
+    for (int j = 0; j < 4; j++) kr[j] = ldcg_v4_ordered(reinterpret_cast<const uint4 *>(kbase + (size_t)tk * kHd + 32 * sk) + j);
   }
 #pragma unroll
   for (int j = 0; j < kChunk / 8; j++) {
     const int t = tv + 8 * j;
-    if (t < n && t != p) vr[j] = __ldcg(reinterpret_cast<const uint2 *>(vbase + (size_t)t * kHd + dv));
+    if (t < n && t != p) vr[j] = ldcg_v2_ordered(reinterpret_cast<const uint2 *>(vbase + (size_t)t * kHd + dv));
   }
   mv::pdl_wait();
   // the next kernel (the o projection) may launch now: its weight stream does
