@@ -208,9 +208,17 @@ __device__ void prep_float(const Params &a, uint8_t *xr, int *flag) {
         }
       }
       if (e < K) {
-        *reinterpret_cast<uint32_t *>(dig + e) = ph;
-        *reinterpret_cast<uint32_t *>(dig + K + e) = p1;
-        if (ND > 2) *reinterpret_cast<uint32_t *>(dig + 2 * K + e) = p2;
+        // Q4_0: within a 32-element block, the 4-byte words of elements 4t..
+        // and 16+4t.. sit side by side (word 2t and 2t+1), so a lane reads its
+        // low- and high-nibble digits with one conflict-free 8-byte load
+        int pe = e;
+        if constexpr (W == TCB_Q4_0) {
+          const int w = (e & 31) >> 2;
+          pe = (e & ~31) + 4 * (2 * (w & 3) + (w >> 2));
+        }
+        *reinterpret_cast<uint32_t *>(dig + pe) = ph;
+        *reinterpret_cast<uint32_t *>(dig + K + pe) = p1;
+        if (ND > 2) *reinterpret_cast<uint32_t *>(dig + 2 * K + pe) = p2;
         if ((tid & (LPG - 1)) == 0) {
           const int gi = e / G;
           sg[gi] = ND > 2 ? sigma * (1.0f / 64516.0f) : sigma * (1.0f / 254.0f);
@@ -508,7 +516,7 @@ __device__ __forceinline__ void body_q32(const uint8_t *s0, const uint8_t *s1, i
 #pragma unroll
   for (int p = 0; p < ND; p++) {
     const uint8_t *pl = xr + p * K + (bg0 + L.g) * 32;
-    if constexpr (W == TCB_Q8_0) own[p] = *reinterpret_cast<const uint2 *>(pl + 8 * L.t);
+    if constexpr (W == TCB_Q8_0 || !ACT8) own[p] = *reinterpret_cast<const uint2 *>(pl + 8 * L.t);  // float Q4_0: paired words
     else own[p] = make_uint2(*reinterpret_cast<const uint32_t *>(pl + 4 * L.t), *reinterpret_cast<const uint32_t *>(pl + 16 + 4 * L.t));
   }
   // four accumulator chains per digit: set j & 3 for block j of the round
