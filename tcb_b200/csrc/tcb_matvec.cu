@@ -707,8 +707,7 @@ __global__ void __launch_bounds__(32 * kWarpsAll, 1) k_mv1(const __grid_constant
           for (int m = 0; m < MR; m++)
             if (m < M) store_out_old(a.c, (long)m * a.ldc + row, a.cdt, vs[m], a.accumulate != 0, cold[m]);
         }
-        continue;
-      }
+      } else {
       float cold[MR], v[MR];
 #pragma unroll
       for (int m = 0; m < MR; m++) {
@@ -752,6 +751,7 @@ __global__ void __launch_bounds__(32 * kWarpsAll, 1) k_mv1(const __grid_constant
 #pragma unroll
         for (int m = 0; m < MR; m++)
           if (m < M) store_out_old(a.c, (long)m * a.ldc + row, a.cdt, v[m], a.accumulate != 0, cold[m]);
+      }
       }
     }
     return;
