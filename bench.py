@@ -42,7 +42,8 @@ Q4_0, Q8_0, Q4_K = 2, 8, 12
 
 
 def algorithmic_bytes(N: int, K: int, M: int = 1) -> int:
-    """weight blocks + x (f32) + y (f32), SURVEY/BASELINE accounting."""
+    """Bytes one Q4_K product must move: the weight blocks (144 B per 256
+    weights), x (f32) and y (f32)."""
     return N * K // 256 * 144 + M * K * 4 + M * N * 4
 
 
