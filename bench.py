@@ -549,30 +549,58 @@ def main():
     peaks = load_peaks()
     achieved = per_launch_bytes / kernel_s / 1e9
 
-    # e2e through the public API with host buffers (eager calls)
+    # e2e with host buffers, eager calls, every step: x copied in from pinned
+    # memory, the product, y copied back.  Headline: the C ABI called as a
+    # cgo/purego host calls it (cudaMemcpyAsync, tcb_qgemm, cudaMemcpyAsync,
+    # the pointers resolved once).  Beside it: the Python mirror (torch
+    # tensor copies and Context.qgemm).
+    import ctypes
+
     xh = torch.from_numpy(synth.activations(1, K, seed=2 + rank)).pin_memory()
     yh = torch.empty((1, N), dtype=torch.float32).pin_memory()
     e2e_steps = max(200, args.steps // 4)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        for i in range(20):
-            x.copy_(xh, non_blocking=True)
-            ctx.qgemm(Q4_K, weights[i % ring], x, ys[0], accumulate=False, stream=stream)
-            yh.copy_(ys[0], non_blocking=True)
-        barrier()
-        e0.record(stream)
-        for i in range(e2e_steps):
-            x.copy_(xh, non_blocking=True)
-            ctx.qgemm(Q4_K, weights[i % ring], x, ys[0], accumulate=False, stream=stream)
-            yh.copy_(ys[0], non_blocking=True)
-        e1.record(stream)
-        e1.synchronize()
-    et = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-    if world > 1:
-        import torch.distributed as dist
+    rt = ctypes.CDLL("libcudart.so.12")
+    rt.cudaMemcpyAsync.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_void_p]
+    rt.cudaMemcpyAsync.restype = ctypes.c_int
+    qgemm = T.lib().tcb_qgemm
+    sh, hctx = stream.cuda_stream, ctx._h
+    xp, xhp, yp, yhp = x.data_ptr(), xh.data_ptr(), ys[0].data_ptr(), yh.data_ptr()
+    wps = [w.data_ptr() for w in weights]
 
-        dist.all_reduce(et, op=dist.ReduceOp.MAX)
-    e2e_value = per_launch_bytes * e2e_steps * world / (float(et.item()) / 1e3) / 1e9
+    def capi_step(i):
+        rc = rt.cudaMemcpyAsync(xp, xhp, K * 4, 1, sh)  # cudaMemcpyHostToDevice
+        rc |= qgemm(hctx, Q4_K, 1, N, K, wps[i % ring], xp, T.F32, K, yp, T.F32, N, 0, sh)
+        return rc | rt.cudaMemcpyAsync(yhp, yp, N * 4, 2, sh)  # cudaMemcpyDeviceToHost
+
+    def torch_step(i):
+        x.copy_(xh, non_blocking=True)
+        ctx.qgemm(Q4_K, weights[i % ring], x, ys[0], accumulate=False, stream=stream)
+        yh.copy_(ys[0], non_blocking=True)
+        return 0
+
+    def e2e(step_fn):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        rc = 0
+        with torch.cuda.stream(stream):
+            for i in range(20):
+                rc |= step_fn(i)
+            barrier()
+            e0.record(stream)
+            for i in range(e2e_steps):
+                rc |= step_fn(i)
+            e1.record(stream)
+            e1.synchronize()
+        if rc:
+            raise RuntimeError(f"e2e step failed (status {rc})")
+        et = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(et, op=dist.ReduceOp.MAX)
+        return per_launch_bytes * e2e_steps * world / (float(et.item()) / 1e3) / 1e9
+
+    e2e_value = e2e(capi_step)
+    e2e_torch = e2e(torch_step)
     del g
     decode = None
     if not args.no_decode:
@@ -598,7 +626,10 @@ def main():
                          "traffic": load_traffic("q4k_matvec_11008x4096.md"),
                          "algorithmic_bytes_per_launch": per_launch_bytes},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": K * 4,
-                    "d2h_bytes_per_step": N * 4, "steps": e2e_steps},
+                    "d2h_bytes_per_step": N * 4, "steps": e2e_steps,
+                    "calls": "per step: cudaMemcpyAsync x from pinned memory, tcb_qgemm, cudaMemcpyAsync y back",
+                    "python_mirror": {"value": round(e2e_torch, 2),
+                                      "calls": "torch copy_ of x, Context.qgemm, torch copy_ of y, per step"}},
             "gpu_launches": launches,
             "clocks": clk.summary(),
         }
