@@ -449,10 +449,30 @@ def run_reference(args, rank: int):
             "warmup": args.warmup, "impl": "reference", "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": WORKLOAD, "cpu_baseline": cb,
             "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
+
+
+_RESULT = None  # the process's original stdout, kept for the JSON line
+
+
+def claim_stdout():
+    """Point fd 1 at stderr for the rest of the run, so that what libraries
+    print on stdout (NCCL's version banner when a debug level is set) cannot
+    mix with the result; the JSON line goes to the original stdout."""
+    global _RESULT
+    sys.stdout.flush()
+    _RESULT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+
+
+def emit(obj: dict):
+    out = _RESULT if _RESULT is not None else sys.stdout
+    out.write(json.dumps(obj) + "\n")
+    out.flush()
 
 
 def main():
+    claim_stdout()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
@@ -486,8 +506,7 @@ def main():
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     if args.only_model_prefill:
-        print(json.dumps({"model_prefill": model_prefill_bench(T.Context(local), load_peaks(), args.layers)}),
-              flush=True)
+        emit({"model_prefill": model_prefill_bench(T.Context(local), load_peaks(), args.layers)})
         return
     N, K = WORKLOAD["N"], WORKLOAD["K"]
     wbytes = N * K // 256 * 144
@@ -643,7 +662,7 @@ def main():
             line["matvec_configs"] = table
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         import torch.distributed as dist
 
