@@ -127,16 +127,21 @@ def cpu_baseline(seconds: float = 12.0) -> dict:
     N, K = WORKLOAD["N"], WORKLOAD["K"]
     w = synth.weight(Q4_K, N, K, seed=7)
     x = synth.activations(1, K, seed=8)
-    threads = os.cpu_count() or 1
-    O.qgemm_float(Q4_K, x, w, N, nthreads=threads)  # warm
-    n, t0 = 0, time.perf_counter()
-    while time.perf_counter() - t0 < seconds:
-        O.qgemm_float(Q4_K, x, w, N, nthreads=threads)
-        n += 1
-    dt = time.perf_counter() - t0
+    threads = len(os.sched_getaffinity(0))
+    O.set_pinning(True)
+    try:
+        O.qgemm_float(Q4_K, x, w, N, nthreads=threads)  # warm
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds:
+            O.qgemm_float(Q4_K, x, w, N, nthreads=threads)
+            n += 1
+        dt = time.perf_counter() - t0
+    finally:
+        O.set_pinning(False)
     return {"value": round(algorithmic_bytes(N, K) * n / dt / 1e9, 3), "unit": "GB/s", "cores": threads,
-            "kind": "port", "sample": f"{n} matvecs of Q4_K 11008x4096 (float path, oracle AVX2 restatement) "
-                                      f"in {dt:.1f} s"}
+            "kind": "port", "pinning": f"one worker thread per allowed CPU ({threads} of os.cpu_count() = "
+                                       f"{os.cpu_count()}), pthread_setaffinity_np",
+            "sample": f"{n} matvecs of Q4_K 11008x4096 (float path, oracle AVX2 restatement) in {dt:.1f} s"}
 
 
 def decode_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
@@ -152,9 +157,9 @@ def decode_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
     from tcb_b200 import llama
 
     cfg = llama.LLAMA3_8B
-    model = llama.device_model(cfg, seed=7 + rank)
+    model = llama.device_model(cfg, seed=7, varied=True)
     eng = llama.Llama(ctx, model)
-    prompt = np.random.default_rng(11 + rank).integers(0, cfg.vocab, 512)
+    prompt = np.random.default_rng(11).integers(0, cfg.vocab, 512)
     stream = torch.cuda.Stream()
     eng.start(prompt, stream)
     eng.capture(stream)
@@ -189,7 +194,8 @@ def decode_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
         "roofline": {"bound": "hbm", "achieved": round((bpt + kv) / per_tok_s / 1e9, 2), "peak": peak_gbs,
                      "unit": "GB/s", "frac": round((bpt + kv) / per_tok_s / 1e9 / peak_gbs, 4),
                      "ceiling_tokens_per_s": round(peak_gbs * 1e9 / (bpt + kv), 1)},
-        "gpu_launches_per_token": 1 + 6 * cfg.n_layers + 4, "last_tokens": [int(v) for v in toks[-4:]],
+        "gpu_launches_per_token": 1 + 6 * cfg.n_layers + 4, "last_tokens": [int(v) for v in toks[-8:]],
+        "distinct_generated_tokens": len(set(int(v) for v in toks[512:])),
         "timing": "CUDA events around 256 graph replays on the engine's stream",
     }
 
@@ -250,12 +256,13 @@ def matvec_table_bench(ctx, rank: int, peak_gbs: float) -> dict:
                     e1.synchronize()
                 us = e0.elapsed_time(e1) * 1e3 / (20 * ring)
                 gbs = (wbytes + M * K * 4 + M * N * 4) / (us * 1e-6) / 1e9
-                rows.append({"wtype": names[wt], "N": N, "K": K, "M": M, "path": "int8 activations" if act8 else "float",
-                             "us_per_call": round(us, 2), "GB/s": round(gbs, 1), "frac": round(gbs / peak_gbs, 4)})
+                rows.append([names[wt], N, K, M, "act8" if act8 else "float", round(us, 2), round(gbs, 1),
+                             round(gbs / peak_gbs, 4)])
                 del g
         del weights, base
     return {"timing": "CUDA graph of one sweep over a cold weight ring (>= 512 MiB), 20 sweeps",
-            "peak_gbs": peak_gbs, "cases": rows}
+            "peak_gbs": peak_gbs, "columns": ["wtype", "N", "K", "M", "path", "us_per_call", "GB/s", "frac"],
+            "cases": rows}
 
 
 def model_prefill_bench(ctx, peaks: dict, layers: int = 0) -> dict:
@@ -376,20 +383,22 @@ def prefill_bench(ctx, rank: int, peaks: dict, cpu: bool) -> dict:
 
 
 def decode_tp_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
-    """70B-shape Q4_K_M greedy decode at batch 1, tensor-parallel over the
-    world's GPUs (QKV/gate/up column-parallel, o/down
-    row-parallel with an NCCL all-reduce each, vocabulary-parallel head):
-    a 1024-token random prompt fed by the prompt pass (1023 rows through the
-    tensor-core products, residual rows summed by NCCL), then 128 greedy
-    tokens, every step one replay of the captured graph.  Batch 16 is not
-    provided (the engine is batch 1)."""
+    """70B-shape Q4_K_M greedy decode at batch 1, on one GPU or
+    tensor-parallel over the world's GPUs (QKV/gate/up
+    column-parallel, o/down row-parallel with a residual all-reduce each,
+    vocabulary-parallel head): a 1024-token random prompt fed by the prompt
+    pass (1023 rows through the tensor-core products, residual rows summed by
+    NCCL), then 128 greedy tokens, every step one replay of the captured
+    graph.  The weights are one model at every degree (each global tensor
+    from its own counter-based generator, each rank keeping its slice), so
+    the tokens are comparable across N."""
     import torch
     import torch.distributed as dist
 
     from tcb_b200 import llama
 
     cfg = llama.LLAMA3_70B
-    model = llama.device_model(cfg, seed=9, tp=(world, rank))
+    model = llama.device_model(cfg, seed=9, tp=(world, rank), varied=True)
     eng = llama.Llama(ctx, model, tp=(world, rank))
     eng.tp_init(llama.share_id(llama.nccl_unique_id, rank))
     prompt = np.random.default_rng(13).integers(0, cfg.vocab, 1024)
@@ -408,7 +417,8 @@ def decode_tp_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
         e2.record(stream)
     e2.synchronize()
     t = torch.tensor([e1.elapsed_time(e2), e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, pms = float(t[0].item()), float(t[1].item())
     toks = eng.tokens(1152, stream)
     eng.close()
@@ -423,7 +433,11 @@ def decode_tp_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
         "roofline": {"bound": "hbm", "achieved_per_gpu": round(per_gpu / (ms / 1e3 / 128) / 1e9, 2),
                      "peak": peak_gbs, "unit": "GB/s", "frac": round(per_gpu / (ms / 1e3 / 128) / 1e9 / peak_gbs, 4),
                      "ceiling_tokens_per_s": round(peak_gbs * 1e9 / per_gpu, 1)},
-        "allreduce": "peer memory (NVLink)" if getattr(eng, "peer_active", False) else "nccl", "collectives_per_token": 2 * cfg.n_layers + 1, "last_tokens": [int(v) for v in toks[-4:]],
+        "allreduce": ("none (one GPU)" if world == 1 else
+                      "peer memory (NVLink)" if getattr(eng, "peer_active", False) else "nccl"),
+        "collectives_per_token": 0 if world == 1 else 2 * cfg.n_layers + 1,
+        "last_tokens": [int(v) for v in toks[-8:]],
+        "distinct_generated_tokens": len(set(int(v) for v in toks[1024:])),
         "timing": "CUDA events around 128 graph replays, max over ranks",
     }
 
@@ -441,13 +455,21 @@ def dist_init():
     return rank, world, local
 
 
-def run_reference(args, rank: int):
+def run_config(world: int) -> dict:
+    """The workload's config object, the same on both arms."""
+    wbytes = WORKLOAD["N"] * WORKLOAD["K"] // 256 * 144
+    ring = max(4, -(-512 * 2 ** 20 // wbytes))  # >= 512 MiB of distinct weights
+    return dict(WORKLOAD, ring=ring, ring_bytes=ring * wbytes, l2="inputs larger than L2 (cold ring)",
+                parallelism=f"replicas{world}")
+
+
+def run_reference(args, rank: int, world: int):
     if rank != 0:
         return
     cb = cpu_baseline()
     line = {"metric": METRIC, "value": cb["value"], "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "impl": "reference", "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": WORKLOAD, "cpu_baseline": cb,
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": run_config(world), "cpu_baseline": cb,
             "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     emit(line)
 
@@ -491,7 +513,7 @@ def main():
 
     rank, world, local = dist_init()
     if args.impl == "reference":
-        run_reference(args, rank)
+        run_reference(args, rank, world)
         if world > 1:
             import torch.distributed as dist
 
@@ -509,8 +531,8 @@ def main():
         emit({"model_prefill": model_prefill_bench(T.Context(local), load_peaks(), args.layers)})
         return
     N, K = WORKLOAD["N"], WORKLOAD["K"]
-    wbytes = N * K // 256 * 144
-    ring = max(4, -(-512 * 2 ** 20 // wbytes))  # >= 512 MiB of distinct weights
+    config = run_config(world)
+    ring = config["ring"]
     ctx = T.Context(local)
     base = torch.from_numpy(synth.weight(Q4_K, N, K, seed=1 + rank)).to(dev)
     weights = [base]
@@ -621,10 +643,13 @@ def main():
     e2e_value = e2e(capi_step)
     e2e_torch = e2e(torch_step)
     del g
-    decode = None
+    decode = decode70 = None
     if not args.no_decode:
-        decode = (decode_bench(ctx, rank, world, peaks["hbm_gbs"]) if world == 1
-                  else decode_tp_bench(ctx, rank, world, peaks["hbm_gbs"]))
+        if world == 1:
+            decode = decode_bench(ctx, rank, world, peaks["hbm_gbs"])
+        torch.cuda.empty_cache()
+        decode70 = decode_tp_bench(ctx, rank, world, peaks["hbm_gbs"])
+        torch.cuda.empty_cache()
 
     table = matvec_table_bench(ctx, rank, peaks["hbm_gbs"]) if world == 1 and not args.no_configs else None
     prefill = model_prefill = None
@@ -638,11 +663,12 @@ def main():
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 6), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "pct_of_peak": round(100 * value / world / peaks["hbm_gbs"], 2),
-            "config": dict(WORKLOAD, ring=ring, ring_bytes=ring * wbytes, l2="inputs larger than L2 (cold ring)",
-                           parallelism=f"replicas{world}"),
+            "config": config,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
                          "traffic": load_traffic("q4k_matvec_11008x4096.md"),
+                         "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum of one launch of this "
+                                           "kernel under ncu, summarised in profiles/q4k_matvec_11008x4096.md",
                          "algorithmic_bytes_per_launch": per_launch_bytes},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": K * 4,
                     "d2h_bytes_per_step": N * 4, "steps": e2e_steps,
@@ -652,16 +678,20 @@ def main():
             "gpu_launches": launches,
             "clocks": clk.summary(),
         }
-        if decode is not None:
-            line["decode"] = decode
+        # the driver keeps the end of stdout: the long table first, the
+        # decoder figures last
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline()
+        if table is not None:
+            line["matvec_configs"] = table
         if prefill is not None:
             line["prefill"] = prefill
         if model_prefill is not None:
             line["model_prefill"] = model_prefill
-        if table is not None:
-            line["matvec_configs"] = table
-        if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline()
+        if decode70 is not None:
+            line["decode_70b"] = decode70
+        if decode is not None:
+            line["decode"] = decode
         emit(line)
     if world > 1:
         import torch.distributed as dist

@@ -58,6 +58,14 @@ const char *tcb_strerror(int status);
 /* The last CUDA error string seen by this context (for TCB_ERR_CUDA). */
 const char *tcb_last_cuda_error(tcb_ctx *ctx);
 
+/* The context's device error word: TCB_OK, or the status a kernel recorded
+ * when one of its bounded device-side waits gave up (TCB_ERR_TIMEOUT), so a
+ * result computed past such a wait is never taken for a good one.  Waits for
+ * all work on the device first; clear = 1 resets the word.  TR panics with a
+ * coded message where a driver call fails (gpu/gpu.go, the H4xxx codes); the
+ * shim's kernels report through this word instead. */
+int tcb_device_error(tcb_ctx *ctx, int *status, int clear);
+
 /* elements and bytes of one block; 0,0 for an unknown type
  * (tensor.DType.QuantBlock, tensor/quant.go:35-47) */
 int tcb_block_shape(int wtype, int *elems, int *bytes);

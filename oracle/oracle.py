@@ -56,6 +56,7 @@ def lib():
     L.tcbo_dot_act8.argtypes = [I, I, P, P, P, P]
     L.tcbo_dot_act8.restype = ctypes.c_float
     L.tcbo_qgemm_act8.argtypes = [I, I, I, I, P, P, P, I]
+    L.tcbo_set_pinning.argtypes = [I]
     L.tcbo_embedding.argtypes = [I, P, I, P, I, P]
     L.tcbo_check_scales.argtypes = [I, P, Z]
     L.tcbo_check_scales.restype = ctypes.c_long
@@ -118,6 +119,12 @@ def qgemm_act8(fmt: int, a: np.ndarray, w: np.ndarray, N: int, c: np.ndarray | N
     out = np.zeros((M, N), np.float32) if c is None else np.array(c, dtype=np.float32, copy=True)
     lib().tcbo_qgemm_act8(fmt, M, N, K, _p(a), _p(w), _p(out), nthreads or os.cpu_count() or 1)
     return out
+
+
+def set_pinning(on: bool) -> None:
+    """Pin the row-parallel workers of the products, worker t to the t-th
+    CPU the process may run on (the timed CPU baseline)."""
+    lib().tcbo_set_pinning(1 if on else 0)
 
 
 def quantize_q8(x: np.ndarray, blk: int):

@@ -1,3 +1,4 @@
+#define _GNU_SOURCE
 /*
  * tcb_oracle.c - CPU restatement of TR's quantized-weight matvec path.
  *
@@ -302,10 +303,35 @@ float tcbo_quant_dot_scalar(int fmt, const float *x, const uint8_t *wrow, int K)
  * the result does not depend on the split */
 
 typedef void (*row_fn)(void *ctx, int lo, int hi);
-typedef struct { row_fn fn; void *ctx; int lo, hi; } row_job;
+typedef struct { row_fn fn; void *ctx; int lo, hi, cpu; } row_job;
+
+/* thread pinning for the timed CPU baseline: worker t runs on the t-th CPU
+ * of the process's allowed set (off unless tcbo_set_pinning(1)) */
+static int g_pin = 0;
+void tcbo_set_pinning(int on) { g_pin = on; }
+
+static int nth_allowed_cpu(int t) {
+  cpu_set_t set;
+  if (sched_getaffinity(0, sizeof set, &set) != 0) return -1;
+  const int n = CPU_COUNT(&set);
+  if (n <= 0) return -1;
+  int k = t % n;
+  for (int c = 0; c < CPU_SETSIZE; c++)
+    if (CPU_ISSET(c, &set) && k-- == 0) return c;
+  return -1;
+}
+
+static void pin_self(int cpu) {
+  if (cpu < 0) return;
+  cpu_set_t one;
+  CPU_ZERO(&one);
+  CPU_SET(cpu, &one);
+  pthread_setaffinity_np(pthread_self(), sizeof one, &one);
+}
 
 static void *row_thread(void *p) {
   row_job *j = (row_job *)p;
+  pin_self(j->cpu);
   j->fn(j->ctx, j->lo, j->hi);
   return NULL;
 }
@@ -324,12 +350,18 @@ static void parallel_rows(int n, int nthreads, row_fn fn, void *ctx) {
     jobs[t].ctx = ctx;
     jobs[t].lo = (int)((long)n * t / nthreads);
     jobs[t].hi = (int)((long)n * (t + 1) / nthreads);
+    jobs[t].cpu = g_pin ? nth_allowed_cpu(t) : -1;
     if (t == nthreads - 1) break;
     if (pthread_create(&th[t], NULL, row_thread, &jobs[t]) != 0) break;
     started = t + 1;
   }
-  /* this thread takes every slice a worker did not start */
+  /* this thread takes every slice a worker did not start (on the last
+   * slice's CPU when pinned; its own affinity is put back afterwards) */
+  cpu_set_t saved;
+  const int restore = g_pin && pthread_getaffinity_np(pthread_self(), sizeof saved, &saved) == 0;
+  if (g_pin) pin_self(jobs[nthreads - 1].cpu);
   for (int t = started; t < nthreads; t++) fn(ctx, jobs[t].lo, jobs[t].hi);
+  if (restore) pthread_setaffinity_np(pthread_self(), sizeof saved, &saved);
   for (int t = 0; t < started; t++) pthread_join(th[t], NULL);
 }
 

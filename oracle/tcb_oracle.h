@@ -5,7 +5,7 @@
  * it is the checker that tests/, __graft_entry__.smoke() and bench.py's
  * cpu_baseline leg compare the CUDA path against.
  *
- * Parity is pinned: tests/test_oracle_golden.py checks tcbo_dequant against
+ * Parity is pinned: tests/test_oracle.py checks tcbo_dequant against
  * the golden FNV-1a hashes of TR's TestDequantMatchesLlamaCpp
  * (internal/compute/tensor/quant_test.go:55-87) and the hand-computed blocks
  * of TestDequantKnownValues (quant_test.go:89-137).  The int8-activation
@@ -85,6 +85,9 @@ void tcbo_zero_raw(int fmt, uint8_t *raw, size_t nblocks);
 void tcbo_random_quant(int fmt, uint32_t seed, size_t nblocks, uint8_t *raw);
 
 /* FNV-1a 64 over the float32 bit patterns, little endian */
+/* pin the row-parallel workers, one per allowed CPU (timed baseline) */
+void tcbo_set_pinning(int on);
+
 uint64_t tcbo_fnv1a_f32(const float *y, size_t n);
 
 #ifdef __cplusplus

@@ -70,6 +70,7 @@ def lib() -> ctypes.CDLL:
     L.tcb_last_cuda_error.argtypes = [P]
     L.tcb_ctx_create.argtypes = [I, ctypes.POINTER(P)]
     L.tcb_ctx_destroy.argtypes = [P]
+    L.tcb_device_error.argtypes = [P, ctypes.POINTER(I), I]
     L.tcb_block_shape.argtypes = [I, ctypes.POINTER(I), ctypes.POINTER(I)]
     L.tcb_qgemm.argtypes = [P, I, I, I, I, P, P, I, Lg, P, I, Lg, I, P]
     L.tcb_qgemm_act8.argtypes = [P, I, I, I, I, P, P, I, Lg, P, I, Lg, I, P]
@@ -140,6 +141,13 @@ class Context:
             self.close()
         except Exception:
             pass
+
+    def device_error(self, clear: bool = False) -> int:
+        """The status a kernel of this context recorded when a bounded
+        device-side wait gave up (0 = none); waits for the device first."""
+        st = ctypes.c_int(0)
+        self._check(lib().tcb_device_error(self._h, ctypes.byref(st), int(clear)), "tcb_device_error")
+        return st.value
 
     def _check(self, rc: int, what: str):
         if rc:

@@ -10,6 +10,7 @@ from __future__ import annotations
 import os
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
@@ -33,16 +34,23 @@ def build(verbose: bool = False, force: bool = False) -> str:
     os.makedirs(bdir, exist_ok=True)
     headers = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".h", ".cuh"))]
     headers.append(os.path.join(os.path.dirname(HERE), "include", "tcb.h"))
-    objs = []
+    objs, cmds = [], []
     for src in SOURCES:
         s = os.path.join(CSRC, src)
         o = os.path.join(bdir, src.replace(".cu", ".o"))
         objs.append(o)
         if force or _stale([o], [s] + headers):
-            cmd = [NVCC, *ARCH, *FLAGS, "-c", s, "-o", o]
-            if verbose:
-                print(" ".join(cmd), flush=True)
-            subprocess.run(cmd, check=True)
+            cmds.append([NVCC, *ARCH, *FLAGS, "-c", s, "-o", o])
+
+    def compile_one(cmd):
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.run(cmd, check=True)
+
+    # the translation units are independent: compile them side by side
+    with ThreadPoolExecutor(max_workers=max(1, min(len(cmds), os.cpu_count() or 1))) as ex:
+        for f in [ex.submit(compile_one, c) for c in cmds]:
+            f.result()
     if force or _stale([LIB], objs):
         cmd = [NVCC, *ARCH, "-shared", "-cudart", "static", "-o", LIB, *objs]
         if verbose:

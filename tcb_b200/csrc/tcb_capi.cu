@@ -216,6 +216,18 @@ int tcb_ctx_create(int device, tcb_ctx **out) {
   return TCB_OK;
 }
 
+int tcb_device_error(tcb_ctx *ctx, int *status, int clear) {
+  if (!ctx || !status) return TCB_ERR_NULL;
+  *status = TCB_OK;
+  if (cudaSetDevice(ctx->dev) != cudaSuccess) return TCB_ERR_CUDA;
+  // every stream's work first: the word is set by kernels still in flight
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpy(status, ctx->derr, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && clear) e = cudaMemset(ctx->derr, 0, sizeof(int));
+  if (e == cudaSuccess && clear) e = cudaDeviceSynchronize();
+  return e == cudaSuccess ? TCB_OK : cuda_fail(ctx, e);
+}
+
 int tcb_ctx_destroy(tcb_ctx *ctx) {
   if (!ctx) return TCB_OK;
   int rc = TCB_OK;

@@ -76,62 +76,118 @@ def local_shapes(cfg: LlamaConfig, tp: int) -> dict:
             "gate_up": (2 * F, D), "down": (D, F), "head": (cfg.vocab // tp, D)}
 
 
-def _rows(a: np.ndarray, kind: str, K: int, r0: int, r1: int) -> np.ndarray:
+# The "varied" decoder (parity tests and the benchmark models): Q4_K blocks
+# centred (mins = sub-scales, dmin = 7.5 d, so a sub-block dequantises to
+# d*sc*(q - 7.5)), the qkv scales 5x and the o/down scales 2x D_STD (sharper
+# attention, larger sublayer outputs), and the head's block scales in a narrow
+# band.  With the plain blocks a random decoder's greedy continuation
+# collapses onto one or two tokens; this one visits tens of distinct tokens in
+# 64 steps, so token-level parity checks the attention over a growing context.
+VARIED_SCALE = {"qkv": 5.0, "o": 2.0, "down": 2.0}
+VARIED_HEAD_BAND = (1.0e-5, 1.4e-5)
+KINDS = ("tok_emb", "head", "qkv", "o", "gate_up", "down")
+
+
+def _rows(a, kind: str, K: int, r0: int, r1: int):
     """rows [r0, r1) of a block store with K columns"""
     e, b = BLOCK[TYPES[kind]]
     rb = K // e * b
     return a[r0 * rb:r1 * rb]
 
 
-def _cols(a: np.ndarray, kind: str, N: int, K: int, k0: int, k1: int) -> np.ndarray:
+def _cols(a, kind: str, N: int, K: int, k0: int, k1: int):
     """columns [k0, k1) (block aligned) of a block store of N rows"""
     e, b = BLOCK[TYPES[kind]]
     return a.reshape(N, K // e, b)[:, k0 // e:k1 // e].reshape(-1)
 
 
-def shard(cfg: LlamaConfig, model: dict, tp: int, r: int) -> dict:
-    """Rank r's part of a host model for tensor parallelism over tp ranks:
-    column-parallel qkv (its query heads and their KV heads) and gate/up
-    (its rows of each half), row-parallel (K-split) o and down,
-    vocabulary-parallel head; embedding and norms replicated."""
-    if tp == 1:
-        return model
+def _cat(parts):
+    if isinstance(parts[0], np.ndarray):
+        return np.concatenate(parts)
+    import torch
+
+    return torch.cat(parts).contiguous()
+
+
+def shard_tensor(cfg: LlamaConfig, kind: str, w, tp: int, r: int):
+    """Rank r's part of one global weight (numpy array or torch tensor) for
+    tensor parallelism over tp ranks: column-parallel qkv (its query heads and
+    their KV heads) and gate/up (its rows of each half), row-parallel (K-split)
+    o and down, vocabulary-parallel head; the embedding and the norms are
+    replicated (returned as they are)."""
+    if tp == 1 or kind in ("tok_emb", "attn_norm", "ffn_norm", "final_norm"):
+        return w
     H, KVH, hd, D, F, V = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.d_model, cfg.ffn_dim, cfg.vocab
     h, kv, f, v = H // tp, KVH // tp, F // tp, V // tp
-    out = {"cfg": cfg, "tok_emb": model["tok_emb"], "final_norm": model["final_norm"],
-           "attn_norm": model["attn_norm"], "ffn_norm": model["ffn_norm"],
-           "head": _rows(model["head"], "head", D, r * v, (r + 1) * v)}
-    out["qkv"] = [np.concatenate([_rows(w, "qkv", D, r * h * hd, (r + 1) * h * hd),
-                                  _rows(w, "qkv", D, (H + r * kv) * hd, (H + (r + 1) * kv) * hd),
-                                  _rows(w, "qkv", D, (H + KVH + r * kv) * hd, (H + KVH + (r + 1) * kv) * hd)])
-                  for w in model["qkv"]]
-    out["o"] = [_cols(w, "o", D, H * hd, r * h * hd, (r + 1) * h * hd) for w in model["o"]]
-    out["gate_up"] = [np.concatenate([_rows(w, "gate_up", D, r * f, (r + 1) * f),
-                                      _rows(w, "gate_up", D, F + r * f, F + (r + 1) * f)]) for w in model["gate_up"]]
-    out["down"] = [_cols(w, "down", D, F, r * f, (r + 1) * f) for w in model["down"]]
+    if kind == "head":
+        return _rows(w, "head", D, r * v, (r + 1) * v)
+    if kind == "qkv":
+        return _cat([_rows(w, "qkv", D, r * h * hd, (r + 1) * h * hd),
+                     _rows(w, "qkv", D, (H + r * kv) * hd, (H + (r + 1) * kv) * hd),
+                     _rows(w, "qkv", D, (H + KVH + r * kv) * hd, (H + KVH + (r + 1) * kv) * hd)])
+    if kind == "o":
+        return _cols(w, "o", D, H * hd, r * h * hd, (r + 1) * h * hd)
+    if kind == "gate_up":
+        return _cat([_rows(w, "gate_up", D, r * f, (r + 1) * f), _rows(w, "gate_up", D, F + r * f, F + (r + 1) * f)])
+    if kind == "down":
+        return _cols(w, "down", D, F, r * f, (r + 1) * f)
+    raise ValueError(kind)
+
+
+def shard(cfg: LlamaConfig, model: dict, tp: int, r: int) -> dict:
+    """Rank r's part of a host model for tensor parallelism over tp ranks
+    (shard_tensor applied to every tensor)."""
+    if tp == 1:
+        return model
+    out = {"cfg": cfg}
+    for k, v in model.items():
+        if k == "cfg":
+            continue
+        if k in ("tok_emb", "attn_norm", "ffn_norm", "final_norm"):
+            out[k] = v  # replicated
+        else:
+            out[k] = [shard_tensor(cfg, k, x, tp, r) for x in v] if isinstance(v, list) else shard_tensor(cfg, k, v, tp, r)
     return out
 
 
-def host_model(cfg: LlamaConfig, seed: int) -> dict:
+def _d_std(kind: str, varied: bool) -> float:
+    return D_STD[TYPES[kind]] * (VARIED_SCALE.get(kind, 1.0) if varied else 1.0)
+
+
+def host_model(cfg: LlamaConfig, seed: int, varied: bool = False) -> dict:
     """Seeded model as numpy arrays (small configurations: parity tests)."""
     sh = shapes(cfg)
     m = {"cfg": cfg}
     rng = np.random.default_rng(seed)
     s = seed * 1000
-    m["tok_emb"] = synth.weight(TYPES["tok_emb"], *sh["tok_emb"], s + 1, D_STD[TYPES["tok_emb"]])
-    m["head"] = synth.weight(TYPES["head"], *sh["head"], s + 2, D_STD[TYPES["head"]])
+
+    def w(kind, sd):
+        wt = TYPES[kind]
+        return synth.weight(wt, *sh[kind], sd, _d_std(kind, varied), centered=varied and wt == Q4_K,
+                            d_band=VARIED_HEAD_BAND if varied and kind == "head" else None)
+
+    m["tok_emb"] = w("tok_emb", s + 1)
+    m["head"] = w("head", s + 2)
     m["final_norm"] = (1.0 + 0.1 * rng.standard_normal(cfg.d_model)).astype(np.float32)
     for k in ("attn_norm", "ffn_norm"):
         m[k] = [(1.0 + 0.1 * rng.standard_normal(cfg.d_model)).astype(np.float32) for _ in range(cfg.n_layers)]
     for j, k in enumerate(("qkv", "o", "gate_up", "down")):
-        m[k] = [synth.weight(TYPES[k], *sh[k], s + 10 + 4 * l + j, D_STD[TYPES[k]]) for l in range(cfg.n_layers)]
+        m[k] = [w(k, s + 10 + 4 * l + j) for l in range(cfg.n_layers)]
     return m
 
 
-def device_model(cfg: LlamaConfig, seed: int, host: dict | None = None, tp: tuple = (1, 0)) -> dict:
-    """The model on cuda:0: uploads `host` if given, else generates the
-    blocks on the GPU (fp16 block scales |N(0, D_STD)|, every other byte
-    uniform, as host_model)."""
+def device_model(cfg: LlamaConfig, seed: int, host: dict | None = None, tp: tuple = (1, 0),
+                 varied: bool = False) -> dict:
+    """This rank's part of a model on the current CUDA device: uploads `host`
+    (sharded) if given, else generates it on the GPU (fp16 block scales
+    |N(0, D_STD)|, every other byte uniform; `varied` as host_model).
+
+    Generated models are one model at every tensor-parallel degree: each
+    global tensor is drawn from its own counter-based (Philox) CUDA generator
+    seeded by (seed, tensor), and a rank keeps its slice of it
+    (shard_tensor).  Replicated tensors are byte-identical on every rank, and
+    rank r of tp holds the same bytes as the matching slice of the tp = 1
+    model."""
     import torch
 
     def up(a):
@@ -145,30 +201,51 @@ def device_model(cfg: LlamaConfig, seed: int, host: dict | None = None, tp: tupl
                 continue
             d[k] = [up(x) for x in v] if isinstance(v, list) else up(v)
         return d
-    sh = local_shapes(cfg, tp[0])
+    sh = shapes(cfg)
     gen = torch.Generator(device="cuda")
-    gen.manual_seed(seed * 64 + tp[1])
 
-    def blocks(kind):
+    def seeded(tid: int):
+        gen.manual_seed((seed * 1000003 + tid) & 0x7FFFFFFFFFFFFFFF)
+        return gen
+
+    def blocks(kind, tid):
+        g = seeded(tid)
         wt = TYPES[kind]
         n, k = sh[kind]
         e, size = BLOCK[wt]
         nb = n * k // e
-        out = torch.randint(0, 256, (nb, size), dtype=torch.uint8, device="cuda", generator=gen)
+        out = torch.randint(0, 256, (nb, size), dtype=torch.uint8, device="cuda", generator=g)
+        sd = _d_std(kind, varied)
         if wt == Q4_K:
-            out[:, 0:4] = (torch.randn(nb, 2, device="cuda", generator=gen).abs() * D_STD[wt]).half().view(torch.uint8)
+            out[:, 0:4] = (torch.randn(nb, 2, device="cuda", generator=g).abs() * sd).half().view(torch.uint8)
+            if varied:
+                # mins = sub-scales (get_scale_min_k4 packing), dmin = 7.5 d
+                out[:, 8:12] = (out[:, 8:12] & 0x0F) | ((out[:, 8:12] & 0x0F) << 4)
+                out[:, 4:8] = out[:, 0:4]
+                d = out[:, 0:2].contiguous().view(torch.float16).float()
+                out[:, 2:4] = (d * 7.5).half().view(torch.uint8)
         elif wt == Q6_K:
-            out[:, 208:210] = (torch.randn(nb, 1, device="cuda", generator=gen).abs() * D_STD[wt]).half().view(torch.uint8)
-        return out.reshape(-1)
+            if varied and kind == "head":
+                lo, hi = VARIED_HEAD_BAND
+                dv = lo + (hi - lo) * torch.rand(nb, 1, device="cuda", generator=g)
+            else:
+                dv = torch.randn(nb, 1, device="cuda", generator=g).abs() * sd
+            out[:, 208:210] = dv.half().view(torch.uint8)
+        out = out.reshape(-1)
+        local = shard_tensor(cfg, kind, out, *tp)
+        if local.numel() != out.numel() and local.untyped_storage().data_ptr() == out.untyped_storage().data_ptr():
+            local = local.clone()  # a view would keep the whole global tensor alive
+        return local
 
-    def norm():
-        return 1.0 + 0.1 * torch.randn(cfg.d_model, device="cuda", generator=gen)
+    def norm(tid):
+        return 1.0 + 0.1 * torch.randn(cfg.d_model, device="cuda", generator=seeded(tid))
 
-    d = {"cfg": cfg, "tok_emb": blocks("tok_emb"), "head": blocks("head"), "final_norm": norm()}
-    d["attn_norm"] = [norm() for _ in range(cfg.n_layers)]
-    d["ffn_norm"] = [norm() for _ in range(cfg.n_layers)]
-    for k in ("qkv", "o", "gate_up", "down"):
-        d[k] = [blocks(k) for _ in range(cfg.n_layers)]
+    L = cfg.n_layers
+    d = {"cfg": cfg, "tok_emb": blocks("tok_emb", 1), "head": blocks("head", 2), "final_norm": norm(3)}
+    d["attn_norm"] = [norm(16 + 8 * l) for l in range(L)]
+    d["ffn_norm"] = [norm(17 + 8 * l) for l in range(L)]
+    for j, k in enumerate(("qkv", "o", "gate_up", "down")):
+        d[k] = [blocks(k, 18 + j + 8 * l) for l in range(L)]
     return d
 
 

@@ -41,4 +41,6 @@ def main(root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: extract_tr_golden.py <TR source tree>")
+    main(sys.argv[1])

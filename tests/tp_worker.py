@@ -1,9 +1,19 @@
-"""One rank of the tensor-parallel decoder check (run with torchrun by
-tests/test_gpu_tp.py): the small decoder sharded over the ranks, greedy
-tokens eager and from the captured graph; with "prefill" a longer prompt fed
-by the prompt pass (residual rows summed over the ranks).  Rank 0 prints the
-tokens as JSON."""
-import json
+"""One rank of the tensor-parallel decoder checks (run with torchrun by
+tests/test_gpu_tp.py).  Every run steps the engine one token at a time and
+records, per step, the full logits (the ranks' vocabulary slices gathered
+in rank order); rank 0 writes them with the token histories to an .npz.
+
+    tp_worker.py OUT.npz steps            the small decoder (host model, the
+                                          CPU reference's test model), greedy
+    tp_worker.py OUT.npz prefill          the same, a 100-token prompt fed by
+                                          the prompt pass
+    tp_worker.py OUT.npz shape70 [FORCED.npy]
+                                          a 2-layer 70B-shaped decoder
+                                          generated on the device (the same
+                                          weights at every tensor-parallel
+                                          degree), greedy, or fed the token
+                                          history in FORCED.npy
+"""
 import os
 import sys
 
@@ -17,8 +27,22 @@ from tcb_b200 import llama  # noqa: E402
 
 CFG = llama.LlamaConfig(n_layers=2, d_model=512, n_heads=4, n_kv_heads=2, head_dim=128, ffn_dim=1024,
                         vocab=2048, max_ctx=160, eps=1e-5, rope_theta=500000.0)
+SEED = 15
 PROMPT = np.array([17, 901, 5, 1333, 42, 2047, 0, 777], np.int64)
 LONG_PROMPT = np.random.default_rng(23).integers(0, CFG.vocab, 100).astype(np.int64)
+GEN = {"steps": 64, "prefill": 40, "shape70": 40}
+
+CFG70 = llama.LlamaConfig(n_layers=2, d_model=8192, n_heads=64, n_kv_heads=8, head_dim=128, ffn_dim=28672,
+                          vocab=128256, max_ctx=96, eps=1e-5, rope_theta=500000.0)
+SEED70 = 4
+PROMPT70 = np.random.default_rng(29).integers(0, CFG70.vocab, 16).astype(np.int64)
+
+
+def gathered_logits(m, world):
+    lg = torch.from_numpy(m.logits().copy())
+    parts = [None] * world
+    dist.all_gather_object(parts, lg.numpy())
+    return np.concatenate(parts)
 
 
 def main():
@@ -26,34 +50,51 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
     dist.init_process_group("gloo")
+    out_path, mode = sys.argv[1], sys.argv[2]
     ctx = T.Context(local)
-    host = llama.host_model(CFG, seed=5)
-    dev = llama.device_model(CFG, 5, host, tp=(world, rank))
+    if mode == "shape70":
+        cfg = CFG70
+        dev = llama.device_model(cfg, SEED70, tp=(world, rank), varied=True)
+        forced = np.load(sys.argv[3]) if len(sys.argv) > 3 else None
+        prompt = forced if forced is not None else PROMPT70
+    else:
+        cfg = CFG
+        host = llama.host_model(cfg, seed=SEED, varied=True)
+        dev = llama.device_model(cfg, SEED, host, tp=(world, rank))
+        forced = None
+        prompt = LONG_PROMPT if mode == "prefill" else PROMPT
+    gen = 0 if forced is not None else GEN[mode]
+    n = len(prompt) + gen
     m = llama.Llama(ctx, dev, tp=(world, rank))
     m.tp_init(llama.share_id(llama.nccl_unique_id, rank))
-    gen = int(sys.argv[1] if len(sys.argv) > 1 else 64)
-    pre = len(sys.argv) > 2 and sys.argv[2] == "prefill"
-    prompt = LONG_PROMPT if pre else PROMPT
-    n = len(prompt) + gen
 
-    def feed():
-        m.start(prompt)
-        if pre:
-            m.prefill()
-            m.step(gen)
-        else:
-            m.step(n - 1)
-
-    feed()
+    # eager, one step at a time, logits of every step
+    m.start(prompt)
+    first = 0
+    if mode == "prefill":
+        m.prefill()
+        first = len(prompt) - 1
+    logits = []
+    for _ in range(first, n - 1):
+        m.step(1)
+        logits.append(gathered_logits(m, world))
     eager = m.tokens(n)
+    # the captured graph
     m.start(prompt)
     m.capture()
-    feed()
+    m.start(prompt)
+    if mode == "prefill":
+        m.prefill()
+    m.step(n - 1 - first)
     graph = m.tokens(n)
     all_tok = [None] * world
     dist.all_gather_object(all_tok, eager.tolist())
+    err = [None] * world
+    dist.all_gather_object(err, ctx.device_error())
     if rank == 0:
-        print(json.dumps({"eager": eager.tolist(), "graph": graph.tolist(), "same_on_ranks": all(t == all_tok[0] for t in all_tok)}))
+        np.savez(out_path, eager=eager, graph=graph, logits=np.stack(logits), first=first,
+                 same_on_ranks=all(t == all_tok[0] for t in all_tok), peer=bool(getattr(m, "peer_active", False)),
+                 device_errors=np.array(err, np.int64))
     m.close()
     dist.barrier()
     dist.destroy_process_group()
