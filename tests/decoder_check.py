@@ -10,6 +10,9 @@ exactly the context the GPU saw:
     first maximum, or its reference logit is within TOL * max|logit| of that
     maximum (a tie at float precision, counted and returned).
 
+tol replaces TOL for paths whose operands are rounded to fp16 on purpose
+(the prompt pass's tensor-core products and attention).
+
 Nothing is skipped after a mismatch: a token outside the tie band fails the
 check at the position where it happens.
 """
@@ -30,7 +33,7 @@ def distinct_generated(tokens, n_prompt: int) -> int:
     return len(set(int(t) for t in tokens[n_prompt:]))
 
 
-def check_history(host: dict, tokens, n_prompt: int, gpu_logits: dict | None = None) -> dict:
+def check_history(host: dict, tokens, n_prompt: int, gpu_logits: dict | None = None, tol: float = TOL) -> dict:
     """Feed tokens[0..n-2] to a fresh reference decoder and check the GPU
     history `tokens` (prompt, then greedy) position by position.
 
@@ -46,7 +49,7 @@ def check_history(host: dict, tokens, n_prompt: int, gpu_logits: dict | None = N
         lg = ref.step(tokens[pos], pos)
         if gpu_logits is not None and pos in gpu_logits:
             e = rel_l2(gpu_logits[pos], lg)
-            assert e <= TOL, f"logits at position {pos}: rel-L2 {e:.3e}"
+            assert e <= tol, f"logits at position {pos}: rel-L2 {e:.3e}"
             worst = max(worst, e)
             nl += 1
         nxt = pos + 1
@@ -56,7 +59,7 @@ def check_history(host: dict, tokens, n_prompt: int, gpu_logits: dict | None = N
         got = tokens[nxt]
         nt += 1
         if got != best:
-            band = TOL * float(np.abs(lg).max())
+            band = tol * float(np.abs(lg).max())
             gap = float(lg[best] - lg[got])
             assert gap < band, f"token at position {nxt}: {got} (reference {best}, gap {gap:.4g} > tie band {band:.4g})"
             ties.append(nxt)

@@ -4,7 +4,8 @@ box has fewer GPUs), one process per GPU under torchrun (tests/tp_worker.py).
   * The small test decoder sharded over 2 ranks against the CPU reference
     (oracle/llama_ref.py), fed the GPU's own history: logits within rel-L2
     1e-3 at every step, all 64 greedy tokens equal to the reference's, the
-    same on every rank, eager and graph alike; the same after a prompt pass.
+    same on every rank, eager and graph alike; after a prompt pass (fp16
+    tensor-core products and attention) within 5e-3.
   * A 2-layer 70B-shaped decoder generated on the device (one model at every
     degree: each global tensor drawn from its own counter-based generator,
     every rank keeping its slice) at TP 2/4/8 against the same model at
@@ -72,7 +73,8 @@ def test_tp2_matches_reference(oracle, tmp_path, mode):
     assert list(got[:len(prompt)]) == list(prompt)
     first = int(d["first"])
     logits = {first + i: lg for i, lg in enumerate(d["logits"])}
-    res = check_history(host, got, len(prompt), logits)
+    # the prompt pass rounds to fp16 on the tensor cores (tests/test_gpu_llama_prefill.py)
+    res = check_history(host, got, len(prompt), logits, tol=5e-3 if mode == "prefill" else TOL)
     assert res["checked_tokens"] == gen and res["checked_logits"] == len(logits)
     ref, _, _ = Reference(host).generate(prompt, len(prompt) + gen - 1)
     assert distinct_generated(ref, len(prompt)) >= 16
