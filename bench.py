@@ -400,7 +400,8 @@ def decode_tp_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
     cfg = llama.LLAMA3_70B
     model = llama.device_model(cfg, seed=9, tp=(world, rank), varied=True)
     eng = llama.Llama(ctx, model, tp=(world, rank))
-    eng.tp_init(llama.share_id(llama.nccl_unique_id, rank))
+    if world > 1:
+        eng.tp_init(llama.share_id(llama.nccl_unique_id, rank))
     prompt = np.random.default_rng(13).integers(0, cfg.vocab, 1024)
     stream = torch.cuda.Stream()
     eng.start(prompt, stream)

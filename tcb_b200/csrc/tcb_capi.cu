@@ -59,6 +59,25 @@ int ensure_ws(tcb_ctx *ctx, size_t bytes) {
   return TCB_OK;
 }
 
+// grow the matvec kernels' scratch to at least `bytes` (zeroed; launches
+// leave it zeroed), after the device has finished with the old one
+int ensure_sk(tcb_ctx *ctx, size_t bytes) {
+  if (bytes <= ctx->sk_cap) return TCB_OK;
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  if (bytes <= ctx->sk_cap) return TCB_OK;
+  if (ctx->sk) {
+    TCB_CU(ctx, cudaDeviceSynchronize());
+    cudaFree(ctx->sk);
+    ctx->sk = nullptr;
+    ctx->sk_cap = 0;
+  }
+  const size_t cap = bytes + (bytes >> 1);
+  TCB_CU(ctx, cudaMalloc(&ctx->sk, cap));
+  TCB_CU(ctx, cudaMemset(ctx->sk, 0, cap));
+  ctx->sk_cap = cap;
+  return TCB_OK;
+}
+
 // The TMA matvec kernels: plan, scratch, launch; *taken = false when the
 // shape goes to another kernel.  They take the float product below the
 // tensor-core path's minimum M and the int8-activation product at every M,
@@ -80,6 +99,8 @@ int run_matvec(tcb_ctx *ctx, int wtype, int act8, int M, int N, int K, const voi
     for (int mr = 8; mr >= 2 && !pq.ok; mr /= 2)
       if (mr <= 2 * M - 1 || mr == 2) pq = tcb::matvec_plan_rows(wtype, act8, N, K, w, ctx->sms, mr);
     if (pq.ok) {
+      int rc = ensure_sk(ctx, pq.split_bytes);
+      if (rc != TCB_OK) return rc;
       *taken = true;
       for (int m0 = 0; m0 < M; m0 += pq.rows) {
         const int rows = M - m0 < pq.rows ? M - m0 : pq.rows;
@@ -94,22 +115,8 @@ int run_matvec(tcb_ctx *ctx, int wtype, int act8, int M, int N, int K, const voi
   }
   tcb::MvPlan pl = tcb::matvec_plan(wtype, act8, 1, N, K, w, ctx->sms);
   if (!pl.ok) return TCB_OK;
-  if (pl.split_bytes > ctx->sk_cap) {
-    // grow the split-K scratch (after the device has finished with the old one)
-    std::lock_guard<std::mutex> lock(ctx->mu);
-    if (pl.split_bytes > ctx->sk_cap) {
-      if (ctx->sk) {
-        TCB_CU(ctx, cudaDeviceSynchronize());
-        cudaFree(ctx->sk);
-        ctx->sk = nullptr;
-        ctx->sk_cap = 0;
-      }
-      const size_t cap = pl.split_bytes + (pl.split_bytes >> 1);
-      TCB_CU(ctx, cudaMalloc(&ctx->sk, cap));
-      TCB_CU(ctx, cudaMemset(ctx->sk, 0, cap));
-      ctx->sk_cap = cap;
-    }
-  }
+  int rc = ensure_sk(ctx, pl.split_bytes);
+  if (rc != TCB_OK) return rc;
   *taken = true;
   for (int m = 0; m < M; m++) {
     const void *xm = static_cast<const char *>(x) + (size_t)m * ldx * elem_size(xdt);

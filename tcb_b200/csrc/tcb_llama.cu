@@ -777,8 +777,8 @@ cudaError_t matvec(tcb_llama *m, const Mat &mt, const float *x, float *y, int ac
 cudaError_t norm_matvec(tcb_llama *m, const Mat &mt, const float *nw, float *y, cudaStream_t s) {
   const tcb_llama_config &c = m->cfg;
   if (mt.plan.ok && mt.plan.kind == 1)
-    return tcb::q4k_launch(mt.plan, mt.N, mt.K, mt.w, m->x, TCB_F32, y, TCB_F32, 0, m->ctx->derr, s, nw, c.eps, mt.pf,
-                           mt.pf_bytes);
+    return tcb::q4k_launch(mt.plan, mt.N, mt.K, mt.w, m->x, TCB_F32, y, TCB_F32, 0, m->ctx->derr, m->sk, s, nw, c.eps,
+                           mt.pf, mt.pf_bytes);
   cudaError_t e = tcb::ll::launch(tcb::ll::k_rmsnorm, dim3(1), dim3(1024), s, m->x, nw, m->h, c.d_model, c.eps);
   return e == cudaSuccess ? matvec(m, mt, m->h, y, 0, s) : e;
 }

@@ -24,6 +24,13 @@ struct MvPlan {
 // smallest N that takes the Q6_K float kernel (kind 2)
 constexpr int kQ6kMinRows = 32768;
 
+// The matvec kernels' scratch (plan.split_bytes, shared by every launch of a
+// context or decoder): [0, kScratchCntBytes) arrival counters, which start at
+// zero and are left at zero by every launch, then partial sums, which any
+// launch may overwrite.  The layout does not depend on the shape, so one
+// launch's partials never land on another's counters.
+constexpr size_t kScratchCntBytes = 1024;
+
 MvPlan matvec_plan(int wtype, int act8, int M, int N, int K, const void *w, int sms);
 // up to mr (2, 4, 8) rows of x per launch streaming the weights once, float
 // or int8-activation path (ok = false when the rows' x regions leave too
@@ -35,10 +42,12 @@ MvPlan matvec_plan_rows(int wtype, int act8, int N, int K, const void *w, int sm
 // assumed) is fused into the prologue.
 // mr (1, 2, 4, 8): the most rows of x one launch takes; a launch of M <= mr
 // rows (row strides ldx, ldc) streams the weights once for all of them.
+// scratch: plan.split_bytes of the matvec scratch (none for this kernel).
 MvPlan q4k_plan(int N, int K, const void *w, int sms, int mr = 1);
 cudaError_t q4k_launch(const MvPlan &pl, int N, int K, const void *w, const void *x, int xdt, void *c, int cdt,
-                       int accumulate, int *err, cudaStream_t s, const float *nw = nullptr, float eps = 0.f,
-                       const void *pf = nullptr, size_t pf_bytes = 0, int M = 1, long ldx = 0, long ldc = 0);
+                       int accumulate, int *err, void *scratch, cudaStream_t s, const float *nw = nullptr,
+                       float eps = 0.f, const void *pf = nullptr, size_t pf_bytes = 0, int M = 1, long ldx = 0,
+                       long ldc = 0);
 
 // Q6_K float path (kind 2).  With gated, x holds [G | U] (2K elements) and
 // the input is silu(G) * U (a SwiGLU gate fused into the prologue).

@@ -1,37 +1,23 @@
-// tcb_mv_q4k.cu - Q4_K matvec, float path (x in f32/bf16/f16), 1 to 8 rows
-// of x per launch:
+// tcb_mv_q4k.cu - batch-1 Q4_K matvec, float path (x in f32/bf16/f16):
 //
-//   y[m, n] (+)= sum_k x[m, k] * dequant(W)[n, k]     W: [N, K] Q4_K blocks
+//   y[n] (+)= sum_k x[k] * dequant(W)[n, k]     W: [N, K] Q4_K blocks
 //
 // The kernel is a weight stream: every byte of W is read once, so its speed
-// is HBM bandwidth, and at 14-140 MB per call the launch ramp and the tail
-// are a large part of it.  Two choices follow from that.
+// is HBM bandwidth, and at 25-140 MB per call the launch ramp and tail are a
+// large part of it.  The design therefore keeps each CTA small (about
+// 90-110 KB of shared memory, 10 warps) so that two fit on an SM: with
+// programmatic dependent launch the next call's CTAs start on an SM as soon
+// as one of this call's CTAs leaves it, and stream their first weight
+// stages while this call finishes.
 //
-//  * Balanced work.  The weight is cut into units of (32-row tile, Q4_K
-//    block), tile-major, and a launch of G = min(148, units) CTAs gives CTA c
-//    the units [U c / G, U (c + 1) / G): every CTA streams the same bytes to
-//    within one block column of a tile, whatever N and K are.  (Whole tiles
-//    per CTA left 48 of 148 SMs a third tile on the 11008 x 4096 product,
-//    1.29 times the mean, and 4096-row products 20 SMs idle.)  A tile whose
-//    blocks fall to several CTAs is reduced deterministically: each
-//    contributor writes its row partials to scratch, counts itself in a
-//    per-tile counter, and the last to arrive adds the partials in CTA order
-//    and stores y, then resets the counter (scratch counters start at zero
-//    and are left at zero).  G does not depend on the device, so neither do
-//    the partition and the summation order.
-//  * One CTA per SM, at most 113 KB of shared memory, so that the next
-//    kernel of the stream (programmatic dependent launch, triggered at entry)
-//    fits beside it and fills its first weight stages before this one ends.
-//    Weights are only read, so the producer issues its first stages before
-//    the dependency wait; x, c and the scratch are touched after it.
-//
-//  * A stage is one chunk of a tile: blocks 8j .. 8j+7 of its 32 rows (cut to
-//    the CTA's units), each block loaded by its own TMA box of 32 rows x 144
-//    bytes into slot (block mod 8) of the stage: [slot][row][144 B].  Rows
-//    past N are zero-filled by the copy engine.  Compute warp w (of 8) takes
-//    slot (w + c) mod 8 of every stage for both 16-row slices of the tile.
-//    Row g of a slot starts at 144 g bytes, so the lanes' 16-byte reads of 8
-//    rows fall in distinct banks.
+//  * A tile is 32 rows.  A stage is one 2-D TMA box of those 32 rows x 8
+//    Q4_K blocks (1152 bytes + 16 bytes of padding per row, so the staged
+//    row pitch is 16 mod 128 and the lane reads below are conflict-free),
+//    issued by a producer warp; rows past N and bytes past the row end are
+//    zero-filled by the copy engine.  Compute warp w (of 8) takes block w of
+//    every stage for both 16-row slices of the tile, sharing the x
+//    fragments (measured faster than 16-row tiles, although those balance
+//    the CTAs better).
 //  * x is split per 32-element sub-block into two int8 digits,
 //    x ~= sigma * (h + l/254), sigma = amax/127 (relative error of the x
 //    representation below 1/(2*127*254) of the sub-block maximum).  Each
@@ -54,11 +40,10 @@
 //    The MMAs of a block are issued before the epilogue of the warp's
 //    previous block, so tensor-core latency hides behind ALU work.
 //  * Tile partials: each warp's row sums go to shared memory; an epilogue
-//    warp adds the 8 warp partials of a row in slot order and stores y (or
-//    the CTA's partial, see above).
+//    warp adds the 8 warp partials of a row in warp order and stores y.
+//    Results do not depend on the grid or on timing.
 //  * A NaN or Inf in x (any sub-block sum non-finite) sends the whole call
-//    down TR's fp32 path, one warp per row (each tile computed whole by the
-//    CTA that holds its first unit), so NaN/Inf propagate as in TR.
+//    down TR's fp32 path, one warp per row, so NaN/Inf propagate as in TR.
 #include <string.h>
 
 #include "tcb_common.cuh"
@@ -75,18 +60,17 @@ constexpr int kC = 8;                       // compute warps
 constexpr int kProd = kC;                   // producer warp
 constexpr int kEpi = kC + 1;                // epilogue warp
 constexpr int kWarps = kC + 2;
-constexpr int kRows = 32;                   // rows per tile
+constexpr int kRows = 32;                   // rows per tile (one box)
 constexpr int kHalves = kRows / 16;         // 16-row MMA slices per tile
-constexpr int kBlk = 8;                     // Q4_K blocks per stage (one chunk of a tile)
-constexpr int kBox8 = 18;                   // box width, 8-byte elements (one 144-byte block)
-constexpr int kPitch = 144;                 // staged row pitch inside a block slot
-constexpr int kSlotBytes = kRows * kPitch;  // one block of a tile: one TMA box
-constexpr int kStageBytes = kBlk * kSlotBytes;
+constexpr int kBlk = 8;                     // Q4_K blocks per box
+constexpr int kBox8 = 146;                  // box width, 8-byte elements (8 * 18 + 2)
+constexpr int kPitch = kBox8 * 8;           // staged row pitch (1168 = 16 mod 128)
+constexpr int kBoxBytes = kRows * kPitch;   // one stage
 constexpr int kSlots = 4;                   // tile partial slots in flight
 constexpr int kFrag = 512, kScl = 64;       // per block: B fragments, lane scales
 constexpr int kBarOff = 0, kFlagOff = 256, kNormOff = 288, kPartOff = 512;
 constexpr int kPartBytes = kSlots * kC * kRows * 4;
-constexpr int kGridMax = 148;               // CTAs of a launch: the B200's SMs, fixed (see above)
+constexpr int kXOff = kPartOff + kPartBytes;
 
 struct Params {
   const uint8_t *w;
@@ -96,8 +80,7 @@ struct Params {
   void *c;
   int cdt;
   int accumulate;
-  long long U;      // units: tiles * nb
-  int S;            // stages
+  int tiles, nch, S;
   int *err;
   int soff;         // stage offset in shared memory
   const float *nw;  // RMSNorm weight fused into the prologue (nullptr: none)
@@ -107,14 +90,7 @@ struct Params {
   int M;            // activation rows of this launch (1 .. MR of the kernel)
   long ldx, ldc;    // row strides of x and c, elements
   int xstride;      // bytes between the x regions of consecutive rows
-  unsigned *cnt;    // scratch: per-tile arrival counters (zero between launches)
-  float *ws;        // scratch: [G][2][MR][kRows] partials of split tiles
 };
-
-// the CTA whose units start at or before unit u (units [U c / G, U (c+1) / G))
-__device__ __forceinline__ int unit_owner(long long u, long long U, int G) {
-  return (int)(((u + 1) * G - 1) / U);
-}
 
 // x region: [nb][kFrag] B fragments ([set s][round pair rp][column n][16
 // digits]), [nb][kScl] lane scales ([t][sigma'_c0, sigma'_c1, S_c0, S_c1]),
@@ -743,8 +719,9 @@ MvPlan q4k_plan(int N, int K, const void *w, int sms, int mr) {
 }
 
 cudaError_t q4k_launch(const MvPlan &pl, int N, int K, const void *w, const void *x, int xdt, void *c, int cdt,
-                       int accumulate, int *err, cudaStream_t s, const float *nw, float eps, const void *pf,
-                       size_t pf_bytes, int M, long ldx, long ldc) {
+                       int accumulate, int *err, void *scratch, cudaStream_t s, const float *nw, float eps,
+                       const void *pf, size_t pf_bytes, int M, long ldx, long ldc) {
+  (void)scratch;  // this kernel keeps no state between launches
   using namespace mvk;
   if (M < 1 || M > pl.rows || (M > 1 && nw)) return cudaErrorInvalidValue;
   Params a{};

@@ -569,7 +569,10 @@ MvPlan q6k_plan(int N, int K, const void *w, int sms) {
   pl.cbc = kBlk;
   pl.ksplit = ksplit;
   pl.cpk = cpk;
-  pl.split_bytes = ksplit > 1 ? (size_t)tiles * (ksplit * kRows * 4 + 4) : 0;
+  // counters (one per tile: split only when tiles < sms) in the fixed
+  // counter region, then the partials
+  if (ksplit > 1 && (size_t)tiles * 4 > kScratchCntBytes) return pl;
+  pl.split_bytes = ksplit > 1 ? kScratchCntBytes + (size_t)tiles * ksplit * kRows * 4 : 0;
   pl.stages = S;
   pl.pitch = kPitch;
   pl.xoff = kXOff;
@@ -618,9 +621,9 @@ cudaError_t q6k_launch(const MvPlan &pl, int N, int K, const void *w, const void
   a.ksplit = pl.ksplit;
   a.cpk = pl.cpk;
   if (pl.ksplit > 1) {
-    // [tiles] counters, then [tiles][ksplit][16] partials
+    // [tiles] counters in the counter region, then [tiles][ksplit][16] partials
     a.scnt = static_cast<unsigned *>(scratch);
-    a.spart = reinterpret_cast<float *>(static_cast<char *>(scratch) + (((size_t)pl.tiles * 4 + 255) & ~(size_t)255));
+    a.spart = reinterpret_cast<float *>(static_cast<char *>(scratch) + kScratchCntBytes);
   }
   CUtensorMap tm;
   memcpy(&tm, pl.tmap, sizeof tm);

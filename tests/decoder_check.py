@@ -71,3 +71,64 @@ def min_margin_ratio(logits, margins, n_prompt: int) -> float:
     that step's max|logit| (inf margins mark prompt steps)."""
     r = [m / float(np.abs(lg).max()) for lg, m in zip(logits, margins) if np.isfinite(m)]
     return min(r) if r else float("inf")
+
+
+def fp16_prompt_deviation(host: dict, prompt) -> float:
+    """How far the reference's logits after `prompt` move when the operands
+    the prompt pass rounds to fp16 are rounded: every layer product's
+    activations and dequantised weights (qkv, o, gate_up, down), the
+    attention's scaled q and its softmax weights P.  Relative L2 of the last
+    step's logits, rounded against exact."""
+    import oracle.llama_ref as LR
+    from oracle import oracle as O
+
+    class Rounded(LR.Reference):
+        def __init__(self, model):
+            super().__init__(model)
+            D = model["cfg"].d_model
+            c = model["cfg"]
+            K = {"qkv": D, "o": c.n_heads * c.head_dim, "gate_up": D, "down": c.ffn_dim}
+            self.w16 = {k: [O.dequant(LR.TYPES[k], w).reshape(-1, K[k]).astype(np.float16).astype(np.float64)
+                            for w in model[k]] for k in K}
+
+        def mv(self, kind, l, x):
+            return (self.w16[kind][l] @ x.astype(np.float16).astype(np.float64)).astype(np.float32)
+
+        def step(self, token, pos):
+            c, m = self.c, self.m
+            H, KVH, hd, D, F = c.n_heads, c.n_kv_heads, c.head_dim, c.d_model, c.ffn_dim
+            half, G = hd // 2, c.n_heads // c.n_kv_heads
+            x = O.embedding(LR.TYPES["tok_emb"], m["tok_emb"], D, [token])[0].astype(np.float32)
+            for l in range(c.n_layers):
+                h = LR.rms(x, m["attn_norm"][l], c.eps)
+                qkv = self.mv("qkv", l, h).reshape(H + 2 * KVH, hd)
+                a, b = qkv[:H + KVH, :half], qkv[:H + KVH, half:]
+                cs, sn = self.cos[pos], self.sin[pos]
+                rot = np.concatenate([a * cs - b * sn, a * sn + b * cs], axis=1).astype(np.float32)
+                q = rot[:H]
+                self.kc[l, :, pos] = rot[H:H + KVH].astype(np.float16)
+                self.vc[l, :, pos] = qkv[H + KVH:].astype(np.float16)
+                att = np.empty((H, hd), np.float32)
+                sc = np.float32(np.log2(np.e) / np.sqrt(np.float32(hd)))
+                for hh in range(H):
+                    k = self.kc[l, hh // G, :pos + 1].astype(np.float32)
+                    v = self.vc[l, hh // G, :pos + 1].astype(np.float32)
+                    s_ = k @ (q[hh] * sc).astype(np.float16).astype(np.float32)
+                    p = np.exp2(s_ - s_.max()).astype(np.float16).astype(np.float32)
+                    att[hh] = (p @ v) / p.sum()
+                x = (x + self.mv("o", l, att.reshape(-1))).astype(np.float32)
+                h = LR.rms(x, m["ffn_norm"][l], c.eps)
+                gu = self.mv("gate_up", l, h)
+                g, u = gu[:F], gu[F:]
+                with np.errstate(over="ignore"):
+                    act = (g / (np.float32(1.0) + np.exp(-g)) * u).astype(np.float32)
+                x = (x + self.mv("down", l, act)).astype(np.float32)
+            return LR.matvec("head", m["head"], LR.rms(x, m["final_norm"], c.eps), c.vocab)
+
+    def last(ref):
+        lg = None
+        for pos, t in enumerate(prompt):
+            lg = ref.step(int(t), pos)
+        return lg
+
+    return rel_l2(last(Rounded(host)), last(LR.Reference(host)))

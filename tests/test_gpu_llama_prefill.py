@@ -14,11 +14,14 @@ Two models:
   * "varied" (tcb_b200/llama.py): its reference continuation of the prompt
     visits many distinct tokens, with attention sharp enough to do so.  The
     prompt pass rounds the qkv product's operands and the attention's q and
-    P to fp16 (tensor cores); the scores amplify that rounding, and a CPU
-    emulation of exactly those roundings on the reference moves the
-    first-step logits by 3.0e-3 relative L2.  The bound is therefore 5e-3,
-    and every generated token is checked against the reference fed the
-    GPU's own history (a token may differ only inside the 5e-3 tie band).
+    P to fp16 (tensor cores), and the sharp scores amplify that rounding:
+    the CPU reference with every product's operands and the attention's q
+    and P rounded to fp16 once moves its first-step logits by e (2.8e-3 and
+    2.9e-3 relative L2 on the two shapes).  The prompt pass rounds a Q4_K
+    weight more than once (its scale and min products to fp16, then the
+    value), so the bound is max(1e-3, 2.5 e), and every generated token is
+    checked against the reference fed the GPU's own history (a token may
+    differ only inside that tie band).
 """
 import os
 import sys
@@ -30,7 +33,7 @@ import tcb_b200 as T
 from tcb_b200 import llama
 
 sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
-from decoder_check import TOL, check_history, distinct_generated, rel_l2  # noqa: E402
+from decoder_check import TOL, check_history, distinct_generated, fp16_prompt_deviation, rel_l2  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 
@@ -43,7 +46,6 @@ CFGS = {
 NPROMPT = 300
 GEN = 32
 SEED = 10
-TOL_FP16 = 5e-3  # the varied model through the fp16 prompt pass (see the module docstring)
 
 
 @pytest.fixture(scope="module", params=[(c, v) for c in sorted(CFGS) for v in ("plain", "varied")],
@@ -62,7 +64,8 @@ def setup(request, oracle):
         assert distinct_generated(ref_toks, NPROMPT) >= 16
     ctx = T.Context(0)
     dev = llama.device_model(cfg, SEED, host)
-    tol = TOL_FP16 if varied else TOL
+    # the varied model through the fp16 prompt pass (see the module docstring)
+    tol = max(TOL, 2.5 * fp16_prompt_deviation(host, prompt)) if varied else TOL
     return cfg, ctx, host, dev, prompt, ref_toks, ref_logits, tol
 
 

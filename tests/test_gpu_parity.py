@@ -453,3 +453,37 @@ def test_fast_path_mlp_shapes_16bit(ctx, oracle):
         c = torch.zeros((1, N), dtype=ct, device="cuda")
         ctx.qgemm(T.Q4_K, dev(raw), xd, c)
         assert rel_l2(c.float().cpu().numpy(), want) <= (REL_L2 if ct == torch.float32 else 1e-2)
+
+
+# Q4_K partition over a fixed grid of 148 CTAs: (tile, block) units split
+# evenly, tiles shared by neighbouring CTAs reduced through scratch counters.
+PARTITION_SHAPES = [
+    (32, 300),    # one tile over 300 blocks: every CTA holds a piece of it
+    (40, 3),      # fewer units (6) than CTAs
+    (1, 1),       # one unit
+    (33, 37),     # two tiles, the second one row
+    (4000, 5),    # many tiles, several per CTA, none split evenly
+    (300, 16),    # tiles split at different blocks per CTA
+]
+
+
+@pytest.mark.parametrize("M", [1, 3, 8])
+@pytest.mark.parametrize("accumulate", [False, True])
+def test_q4k_partition(ctx, oracle, M, accumulate):
+    rng = np.random.default_rng(M * 7 + accumulate)
+    for N, kb in PARTITION_SHAPES:
+        K = kb * 256
+        raw = small_scale(oracle, T.Q4_K, N + kb, N * kb)
+        x = rng.standard_normal((M, K), dtype=np.float32)
+        base = rng.standard_normal((M, N), dtype=np.float32)
+        want = oracle.qgemm_float(T.Q4_K, x, raw, N, c=base if accumulate else None)
+        wd, xd = dev(raw), dev(x)
+        outs = []
+        for _ in range(3):  # the counters must be back at zero after every launch
+            c = dev(base)
+            ctx.qgemm(T.Q4_K, wd, xd, c, accumulate=accumulate)
+            got = host(c)
+            assert rel_l2(got, want) <= REL_L2, (N, K, M)
+            outs.append(got.view(np.uint32).copy())
+        assert all(np.array_equal(o, outs[0]) for o in outs), (N, K, M)
+    assert ctx.device_error() == 0
