@@ -382,7 +382,7 @@ def prefill_bench(ctx, rank: int, peaks: dict, cpu: bool) -> dict:
     return out
 
 
-def decode_tp_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
+def decode_tp_bench(ctx, rank: int, world: int, peak_gbs: float, batch16: bool = True) -> dict:
     """70B-shape Q4_K_M greedy decode at batch 1, on one GPU or
     tensor-parallel over the world's GPUs (QKV/gate/up
     column-parallel, o/down row-parallel with a residual all-reduce each,
@@ -423,10 +423,11 @@ def decode_tp_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
     ms, pms = float(t[0].item()), float(t[1].item())
     toks = eng.tokens(1152, stream)
     eng.close()
+    batch = decode_batch_bench(ctx, model, rank, world, peak_gbs, stream) if batch16 else None
     del model
     bpt = llama.weight_bytes_per_token(cfg)
     per_gpu = bpt / world
-    return {
+    out = {
         "model": "llama3-70b-shape q4_k_m (random init, synthetic)", "tensor_parallel": world,
         "prompt_tokens": 1024, "generated_tokens": 128, "tokens_per_s": round(128 / (ms / 1e3), 2),
         "prompt_pass_ms": round(pms, 2),
@@ -441,6 +442,65 @@ def decode_tp_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
         "distinct_generated_tokens": len(set(int(v) for v in toks[1024:])),
         "timing": "CUDA events around 128 graph replays, max over ranks",
     }
+    if batch is not None:
+        out["batch16"] = batch
+    return out
+
+
+def decode_batch_bench(ctx, model, rank: int, world: int, peak_gbs: float, stream, B: int = 16) -> dict:
+    """BASELINE config 5 at batch 16: 16 sequences on the same 70B-shape
+    weights, each with its own 1024-token random prompt and K/V cache, fed by
+    one batched prompt pass (tcb_llama_prefill_batch), then 128 greedy steps
+    of all 16 together (tcb_llama_batch: each product once over the 16 rows,
+    attention per sequence), every step one replay of the captured graph.
+    tokens/s counts the tokens of all sequences."""
+    import torch
+    import torch.distributed as dist
+
+    from tcb_b200 import llama
+
+    cfg = llama.LLAMA3_70B
+    engines = [llama.Llama(ctx, model, tp=(world, rank)) for _ in range(B)]
+    if world > 1:
+        engines[0].tp_init(llama.share_id(llama.nccl_unique_id, rank), peer=False)
+    rng = np.random.default_rng(19)
+    prompts = [rng.integers(0, cfg.vocab, 1024) for _ in range(B)]
+    for e, p in zip(engines, prompts):
+        e.start(p, stream)
+    batch = llama.Batch(engines)
+    batch.step(1, stream)  # sizes the products' scratch before the capture
+    batch.capture(stream)
+    for e, p in zip(engines, prompts):
+        e.start(p, stream)
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        llama.prefill_batch(engines, stream)
+        e1.record(stream)
+        batch.step(128, stream)
+        e2.record(stream)
+    e2.synchronize()
+    t = torch.tensor([e1.elapsed_time(e2), e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, pms = float(t[0].item()), float(t[1].item())
+    toks = [e.tokens(1152, stream) for e in engines]
+    batch.close()
+    for e in engines:
+        e.close()
+    bpt = llama.weight_bytes_per_token(cfg)
+    per_gpu_step = bpt / world
+    return {"batch": B, "prompt_tokens": 1024, "generated_tokens": 128,
+            "tokens_per_s": round(B * 128 / (ms / 1e3), 2), "ms_per_step": round(ms / 128, 4),
+            "prompt_pass_ms": round(pms, 2),
+            "roofline": {"bound": "hbm", "achieved_per_gpu": round(per_gpu_step / (ms / 1e3 / 128) / 1e9, 2),
+                         "peak": peak_gbs, "unit": "GB/s",
+                         "frac": round(per_gpu_step / (ms / 1e3 / 128) / 1e9 / peak_gbs, 4),
+                         "note": "weight bytes of one step (once per step, as if every product streamed "
+                                 "its weights once for all rows)"},
+            "last_tokens": [[int(v) for v in t[-4:]] for t in toks[:4]],
+            "distinct_generated_tokens": len(set(int(v) for t in toks for v in t[1024:])),
+            "timing": "CUDA events around 128 replays of the batch step graph, max over ranks"}
 
 
 def dist_init():

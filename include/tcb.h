@@ -229,6 +229,37 @@ int tcb_llama_tp_init(tcb_llama *m, const unsigned char *id128);
 int tcb_llama_peer_handle(tcb_llama *m, unsigned char *handle64);
 int tcb_llama_peer_init(tcb_llama *m, const unsigned char *handles);
 
+/* Greedy decode of several sequences together (TR's generate over a batch
+ * of prompts, lib/layers.tr 712-770: one GPT.single_step per generated
+ * position for every row of the batch).  The count engines (at most
+ * TCB_LLAMA_MAX_BATCH) are made from the same weights and shapes and
+ * started with their own prompts (tcb_llama_start, optionally
+ * tcb_llama_prefill_batch); the batch keeps pointers to them, each keeps
+ * its own K/V cache, position and token history (tcb_llama_buffers).  A
+ * step feeds every sequence its current token: each product runs once over
+ * the count rows (tcb_qgemm: up to 8 rows of x per matvec launch, the
+ * weights streamed once for them), attention runs per sequence in one
+ * launch, and every sequence takes its own greedy token.  Under tensor
+ * parallelism the residual rows are summed by NCCL (tcb_llama_tp_init on
+ * the first engine) and the candidates of all sequences are gathered in
+ * one all-gather.  Returns TCB_ERR_SHAPE when the engines differ in model
+ * or count is out of range, TCB_ERR_UNSUPPORTED when an engine is given
+ * twice. */
+#define TCB_LLAMA_MAX_BATCH 64
+typedef struct tcb_llama_batch tcb_llama_batch;
+int tcb_llama_batch_create(tcb_llama *const *engines, int count, tcb_llama_batch **out);
+int tcb_llama_batch_destroy(tcb_llama_batch *b);
+/* One step of every sequence (the captured graph once
+ * tcb_llama_batch_capture has made one).  TCB_ERR_BOUNDS when a sequence has
+ * no cache position left. */
+int tcb_llama_batch_step(tcb_llama_batch *b, void *stream);
+/* Capture one batch step into a CUDA graph (as tcb_llama_capture).  Run one
+ * eager step first: it sizes the scratch of the products. */
+int tcb_llama_batch_capture(tcb_llama_batch *b, void *stream);
+/* Device pointer of the last step's logits, float [count][vocab] (this
+ * rank's vocabulary rows). */
+int tcb_llama_batch_logits(tcb_llama_batch *b, float **logits);
+
 /* Size of the device array that tcb_qgemm_act8_static works in. */
 #define TCB_STATIC_SCRATCH_BYTES (4u << 20)
 

@@ -268,7 +268,7 @@ __device__ __forceinline__ void dequant8(const uint8_t *b, int j, float (&v)[8])
 }
 
 // k_tc_wdeq: the weights of the other block types for the tensor-core
-// kernel: row n dequantised exactly (TR's dequant), scaled by a power of two
+// kernel (rows of at most kWdeqMaxRowBytes): row n dequantised exactly (TR's dequant), scaled by a power of two
 // and rounded once to fp16 (natural K order); iw[n] holds the inverse
 // factor.  The factor brings the row's bound -- the largest magnitude its
 // blocks' scales allow: 32|d|max|sc| (Q6_K), 128|d| (Q8_0), 8|d| (Q4_0) --
@@ -277,7 +277,10 @@ __device__ __forceinline__ void dequant8(const uint8_t *b, int j, float (&v)[8])
 // row's blocks are first copied into shared memory with 16-byte loads (the
 // whole row in flight at once) and dequantised from there in one pass; little
 // register and shared-memory use per CTA keeps many rows in flight per SM.
-constexpr int kWdeqMaxK = 16384;  // rows of at most this many elements
+// a weight row's blocks fit the default 48 KB of dynamic shared memory
+constexpr size_t kWdeqMaxRowBytes = 48 * 1024;
+// rows of a fused activation prologue (k_tc_prep_pro keeps a row in registers)
+constexpr int kProMaxK = 16384;
 template <int W>
 __device__ __forceinline__ float block_bound(const uint8_t *b) {
   if constexpr (W == TCB_Q6_K) {
@@ -1009,12 +1012,22 @@ TcPlan tc_plan(int wtype, int M, int N, int K) {
 
 }  // namespace
 
+bool tc_eligible_rows(int wtype, int N, int K, const void *w) {
+  const bool typ = (wtype == TCB_Q4_K && (reinterpret_cast<uintptr_t>(w) & 15) == 0) || wtype == TCB_Q6_K ||
+                   wtype == TCB_Q8_0 || wtype == TCB_Q4_0;
+  return typ && N > 0 && K >= 256 && K % 256 == 0 &&
+         (wtype == TCB_Q4_K ||
+          (size_t)K / block_elems(wtype) * block_bytes(wtype) <= tc::kWdeqMaxRowBytes) &&
+         tensor_map_encoder() != nullptr && max_pairs() > 0;
+}
+
 bool tc_eligible(int wtype, int M, int N, int K, const void *w) {
   const bool typ = (wtype == TCB_Q4_K && (reinterpret_cast<uintptr_t>(w) & 15) == 0) || wtype == TCB_Q6_K ||
                    wtype == TCB_Q8_0 || wtype == TCB_Q4_0;
   return typ && M >= kTcMinM && N > 0 && K >= 256 && K % 256 == 0 &&
-         (wtype == TCB_Q4_K || K <= tc::kWdeqMaxK) && tensor_map_encoder() != nullptr &&
-         max_pairs() > 0;
+         (wtype == TCB_Q4_K ||
+          (size_t)K / block_elems(wtype) * block_bytes(wtype) <= tc::kWdeqMaxRowBytes) &&
+         tensor_map_encoder() != nullptr && max_pairs() > 0;
 }
 
 size_t tc_workspace_bytes(int wtype, int M, int N, int K) {
@@ -1024,7 +1037,7 @@ size_t tc_workspace_bytes(int wtype, int M, int N, int K) {
 
 bool tc_prologue_ok(const TcPrologue &pro, int K, const void *x, long ldx) {
   if (pro.kind == kTcProNone) return true;
-  if (K > tc::kWdeqMaxK || ldx % 4 || (reinterpret_cast<uintptr_t>(x) & 15)) return false;
+  if (K > tc::kProMaxK || ldx % 4 || (reinterpret_cast<uintptr_t>(x) & 15)) return false;
   if (pro.kind == kTcProRms) return pro.w && (reinterpret_cast<uintptr_t>(pro.w) & 15) == 0 && ldx >= K;
   return pro.kind == kTcProSwiglu && ldx >= 2L * K;
 }

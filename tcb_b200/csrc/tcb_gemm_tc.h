@@ -16,6 +16,9 @@ constexpr int kTcMinM = 64;
 // (Q4_K dequantised in the kernel; Q6_K, Q8_0, Q4_0 dequantised exactly to
 // row-scaled fp16 in workspace first)
 bool tc_eligible(int wtype, int M, int N, int K, const void *w);
+// the same shape and type rules for any number of rows (tc_eligible also
+// asks M >= kTcMinM, the public product's routing)
+bool tc_eligible_rows(int wtype, int N, int K, const void *w);
 // context scratch the call needs (fp16 activations and row multipliers)
 size_t tc_workspace_bytes(int wtype, int M, int N, int K);
 // a step applied to the f32 activation rows as they are converted (the
@@ -40,5 +43,8 @@ cudaError_t launch_qgemm_tc(int wtype, const void *w, int M, int N, int K, const
 // step and tcb_qgemm separately)
 int qgemm_tc_prologue(tcb_ctx *ctx, int wtype, int M, int N, int K, const void *w, const float *x, long ldx, float *c,
                       long ldc, int accumulate, const TcPrologue &pro, cudaStream_t s);
+// the float product of a few rows on the tensor cores (tcb_capi.cu)
+int qgemm_tc_rows(tcb_ctx *ctx, int wtype, int M, int N, int K, const void *w, const float *x, long ldx, float *c,
+                  long ldc, int accumulate, cudaStream_t s);
 
 }  // namespace tcb

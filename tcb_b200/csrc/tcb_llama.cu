@@ -96,8 +96,25 @@ __global__ void k_rmsnorm(const float *x, const float *w, float *out, int D, flo
   for (int i = threadIdx.x; i < D; i += blockDim.x) out[i] = __fmul_rn(__fdiv_rn(x[i], s), w[i]);
 }
 
+// One sequence of a batched decode step (tcb_llama_batch): where its
+// position, current token and (layer 0 of its) K/V cache live.
+struct BatchSeq {
+  const int *pos;
+  __half *kc, *vc;
+  const int64_t *tok;
+};
+
+// The current tokens of a batch's sequences, gathered into one array.
+__global__ void k_gather_tok(const BatchSeq *bs, int B, int64_t *tok) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < B) tok[b] = *bs[b].tok;
+}
+
 // One layer's attention at position *pos: CTA (KV head blockIdx.x, chunk
-// blockIdx.y of kChunk positions), 256 threads.  Every cached K and V byte of
+// blockIdx.y of kChunk positions), 256 threads.  In a batched step
+// (bs != nullptr) blockIdx.z is the sequence: its position and cache come
+// from bs[z] (plus layer_off), and its qkv row, output row, chunk partials
+// and chunk counters are z strides into the batch's buffers.  Every cached K and V byte of
 // the chunk is requested before the dependency wait (K: thread = (position
 // t/4, 32 dimensions (t%4)*32); V: thread = (dimensions (t%32)*4, positions
 // t/32 + 8j)), so the loads overlap the qkv product.  The CTA rotates the
@@ -110,8 +127,19 @@ __global__ void k_rmsnorm(const float *x, const float *w, float *out, int D, flo
 template <int G>
 __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cosT, const float *sinT, const int *pos,
                                               __half *kc, __half *vc, float *part, unsigned *count, float *out, int H,
-                                              int KVH, int max_ctx, int nch_max, float scale) {
+                                              int KVH, int max_ctx, int nch_max, float scale, const BatchSeq *bs,
+                                              size_t layer_off) {
   constexpr int half = kHd / 2;
+  if (bs) {
+    const int z = blockIdx.z;
+    pos = bs[z].pos;
+    kc = bs[z].kc + layer_off;
+    vc = bs[z].vc + layer_off;
+    qkv += (size_t)z * (H + 2 * KVH) * kHd;
+    out += (size_t)z * H * kHd;
+    part += (size_t)z * H * nch_max * (2 + kHd);
+    count += (size_t)z * KVH;
+  }
   __shared__ __align__(16) float qs[G][kHd];
   __shared__ float knew[kHd], vnew[kHd];
   __shared__ float sc[G][kChunk];
@@ -586,15 +614,15 @@ __global__ void k_local_best(const float *pm, const int *pi, int nb, int off, in
 
 // the next token from the ranks' candidates (rank order = vocabulary order,
 // so ties still go to the lowest index)
-__global__ void k_pick_tp(const int2 *cand, int n, int *pos, int64_t *tok, int64_t *hist, const int64_t *prompt,
-                          const int *nprompt, int max_ctx) {
+__global__ void k_pick_tp(const int2 *cand, int n, int stride, int *pos, int64_t *tok, int64_t *hist,
+                          const int64_t *prompt, const int *nprompt, int max_ctx) {
   mv::pdl_wait();
   if (threadIdx.x != 0) return;
   float best = -INFINITY;
   int bi = 0x7FFFFFFF;
   for (int r = 0; r < n; r++) {
-    const float v = __int_as_float(cand[r].x);
-    const int i = cand[r].y;
+    const float v = __int_as_float(cand[(size_t)r * stride].x);
+    const int i = cand[(size_t)r * stride].y;
     if (i != 0x7FFFFFFF && (bi == 0x7FFFFFFF || v > best || (v == best && i < bi))) {
       best = v;
       bi = i;
@@ -816,7 +844,7 @@ cudaError_t issue_step(tcb_llama *m, cudaStream_t s) {
 #define TCB_ATTN(GG)                                                                                              \
   case GG:                                                                                                        \
     e = launch(k_attn<GG>, ag, dim3(256), s, m->qkvb, m->cosT, m->sinT, m->pos, kc, vc, m->part, m->acount, m->att, H, \
-               KVH, c.max_ctx, m->nch_max, scale);                                                                \
+               KVH, c.max_ctx, m->nch_max, scale, (const BatchSeq *)nullptr, (size_t)0);                          \
     break;
       TCB_ATTN(1)
       TCB_ATTN(2)
@@ -862,7 +890,7 @@ cudaError_t issue_step(tcb_llama *m, cudaStream_t s) {
   const Nccl *nc = nccl();
   if (!nc || !m->comm) return cudaErrorNotReady;
   if ((m->nccl_rc = nc->all_gather(m->cand + m->tr, m->cand, 2, kNcclInt32, m->comm, s)) != 0) return cudaErrorUnknown;
-  return launch(k_pick_tp, dim3(1), dim3(32), s, m->cand, m->tp, m->pos, m->tok, m->hist, m->prompt, m->nprompt,
+  return launch(k_pick_tp, dim3(1), dim3(32), s, m->cand, m->tp, 1, m->pos, m->tok, m->hist, m->prompt, m->nprompt,
                 c.max_ctx);
 }
 
@@ -1253,6 +1281,254 @@ int tcb_llama_capture(tcb_llama *m, void *stream) {
     m->exec = nullptr;
     return fail(m, e);
   }
+  return TCB_OK;
+}
+
+// ----------------------------------------------------------------- batch
+
+// A batch of sequences decoded together (tcb_llama_batch_*): engines made from
+// the same weights, each with its own K/V cache, position and token history.
+// A step runs every product once over the batch's rows, attention per
+// sequence in one launch (blockIdx.z), and each sequence's greedy pick.
+struct tcb_llama_batch {
+  std::vector<tcb_llama *> ms;
+  tcb_llama *m0 = nullptr;
+  int B = 0;
+  float *x = nullptr, *h = nullptr, *qkv = nullptr, *att = nullptr, *gu = nullptr, *a = nullptr, *logits = nullptr;
+  float *part = nullptr, *am_v = nullptr;
+  int *am_i = nullptr;
+  unsigned *count = nullptr;
+  int64_t *tok = nullptr;
+  tcb::ll::BatchSeq *seq = nullptr;
+  int2 *cand = nullptr;
+  std::vector<void *> allocs;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  cudaStream_t cap = nullptr;
+};
+
+namespace {
+
+cudaError_t balloc_bytes(tcb_llama_batch *b, void **p, size_t bytes) {
+  void *q = nullptr;
+  cudaError_t e = cudaMalloc(&q, bytes + 16);
+  if (e == cudaSuccess) {
+    b->allocs.push_back(q);
+    *p = q;
+  }
+  return e;
+}
+#define balloc(b, pp, n) balloc_bytes((b), reinterpret_cast<void **>(pp), (n) * sizeof(**(pp)))
+
+// rows out (+)= W x_rows: the library's product (up to 8 rows of x per
+// matvec launch, the weights streamed once for them); shapes the multi-row
+// matvec kernels do not take (long Q6_K rows, the wide head) go to the
+// tensor cores for all rows at once rather than one matvec launch per row
+int rows_product(tcb_llama *m0, const Mat &mt, int B, const float *x, float *y, int acc, cudaStream_t s) {
+  if (B > 1 && !tcb::matvec_plan_rows(mt.type, 0, mt.N, mt.K, mt.w, m0->ctx->sms, 2).ok) {
+    const int rc = tcb::qgemm_tc_rows(m0->ctx, mt.type, B, mt.N, mt.K, mt.w, x, mt.K, y, mt.N, acc, s);
+    if (rc != TCB_ERR_UNSUPPORTED) return rc;
+  }
+  return tcb_qgemm(m0->ctx, mt.type, B, mt.N, mt.K, mt.w, x, TCB_F32, mt.K, y, TCB_F32, mt.N, acc, s);
+}
+
+int issue_batch_step(tcb_llama_batch *bt, cudaStream_t s) {
+  using namespace tcb::ll;
+  tcb_llama *m0 = bt->m0;
+  const tcb_llama_config &c = m0->cfg;
+  const int H = c.n_heads, KVH = c.n_kv_heads, hd = c.head_dim, D = c.d_model, F = c.ffn_dim, B = bt->B;
+  const int G = H / KVH, V = c.vocab;
+  const float scale = 1.0f / sqrtf((float)hd);
+  const size_t cache_layer = (size_t)KVH * c.max_ctx * hd;
+  // NCCL: rank 0 adds its o/down partial to the residual rows, the others
+  // write theirs, and the in-place all-reduce of B rows sums them
+  const int acc = m0->tr == 0;
+  auto reduce = [&]() -> int {
+    if (m0->tp == 1) return TCB_OK;
+    m0->nccl_rc = nccl()->all_reduce(bt->x, bt->x, (size_t)B * D, kNcclFloat32, kNcclSum, m0->comm, s);
+    return m0->nccl_rc ? fail(m0, cudaErrorUnknown) : TCB_OK;
+  };
+  // plain launches first: the step starts after the previous one has
+  // completed (k_attn reads the cached K/V and positions before its wait)
+  k_gather_tok<<<(B + 31) / 32, 32, 0, s>>>(bt->seq, B, bt->tok);
+  cudaError_t e = tcb::launch_dequant_rows(m0->tok_emb_type, m0->tok_emb, B, D, bt->tok, bt->x, TCB_F32,
+                                           m0->ctx->sms, s);
+  if (e != cudaSuccess) return fail(m0, e);
+  int rc = TCB_OK;
+  for (int l = 0; l < c.n_layers && rc == TCB_OK; l++) {
+    k_rmsnorm<<<B, 1024, 0, s>>>(bt->x, m0->attn_norm[l], bt->h, D, c.eps);
+    if ((rc = rows_product(m0, m0->qkv[l], B, bt->h, bt->qkv, 0, s)) != TCB_OK) break;
+    const dim3 ag(KVH, m0->nch_max, B);
+    switch (G) {
+#define TCB_ATTN(GG)                                                                                              \
+  case GG:                                                                                                        \
+    e = launch(k_attn<GG>, ag, dim3(256), s, (const float *)bt->qkv, (const float *)m0->cosT,                    \
+               (const float *)m0->sinT, (const int *)nullptr, (__half *)nullptr, (__half *)nullptr, bt->part,    \
+               bt->count, bt->att, H, KVH, c.max_ctx, m0->nch_max, scale, (const BatchSeq *)bt->seq,             \
+               (size_t)l * cache_layer);                                                                          \
+    break;
+      TCB_ATTN(1)
+      TCB_ATTN(2)
+      TCB_ATTN(4)
+      TCB_ATTN(8)
+#undef TCB_ATTN
+    default: e = cudaErrorInvalidValue;
+    }
+    if (e != cudaSuccess) return fail(m0, e);
+    if ((rc = rows_product(m0, m0->o[l], B, bt->att, bt->x, acc, s)) != TCB_OK || (rc = reduce()) != TCB_OK) break;
+    k_rmsnorm<<<B, 1024, 0, s>>>(bt->x, m0->ffn_norm[l], bt->h, D, c.eps);
+    if ((rc = rows_product(m0, m0->gu[l], B, bt->h, bt->gu, 0, s)) != TCB_OK) break;
+    const long na = (long)B * F;
+    k_swiglu_rows<<<(int)((na + 255) / 256 < 4096 ? (na + 255) / 256 : 4096), 256, 0, s>>>(bt->gu, bt->a, F, na);
+    if ((rc = rows_product(m0, m0->down[l], B, bt->a, bt->x, acc, s)) != TCB_OK || (rc = reduce()) != TCB_OK) break;
+  }
+  if (rc != TCB_OK) return rc;
+  k_rmsnorm<<<B, 1024, 0, s>>>(bt->x, m0->final_norm, bt->h, D, c.eps);
+  if ((rc = rows_product(m0, m0->head, B, bt->h, bt->logits, 0, s)) != TCB_OK) return rc;
+  for (int b = 0; b < B; b++)
+    if ((e = launch(k_argmax_part, dim3(kArgBlocks), dim3(256), s, (const float *)(bt->logits + (size_t)b * V), V,
+                    bt->am_v + (size_t)b * kArgBlocks, bt->am_i + (size_t)b * kArgBlocks)) != cudaSuccess)
+      return fail(m0, e);
+  if (m0->tp == 1) {
+    for (int b = 0; b < B; b++) {
+      tcb_llama *m = bt->ms[b];
+      if ((e = launch(k_next_token, dim3(1), dim3(32), s, (const float *)(bt->am_v + (size_t)b * kArgBlocks),
+                      (const int *)(bt->am_i + (size_t)b * kArgBlocks), kArgBlocks, m->pos, m->tok, m->hist,
+                      (const int64_t *)m->prompt, (const int *)m->nprompt, c.max_ctx)) != cudaSuccess)
+        return fail(m0, e);
+    }
+    return TCB_OK;
+  }
+  // tensor parallelism: each rank's candidate per sequence ([rank][B]), one
+  // all-gather, then each sequence's pick over the ranks
+  for (int b = 0; b < B; b++)
+    if ((e = launch(k_local_best, dim3(1), dim3(32), s, (const float *)(bt->am_v + (size_t)b * kArgBlocks),
+                    (const int *)(bt->am_i + (size_t)b * kArgBlocks), kArgBlocks, m0->vocab_off,
+                    bt->cand + (size_t)m0->tr * B + b)) != cudaSuccess)
+      return fail(m0, e);
+  if ((m0->nccl_rc = nccl()->all_gather(bt->cand + (size_t)m0->tr * B, bt->cand, 2 * (size_t)B, kNcclInt32, m0->comm,
+                                        s)) != 0)
+    return fail(m0, cudaErrorUnknown);
+  for (int b = 0; b < B; b++) {
+    tcb_llama *m = bt->ms[b];
+    if ((e = launch(k_pick_tp, dim3(1), dim3(32), s, (const int2 *)(bt->cand + b), m0->tp, B, m->pos, m->tok,
+                    m->hist, (const int64_t *)m->prompt, (const int *)m->nprompt, c.max_ctx)) != cudaSuccess)
+      return fail(m0, e);
+  }
+  return TCB_OK;
+}
+
+}  // namespace
+
+int tcb_llama_batch_destroy(tcb_llama_batch *bt) {
+  if (!bt) return TCB_OK;
+  if (bt->m0) cudaSetDevice(bt->m0->ctx->dev);
+  if (bt->exec) cudaGraphExecDestroy(bt->exec);
+  if (bt->graph) cudaGraphDestroy(bt->graph);
+  if (bt->cap) cudaStreamDestroy(bt->cap);
+  for (void *p : bt->allocs) cudaFree(p);
+  delete bt;
+  return TCB_OK;
+}
+
+int tcb_llama_batch_create(tcb_llama *const *ms, int count, tcb_llama_batch **out) {
+  if (!ms || !out) return TCB_ERR_NULL;
+  *out = nullptr;
+  if (count < 1 || count > TCB_LLAMA_MAX_BATCH) return TCB_ERR_SHAPE;
+  tcb_llama *m0 = ms[0];
+  for (int i = 0; i < count; i++) {
+    if (!ms[i]) return TCB_ERR_NULL;
+    if (!same_model(m0, ms[i])) return TCB_ERR_SHAPE;
+    for (int j = 0; j < i; j++)
+      if (ms[j] == ms[i]) return TCB_ERR_UNSUPPORTED;
+  }
+  const tcb_llama_config &c = m0->cfg;
+  if (c.head_dim != tcb::ll::kHd) return TCB_ERR_UNSUPPORTED;
+  cudaError_t e = cudaSetDevice(m0->ctx->dev);
+  if (e != cudaSuccess) return fail(m0, e);
+  tcb_llama_batch *bt = new (std::nothrow) tcb_llama_batch;
+  if (!bt) return TCB_ERR_NOMEM;
+  bt->ms.assign(ms, ms + count);
+  bt->m0 = m0;
+  bt->B = count;
+  const int H = c.n_heads, KVH = c.n_kv_heads, hd = c.head_dim, D = c.d_model, F = c.ffn_dim, B = count;
+  const size_t qkvn = (size_t)(H + 2 * KVH) * hd;
+  std::vector<tcb::ll::BatchSeq> hs(B);
+  for (int i = 0; i < B; i++) hs[i] = tcb::ll::BatchSeq{ms[i]->pos, ms[i]->kc, ms[i]->vc, ms[i]->tok};
+  if ((e = balloc(bt, &bt->x, (size_t)B * D)) != cudaSuccess || (e = balloc(bt, &bt->h, (size_t)B * D)) != cudaSuccess ||
+      (e = balloc(bt, &bt->qkv, (size_t)B * qkvn)) != cudaSuccess ||
+      (e = balloc(bt, &bt->att, (size_t)B * H * hd)) != cudaSuccess ||
+      (e = balloc(bt, &bt->gu, (size_t)B * 2 * F)) != cudaSuccess || (e = balloc(bt, &bt->a, (size_t)B * F)) != cudaSuccess ||
+      (e = balloc(bt, &bt->logits, (size_t)B * c.vocab)) != cudaSuccess ||
+      (e = balloc(bt, &bt->part, (size_t)B * H * m0->nch_max * (2 + hd))) != cudaSuccess ||
+      (e = balloc(bt, &bt->am_v, (size_t)B * tcb::ll::kArgBlocks)) != cudaSuccess ||
+      (e = balloc(bt, &bt->am_i, (size_t)B * tcb::ll::kArgBlocks)) != cudaSuccess ||
+      (e = balloc(bt, &bt->count, (size_t)B * KVH)) != cudaSuccess || (e = balloc(bt, &bt->tok, (size_t)B)) != cudaSuccess ||
+      (e = balloc(bt, &bt->seq, (size_t)B)) != cudaSuccess ||
+      (e = balloc(bt, &bt->cand, (size_t)B * m0->tp)) != cudaSuccess ||
+      (e = cudaMemset(bt->count, 0, (size_t)B * KVH * sizeof(unsigned))) != cudaSuccess ||
+      (e = cudaMemcpy(bt->seq, hs.data(), B * sizeof(tcb::ll::BatchSeq), cudaMemcpyHostToDevice)) != cudaSuccess) {
+    tcb_llama_batch_destroy(bt);
+    return e == cudaErrorMemoryAllocation ? TCB_ERR_NOMEM : fail(m0, e);
+  }
+  *out = bt;
+  return TCB_OK;
+}
+
+int tcb_llama_batch_step(tcb_llama_batch *bt, void *stream) {
+  if (!bt) return TCB_ERR_NULL;
+  tcb_llama *m0 = bt->m0;
+  for (tcb_llama *m : bt->ms)
+    if (m->host_n < 1 || m->host_pos + 1 >= m->cfg.max_ctx) return TCB_ERR_BOUNDS;
+  if (m0->tp > 1 && (!nccl() || !m0->comm)) return fail(m0, cudaErrorNotReady);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaSetDevice(m0->ctx->dev);
+  if (e != cudaSuccess) return fail(m0, e);
+  int rc = TCB_OK;
+  if (bt->exec) {
+    if ((e = cudaGraphLaunch(bt->exec, s)) != cudaSuccess) return fail(m0, e);
+  } else if ((rc = issue_batch_step(bt, s)) != TCB_OK) {
+    return rc;
+  }
+  for (tcb_llama *m : bt->ms) m->host_pos++;
+  return TCB_OK;
+}
+
+int tcb_llama_batch_capture(tcb_llama_batch *bt, void *stream) {
+  if (!bt) return TCB_ERR_NULL;
+  tcb_llama *m0 = bt->m0;
+  if (m0->tp > 1 && (!nccl() || !m0->comm)) return fail(m0, cudaErrorNotReady);
+  cudaError_t e = cudaSetDevice(m0->ctx->dev);
+  if (e == cudaSuccess && !bt->cap) e = cudaStreamCreateWithFlags(&bt->cap, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(m0, e);
+  if (bt->exec) {
+    cudaGraphExecDestroy(bt->exec);
+    bt->exec = nullptr;
+  }
+  if (bt->graph) {
+    cudaGraphDestroy(bt->graph);
+    bt->graph = nullptr;
+  }
+  if ((e = cudaStreamBeginCapture(bt->cap, cudaStreamCaptureModeThreadLocal)) != cudaSuccess) return fail(m0, e);
+  const int rc = issue_batch_step(bt, bt->cap);
+  cudaGraph_t g = nullptr;
+  e = cudaStreamEndCapture(bt->cap, &g);
+  if (rc != TCB_OK || e != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    return rc != TCB_OK ? rc : fail(m0, e);
+  }
+  bt->graph = g;
+  if ((e = cudaGraphInstantiate(&bt->exec, g, 0)) != cudaSuccess) {
+    bt->exec = nullptr;
+    return fail(m0, e);
+  }
+  return TCB_OK;
+}
+
+int tcb_llama_batch_logits(tcb_llama_batch *bt, float **logits) {
+  if (!bt || !logits) return TCB_ERR_NULL;
+  *logits = bt->logits;
   return TCB_OK;
 }
 

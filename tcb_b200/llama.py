@@ -283,6 +283,11 @@ def _bind():
     L.tcb_llama_tp_init.argtypes = [P, P]
     L.tcb_llama_peer_handle.argtypes = [P, P]
     L.tcb_llama_peer_init.argtypes = [P, P]
+    L.tcb_llama_batch_create.argtypes = [P, ctypes.c_int, ctypes.POINTER(P)]
+    L.tcb_llama_batch_destroy.argtypes = [P]
+    L.tcb_llama_batch_step.argtypes = [P, P]
+    L.tcb_llama_batch_capture.argtypes = [P, P]
+    L.tcb_llama_batch_logits.argtypes = [P, ctypes.POINTER(P)]
     L._llama_bound = True
     return L
 
@@ -385,6 +390,47 @@ class Llama:
     def close(self):
         if getattr(self, "_h", None):
             self._L.tcb_llama_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Batch:
+    """Greedy decode of several engines on the same model together
+    (tcb_llama_batch_*): each step feeds every sequence its current token,
+    the products run once over all of them.  Keeps the engines alive."""
+
+    def __init__(self, engines: list):
+        self.engines = list(engines)
+        e0 = self.engines[0]
+        self._L, self.cfg, self.tp = e0._L, e0.cfg, e0.tp
+        arr = (ctypes.c_void_p * len(engines))(*[e._h.value for e in engines])
+        h = ctypes.c_void_p()
+        e0._check(self._L.tcb_llama_batch_create(arr, len(engines), ctypes.byref(h)), "batch_create")
+        self._h = h
+
+    def step(self, n: int = 1, stream=None):
+        s = _stream(stream)
+        for _ in range(n):
+            self.engines[0]._check(self._L.tcb_llama_batch_step(self._h, s), "batch_step")
+
+    def capture(self, stream=None):
+        self.engines[0]._check(self._L.tcb_llama_batch_capture(self._h, _stream(stream)), "batch_capture")
+
+    def logits(self, stream=None) -> np.ndarray:
+        """[count, vocab] logits of the last step (this rank's vocabulary rows)."""
+        p = ctypes.c_void_p()
+        self.engines[0]._check(self._L.tcb_llama_batch_logits(self._h, ctypes.byref(p)), "batch_logits")
+        n = self.cfg.vocab // self.tp[0]
+        return self.engines[0]._download(p.value, np.empty((len(self.engines), n), np.float32), stream)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._L.tcb_llama_batch_destroy(self._h)
             self._h = None
 
     def __del__(self):

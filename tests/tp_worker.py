@@ -7,6 +7,9 @@ in rank order); rank 0 writes them with the token histories to an .npz.
                                           CPU reference's test model), greedy
     tp_worker.py OUT.npz prefill          the same, a 100-token prompt fed by
                                           the prompt pass
+    tp_worker.py OUT.npz batch            the small decoder, five sequences of
+                                          different lengths stepped together
+                                          (tcb_llama_batch), eager and graph
     tp_worker.py OUT.npz shape70 [FORCED.npy]
                                           a 2-layer 70B-shaped decoder
                                           generated on the device (the same
@@ -38,11 +41,59 @@ SEED70 = 4
 PROMPT70 = np.random.default_rng(29).integers(0, CFG70.vocab, 16).astype(np.int64)
 
 
+def host_for(mode):
+    """the host model of a mode: the varied decoder, the plain one for the
+    prompt pass"""
+    return llama.host_model(CFG, seed=7) if mode == "prefill" else llama.host_model(CFG, seed=SEED, varied=True)
+
+
 def gathered_logits(m, world):
     lg = torch.from_numpy(m.logits().copy())
     parts = [None] * world
     dist.all_gather_object(parts, lg.numpy())
     return np.concatenate(parts)
+
+
+BATCH_PROMPTS = [np.random.default_rng(41).integers(0, CFG.vocab, n).astype(np.int64) for n in (8, 3, 13, 1, 8)]
+BATCH_STEPS = 36
+
+
+def batch_main(ctx, rank, world, out_path):
+    host = llama.host_model(CFG, seed=SEED, varied=True)
+    dev = llama.device_model(CFG, SEED, host, tp=(world, rank))
+    engines = [llama.Llama(ctx, dev, tp=(world, rank)) for _ in BATCH_PROMPTS]
+    engines[0].tp_init(llama.share_id(llama.nccl_unique_id, rank), peer=False)
+    runs = {}
+    for mode in ("eager", "graph"):
+        for e, p in zip(engines, BATCH_PROMPTS):
+            e.start(p)
+        b = llama.Batch(engines)
+        if mode == "graph":
+            b.step(1)
+            b.capture()
+            for e, p in zip(engines, BATCH_PROMPTS):
+                e.start(p)
+        logits = []
+        for _ in range(BATCH_STEPS):
+            b.step(1)
+            lg = b.logits().copy()
+            parts = [None] * world
+            dist.all_gather_object(parts, lg)
+            logits.append(np.concatenate(parts, axis=1))
+        runs[mode] = ([e.tokens(BATCH_STEPS + 1) for e in engines], np.stack(logits, 1))
+        b.close()
+    all_tok = [None] * world
+    dist.all_gather_object(all_tok, [t.tolist() for t in runs["eager"][0]])
+    err = [None] * world
+    dist.all_gather_object(err, ctx.device_error())
+    if rank == 0:
+        np.savez(out_path, eager=np.stack(runs["eager"][0]), graph=np.stack(runs["graph"][0]),
+                 logits=runs["eager"][1], same_on_ranks=all(t == all_tok[0] for t in all_tok), peer=False,
+                 device_errors=np.array(err, np.int64), first=0)
+    for e in engines:
+        e.close()
+    dist.barrier()
+    dist.destroy_process_group()
 
 
 def main():
@@ -52,6 +103,8 @@ def main():
     dist.init_process_group("gloo")
     out_path, mode = sys.argv[1], sys.argv[2]
     ctx = T.Context(local)
+    if mode == "batch":
+        return batch_main(ctx, rank, world, out_path)
     if mode == "shape70":
         cfg = CFG70
         dev = llama.device_model(cfg, SEED70, tp=(world, rank), varied=True)
@@ -59,7 +112,9 @@ def main():
         prompt = forced if forced is not None else PROMPT70
     else:
         cfg = CFG
-        host = llama.host_model(cfg, seed=SEED, varied=True)
+        # the prompt pass on the plain model (its fp16 rounding stays within
+        # the float bound there; tests/test_gpu_llama_prefill.py)
+        host = host_for(mode)
         dev = llama.device_model(cfg, SEED, host, tp=(world, rank))
         forced = None
         prompt = LONG_PROMPT if mode == "prefill" else PROMPT
