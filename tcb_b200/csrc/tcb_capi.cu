@@ -12,6 +12,7 @@
 #include "tcb_common.cuh"
 #include "tcb_launch.h"
 #include "tcb_ctx.h"
+#include "tcb_gemm_i8.h"
 #include "tcb_gemm_tc.h"
 #include "tcb_matvec.h"
 
@@ -292,6 +293,18 @@ int tcb_qgemm_act8(tcb_ctx *ctx, int wtype, int M, int N, int K, const void *w, 
   if ((rc = bind(ctx)) != TCB_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (K == 0) return empty_sum(ctx, M, N, c, cdtype, ldc, accumulate, s);
+  if (tcb::i8_eligible(wtype, M, N, K, w)) {
+    // many rows of Q4_K: the integer block sums on the tensor cores
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    const size_t qb = tcb::act8_scratch_bytes(M, K, 256);
+    if ((rc = ensure_ws(ctx, qb + tcb::i8_extra_bytes(M))) != TCB_OK) return rc;
+    tcb::Act8Scratch sc = tcb::act8_scratch_carve(ctx->ws, M, K, 256);
+    cudaError_t e = tcb::launch_act8_quantize(256, M, K, x, xdtype, ldx, sc, ctx->sms, s);
+    if (e == cudaSuccess)
+      e = tcb::launch_qgemm_i8(w, M, N, K, sc, static_cast<char *>(ctx->ws) + qb, x, xdtype, ldx, c, cdtype, ldc,
+                               accumulate, ctx->derr, ctx->sms, s);
+    return e == cudaSuccess ? TCB_OK : cuda_fail(ctx, e);
+  }
   bool taken = false;
   rc = run_matvec(ctx, wtype, 1, M, N, K, w, x, xdtype, ldx, c, cdtype, ldc, accumulate, s, &taken);
   if (taken || rc != TCB_OK) return rc;

@@ -487,3 +487,77 @@ def test_q4k_partition(ctx, oracle, M, accumulate):
             outs.append(got.view(np.uint32).copy())
         assert all(np.array_equal(o, outs[0]) for o in outs), (N, K, M)
     assert ctx.device_error() == 0
+
+
+# ---------------------------------------------------------------- int8 activations on the tensor cores
+
+
+@pytest.mark.parametrize("M", [64, 129, 300])
+def test_act8_tensor_cores_bit_exact(ctx, oracle, M):
+    """Q4_K x Q8 activations from 64 rows on: the integer block sums on
+    tcgen05 (kind::i8), the fold in TR's order -- bit for bit TR's
+    quantGemmQ8 (cpu_quant_q8.go:186-259), on ragged tiles of activation
+    rows (128) and weight rows (64), GemmSet and Gemm."""
+    rng = np.random.default_rng(M)
+    for N, kb in [(64, 1), (100, 4), (257, 16)]:
+        K = kb * 256
+        raw = small_scale(oracle, T.Q4_K, N + kb + M, N * kb)
+        x = rng.standard_normal((M, K), dtype=np.float32)
+        c = torch.zeros((M, N), dtype=torch.float32, device="cuda")
+        ctx.qgemm_act8(T.Q4_K, dev(raw), dev(x), c)
+        assert np.array_equal(bits(host(c)), bits(oracle.qgemm_act8(T.Q4_K, x, raw, N))), (N, K)
+        base = rng.standard_normal((M, N), dtype=np.float32)
+        c = dev(base)
+        ctx.qgemm_act8(T.Q4_K, dev(raw), dev(x), c, accumulate=True)
+        assert np.array_equal(bits(host(c)), bits(oracle.qgemm_act8(T.Q4_K, x, raw, N, c=base))), (N, K)
+    assert ctx.device_error() == 0
+
+
+def test_act8_tensor_cores_inputs_and_non_finite(ctx, oracle):
+    """bf16 and f16 activations, strided rows, BASELINE-distribution blocks
+    (every fp16 scale |N(0, 0.01)|), and rows holding NaN / Inf (TR's float
+    path for those rows only)."""
+    M, N, K = 96, 192, 4096
+    raw = synth.weight(T.Q4_K, N, K, seed=12)
+    rng = np.random.default_rng(12)
+    xf = rng.standard_normal((M, K + 8), dtype=np.float32)
+    for xt in (torch.bfloat16, torch.float16):
+        xd = dev(xf[:, :K]).to(xt)
+        c = torch.zeros((M, N), dtype=torch.float32, device="cuda")
+        ctx.qgemm_act8(T.Q4_K, dev(raw), xd, c)
+        want = oracle.qgemm_act8(T.Q4_K, xd.float().cpu().numpy(), raw, N)
+        assert np.array_equal(bits(host(c)), bits(want))
+    xs = dev(xf)[:, 4:4 + K]  # row stride K + 8, 16-byte offset
+    c = torch.zeros((M, N), dtype=torch.float32, device="cuda")
+    ctx.qgemm_act8(T.Q4_K, dev(raw), xs, c)
+    assert np.array_equal(bits(host(c)), bits(oracle.qgemm_act8(T.Q4_K, np.ascontiguousarray(xf[:, 4:4 + K]), raw, N)))
+    x = xf[:, :K].copy()
+    x[3, 100] = np.nan
+    x[70, 4000] = np.inf
+    c = torch.zeros((M, N), dtype=torch.float32, device="cuda")
+    ctx.qgemm_act8(T.Q4_K, dev(raw), dev(x), c)
+    got, want = host(c), oracle.qgemm_act8(T.Q4_K, x, raw, N)
+    for m in range(M):
+        if m in (3, 70):
+            assert np.array_equal(np.isnan(got[m]), np.isnan(want[m]))
+            fin = ~np.isnan(want[m])
+            assert np.array_equal(got[m][fin], want[m][fin])
+        else:
+            assert np.array_equal(bits(got[m]), bits(want[m])), m
+    assert ctx.device_error() == 0
+
+
+def test_act8_tensor_cores_prefill_rows(ctx, oracle):
+    """BASELINE config 4's product (Q4_K 14336 x 4096) with 2048 activation
+    rows through the tensor-core kernel; rows spread over the launch checked
+    bit for bit against the oracle (the full product takes the CPU minutes)."""
+    N, K, M = 14336, 4096, 2048
+    raw = synth.weight(T.Q4_K, N, K, seed=21)
+    x = synth.activations(M, K, seed=22)
+    c = torch.zeros((M, N), dtype=torch.float32, device="cuda")
+    ctx.qgemm_act8(T.Q4_K, dev(raw), dev(x), c)
+    got = host(c)
+    rows = [0, 1, 127, 128, 1000, 2047]
+    want = oracle.qgemm_act8(T.Q4_K, x[rows], raw, N)
+    assert np.array_equal(bits(got[rows]), bits(want))
+    assert ctx.device_error() == 0
