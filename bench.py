@@ -378,6 +378,25 @@ def prefill_bench(ctx, rank: int, peaks: dict, cpu: bool) -> dict:
                                    "cores": os.cpu_count(), "kind": "port",
                                    "sample": f"16 of {M} rows through the oracle's float path"}
         out["shapes"].append(row)
+        if N == 14336:
+            # the same product with int8-quantised activations (TR's
+            # quantGemmQ8, bit-exact): integer block sums on tcgen05 kind::i8
+            with torch.cuda.stream(stream):
+                for i in range(2):
+                    ctx.qgemm_act8(Q4_K, ring[i % 4], x, c, stream=stream)
+                e0.record(stream)
+                for i in range(n):
+                    ctx.qgemm_act8(Q4_K, ring[i % 4], x, c, stream=stream)
+                e1.record(stream)
+                e1.synchronize()
+            ms8 = e0.elapsed_time(e1) / n
+            tops = 2.0 * M * N * K / (ms8 / 1e3) / 1e12
+            peak8 = 2.0 * peak if peak else None
+            out["act8"] = {"N": N, "K": K, "M": M, "us_per_call": round(ms8 * 1e3, 1), "tops": round(tops, 1),
+                           "roofline": {"bound": "tensor", "achieved": round(tops, 1), "peak": peak8, "unit": "TOP/s",
+                                        "frac": round(tops / peak8, 4) if peak8 else None,
+                                        "peak_source": "int8 dense = 2 x the measured dense bf16 burst"},
+                           "path": "int8 activations (bit-exact), tcgen05.mma.kind::i8"}
         del ring, x, c
     return out
 
