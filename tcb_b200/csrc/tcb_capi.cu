@@ -161,23 +161,6 @@ int qgemm_tc_prologue(tcb_ctx *ctx, int wtype, int M, int N, int K, const void *
                                   s, &pro);
   return e == cudaSuccess ? TCB_OK : cuda_fail(ctx, e);
 }
-// The float product of a few rows (2 .. kTcMinM-1) on the tensor cores, the
-// weights streamed once for all of them: for row counts whose matvec
-// kernels would stream the weights once per row.  fp16 operands (about 2e-4
-// relative L2 against TR's f32 path).  TCB_ERR_UNSUPPORTED when the shape
-// is not taken or its workspace would pass 1 GiB.
-int qgemm_tc_rows(tcb_ctx *ctx, int wtype, int M, int N, int K, const void *w, const float *x, long ldx, float *c,
-                  long ldc, int accumulate, cudaStream_t s) {
-  if (!ctx) return TCB_ERR_NULL;
-  if (M <= 0 || N <= 0 || !tc_eligible_rows(wtype, N, K, w) || ldc < N || ldx < K) return TCB_ERR_UNSUPPORTED;
-  const size_t ws = tc_workspace_bytes(wtype, M, N, K);
-  if (ws > ((size_t)1 << 30)) return TCB_ERR_UNSUPPORTED;
-  int rc = bind(ctx);
-  if (rc != TCB_OK || (rc = ensure_ws(ctx, ws)) != TCB_OK) return rc;
-  cudaError_t e = launch_qgemm_tc(wtype, w, M, N, K, x, TCB_F32, ldx, c, TCB_F32, ldc, accumulate, ctx->ws, ctx->derr,
-                                  s, nullptr);
-  return e == cudaSuccess ? TCB_OK : cuda_fail(ctx, e);
-}
 }  // namespace tcb
 
 namespace {

@@ -43,8 +43,5 @@ cudaError_t launch_qgemm_tc(int wtype, const void *w, int M, int N, int K, const
 // step and tcb_qgemm separately)
 int qgemm_tc_prologue(tcb_ctx *ctx, int wtype, int M, int N, int K, const void *w, const float *x, long ldx, float *c,
                       long ldc, int accumulate, const TcPrologue &pro, cudaStream_t s);
-// the float product of a few rows on the tensor cores (tcb_capi.cu)
-int qgemm_tc_rows(tcb_ctx *ctx, int wtype, int M, int N, int K, const void *w, const float *x, long ldx, float *c,
-                  long ldc, int accumulate, cudaStream_t s);
 
 }  // namespace tcb

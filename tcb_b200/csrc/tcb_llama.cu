@@ -1290,10 +1290,22 @@ int tcb_llama_capture(tcb_llama *m, void *stream) {
 // the same weights, each with its own K/V cache, position and token history.
 // A step runs every product once over the batch's rows, attention per
 // sequence in one launch (blockIdx.z), and each sequence's greedy pick.
+// how a batch step runs one product over its B rows (fixed at creation)
+struct BatchMat {
+  int how = 0;  // 0: multi-row matvec launches, 1: tensor cores, 2: a matvec launch per row, 3: portable kernel
+  tcb::MvPlan plan{};
+};
+
 struct tcb_llama_batch {
   std::vector<tcb_llama *> ms;
   tcb_llama *m0 = nullptr;
   int B = 0;
+  // the products' launch plans and the scratch they use: owned here, so a
+  // captured step never refers to the context's workspace, which later calls
+  // may grow (and so move)
+  std::vector<BatchMat> qkv_, o, gu_, down;
+  BatchMat head;
+  void *ws = nullptr, *sk = nullptr;
   float *x = nullptr, *h = nullptr, *qkv = nullptr, *att = nullptr, *gu = nullptr, *a = nullptr, *logits = nullptr;
   float *part = nullptr, *am_v = nullptr;
   int *am_i = nullptr;
@@ -1320,16 +1332,61 @@ cudaError_t balloc_bytes(tcb_llama_batch *b, void **p, size_t bytes) {
 }
 #define balloc(b, pp, n) balloc_bytes((b), reinterpret_cast<void **>(pp), (n) * sizeof(**(pp)))
 
-// rows out (+)= W x_rows: the library's product (up to 8 rows of x per
-// matvec launch, the weights streamed once for them); shapes the multi-row
-// matvec kernels do not take (long Q6_K rows, the wide head) go to the
-// tensor cores for all rows at once rather than one matvec launch per row
-int rows_product(tcb_llama *m0, const Mat &mt, int B, const float *x, float *y, int acc, cudaStream_t s) {
-  if (B > 1 && !tcb::matvec_plan_rows(mt.type, 0, mt.N, mt.K, mt.w, m0->ctx->sms, 2).ok) {
-    const int rc = tcb::qgemm_tc_rows(m0->ctx, mt.type, B, mt.N, mt.K, mt.w, x, mt.K, y, mt.N, acc, s);
-    if (rc != TCB_ERR_UNSUPPORTED) return rc;
+// How B rows of a product run (tcb_qgemm's routing for B < 64 rows): up to
+// 8 rows of x per matvec launch, the weights streamed once for them; shapes
+// the multi-row matvec kernels do not take (long Q6_K rows, the wide head)
+// on the tensor cores for all rows at once when their workspace stays under
+// 1 GiB, else one matvec launch per row.  ws / sk: the workspace and matvec
+// scratch this product needs.
+BatchMat batch_mat(const tcb_llama *m0, const Mat &mt, int B, size_t &ws, size_t &sk) {
+  BatchMat bm;
+  const int sms = m0->ctx->sms;
+  if (B > 1)
+    for (int mr = 8; mr >= 2 && !bm.plan.ok; mr /= 2)
+      if (mr <= 2 * B - 1 || mr == 2) bm.plan = tcb::matvec_plan_rows(mt.type, 0, mt.N, mt.K, mt.w, sms, mr);
+  if (bm.plan.ok) {
+    bm.how = 0;
+  } else if (B > 1 && tcb::tc_eligible_rows(mt.type, mt.N, mt.K, mt.w) &&
+             tcb::tc_workspace_bytes(mt.type, B, mt.N, mt.K) <= ((size_t)1 << 30)) {
+    bm.how = 1;
+    const size_t w = tcb::tc_workspace_bytes(mt.type, B, mt.N, mt.K);
+    ws = w > ws ? w : ws;
+  } else {
+    bm.plan = tcb::matvec_plan(mt.type, 0, 1, mt.N, mt.K, mt.w, sms);
+    bm.how = bm.plan.ok ? 2 : 3;
   }
-  return tcb_qgemm(m0->ctx, mt.type, B, mt.N, mt.K, mt.w, x, TCB_F32, mt.K, y, TCB_F32, mt.N, acc, s);
+  if (bm.plan.ok && bm.plan.split_bytes > sk) sk = bm.plan.split_bytes;
+  return bm;
+}
+
+// rows y (+)= W x_rows for the batch's B rows
+int rows_product(tcb_llama_batch *bt, const Mat &mt, const BatchMat &bm, const float *x, float *y, int acc,
+                 cudaStream_t s) {
+  tcb_llama *m0 = bt->m0;
+  const int B = bt->B;
+  cudaError_t e = cudaSuccess;
+  switch (bm.how) {
+  case 0:
+    for (int r0 = 0; r0 < B && e == cudaSuccess; r0 += bm.plan.rows) {
+      const int rows = B - r0 < bm.plan.rows ? B - r0 : bm.plan.rows;
+      e = tcb::matvec_launch(bm.plan, mt.type, 0, mt.N, mt.K, mt.w, x + (size_t)r0 * mt.K, TCB_F32,
+                             y + (size_t)r0 * mt.N, TCB_F32, acc, m0->ctx->derr, s, nullptr, 0, bt->sk, rows, mt.K,
+                             mt.N);
+    }
+    break;
+  case 1:
+    e = tcb::launch_qgemm_tc(mt.type, mt.w, B, mt.N, mt.K, x, TCB_F32, mt.K, y, TCB_F32, mt.N, acc, bt->ws,
+                             m0->ctx->derr, s, nullptr);
+    break;
+  case 2:
+    for (int r = 0; r < B && e == cudaSuccess; r++)
+      e = tcb::matvec_launch(bm.plan, mt.type, 0, mt.N, mt.K, mt.w, x + (size_t)r * mt.K, TCB_F32, y + (size_t)r * mt.N,
+                             TCB_F32, acc, m0->ctx->derr, s, nullptr, 0, bt->sk);
+    break;
+  default:
+    e = tcb::launch_qgemm_simt(mt.type, mt.w, B, mt.N, mt.K, x, TCB_F32, mt.K, y, TCB_F32, mt.N, acc, m0->ctx->sms, s);
+  }
+  return e == cudaSuccess ? TCB_OK : fail(m0, e);
 }
 
 int issue_batch_step(tcb_llama_batch *bt, cudaStream_t s) {
@@ -1357,7 +1414,7 @@ int issue_batch_step(tcb_llama_batch *bt, cudaStream_t s) {
   int rc = TCB_OK;
   for (int l = 0; l < c.n_layers && rc == TCB_OK; l++) {
     k_rmsnorm<<<B, 1024, 0, s>>>(bt->x, m0->attn_norm[l], bt->h, D, c.eps);
-    if ((rc = rows_product(m0, m0->qkv[l], B, bt->h, bt->qkv, 0, s)) != TCB_OK) break;
+    if ((rc = rows_product(bt, m0->qkv[l], bt->qkv_[l], bt->h, bt->qkv, 0, s)) != TCB_OK) break;
     const dim3 ag(KVH, m0->nch_max, B);
     switch (G) {
 #define TCB_ATTN(GG)                                                                                              \
@@ -1375,16 +1432,19 @@ int issue_batch_step(tcb_llama_batch *bt, cudaStream_t s) {
     default: e = cudaErrorInvalidValue;
     }
     if (e != cudaSuccess) return fail(m0, e);
-    if ((rc = rows_product(m0, m0->o[l], B, bt->att, bt->x, acc, s)) != TCB_OK || (rc = reduce()) != TCB_OK) break;
+    if ((rc = rows_product(bt, m0->o[l], bt->o[l], bt->att, bt->x, acc, s)) != TCB_OK || (rc = reduce()) != TCB_OK)
+      break;
     k_rmsnorm<<<B, 1024, 0, s>>>(bt->x, m0->ffn_norm[l], bt->h, D, c.eps);
-    if ((rc = rows_product(m0, m0->gu[l], B, bt->h, bt->gu, 0, s)) != TCB_OK) break;
+    if ((rc = rows_product(bt, m0->gu[l], bt->gu_[l], bt->h, bt->gu, 0, s)) != TCB_OK) break;
     const long na = (long)B * F;
     k_swiglu_rows<<<(int)((na + 255) / 256 < 4096 ? (na + 255) / 256 : 4096), 256, 0, s>>>(bt->gu, bt->a, F, na);
-    if ((rc = rows_product(m0, m0->down[l], B, bt->a, bt->x, acc, s)) != TCB_OK || (rc = reduce()) != TCB_OK) break;
+    if ((rc = rows_product(bt, m0->down[l], bt->down[l], bt->a, bt->x, acc, s)) != TCB_OK ||
+        (rc = reduce()) != TCB_OK)
+      break;
   }
   if (rc != TCB_OK) return rc;
   k_rmsnorm<<<B, 1024, 0, s>>>(bt->x, m0->final_norm, bt->h, D, c.eps);
-  if ((rc = rows_product(m0, m0->head, B, bt->h, bt->logits, 0, s)) != TCB_OK) return rc;
+  if ((rc = rows_product(bt, m0->head, bt->head, bt->h, bt->logits, 0, s)) != TCB_OK) return rc;
   for (int b = 0; b < B; b++)
     if ((e = launch(k_argmax_part, dim3(kArgBlocks), dim3(256), s, (const float *)(bt->logits + (size_t)b * V), V,
                     bt->am_v + (size_t)b * kArgBlocks, bt->am_i + (size_t)b * kArgBlocks)) != cudaSuccess)
@@ -1468,6 +1528,20 @@ int tcb_llama_batch_create(tcb_llama *const *ms, int count, tcb_llama_batch **ou
       (e = balloc(bt, &bt->cand, (size_t)B * m0->tp)) != cudaSuccess ||
       (e = cudaMemset(bt->count, 0, (size_t)B * KVH * sizeof(unsigned))) != cudaSuccess ||
       (e = cudaMemcpy(bt->seq, hs.data(), B * sizeof(tcb::ll::BatchSeq), cudaMemcpyHostToDevice)) != cudaSuccess) {
+    tcb_llama_batch_destroy(bt);
+    return e == cudaErrorMemoryAllocation ? TCB_ERR_NOMEM : fail(m0, e);
+  }
+  size_t ws = 0, sk = 0;
+  for (int l = 0; l < c.n_layers; l++) {
+    bt->qkv_.push_back(batch_mat(m0, m0->qkv[l], B, ws, sk));
+    bt->o.push_back(batch_mat(m0, m0->o[l], B, ws, sk));
+    bt->gu_.push_back(batch_mat(m0, m0->gu[l], B, ws, sk));
+    bt->down.push_back(batch_mat(m0, m0->down[l], B, ws, sk));
+  }
+  bt->head = batch_mat(m0, m0->head, B, ws, sk);
+  if ((ws && (e = balloc_bytes(bt, &bt->ws, ws)) != cudaSuccess) ||
+      (e = balloc_bytes(bt, &bt->sk, sk + tcb::kScratchCntBytes)) != cudaSuccess ||
+      (e = cudaMemset(bt->sk, 0, sk + tcb::kScratchCntBytes)) != cudaSuccess) {
     tcb_llama_batch_destroy(bt);
     return e == cudaErrorMemoryAllocation ? TCB_ERR_NOMEM : fail(m0, e);
   }

@@ -163,3 +163,43 @@ def test_batch_long_rows_on_tensor_cores(setup):
         res = check_history(host, toks[i], len(p), {pos: logits[i][pos] for pos in range(steps)})
         assert res["checked_tokens"] == steps + 1 - len(p)
     assert ctx.device_error() == 0
+
+
+def test_batch_graph_after_workspace_growth(setup):
+    """A captured batch step keeps working after other calls on the context
+    grow (and so move) its workspace: the batch owns the scratch of its
+    products.  The down projection here runs on the tensor cores."""
+    import torch
+
+    from tcb_b200 import synth
+
+    ctx = setup[0]
+    cfg = llama.LlamaConfig(n_layers=1, d_model=512, n_heads=4, n_kv_heads=2, head_dim=128, ffn_dim=9216,
+                            vocab=2048, max_ctx=64, eps=1e-5, rope_theta=500000.0)
+    host = llama.host_model(cfg, seed=3)
+    dev = llama.device_model(cfg, 3, host)
+    rng = np.random.default_rng(53)
+    prompts = [rng.integers(0, cfg.vocab, n).astype(np.int64) for n in (4, 7)]
+    eager, _ = run_batch(ctx, dev, prompts, 16)
+    engines = [llama.Llama(ctx, dev) for _ in prompts]
+    for e, p in zip(engines, prompts):
+        e.start(p)
+    b = llama.Batch(engines)
+    b.step(1)
+    b.capture()
+    # a large product on the same context: its workspace grows
+    w = torch.from_numpy(synth.weight(T.Q6_K, 4096, 8192, seed=5)).cuda()
+    x = torch.randn((4096, 8192), device="cuda")
+    y = torch.empty((4096, 4096), device="cuda")
+    ctx.qgemm(T.Q6_K, w, x, y)
+    torch.cuda.synchronize()
+    for e, p in zip(engines, prompts):
+        e.start(p)
+    b.step(16)
+    got = [e.tokens(17) for e in engines]
+    b.close()
+    for e in engines:
+        e.close()
+    for a_, b_ in zip(eager, got):
+        assert list(a_) == list(b_)
+    assert ctx.device_error() == 0
