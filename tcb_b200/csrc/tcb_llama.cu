@@ -1332,22 +1332,26 @@ cudaError_t balloc_bytes(tcb_llama_batch *b, void **p, size_t bytes) {
 }
 #define balloc(b, pp, n) balloc_bytes((b), reinterpret_cast<void **>(pp), (n) * sizeof(**(pp)))
 
-// How B rows of a product run (tcb_qgemm's routing for B < 64 rows): up to
-// 8 rows of x per matvec launch, the weights streamed once for them; shapes
-// the multi-row matvec kernels do not take (long Q6_K rows, the wide head)
-// on the tensor cores for all rows at once when their workspace stays under
-// 1 GiB, else one matvec launch per row.  ws / sk: the workspace and matvec
-// scratch this product needs.
+// How B rows of a product run.  From kBatchTcRows rows on, the tensor cores
+// take the product when the shape allows it with a workspace under 1 GiB:
+// the weights stream once for all rows (fp16 operands, about 2e-4 relative
+// L2).  Below that, tcb_qgemm's routing for few rows: up to 8 rows of x per
+// matvec launch (the weights streamed once per launch); shapes the
+// multi-row matvec kernels do not take (long Q6_K rows, the wide head) on
+// the tensor cores as above, else one matvec launch per row.  ws / sk: the
+// workspace and matvec scratch this product needs.
+constexpr int kBatchTcRows = 16;
 BatchMat batch_mat(const tcb_llama *m0, const Mat &mt, int B, size_t &ws, size_t &sk) {
   BatchMat bm;
   const int sms = m0->ctx->sms;
-  if (B > 1)
+  const bool tc = B > 1 && tcb::tc_eligible_rows(mt.type, mt.N, mt.K, mt.w) &&
+                  tcb::tc_workspace_bytes(mt.type, B, mt.N, mt.K) <= ((size_t)1 << 30);
+  if (B > 1 && !(tc && B >= kBatchTcRows))
     for (int mr = 8; mr >= 2 && !bm.plan.ok; mr /= 2)
       if (mr <= 2 * B - 1 || mr == 2) bm.plan = tcb::matvec_plan_rows(mt.type, 0, mt.N, mt.K, mt.w, sms, mr);
   if (bm.plan.ok) {
     bm.how = 0;
-  } else if (B > 1 && tcb::tc_eligible_rows(mt.type, mt.N, mt.K, mt.w) &&
-             tcb::tc_workspace_bytes(mt.type, B, mt.N, mt.K) <= ((size_t)1 << 30)) {
+  } else if (tc) {
     bm.how = 1;
     const size_t w = tcb::tc_workspace_bytes(mt.type, B, mt.N, mt.K);
     ws = w > ws ? w : ws;

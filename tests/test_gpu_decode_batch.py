@@ -203,3 +203,23 @@ def test_batch_graph_after_workspace_growth(setup):
     for a_, b_ in zip(eager, got):
         assert list(a_) == list(b_)
     assert ctx.device_error() == 0
+
+
+def test_batch16_on_tensor_cores(setup):
+    """16 sequences: from 16 rows on every product of the batch step runs on
+    the tensor cores (the weights streamed once for all rows, fp16 operands:
+    about 2e-4 relative L2 per product, as in the prompt pass); each
+    sequence's logits and tokens against the reference fed its history, on
+    the plain test model, within 2e-3 (every product of every step, the head
+    included, carries the fp16 rounding)"""
+    ctx = setup[0]
+    host = llama.host_model(CFG, seed=7)
+    dev = llama.device_model(CFG, 7, host)
+    rng = np.random.default_rng(59)
+    prompts = [rng.integers(0, CFG.vocab, int(n)).astype(np.int64) for n in rng.integers(1, 12, 16)]
+    steps = 24
+    toks, logits = run_batch(ctx, dev, prompts, steps, graph=True)
+    for i, p in enumerate(prompts):
+        res = check_history(host, toks[i], len(p), {pos: logits[i][pos] for pos in range(1, steps)}, tol=2e-3)
+        assert res["checked_tokens"] == steps + 1 - len(p)
+    assert ctx.device_error() == 0
