@@ -274,9 +274,13 @@ int tcb_llama_batch_logits(tcb_llama_batch *b, float **logits);
  * routine: the quantised activations live in one file-scope device array
  * of TCB_STATIC_SCRATCH_BYTES that every GPU loading libtcb holds until the
  * process exits.
- *   - It runs on the calling thread's current device.  The first call on a
- *     device looks up the array's device address (cudaGetSymbolAddress);
- *     make that first call before any stream capture.
+ *   - It runs on the calling thread's current device.  Every call looks up
+ *     the array's device address (cudaGetSymbolAddress), so a device reset
+ *     between calls is safe; the first call on a device may load the
+ *     module, so make it before any stream capture.
+ *   - It runs the portable quantise and dot kernels (about 64 us per
+ *     activation row at 4096 x 4096, against 9.4 us for one row through
+ *     tcb_qgemm_act8), since the faster kernels need per-call scratch.
  *   - Problems needing more than TCB_STATIC_SCRATCH_BYTES of scratch
  *     (about 1.28 bytes per element of x, M*K in all) are refused with
  *     TCB_ERR_TOO_LARGE before anything is launched.

@@ -17,32 +17,26 @@ namespace {
 __device__ __align__(256) unsigned char g_act8_scratch[TCB_STATIC_SCRATCH_BYTES];
 
 constexpr int kMaxDevices = 64;
-struct DeviceSlot {
-  bool ready = false;
-  void *scratch = nullptr;  // device address of g_act8_scratch on this device
-  int sms = 0;
-};
 std::mutex g_mu;
-DeviceSlot g_slots[kMaxDevices];
+int g_sms[kMaxDevices];  // SM count per device (0: not looked up yet)
 
-// once per device, with that device current
-int device_slot(int dev, DeviceSlot **out) {
+// The scratch address is looked up on every call rather than cached: after a
+// device reset the module is loaded again and the array may move.
+int device_scratch(int dev, void **scratch, int *sms) {
   if (dev < 0 || dev >= kMaxDevices) return TCB_ERR_UNSUPPORTED;
-  std::lock_guard<std::mutex> lock(g_mu);
-  DeviceSlot &s = g_slots[dev];
-  if (!s.ready) {
-    void *p = nullptr;
-    int sms = 0;
-    if (cudaGetSymbolAddress(&p, g_act8_scratch) != cudaSuccess || !p ||
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
-      (void)cudaGetLastError();
-      return TCB_ERR_CUDA;
-    }
-    s.scratch = p;
-    s.sms = sms;
-    s.ready = true;
+  void *p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_act8_scratch) != cudaSuccess || !p) {
+    (void)cudaGetLastError();
+    return TCB_ERR_CUDA;
   }
-  *out = &s;
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (g_sms[dev] == 0 && cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    g_sms[dev] = 0;
+    (void)cudaGetLastError();
+    return TCB_ERR_CUDA;
+  }
+  *scratch = p;
+  *sms = g_sms[dev];
   return TCB_OK;
 }
 
@@ -63,13 +57,14 @@ extern "C" int tcb_qgemm_act8_static(int wtype, int M, int N, int K, const void 
   if (tcb::act8_scratch_bytes(M, K, blk) > TCB_STATIC_SCRATCH_BYTES) return TCB_ERR_TOO_LARGE;
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess) return TCB_ERR_CUDA;
-  DeviceSlot *slot = nullptr;
-  if ((rc = device_slot(dev, &slot)) != TCB_OK) return rc;
+  void *scratch = nullptr;
+  int sms = 0;
+  if ((rc = device_scratch(dev, &scratch, &sms)) != TCB_OK) return rc;
   // every scratch byte the dot kernel reads is written by the quantise
   // kernel of this call first (codes, scales, sums and flags of all blocks)
-  const tcb::Act8Scratch sc = tcb::act8_scratch_carve(slot->scratch, M, K, blk);
-  cudaError_t e = tcb::launch_act8_quantize(blk, M, K, x, xdtype, ldx, sc, slot->sms, s);
+  const tcb::Act8Scratch sc = tcb::act8_scratch_carve(scratch, M, K, blk);
+  cudaError_t e = tcb::launch_act8_quantize(blk, M, K, x, xdtype, ldx, sc, sms, s);
   if (e == cudaSuccess)
-    e = tcb::launch_act8_dot(wtype, w, M, N, K, sc, x, xdtype, ldx, c, cdtype, ldc, accumulate, slot->sms, s);
+    e = tcb::launch_act8_dot(wtype, w, M, N, K, sc, x, xdtype, ldx, c, cdtype, ldc, accumulate, sms, s);
   return e == cudaSuccess ? TCB_OK : TCB_ERR_CUDA;
 }

@@ -70,3 +70,23 @@ def test_static_rejects_oversize():
     assert "static scratch" in T.what_msg(rc)
     torch.cuda.synchronize()
     assert bool((c == 1.5).all())
+
+
+def test_static_allocates_no_device_memory():
+    """After one call of each case (module and kernel loading, the runtime's
+    own first-use costs), further calls leave the device's free memory
+    unchanged."""
+    shapes = [(T.Q4_K, 1, 64, 256), (T.Q8_0, 8, 257, 4096), (T.Q6_K, 5, 33, 768), (T.Q4_0, 60, 100, 8192)]
+    cases = []
+    for i, (wt, M, N, K) in enumerate(shapes):
+        w, x = case(wt, M, N, K, 20 + i)
+        cases.append((wt, w, x, torch.zeros((M, N), dtype=torch.float32, device="cuda")))
+    for wt, w, x, c in cases:
+        T.qgemm_act8_static(wt, w, x, c, accumulate=True)
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for _ in range(3):
+        for wt, w, x, c in cases:
+            T.qgemm_act8_static(wt, w, x, c, accumulate=True)
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0
