@@ -19,7 +19,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
          "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]
-SOURCES = ["tcb_capi.cu", "tcb_dequant.cu", "tcb_gemv_simt.cu", "tcb_matvec.cu", "tcb_mv_q4k.cu", "tcb_mv_q6k.cu", "tcb_gemm_tc.cu", "tcb_gemm_i8.cu", "tcb_llama.cu", "tcb_static.cu", "tcb_attn_prefill.cu"]
+SOURCES = ["tcb_capi.cu", "tcb_dequant.cu", "tcb_gemv_simt.cu", "tcb_matvec.cu", "tcb_mv_q4k.cu", "tcb_mv_q6k.cu", "tcb_gemm_tc.cu", "tcb_gemm_i8.cu", "tcb_mv_rows.cu", "tcb_llama.cu", "tcb_static.cu", "tcb_attn_prefill.cu"]
 
 
 def _stale(objs, deps) -> bool:

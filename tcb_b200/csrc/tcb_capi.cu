@@ -92,6 +92,31 @@ int run_matvec(tcb_ctx *ctx, int wtype, int act8, int M, int N, int K, const voi
   // int8-activation product has no other fast kernel, so every M comes here
   // (the portable kernel costs about 240 us a row on the prefill shapes)
   if (M < 1 || (!act8 && M >= tcb::kTcMinM)) return TCB_OK;
+  if (M > 1 && !act8 && (wtype == TCB_Q4_K || wtype == TCB_Q6_K) && tcb::rows_plan(wtype, N, K, w, ctx->sms, 2).ok) {
+    // Q4_K / Q6_K float path: up to 16 rows per weight stream (fewer when
+    // their digits leave too little shared memory); a last single row takes
+    // the batch-1 kernel
+    *taken = true;
+    for (int m0 = 0, rows = 0; m0 < M; m0 += rows) {
+      rows = M - m0 < 16 ? M - m0 : 16;
+      tcb::MvPlan pq{};
+      if (rows == 1) pq = tcb::matvec_plan(wtype, 0, 1, N, K, w, ctx->sms);
+      while (!pq.ok) {
+        pq = tcb::rows_plan(wtype, N, K, w, ctx->sms, rows < 2 ? 2 : rows);
+        if (pq.ok) break;
+        if (rows <= 2) return TCB_ERR_UNSUPPORTED;
+        rows /= 2;
+      }
+      const void *xm = static_cast<const char *>(x) + (size_t)m0 * ldx * elem_size(xdt);
+      void *cm = static_cast<char *>(c) + (size_t)m0 * ldc * elem_size(cdt);
+      int rc = ensure_sk(ctx, pq.split_bytes);
+      if (rc != TCB_OK) return rc;
+      cudaError_t e = tcb::matvec_launch(pq, wtype, 0, N, K, w, xm, xdt, cm, cdt, accumulate, ctx->derr, s, nullptr,
+                                         0, ctx->sk, rows, ldx, ldc);
+      if (e != cudaSuccess) return cuda_fail(ctx, e);
+    }
+    return TCB_OK;
+  }
   if (M > 1) {
     // the kernels take up to 8 rows per launch, streaming the weights once
     // for all of them (fewer rows per launch when their x regions leave too

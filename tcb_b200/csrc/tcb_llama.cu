@@ -1292,7 +1292,8 @@ int tcb_llama_capture(tcb_llama *m, void *stream) {
 // sequence in one launch (blockIdx.z), and each sequence's greedy pick.
 // how a batch step runs one product over its B rows (fixed at creation)
 struct BatchMat {
-  int how = 0;  // 0: multi-row matvec launches, 1: tensor cores, 2: a matvec launch per row, 3: portable kernel
+  int how = 0;  // 0: multi-row matvec launches, 1: tensor cores, 2: a matvec launch per row, 3: portable kernel,
+                // 4: the Q4_K kernel of up to 16 rows (row groups of plan.rows)
   tcb::MvPlan plan{};
 };
 
@@ -1344,6 +1345,19 @@ constexpr int kBatchTcRows = 16;
 BatchMat batch_mat(const tcb_llama *m0, const Mat &mt, int B, size_t &ws, size_t &sk) {
   BatchMat bm;
   const int sms = m0->ctx->sms;
+  // Q4_K / Q6_K with up to 16 rows: one weight stream for all rows, integer scale
+  // math (faster than the tensor-core product, whose weight dequant is
+  // amortised over 16 of the 256 rows it is built for)
+  if ((mt.type == TCB_Q4_K || mt.type == TCB_Q6_K) && B >= 2 && B <= 16) {
+    // groups of fewer rows when the digits of 16 leave too little shared memory
+    for (int r = B; r >= 2 && !bm.plan.ok; r = (r + 1) / 2 == r ? 1 : (r + 1) / 2)
+      bm.plan = tcb::rows_plan(mt.type, mt.N, mt.K, mt.w, sms, r);
+    if (bm.plan.ok) {
+      bm.how = 4;
+      if (bm.plan.split_bytes > sk) sk = bm.plan.split_bytes;
+      return bm;
+    }
+  }
   const bool tc = B > 1 && tcb::tc_eligible_rows(mt.type, mt.N, mt.K, mt.w) &&
                   tcb::tc_workspace_bytes(mt.type, B, mt.N, mt.K) <= ((size_t)1 << 30);
   if (B > 1 && !(tc && B >= kBatchTcRows))
@@ -1376,6 +1390,13 @@ int rows_product(tcb_llama_batch *bt, const Mat &mt, const BatchMat &bm, const f
       e = tcb::matvec_launch(bm.plan, mt.type, 0, mt.N, mt.K, mt.w, x + (size_t)r0 * mt.K, TCB_F32,
                              y + (size_t)r0 * mt.N, TCB_F32, acc, m0->ctx->derr, s, nullptr, 0, bt->sk, rows, mt.K,
                              mt.N);
+    }
+    break;
+  case 4:
+    for (int r0 = 0; r0 < B && e == cudaSuccess; r0 += bm.plan.rows) {
+      const int rows = B - r0 < bm.plan.rows ? B - r0 : bm.plan.rows;
+      e = tcb::rows_launch(bm.plan, mt.N, mt.K, mt.w, x + (size_t)r0 * mt.K, TCB_F32, mt.K, y + (size_t)r0 * mt.N,
+                           TCB_F32, mt.N, acc, rows, m0->ctx->derr, bt->sk, s);
     }
     break;
   case 1:

@@ -10,7 +10,8 @@ namespace tcb {
 // shape is not taken by it (the caller then runs the portable kernel)
 struct MvPlan {
   bool ok;
-  int kind;                    // 0: generic kernel, 1: Q4_K float kernel, 2: Q6_K float kernel
+  int kind;                    // 0: generic kernel, 1: Q4_K float kernel, 2: Q6_K float kernel,
+                               // 3: Q4_K float kernel of 2..16 rows (tcb_mv_rows.cu)
   int tiles, cbc, nch;         // tiles, blocks per staged chunk, chunks per row
   int stages, pitch;           // TMA stages, bytes per staged row
   int xoff, toff, soff, smem;  // shared-memory layout
@@ -57,6 +58,15 @@ MvPlan q6k_plan(int N, int K, const void *w, int sms);
 cudaError_t q6k_launch(const MvPlan &pl, int N, int K, const void *w, const void *x, int xdt, void *c, int cdt,
                        int accumulate, int *err, cudaStream_t s, int gated = 0, const void *pf = nullptr,
                        size_t pf_bytes = 0, void *scratch = nullptr);
+
+// Q4_K / Q6_K float path of 2..16 rows of x in one weight stream (kind 3): the
+// digitising prologue, the product and (when plan.ksplit > 1) the sum of the
+// K-range partials, three launches on s.  plan.rows (4, 8, 12, 16) is the
+// most rows a launch takes; the launch needs plan.split_bytes of scratch
+// (its counter region untouched).
+MvPlan rows_plan(int wtype, int N, int K, const void *w, int sms, int M);
+cudaError_t rows_launch(const MvPlan &pl, int N, int K, const void *w, const void *x, int xdt, long ldx, void *c,
+                        int cdt, long ldc, int accumulate, int M, int *err, void *scratch, cudaStream_t s);
 
 // pf / pf_bytes: the weights of the next kernel of a chain, streamed into L2
 // by this launch's producers (a hint; nullptr for none)

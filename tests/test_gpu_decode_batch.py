@@ -82,11 +82,14 @@ def test_batch_equals_single_engines(setup):
         for pos in range(steps):
             m.step(1)
             single = m.logits()
-            assert rel_l2(logits[i][pos], single) <= TOL, (i, pos)
+            # both are within TOL of the reference, but through different
+            # kernels (the batch's multi-row products digitise x per 256
+            # elements, the single step per 32), so they may differ by 2 TOL
+            assert rel_l2(logits[i][pos], single) <= 2 * TOL, (i, pos)
             got, want = int(m.tokens(pos + 2)[pos + 1]), int(toks[i][pos + 1])
             if got != want:
                 # the two kernels' roundings differ: only a tie may part them
-                assert single[got] - single[want] < TOL * float(np.abs(single).max()), (i, pos)
+                assert single[got] - single[want] < 2 * TOL * float(np.abs(single).max()), (i, pos)
                 break
         m.close()
 
