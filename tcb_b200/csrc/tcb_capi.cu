@@ -92,8 +92,9 @@ int run_matvec(tcb_ctx *ctx, int wtype, int act8, int M, int N, int K, const voi
   // int8-activation product has no other fast kernel, so every M comes here
   // (the portable kernel costs about 240 us a row on the prefill shapes)
   if (M < 1 || (!act8 && M >= tcb::kTcMinM)) return TCB_OK;
-  if (M > 1 && !act8 && (wtype == TCB_Q4_K || wtype == TCB_Q6_K) && tcb::rows_plan(wtype, N, K, w, ctx->sms, 2).ok) {
-    // Q4_K / Q6_K float path: up to 16 rows per weight stream (fewer when
+  if (M > 1 && !act8 && (wtype == TCB_Q4_K || wtype == TCB_Q6_K || wtype == TCB_Q4_0) &&
+      tcb::rows_plan(wtype, N, K, w, ctx->sms, 2).ok) {
+    // Q4_K / Q6_K / Q4_0 float path: up to 16 rows per weight stream (fewer when
     // their digits leave too little shared memory); a last single row takes
     // the batch-1 kernel
     *taken = true;

@@ -1348,7 +1348,7 @@ BatchMat batch_mat(const tcb_llama *m0, const Mat &mt, int B, size_t &ws, size_t
   // Q4_K / Q6_K with up to 16 rows: one weight stream for all rows, integer scale
   // math (faster than the tensor-core product, whose weight dequant is
   // amortised over 16 of the 256 rows it is built for)
-  if ((mt.type == TCB_Q4_K || mt.type == TCB_Q6_K) && B >= 2 && B <= 16) {
+  if ((mt.type == TCB_Q4_K || mt.type == TCB_Q6_K || mt.type == TCB_Q4_0) && B >= 2 && B <= 16) {
     // groups of fewer rows when the digits of 16 leave too little shared memory
     for (int r = B; r >= 2 && !bm.plan.ok; r = (r + 1) / 2 == r ? 1 : (r + 1) / 2)
       bm.plan = tcb::rows_plan(mt.type, mt.N, mt.K, mt.w, sms, r);

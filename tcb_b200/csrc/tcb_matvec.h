@@ -59,7 +59,7 @@ cudaError_t q6k_launch(const MvPlan &pl, int N, int K, const void *w, const void
                        int accumulate, int *err, cudaStream_t s, int gated = 0, const void *pf = nullptr,
                        size_t pf_bytes = 0, void *scratch = nullptr);
 
-// Q4_K / Q6_K float path of 2..16 rows of x in one weight stream (kind 3): the
+// Q4_K / Q6_K / Q4_0 float path of 2..16 rows of x in one weight stream (kind 3): the
 // digitising prologue, the product and (when plan.ksplit > 1) the sum of the
 // K-range partials, three launches on s.  plan.rows (4, 8, 12, 16) is the
 // most rows a launch takes; the launch needs plan.split_bytes of scratch

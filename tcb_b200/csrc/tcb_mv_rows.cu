@@ -1,5 +1,5 @@
-// tcb_mv_rows.cu - Q4_K and Q6_K float-path product of 2 to 16 activation
-// rows, the weights streamed once for all of them:
+// tcb_mv_rows.cu - Q4_K, Q6_K and Q4_0 float-path product of 2 to 16
+// activation rows, the weights streamed once for all of them:
 //
 //   y[m][n] (+)= sum_k x[m][k] * dequant(W)[n, k]     W: [N, K] blocks
 //
@@ -83,6 +83,12 @@ struct Fmt<TCB_Q4_K> {
   static constexpr int kPitch = 1184;   // 32 mod 128: a warp's 8-byte code loads are conflict-free
 };
 template <>
+struct Fmt<TCB_Q4_0> {
+  static constexpr int kBB = 144;       // eight 18-byte blocks: 256 elements
+  static constexpr int kBox8 = 148;
+  static constexpr int kPitch = 1184;
+};
+template <>
 struct Fmt<TCB_Q6_K> {
   static constexpr int kBB = 210;
   static constexpr int kBox8 = 210;     // 8 superblocks
@@ -145,13 +151,15 @@ struct Params {
 
 // ---------------------------------------------------------------- digits
 
-// One warp per (superblock, row); rows M..4J-1 get zero digits.  Q6: the
-// Q6_K kernel's k-slot order within a 32-element panel column (bytes 8t..8t+3
-// = elements 4t..4t+3, bytes 8t+4..8t+7 = elements 16+4t..16+4t+3: the two
-// 16-element sub-blocks of a lane) and 16 sub-block sums; otherwise element
-// order and 8 sums.  The sums panel: [high byte, low byte][column][16
-// k-slots], S = 64 * high + low with low in 0..63.
-template <int J, bool Q6>
+// One warp per (superblock, row); rows M..4J-1 get zero digits.  Q6_K and
+// Q4_0 take the k-slot order that puts a lane's two 4-byte code groups side
+// by side within a 32-element panel column (bytes 8t..8t+3 = elements
+// 4t..4t+3, bytes 8t+4..8t+7 = elements 16+4t..16+4t+3); Q4_K element order.
+// The ninth panel: Q4_K / Q6_K the sub-block digit sums (32 / 16 elements)
+// for the second-term MMA, [high byte, low byte][column][16 k-slots], S = 64
+// * high + low with low in 0..63; Q4_0 the combined sums 254 * Sh + Sl of
+// each 32-element block, int32 [block][row in group].
+template <int J, int W>
 __global__ void __launch_bounds__(256) k_xdig(const void *x, int xdt, long ldx, int M, int nb, uint8_t *dig, float *sig,
                                              uint8_t *bad) {
   pdl_launch_dependents();
@@ -198,7 +206,8 @@ __global__ void __launch_bounds__(256) k_xdig(const void *x, int xdt, long ldx, 
   const int u = lane & 3;
   uint8_t *grp = dig + (size_t)(b * J + j) * kGroupBytes;
   uint8_t *p = grp + (lane >> 2) * kPanel;
-  if (Q6) {
+  constexpr bool Q6 = W == TCB_Q6_K, NAT = W != TCB_Q4_K;
+  if (NAT) {
     const int o = 16 * (u & 1) + 4 * (u >> 1);
     uint32_t *ph = reinterpret_cast<uint32_t *>(p + (2 * r) * 32 + o), *pl = reinterpret_cast<uint32_t *>(p + (2 * r + 1) * 32 + o);
     ph[0] = h[0];
@@ -218,13 +227,15 @@ __global__ void __launch_bounds__(256) k_xdig(const void *x, int xdt, long ldx, 
   }
   uint8_t *ps = grp + 8 * kPanel;
   const int kslot = Q6 ? 2 * (lane >> 2) + (u >> 1) : (lane >> 2);
-  if (Q6 ? (u & 1) == 0 : u == 0) {
+  if (W == TCB_Q4_0) {
+    if (u == 0) reinterpret_cast<int *>(ps)[kslot * 4 + r] = 254 * sh + sl;
+  } else if (Q6 ? (u & 1) == 0 : u == 0) {
     ps[(2 * r) * 16 + kslot] = (uint8_t)(sh >> 6);
     ps[128 + (2 * r) * 16 + kslot] = (uint8_t)(sh & 63);
     ps[(2 * r + 1) * 16 + kslot] = (uint8_t)(sl >> 6);
     ps[128 + (2 * r + 1) * 16 + kslot] = (uint8_t)(sl & 63);
   }
-  if (!Q6 && lane < 8) {
+  if (W == TCB_Q4_K && lane < 8) {
     // k-slots 8..15 of the Q4_K sums (eight sub-blocks only)
     ps[(2 * r + (lane >> 2)) * 16 + 8 + (lane & 3) * 2] = 0;
     ps[(2 * r + (lane >> 2)) * 16 + 9 + (lane & 3) * 2] = 0;
@@ -405,6 +416,55 @@ __device__ __forceinline__ void block_q6k(const uint8_t *r0, const uint8_t *dg, 
   }
 }
 
+// Q4_0: eight 18-byte blocks (d, then 16 bytes: element i in the low nibble
+// of byte i, element 16 + i in the high nibble) make one 256-element unit;
+// value = d * (q - 8) (TR tensor/quant.go Q4_0 dequant).  Each block is one
+// k32 MMA (lane t: low nibbles of bytes 4t..4t+3 = elements 4t..4t+3, high
+// nibbles = elements 16+4t..), then per (weight row, x row) with the digit
+// sums S of the block:  acc += d * sigma / 254 * ((254 Dh + Dl) - 8 (254 Sh + Sl)).
+template <int J>
+__device__ __forceinline__ void block_q40(const uint8_t *r0, const uint8_t *dg, const float *sg, int g, int t, bool has,
+                                          uint64_t *emptyb, int lane, float (&facc)[2][J]) {
+  constexpr int P = Fmt<TCB_Q4_0>::kPitch;
+  uint32_t qw[2][8];
+  float dd[2][8];
+  if (has) {
+#pragma unroll
+    for (int q = 0; q < 2; q++) {
+      const uint8_t *rp = r0 + 8 * q * P;
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        qw[q][k] = ld4(rp + 18 * k + 2 + 4 * t);
+        dd[q][k] = half_exact(*reinterpret_cast<const uint16_t *>(rp + 18 * k));
+      }
+    }
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(emptyb);
+  if (!has) return;
+  float sgs[J];
+#pragma unroll
+  for (int j = 0; j < J; j++) sgs[j] = sg[j] * (1.f / 254.f);
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    const uint32_t a0 = qw[0][k] & 0x0F0F0F0Fu, a1 = qw[1][k] & 0x0F0F0F0Fu;
+    const uint32_t a2 = (qw[0][k] >> 4) & 0x0F0F0F0Fu, a3 = (qw[1][k] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+    for (int j = 0; j < J; j++) {
+      const uint8_t *pj = dg + j * kGroupBytes;
+      const uint2 bf = *reinterpret_cast<const uint2 *>(pj + k * kPanel + g * 32 + 8 * t);
+      const int so = 8 * reinterpret_cast<const int *>(pj + 8 * kPanel)[k * 4 + t];
+      int D[4] = {0, 0, 0, 0};
+      imma_u8(D, a0, a1, a2, a3, bf.x, bf.y);
+#pragma unroll
+      for (int q = 0; q < 2; q++) {
+        const int v = 254 * D[2 * q] + D[2 * q + 1] - so;
+        facc[q][j] = fmaf(dd[q][k] * sgs[j], (float)v, facc[q][j]);
+      }
+    }
+  }
+}
+
 template <int W, int J>
 __global__ void __launch_bounds__(32 * kWarps, 1) k_mvrows(const __grid_constant__ CUtensorMap tmap, const Params a) {
   constexpr int kPitch = Fmt<W>::kPitch, kBB = Fmt<W>::kBB;
@@ -513,6 +573,7 @@ __global__ void __launch_bounds__(32 * kWarps, 1) k_mvrows(const __grid_constant
       const uint8_t *dg = digs + (size_t)lb * J * kGroupBytes;
       const float *sg = sigs + (size_t)lb * 4 * J + t * J;
       if constexpr (W == TCB_Q4_K) block_q4k<J>(r0, dg, sg, g, t, lb < nbr, &empty[buf], lane, facc);
+      else if constexpr (W == TCB_Q4_0) block_q40<J>(r0, dg, sg, g, t, lb < nbr, &empty[buf], lane, facc);
       else block_q6k<J>(r0, dg, sg, g, t, lb < nbr, &empty[buf], lane, facc);
       if (ch == a.nch - 1) {
         // the tile: this warp's partials (rows g + 8q of half hw, x rows
@@ -616,8 +677,8 @@ __global__ void __launch_bounds__(256) k_rows_red(const float *part, int ksplit,
 MvPlan rows_plan(int wtype, int N, int K, const void *w, int sms, int M) {
   using namespace mvr;
   MvPlan pl{};
-  if (wtype != TCB_Q4_K && wtype != TCB_Q6_K) return pl;
-  const bool q6 = wtype == TCB_Q6_K;
+  if (wtype != TCB_Q4_K && wtype != TCB_Q6_K && wtype != TCB_Q4_0) return pl;
+  const bool q6 = wtype == TCB_Q6_K;  // Q4_0 units of 8 blocks stage like Q4_K superblocks
   const int bb = q6 ? mvr::Fmt<TCB_Q6_K>::kBB : mvr::Fmt<TCB_Q4_K>::kBB;
   const int pitch = q6 ? mvr::Fmt<TCB_Q6_K>::kPitch : mvr::Fmt<TCB_Q4_K>::kPitch;
   const int box8 = q6 ? mvr::Fmt<TCB_Q6_K>::kBox8 : mvr::Fmt<TCB_Q4_K>::kBox8;
@@ -713,7 +774,7 @@ cudaError_t rows_launch_j(const MvPlan &pl, mvr::Params &a, cudaStream_t s) {
   cudaLaunchAttribute at[1];
   const int warps = a.nb * 4 * J;
   cudaLaunchConfig_t c1 = pdl_cfg(dim3((warps + 7) / 8), dim3(256), 0, s, at);
-  cudaError_t e = cudaLaunchKernelEx(&c1, k_xdig<J, W == TCB_Q6_K>, a.x, a.xdt, a.ldx, a.M, a.nb, const_cast<uint8_t *>(a.dig),
+  cudaError_t e = cudaLaunchKernelEx(&c1, k_xdig<J, W>, a.x, a.xdt, a.ldx, a.M, a.nb, const_cast<uint8_t *>(a.dig),
                                      const_cast<float *>(a.sig), const_cast<uint8_t *>(a.bad));
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(k_mvrows<W, J>, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem);
@@ -765,13 +826,18 @@ cudaError_t rows_launch(const MvPlan &pl, int N, int K, const void *w, const voi
   a.bad = base + L.bad;
   a.part = reinterpret_cast<float *>(base + L.part);
   a.err = err;
-  const bool q6 = pl.cbc == TCB_Q6_K;
+#define TCB_ROWS_J(JJ)                                                                \
+  case JJ:                                                                            \
+    return pl.cbc == TCB_Q6_K   ? rows_launch_j<TCB_Q6_K, JJ>(pl, a, s)               \
+           : pl.cbc == TCB_Q4_0 ? rows_launch_j<TCB_Q4_0, JJ>(pl, a, s)               \
+                                : rows_launch_j<TCB_Q4_K, JJ>(pl, a, s);
   switch (J) {
-  case 1: return q6 ? rows_launch_j<TCB_Q6_K, 1>(pl, a, s) : rows_launch_j<TCB_Q4_K, 1>(pl, a, s);
-  case 2: return q6 ? rows_launch_j<TCB_Q6_K, 2>(pl, a, s) : rows_launch_j<TCB_Q4_K, 2>(pl, a, s);
-  case 3: return q6 ? rows_launch_j<TCB_Q6_K, 3>(pl, a, s) : rows_launch_j<TCB_Q4_K, 3>(pl, a, s);
-  case 4: return q6 ? rows_launch_j<TCB_Q6_K, 4>(pl, a, s) : rows_launch_j<TCB_Q4_K, 4>(pl, a, s);
+    TCB_ROWS_J(1)
+    TCB_ROWS_J(2)
+    TCB_ROWS_J(3)
+    TCB_ROWS_J(4)
   }
+#undef TCB_ROWS_J
   return cudaErrorInvalidValue;
 }
 

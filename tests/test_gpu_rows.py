@@ -1,4 +1,4 @@
-"""The Q4_K and Q6_K float product of 2..16 activation rows in one weight
+"""The Q4_K, Q6_K and Q4_0 float product of 2..16 activation rows in one weight
 stream (tcb_mv_rows.cu) against the oracle's float path, through the C ABI.
 
 TR's quantGemm with a few rows (tensor/cpu_quant.go:47-160): every row's
@@ -22,7 +22,7 @@ from tcb_b200 import synth
 pytestmark = pytest.mark.gpu
 
 REL_L2 = 1e-3
-FMTS = [T.Q4_K, T.Q6_K]
+FMTS = [T.Q4_K, T.Q6_K, T.Q4_0]
 
 
 @pytest.fixture(scope="module")
@@ -127,7 +127,7 @@ def test_rows_16bit_and_views(ctx, oracle, fmt):
     c = torch.zeros((M, N + 5), dtype=torch.float32, device="cuda")[:, :N]
     ctx.qgemm(fmt, dev(raw), xs, c)
     check(host(c), oracle.qgemm_float(fmt, np.ascontiguousarray(xf[:, 1:]), raw, N), K)
-    rb = K // 256 * (144 if fmt == T.Q4_K else 210)
+    rb = K // 256 * (210 if fmt == T.Q6_K else 144)
     c2 = torch.zeros((M, 20), dtype=torch.float32, device="cuda")
     ctx.qgemm(fmt, dev(raw)[5 * rb:], dev(xf[:, :K]), c2)
     check(host(c2), oracle.qgemm_float(fmt, np.ascontiguousarray(xf[:, :K]), raw[5 * rb:25 * rb], 20), K)
