@@ -35,10 +35,11 @@
 //  * Staging: one CTA per SM; a stage is one TMA box of 32 weight rows x 8
 //    superblocks.  16 compute warps: warp w owns the 16-row half w / 8 of
 //    superblock w % 8 of every stage; it copies its operands to registers
-//    and releases the stage before the math.  Thread 0 also issues the
-//    copies: the first stages before the dependency wait, then each stage
-//    once every warp has released the buffer it reuses.  The activation
-//    digits of the CTA's K range stay resident in shared memory.
+//    and releases the stage before the math.  Thread 0 issues the first
+//    stages before the dependency wait; after that the last warp to release
+//    a buffer (a shared counter per buffer) issues its next stage at once,
+//    so no warp waits on a producer.  The activation digits of the CTA's K
+//    range stay resident in shared memory.
 //  * Split K: when the digits of the whole row do not fit beside the stages
 //    (or more CTAs balance the tiles better), the CTAs are split into ksplit
 //    groups, each owning one K range for its lifetime; their partials go to
@@ -254,9 +255,9 @@ __global__ void __launch_bounds__(256) k_xdig(const void *x, int xdt, long ldx, 
 // Q4_K superblock, the 16 rows g, g + 8 (+ 16h) of this warp: operands to
 // registers, the stage released, then the MMAs and the integer scale math,
 // folded into facc[q][j] (row g + 8q, x row 4j + t).
-template <int J>
+template <int J, class Rel>
 __device__ __forceinline__ void block_q4k(const uint8_t *r0, const uint8_t *dg, const float *sg, int g, int t, bool has,
-                                          uint64_t *emptyb, int lane, float (&facc)[2][J]) {
+                                          const Rel &rel, int lane, float (&facc)[2][J]) {
   constexpr int P = Fmt<TCB_Q4_K>::kPitch;
   uint4 hd[2];
   uint2 qs[2][4];
@@ -270,7 +271,7 @@ __device__ __forceinline__ void block_q4k(const uint8_t *r0, const uint8_t *dg, 
     }
   }
   __syncwarp();
-  if (lane == 0) mbar_arrive(emptyb);
+  if (lane == 0) rel();
   if (!has) return;
   // scales and mins of sub-blocks 0-3 / 4-7, one byte each
   uint32_t sc[2][2], mn[2][2];
@@ -338,9 +339,9 @@ __device__ __forceinline__ void block_q4k(const uint8_t *r0, const uint8_t *dg, 
 // s8 digits; lane t's k-slots are elements 4t..4t+3 of the sub-block), its
 // signed scale applied in integers; the -32 offset is sum_j sc_j S_j, one
 // k16 MMA per digit-sum byte with A = the 16 scales.
-template <int J>
+template <int J, class Rel>
 __device__ __forceinline__ void block_q6k(const uint8_t *r0, const uint8_t *dg, const float *sg, int g, int t, bool has,
-                                          uint64_t *emptyb, int lane, float (&facc)[2][J]) {
+                                          const Rel &rel, int lane, float (&facc)[2][J]) {
   constexpr int P = Fmt<TCB_Q6_K>::kPitch;
   uint32_t ql[2][2][4], qh[2][2][2], scw[2][4];
   float dd[2];
@@ -361,7 +362,7 @@ __device__ __forceinline__ void block_q6k(const uint8_t *r0, const uint8_t *dg, 
     }
   }
   __syncwarp();
-  if (lane == 0) mbar_arrive(emptyb);
+  if (lane == 0) rel();
   if (!has) return;
   int ah[2][J], al[2][J];
 #pragma unroll
@@ -422,9 +423,9 @@ __device__ __forceinline__ void block_q6k(const uint8_t *r0, const uint8_t *dg, 
 // k32 MMA (lane t: low nibbles of bytes 4t..4t+3 = elements 4t..4t+3, high
 // nibbles = elements 16+4t..), then per (weight row, x row) with the digit
 // sums S of the block:  acc += d * sigma / 254 * ((254 Dh + Dl) - 8 (254 Sh + Sl)).
-template <int J>
+template <int J, class Rel>
 __device__ __forceinline__ void block_q40(const uint8_t *r0, const uint8_t *dg, const float *sg, int g, int t, bool has,
-                                          uint64_t *emptyb, int lane, float (&facc)[2][J]) {
+                                          const Rel &rel, int lane, float (&facc)[2][J]) {
   constexpr int P = Fmt<TCB_Q4_0>::kPitch;
   uint32_t qw[2][8];
   float dd[2][8];
@@ -440,7 +441,7 @@ __device__ __forceinline__ void block_q40(const uint8_t *r0, const uint8_t *dg, 
     }
   }
   __syncwarp();
-  if (lane == 0) mbar_arrive(emptyb);
+  if (lane == 0) rel();
   if (!has) return;
   float sgs[J];
 #pragma unroll
@@ -471,7 +472,7 @@ __global__ void __launch_bounds__(32 * kWarps, 1) k_mvrows(const __grid_constant
   constexpr int kStage = kRows * kPitch;
   extern __shared__ __align__(128) uint8_t sm[];
   uint64_t *full = reinterpret_cast<uint64_t *>(sm + kBarOff);  // [S]
-  uint64_t *empty = full + kMaxS;                              // [S]
+  int *relcnt = reinterpret_cast<int *>(full + kMaxS);         // [S] warps' releases of each buffer
   uint64_t *xfull = full + 2 * kMaxS;                          // digits of the K range landed
   uint64_t *tfree = xfull + 1;                                 // [slots] partials summed
   int *cnt = reinterpret_cast<int *>(sm + kCntOff);            // [slots] warps done with the tile
@@ -493,7 +494,7 @@ __global__ void __launch_bounds__(32 * kWarps, 1) k_mvrows(const __grid_constant
   if (producer) {
     for (int s = 0; s < a.S; s++) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kC);
+      relcnt[s] = 0;
     }
     mbar_init(xfull, 1);
     for (int s = 0; s < a.slots; s++) {
@@ -507,7 +508,6 @@ __global__ void __launch_bounds__(32 * kWarps, 1) k_mvrows(const __grid_constant
   // multiple of 8 superblocks for Q6_K), rows of tile gidx + (it / nch) gsz
   auto bx = [&](int it) { return (b0 + (it % a.nch) * kBlk) * kBB / 8; };
   auto by = [&](int it) { return (gidx + (it / a.nch) * gsz) * kRows; };
-  int issued = 0;  // stages issued so far (thread 0)
   if (producer) {
     // the split-K sum is the next kernel when ksplit > 1: its CTAs would
     // wait on this grid from every SM, so it is released at the end
@@ -520,7 +520,6 @@ __global__ void __launch_bounds__(32 * kWarps, 1) k_mvrows(const __grid_constant
       mbar_expect_tx(&full[it], (uint32_t)kStage);
       tma_load_2d(stages + it * kStage, &tmap, bx(it), by(it), &full[it]);
     }
-    issued = first;
     pdl_wait();
     const uint32_t db = (uint32_t)nbr * J * kGroupBytes, sb = (uint32_t)nbr * 16 * J;
     mbar_expect_tx(xfull, db + sb);
@@ -553,18 +552,15 @@ __global__ void __launch_bounds__(32 * kWarps, 1) k_mvrows(const __grid_constant
   for (int ti = 0; ti < my_tiles; ti++) {
     for (int ch = 0; ch < a.nch; ch++, it++) {
       const int buf = it % a.S;
-      if (producer) {
-        // issue every stage whose buffer all warps have released, without
-        // waiting; wait only when the stage this iteration reads is not out
-        while (issued < nstages && issued < it + a.S) {
-          const int nb2 = issued % a.S;
-          const uint32_t ph = (uint32_t)(((issued / a.S) & 1) ^ 1);
-          if (issued > it ? !mbar_test_wait(&empty[nb2], ph) : !spin_bar_ns(&empty[nb2], ph, a.err, 32)) break;
-          mbar_expect_tx(&full[nb2], (uint32_t)kStage);
-          tma_load_2d(stages + nb2 * kStage, &tmap, bx(issued), by(issued), &full[nb2]);
-          issued++;
+      // a warp's release of this stage (lane 0, after the warp's reads of it):
+      // the last of the 16 warps refills the buffer with stage it + S at once
+      const auto rel = [&]() {
+        __threadfence_block();
+        if (atomicAdd(&relcnt[buf], 1) % kC == kC - 1 && it + a.S < nstages) {
+          mbar_expect_tx(&full[buf], (uint32_t)kStage);
+          tma_load_2d(stages + buf * kStage, &tmap, bx(it + a.S), by(it + a.S), &full[buf]);
         }
-      }
+      };
       bool ok = true;
       if (lane == 0) ok = wait_bar(&full[buf], (uint32_t)((it / a.S) & 1), a.err);
       if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) return;
@@ -572,9 +568,9 @@ __global__ void __launch_bounds__(32 * kWarps, 1) k_mvrows(const __grid_constant
       const uint8_t *r0 = stages + buf * kStage + (16 * hw + g) * kPitch + bw * kBB;
       const uint8_t *dg = digs + (size_t)lb * J * kGroupBytes;
       const float *sg = sigs + (size_t)lb * 4 * J + t * J;
-      if constexpr (W == TCB_Q4_K) block_q4k<J>(r0, dg, sg, g, t, lb < nbr, &empty[buf], lane, facc);
-      else if constexpr (W == TCB_Q4_0) block_q40<J>(r0, dg, sg, g, t, lb < nbr, &empty[buf], lane, facc);
-      else block_q6k<J>(r0, dg, sg, g, t, lb < nbr, &empty[buf], lane, facc);
+      if constexpr (W == TCB_Q4_K) block_q4k<J>(r0, dg, sg, g, t, lb < nbr, rel, lane, facc);
+      else if constexpr (W == TCB_Q4_0) block_q40<J>(r0, dg, sg, g, t, lb < nbr, rel, lane, facc);
+      else block_q6k<J>(r0, dg, sg, g, t, lb < nbr, rel, lane, facc);
       if (ch == a.nch - 1) {
         // the tile: this warp's partials (rows g + 8q of half hw, x rows
         // 4j + t) into the slot; the last warp to finish sums them
