@@ -229,6 +229,15 @@ int tcb_llama_tp_init(tcb_llama *m, const unsigned char *id128);
 int tcb_llama_peer_handle(tcb_llama *m, unsigned char *handle64);
 int tcb_llama_peer_init(tcb_llama *m, const unsigned char *handles);
 
+/* Self-test of the peer all-reduce's bounded wait, on one device: runs the
+ * all-reduce kernel once as rank `rank` of `tp` with every rank's exchange
+ * buffer allocated locally, so for tp > 1 the other ranks' flags never
+ * arrive and each wait gives up after `polls` polls, leaving
+ * TCB_ERR_TIMEOUT in the device error word (tcb_device_error); with tp = 1
+ * the rank's own flag completes the wait.  Synchronises the stream; the
+ * context stays usable.  No counterpart in TR. */
+int tcb_peer_ar_selftest(tcb_ctx *ctx, int tp, int rank, int d_model, unsigned polls, void *stream);
+
 /* Greedy decode of several sequences together (TR's generate over a batch
  * of prompts, lib/layers.tr 712-770: one GPT.single_step per generated
  * position for every row of the batch).  The count engines (at most

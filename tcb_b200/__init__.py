@@ -71,6 +71,7 @@ def lib() -> ctypes.CDLL:
     L.tcb_ctx_create.argtypes = [I, ctypes.POINTER(P)]
     L.tcb_ctx_destroy.argtypes = [P]
     L.tcb_device_error.argtypes = [P, ctypes.POINTER(I), I]
+    L.tcb_peer_ar_selftest.argtypes = [P, I, I, I, ctypes.c_uint, P]
     L.tcb_block_shape.argtypes = [I, ctypes.POINTER(I), ctypes.POINTER(I)]
     L.tcb_qgemm.argtypes = [P, I, I, I, I, P, P, I, Lg, P, I, Lg, I, P]
     L.tcb_qgemm_act8.argtypes = [P, I, I, I, I, P, P, I, Lg, P, I, Lg, I, P]
@@ -148,6 +149,13 @@ class Context:
         st = ctypes.c_int(0)
         self._check(lib().tcb_device_error(self._h, ctypes.byref(st), int(clear)), "tcb_device_error")
         return st.value
+
+    def peer_ar_selftest(self, tp: int, rank: int, d_model: int, polls: int, stream=None):
+        """tcb_peer_ar_selftest: one peer all-reduce with every rank's buffer
+        local to this device, each wait limited to `polls` polls (tp > 1:
+        the other ranks never arrive, so the waits give up)."""
+        self._check(lib().tcb_peer_ar_selftest(self._h, tp, rank, d_model, polls, _stream(stream)),
+                    "tcb_peer_ar_selftest")
 
     def _check(self, rc: int, what: str):
         if rc:

@@ -387,8 +387,9 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
   return v;
 }
 
+constexpr unsigned kArPolls = 1u << 22;  // flag polls before a wait gives up (about a second)
 __global__ void __launch_bounds__(kArThreads) k_peer_ar(const __grid_constant__ PeerBufs pb, const float *yp, float *x, int D, int tp,
-                                                       int rank, unsigned *epoch, unsigned *done, int *err) {
+                                                       int rank, unsigned *epoch, unsigned *done, int *err, unsigned polls) {
   mv::pdl_wait();
   mv::pdl_launch_dependents();
   const unsigned e = *reinterpret_cast<volatile unsigned *>(epoch) + 1u;
@@ -406,7 +407,7 @@ __global__ void __launch_bounds__(kArThreads) k_peer_ar(const __grid_constant__ 
   if ((int)threadIdx.x < tp) {
     const unsigned *f = pb.flag[rank] + ((size_t)par * tp + threadIdx.x) * nb + b;
     bool ok = false;
-    for (uint32_t it = 0; it < (1u << 22); it++) {
+    for (uint32_t it = 0; it < polls; it++) {
       if (ld_acquire_sys(f) == e) {
         ok = true;
         break;
@@ -818,7 +819,7 @@ cudaError_t all_reduce_x(tcb_llama *m, cudaStream_t s) {
   if (m->peer)
     return tcb::ll::launch(tcb::ll::k_peer_ar, dim3(tcb::ll::kArBlocks), dim3(tcb::ll::kArThreads), s, m->pb,
                            (const float *)m->yp, m->x, m->cfg.d_model, m->tp, m->tr, m->ar_epoch, m->ar_done,
-                           m->ctx->derr);
+                           m->ctx->derr, tcb::ll::kArPolls);
   const Nccl *nc = nccl();
   if (!nc || !m->comm) return cudaErrorNotReady;
   m->nccl_rc = nc->all_reduce(m->x, m->x, (size_t)m->cfg.d_model, kNcclFloat32, kNcclSum, m->comm, s);
@@ -1710,6 +1711,44 @@ int tcb_llama_peer_init(tcb_llama *m, const unsigned char *handles) {
   }
   m->peer = true;
   return TCB_OK;
+}
+
+int tcb_peer_ar_selftest(tcb_ctx *ctx, int tp, int rank, int d_model, unsigned polls, void *stream) {
+  using namespace tcb::ll;
+  if (!ctx) return TCB_ERR_NULL;
+  if (tp < 1 || tp > kMaxTp || rank < 0 || rank >= tp || d_model <= 0 || d_model % 4 || polls == 0)
+    return TCB_ERR_UNSUPPORTED;
+  auto cuda_fail = [ctx](cudaError_t err) {
+    snprintf(ctx->err, sizeof ctx->err, "%s: %s", cudaGetErrorName(err), cudaGetErrorString(err));
+    return TCB_ERR_CUDA;
+  };
+  cudaError_t e = cudaSetDevice(ctx->dev);
+  if (e != cudaSuccess) return cuda_fail(e);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // every rank's exchange buffer local to this device; nothing but this
+  // call writes them, so the other ranks' flags never arrive
+  const size_t flags = ((size_t)2 * tp * kArBlocks * 4 + 255) & ~(size_t)255;
+  const size_t bytes = flags + (size_t)2 * tp * d_model * 4;
+  char *buf = nullptr;
+  float *vec = nullptr;
+  unsigned *cnt = nullptr;
+  PeerBufs pb{};
+  if ((e = cudaMalloc(&buf, bytes * tp)) == cudaSuccess && (e = cudaMalloc(&vec, (size_t)2 * d_model * 4)) == cudaSuccess &&
+      (e = cudaMalloc(&cnt, 2 * sizeof(unsigned))) == cudaSuccess && (e = cudaMemsetAsync(buf, 0, bytes * tp, s)) == cudaSuccess &&
+      (e = cudaMemsetAsync(vec, 0, (size_t)2 * d_model * 4, s)) == cudaSuccess &&
+      (e = cudaMemsetAsync(cnt, 0, 2 * sizeof(unsigned), s)) == cudaSuccess) {
+    for (int r = 0; r < tp; r++) {
+      pb.flag[r] = reinterpret_cast<unsigned *>(buf + bytes * r);
+      pb.slot[r] = reinterpret_cast<float *>(buf + bytes * r + flags);
+    }
+    e = launch(k_peer_ar, dim3(kArBlocks), dim3(kArThreads), s, pb, (const float *)vec, vec + d_model, d_model, tp, rank,
+               cnt, cnt + 1, ctx->derr, polls);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  }
+  cudaFree(buf);
+  cudaFree(vec);
+  cudaFree(cnt);
+  return e == cudaSuccess ? TCB_OK : cuda_fail(e);
 }
 
 int tcb_llama_buffers(tcb_llama *m, int64_t **tokens, float **logits) {
