@@ -163,6 +163,7 @@ def decode_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
     stream = torch.cuda.Stream()
     eng.start(prompt, stream)
     eng.capture(stream)
+    kernels_per_token = eng.step_kernels()
     eng.start(prompt, stream)
     eng.prefill(stream)  # warm-up of the prompt pass (workspace, kernel attributes)
     eng.start(prompt, stream)
@@ -194,7 +195,7 @@ def decode_bench(ctx, rank: int, world: int, peak_gbs: float) -> dict:
         "roofline": {"bound": "hbm", "achieved": round((bpt + kv) / per_tok_s / 1e9, 2), "peak": peak_gbs,
                      "unit": "GB/s", "frac": round((bpt + kv) / per_tok_s / 1e9 / peak_gbs, 4),
                      "ceiling_tokens_per_s": round(peak_gbs * 1e9 / (bpt + kv), 1)},
-        "gpu_launches_per_token": 1 + 6 * cfg.n_layers + 4, "last_tokens": [int(v) for v in toks[-8:]],
+        "gpu_launches_per_token": kernels_per_token, "last_tokens": [int(v) for v in toks[-8:]],
         "distinct_generated_tokens": len(set(int(v) for v in toks[512:])),
         "timing": "CUDA events around 256 graph replays on the engine's stream",
     }

@@ -210,6 +210,9 @@ int tcb_llama_step(tcb_llama *m, void *stream);
  * after the caller's stream has drained); tcb_llama_step replays it on the
  * caller's stream from then on. */
 int tcb_llama_capture(tcb_llama *m, void *stream);
+/* Kernel launches in one captured step (the kernel nodes of the graph
+ * tcb_llama_capture made); TCB_ERR_UNSUPPORTED before a capture. */
+int tcb_llama_step_kernels(tcb_llama *m, int *kernels);
 /* Device pointers of the token history (int64 [max_ctx]) and the logits of
  * the last step (float [vocab], this rank's vocabulary rows). */
 int tcb_llama_buffers(tcb_llama *m, int64_t **tokens, float **logits);

@@ -706,6 +706,7 @@ struct Mat {
   const void *w = nullptr;
   int type = 0, N = 0, K = 0;
   tcb::MvPlan plan{};
+  tcb::MvPlan swi{};         // gate_up (Q4_K): the launch that writes silu(g) * u itself
   const void *pf = nullptr;  // the next matvec's weights in the step (L2 prefetch while this one runs)
   size_t pf_bytes = 0;
   size_t bytes() const { return (size_t)N * K / tcb::block_elems(type) * tcb::block_bytes(type); }
@@ -864,16 +865,16 @@ cudaError_t issue_step(tcb_llama *m, cudaStream_t s) {
     const int acc = m->peer ? 0 : m->tr == 0;
     if ((e = matvec(m, m->o[l], m->att, dst, acc, s)) != cudaSuccess) break;
     if ((e = all_reduce_x(m, s)) != cudaSuccess) break;
-    if ((e = norm_matvec(m, m->gu[l], m->ffn_norm[l], m->gub, s)) != cudaSuccess) break;
-    if (m->down[l].plan.ok && m->down[l].plan.kind == 2) {
-      // SwiGLU fused into the Q6_K matvec's prologue
-      const Mat &dm = m->down[l];
-      e = tcb::q6k_launch(dm.plan, dm.N, dm.K, dm.w, m->gub, TCB_F32, dst, TCB_F32, acc, m->ctx->derr, s, 1,
-                          dm.pf, dm.pf_bytes, m->sk);
-    } else {
-      if ((e = launch(k_swiglu, dim3((F + 255) / 256), dim3(256), s, m->gub, m->a, F)) != cudaSuccess) break;
-      e = matvec(m, m->down[l], m->a, dst, acc, s);
+    const Mat &gm = m->gu[l];
+    if (gm.swi.ok) {
+      // the FFN RMSNorm in the prologue and SwiGLU in the epilogue of one launch
+      e = tcb::q4k_launch(gm.swi, gm.N, gm.K, gm.w, m->x, TCB_F32, nullptr, TCB_F32, 0, m->ctx->derr, m->sk, s,
+                          m->ffn_norm[l], c.eps, gm.pf, gm.pf_bytes, 1, 0, 0, m->a);
+    } else if ((e = norm_matvec(m, gm, m->ffn_norm[l], m->gub, s)) == cudaSuccess) {
+      e = launch(k_swiglu, dim3((F + 255) / 256), dim3(256), s, m->gub, m->a, F);
     }
+    if (e != cudaSuccess) break;
+    e = matvec(m, m->down[l], m->a, dst, acc, s);
     if (e != cudaSuccess) break;
     e = all_reduce_x(m, s);
   }
@@ -953,6 +954,8 @@ int tcb_llama_create(tcb_ctx *ctx, const tcb_llama_config *cfg, const tcb_llama_
     m->qkv.push_back(make_mat(w->qkv[l], w->qkv_type, (H + 2 * KVH) * hd, D, ctx->sms));
     m->o.push_back(make_mat(w->o[l], w->o_type, D, H * hd, ctx->sms));
     m->gu.push_back(make_mat(w->gate_up[l], w->gate_up_type, 2 * F, D, ctx->sms));
+    if (w->gate_up_type == TCB_Q4_K && F % 16 == 0)
+      m->gu.back().swi = tcb::q4k_plan(2 * F, D, w->gate_up[l], ctx->sms, 1, F);
     m->down.push_back(make_mat(w->down[l], w->down_type, D, F, ctx->sms));
   }
   // each matvec streams the next one's weights into L2 (qkv -> o -> gate_up
@@ -1749,6 +1752,21 @@ int tcb_peer_ar_selftest(tcb_ctx *ctx, int tp, int rank, int d_model, unsigned p
   cudaFree(vec);
   cudaFree(cnt);
   return e == cudaSuccess ? TCB_OK : cuda_fail(e);
+}
+
+int tcb_llama_step_kernels(tcb_llama *m, int *kernels) {
+  if (!m || !kernels) return TCB_ERR_NULL;
+  *kernels = 0;
+  if (!m->graph) return TCB_ERR_UNSUPPORTED;
+  size_t n = 0;
+  cudaError_t e = cudaGraphGetNodes(m->graph, nullptr, &n);
+  std::vector<cudaGraphNode_t> nodes(n);
+  if (e == cudaSuccess && n) e = cudaGraphGetNodes(m->graph, nodes.data(), &n);
+  for (size_t i = 0; i < n && e == cudaSuccess; i++) {
+    cudaGraphNodeType t;
+    if ((e = cudaGraphNodeGetType(nodes[i], &t)) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++*kernels;
+  }
+  return e == cudaSuccess ? TCB_OK : fail(m, e);
 }
 
 int tcb_llama_buffers(tcb_llama *m, int64_t **tokens, float **logits) {

@@ -1002,7 +1002,7 @@ cudaError_t matvec_launch(const MvPlan &pl, int wtype, int act8, int N, int K, c
   if (pl.kind == 3) return rows_launch(pl, N, K, w, x, xdt, ldx, c, cdt, ldc, accumulate, M, err, scratch, s);
   if (pl.kind == 2) {
     if (M != 1) return cudaErrorInvalidValue;
-    return q6k_launch(pl, N, K, w, x, xdt, c, cdt, accumulate, err, s, 0, pf, pf_bytes, scratch);
+    return q6k_launch(pl, N, K, w, x, xdt, c, cdt, accumulate, err, s, pf, pf_bytes, scratch);
   }
   switch (wtype) {
   case TCB_Q4_K: TCB_MV(TCB_Q4_K);

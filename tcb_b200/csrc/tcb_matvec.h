@@ -19,6 +19,7 @@ struct MvPlan {
   int ksplit, cpk;             // K splits and chunks per split (kind 2); 1 when not split
   size_t split_bytes;          // device scratch a launch needs (zeroed once; launches leave it zeroed), 0 if none
   int rows, xstride;           // kind 1: rows of x a launch takes, bytes between their digit regions
+  int pair;                    // kind 1: F when the launch pairs gate and up rows for SwiGLU, else 0
   alignas(64) unsigned char tmap[128];  // TMA descriptor of the weight (CUtensorMap)
 };
 
@@ -44,20 +45,24 @@ MvPlan matvec_plan_rows(int wtype, int act8, int N, int K, const void *w, int sm
 // mr (1, 2, 4, 8): the most rows of x one launch takes; a launch of M <= mr
 // rows (row strides ldx, ldc) streams the weights once for all of them.
 // scratch: plan.split_bytes of the matvec scratch (none for this kernel).
-MvPlan q4k_plan(int N, int K, const void *w, int sms, int mr = 1);
+// pair = F: the weight holds gate rows then up rows, F each (N = 2F, F a
+// multiple of 16), and the launch (M = 1, f32 x, no accumulate) writes
+// swi[i] = silu(g_i) * u_i for i < F instead of c: a tile stages gate rows
+// 16t.. and up rows F + 16t.. side by side (two 16-row boxes).
+MvPlan q4k_plan(int N, int K, const void *w, int sms, int mr = 1, int pair = 0);
 cudaError_t q4k_launch(const MvPlan &pl, int N, int K, const void *w, const void *x, int xdt, void *c, int cdt,
                        int accumulate, int *err, void *scratch, cudaStream_t s, const float *nw = nullptr,
                        float eps = 0.f, const void *pf = nullptr, size_t pf_bytes = 0, int M = 1, long ldx = 0,
-                       long ldc = 0);
+                       long ldc = 0, float *swi = nullptr);
 
-// Q6_K float path (kind 2).  With gated, x holds [G | U] (2K elements) and
-// the input is silu(G) * U (a SwiGLU gate fused into the prologue).
-// Small N with large K is split along K (plan.ksplit > 1): the launch then
-// needs plan.split_bytes of scratch that starts zeroed (and is left zeroed).
+// Q6_K float path (kind 2; taken from kQ6kMinRows rows, the output head).
+// Small N with large K would be split along K (plan.ksplit > 1; the launch
+// then needs plan.split_bytes of scratch that starts zeroed and is left
+// zeroed); at the rows this kernel is routed for the split is never chosen.
 MvPlan q6k_plan(int N, int K, const void *w, int sms);
 cudaError_t q6k_launch(const MvPlan &pl, int N, int K, const void *w, const void *x, int xdt, void *c, int cdt,
-                       int accumulate, int *err, cudaStream_t s, int gated = 0, const void *pf = nullptr,
-                       size_t pf_bytes = 0, void *scratch = nullptr);
+                       int accumulate, int *err, cudaStream_t s, const void *pf = nullptr, size_t pf_bytes = 0,
+                       void *scratch = nullptr);
 
 // Q4_K / Q6_K / Q4_0 float path of 2..16 rows of x in one weight stream (kind 3): the
 // digitising prologue, the product and (when plan.ksplit > 1) the sum of the

@@ -90,6 +90,8 @@ struct Params {
   int M;            // activation rows of this launch (1 .. MR of the kernel)
   long ldx, ldc;    // row strides of x and c, elements
   int xstride;      // bytes between the x regions of consecutive rows
+  float *swi;       // SwiGLU output (M = 1, rows [G | U] of F each), or nullptr
+  int swiF;         // F: tile t stages gate rows 16t.. and up rows F + 16t..
 };
 
 // x region: [nb][kFrag] B fragments ([set s][round pair rp][column n][16
@@ -455,7 +457,14 @@ __global__ void __launch_bounds__(32 * kWarps, MR == 1 ? 2 : 1) k_mvq4k(const __
         if (it == 1 && !spin_bar_ns(xgo, 0u, a.err, 32)) return;
         if (it >= a.S && !spin_bar_ns(&empty[buf], (uint32_t)(((it / a.S) & 1) ^ 1), a.err, 64)) return;
         mbar_expect_tx(&full[buf], (uint32_t)kBoxBytes);
-        tma_load_2d(stages + buf * kBoxBytes, &tmap, bx(it), by(it), &full[buf]);
+        if (a.swiF) {
+          // 16 gate rows and the 16 matching up rows (a 16-row box each)
+          const int t = (int)blockIdx.x + (it / a.nch) * (int)gridDim.x;
+          tma_load_2d(stages + buf * kBoxBytes, &tmap, bx(it), 16 * t, &full[buf]);
+          tma_load_2d(stages + buf * kBoxBytes + 16 * kPitch, &tmap, bx(it), a.swiF + 16 * t, &full[buf]);
+        } else {
+          tma_load_2d(stages + buf * kBoxBytes, &tmap, bx(it), by(it), &full[buf]);
+        }
         if (it == (nstages < a.S ? nstages : a.S) - 1) prefetch_slice_l2(a.pf, a.pf_bytes);
       }
     }
@@ -513,6 +522,14 @@ __global__ void __launch_bounds__(32 * kWarps, MR == 1 ? 2 : 1) k_mvq4k(const __
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&tfree[slot]);
+      if (a.swiF) {
+        // lanes 0-15 hold gate rows 16t + lane, lanes 16-31 the up rows:
+        // a = silu(g) * u, as the separate SwiGLU kernel computes it
+        const float u = __shfl_down_sync(0xFFFFFFFFu, v[0], 16);
+        const int i = 16 * ((int)blockIdx.x + ti * (int)gridDim.x) + lane;
+        if (lane < 16 && i < a.swiF) a.swi[i] = __fmul_rn(__fmul_rn(v[0], __frcp_rn(__fadd_rn(1.0f, expf(-v[0])))), u);
+        continue;
+      }
       if (mine) {
 #pragma unroll
         for (int m = 0; m < MR; m++)
@@ -629,6 +646,23 @@ __global__ void __launch_bounds__(32 * kWarps, MR == 1 ? 2 : 1) k_mvq4k(const __
     }
     const int widx = warp == kEpi ? kC : warp;  // 0..kC
     const long rowBytes = (long)a.nb * 144;
+    if (a.swiF) {
+      for (int ti = 0; ti < my_tiles; ti++) {
+        const int i0 = 16 * ((int)blockIdx.x + ti * (int)gridDim.x);
+        for (int i = i0 + widx; i < i0 + 16 && i < a.swiF; i += kC + 1) {
+          float g = __int_as_float(0x7FC00000), u = g;  // rms(x) with a NaN or Inf: NaN inputs
+          if (!a.nw) {
+            float ag[1] = {0.0f}, au[1] = {0.0f};
+            lane_row_float<TCB_Q4_K, 1>(a.w + (long)i * rowBytes, a.K, lane, XGlobal{a.x, 0, a.xdt}, ag);
+            lane_row_float<TCB_Q4_K, 1>(a.w + (long)(a.swiF + i) * rowBytes, a.K, lane, XGlobal{a.x, 0, a.xdt}, au);
+            g = warp_sum(ag[0]);
+            u = warp_sum(au[0]);
+          }
+          if (lane == 0) a.swi[i] = __fmul_rn(__fmul_rn(g, __frcp_rn(__fadd_rn(1.0f, expf(-g)))), u);
+        }
+      }
+      return;
+    }
     if (a.nw) {
       // rms(x) of an x with a NaN or Inf has a NaN in every row's inputs
       for (int ti = 0; ti < my_tiles; ti++) {
@@ -665,13 +699,14 @@ constexpr int kSmemOne = 227 * 1024;
 // memory (mr = 1 only), else one CTA with more stages.  Every row of x has
 // its own digit region and tile partials; the plan fails (ok = false) when
 // fewer than two stages fit beside them.
-MvPlan q4k_plan(int N, int K, const void *w, int sms, int mr) {
+MvPlan q4k_plan(int N, int K, const void *w, int sms, int mr, int pair) {
   using namespace mvk;
   MvPlan pl{};
   const int nb = K / 256;
   const long rowBytes = (long)nb * 144;
   if (K % 256 || nb == 0 || rowBytes % 16 || reinterpret_cast<uintptr_t>(w) % 16) return pl;
   if (mr != 1 && mr != 2 && mr != 4 && mr != 8) return pl;
+  if (pair && (mr != 1 || pair % 16 || N != 2 * pair)) return pl;
   auto enc = tensor_map_encoder();
   if (!enc) return pl;
   const int xstride = (x_bytes(nb) + 127) & ~127;
@@ -689,7 +724,8 @@ MvPlan q4k_plan(int N, int K, const void *w, int sms, int mr) {
     per_sm = 1;
   }
   if (S < 2) return pl;
-  pl.tiles = (N + kRows - 1) / kRows;
+  pl.tiles = pair ? pair / 16 : (N + kRows - 1) / kRows;
+  pl.pair = pair;
   pl.nch = (nb + kBlk - 1) / kBlk;
   pl.cbc = kBlk;
   pl.ksplit = 1;
@@ -706,7 +742,7 @@ MvPlan q4k_plan(int N, int K, const void *w, int sms, int mr) {
   CUtensorMap tm;
   cuuint64_t gdim[2] = {(cuuint64_t)(rowBytes / 8), (cuuint64_t)N};
   cuuint64_t gstride[1] = {(cuuint64_t)rowBytes};
-  cuuint32_t box[2] = {(cuuint32_t)kBox8, (cuuint32_t)kRows};
+  cuuint32_t box[2] = {(cuuint32_t)kBox8, (cuuint32_t)(pair ? 16 : kRows)};
   cuuint32_t estr[2] = {1, 1};
   if (enc(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void *>(w), gdim, gstride, box, estr,
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -720,10 +756,11 @@ MvPlan q4k_plan(int N, int K, const void *w, int sms, int mr) {
 
 cudaError_t q4k_launch(const MvPlan &pl, int N, int K, const void *w, const void *x, int xdt, void *c, int cdt,
                        int accumulate, int *err, void *scratch, cudaStream_t s, const float *nw, float eps,
-                       const void *pf, size_t pf_bytes, int M, long ldx, long ldc) {
+                       const void *pf, size_t pf_bytes, int M, long ldx, long ldc, float *swi) {
   (void)scratch;  // this kernel keeps no state between launches
   using namespace mvk;
   if (M < 1 || M > pl.rows || (M > 1 && nw)) return cudaErrorInvalidValue;
+  if ((pl.pair != 0) != (swi != nullptr) || (swi && (accumulate || xdt != TCB_F32))) return cudaErrorInvalidValue;
   Params a{};
   a.w = static_cast<const uint8_t *>(w);
   a.N = N;
@@ -747,6 +784,8 @@ cudaError_t q4k_launch(const MvPlan &pl, int N, int K, const void *w, const void
   a.ldx = ldx;
   a.ldc = ldc;
   a.xstride = pl.xstride;
+  a.swi = swi;
+  a.swiF = pl.pair;
   CUtensorMap tm;
   memcpy(&tm, pl.tmap, sizeof tm);
   void (*kern)(const CUtensorMap, const Params) = pl.rows == 8   ? k_mvq4k<8>

@@ -1,7 +1,6 @@
-// tcb_mv_q6k.cu - batch-1 Q6_K matvec, float path (x in f32/bf16/f16),
-// optionally with a SwiGLU-gated input (x_eff = silu(x[:K]) * x[K:2K]):
+// tcb_mv_q6k.cu - batch-1 Q6_K matvec, float path (x in f32/bf16/f16):
 //
-//   y[n] (+)= sum_k x_eff[k] * dequant(W)[n, k]     W: [N, K] Q6_K blocks
+//   y[n] (+)= sum_k x[k] * dequant(W)[n, k]     W: [N, K] Q6_K blocks
 //
 // Same structure as the Q4_K kernel (tcb_mv_q4k.cu): small CTAs (two per
 // SM, programmatic dependent launch), a producer warp streaming 2-D TMA
@@ -60,7 +59,6 @@ struct Params {
   int N, K, nb;
   const void *x;
   int xdt;
-  int gated;  // x holds [G | U] (2K elements): the input is silu(G) * U
   void *c;
   int cdt;
   int accumulate;
@@ -135,15 +133,6 @@ __device__ bool prep_warp(const Params &a, uint8_t *xr, int own, int lane, int b
       const int lb = base + kC * j, bg = b0 + lb;
       if (lb < nbl) {
         load8(a.x, bg * 256 + 8 * lane, a.xdt, vec, xv[j]);
-        if (a.gated) {
-          float u[8];
-          load8(a.x, a.K + bg * 256 + 8 * lane, a.xdt, vec, u);
-#pragma unroll
-          for (int i = 0; i < 8; i++) {
-            const float gg = xv[j][i];
-            xv[j][i] = __fmul_rn(__fmul_rn(gg, __frcp_rn(__fadd_rn(1.0f, expf(-gg)))), u[i]);
-          }
-        }
       }
     }
     if (!told) {
@@ -500,10 +489,6 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq6k(const __grid_constant_
     for (int r = 0; r < 2; r++) {
       const int n = tile * kRows + warp + 8 * r;
       if (n >= a.N || kn == 0) continue;
-      if (a.gated) {
-        v[r] = __int_as_float(0x7FC00000);  // a NaN/Inf gate or up value
-        continue;
-      }
       float accs[1] = {0.0f};
       lane_row_float<TCB_Q6_K, 1>(a.w + (long)n * rowBytes + (long)b0 * 210, kn, lane,
                                   XGlobal{static_cast<const char *>(a.x) + (size_t)k0 * xel, 0, a.xdt}, accs);
@@ -596,7 +581,7 @@ MvPlan q6k_plan(int N, int K, const void *w, int sms) {
 }
 
 cudaError_t q6k_launch(const MvPlan &pl, int N, int K, const void *w, const void *x, int xdt, void *c, int cdt,
-                       int accumulate, int *err, cudaStream_t s, int gated, const void *pf, size_t pf_bytes,
+                       int accumulate, int *err, cudaStream_t s, const void *pf, size_t pf_bytes,
                        void *scratch) {
   if (pl.ksplit > 1 && !scratch) return cudaErrorInvalidValue;
   using namespace mv6;
@@ -607,7 +592,6 @@ cudaError_t q6k_launch(const MvPlan &pl, int N, int K, const void *w, const void
   a.nb = K / 256;
   a.x = x;
   a.xdt = xdt;
-  a.gated = gated;
   a.c = c;
   a.cdt = cdt;
   a.accumulate = accumulate;

@@ -278,6 +278,7 @@ def _bind():
     L.tcb_llama_prefill.argtypes = [P, P]
     L.tcb_llama_prefill_batch.argtypes = [P, ctypes.c_int, P]
     L.tcb_llama_capture.argtypes = [P, P]
+    L.tcb_llama_step_kernels.argtypes = [P, ctypes.POINTER(ctypes.c_int)]
     L.tcb_llama_buffers.argtypes = [P, ctypes.POINTER(P), ctypes.POINTER(P)]
     L.tcb_nccl_unique_id.argtypes = [P]
     L.tcb_llama_tp_init.argtypes = [P, P]
@@ -342,6 +343,12 @@ class Llama:
 
     def capture(self, stream=None):
         self._check(self._L.tcb_llama_capture(self._h, _stream(stream)), "capture")
+
+    def step_kernels(self) -> int:
+        """Kernel launches in one captured step (after capture)."""
+        n = ctypes.c_int(0)
+        self._check(self._L.tcb_llama_step_kernels(self._h, ctypes.byref(n)), "step_kernels")
+        return n.value
 
     def _buffers(self):
         t, lg = ctypes.c_void_p(), ctypes.c_void_p()

@@ -100,6 +100,9 @@ def test_graph_replays_eager(setup):
     assert list(eager) == list(ref_toks)
     m.start(PROMPT)
     m.capture()
+    # embedding; per layer qkv (RMSNorm fused), attention, o, gate_up (RMSNorm
+    # and SwiGLU fused), down; final RMSNorm, head, the two-level greedy pick
+    assert m.step_kernels() == 1 + 5 * CFG.n_layers + 4
     m.start(PROMPT)
     m.step(n - 1)
     assert list(m.tokens(n)) == list(eager)
