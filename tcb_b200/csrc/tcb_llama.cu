@@ -103,6 +103,13 @@ struct BatchSeq {
   __half *kc, *vc;
   const int64_t *tok;
 };
+// where a batch's greedy pick writes each sequence's next token
+struct BatchPick {
+  int *pos;
+  int64_t *tok, *hist;
+  const int64_t *prompt;
+  const int *nprompt;
+};
 
 // The current tokens of a batch's sequences, gathered into one array.
 __global__ void k_gather_tok(const BatchSeq *bs, int B, int64_t *tok) {
@@ -510,9 +517,13 @@ __global__ void k_prefill_done(const int64_t *prompt, int n, int *pos, int64_t *
 }
 
 // (max, first index) per CTA
+// blockIdx.y: the row of v (n apart) in a batch, partials gridDim.x apart
 __global__ void k_argmax_part(const float *v, int n, float *pm, int *pi) {
   __shared__ float sm_v[32];
   __shared__ int sm_i[32];
+  v += (size_t)blockIdx.y * n;
+  pm += (size_t)blockIdx.y * gridDim.x;
+  pi += (size_t)blockIdx.y * gridDim.x;
   mv::pdl_wait();
   float best = -INFINITY;
   int bi = 0x7FFFFFFF;
@@ -551,9 +562,15 @@ __global__ void k_argmax_part(const float *v, int n, float *pm, int *pi) {
 
 // The next token: the prompt's next id while the prompt lasts, else the
 // first maximum of the logits; recorded at tokens[pos + 1]; pos advances.
-// One warp.
+// One warp; with bp, warp (CTA) b picks sequence b of a batch.
 __global__ void k_next_token(const float *pm, const int *pi, int nb, int *pos, int64_t *tok, int64_t *hist,
-                             const int64_t *prompt, const int *nprompt, int max_ctx) {
+                             const int64_t *prompt, const int *nprompt, int max_ctx, const BatchPick *bp) {
+  if (bp) {
+    const BatchPick q = bp[blockIdx.x];
+    pm += (size_t)blockIdx.x * nb;
+    pi += (size_t)blockIdx.x * nb;
+    pos = q.pos, tok = q.tok, hist = q.hist, prompt = q.prompt, nprompt = q.nprompt;
+  }
   mv::pdl_wait();
   const int lane = threadIdx.x;
   float best = -INFINITY;
@@ -587,7 +604,11 @@ __global__ void k_next_token(const float *pm, const int *pi, int nb, int *pos, i
 
 // Tensor parallelism: this rank's greedy candidate (first maximum of its
 // vocabulary rows, as a global index), for the all-gather.
+// CTA b: candidate b of a batch (partials nb apart)
 __global__ void k_local_best(const float *pm, const int *pi, int nb, int off, int2 *cand) {
+  pm += (size_t)blockIdx.x * nb;
+  pi += (size_t)blockIdx.x * nb;
+  cand += blockIdx.x;
   mv::pdl_wait();
   const int lane = threadIdx.x;
   float best = -INFINITY;
@@ -616,7 +637,12 @@ __global__ void k_local_best(const float *pm, const int *pi, int nb, int off, in
 // the next token from the ranks' candidates (rank order = vocabulary order,
 // so ties still go to the lowest index)
 __global__ void k_pick_tp(const int2 *cand, int n, int stride, int *pos, int64_t *tok, int64_t *hist,
-                          const int64_t *prompt, const int *nprompt, int max_ctx) {
+                          const int64_t *prompt, const int *nprompt, int max_ctx, const BatchPick *bp) {
+  if (bp) {
+    const BatchPick q = bp[blockIdx.x];
+    cand += blockIdx.x;
+    pos = q.pos, tok = q.tok, hist = q.hist, prompt = q.prompt, nprompt = q.nprompt;
+  }
   mv::pdl_wait();
   if (threadIdx.x != 0) return;
   float best = -INFINITY;
@@ -885,7 +911,7 @@ cudaError_t issue_step(tcb_llama *m, cudaStream_t s) {
     return e;
   if (m->tp == 1)
     return launch(k_next_token, dim3(1), dim3(32), s, m->am_v, m->am_i, kArgBlocks, m->pos, m->tok, m->hist,
-                  m->prompt, m->nprompt, c.max_ctx);
+                  m->prompt, m->nprompt, c.max_ctx, (const BatchPick *)nullptr);
   if ((e = launch(k_local_best, dim3(1), dim3(32), s, m->am_v, m->am_i, kArgBlocks, m->vocab_off, m->cand + m->tr)) !=
       cudaSuccess)
     return e;
@@ -893,7 +919,7 @@ cudaError_t issue_step(tcb_llama *m, cudaStream_t s) {
   if (!nc || !m->comm) return cudaErrorNotReady;
   if ((m->nccl_rc = nc->all_gather(m->cand + m->tr, m->cand, 2, kNcclInt32, m->comm, s)) != 0) return cudaErrorUnknown;
   return launch(k_pick_tp, dim3(1), dim3(32), s, m->cand, m->tp, 1, m->pos, m->tok, m->hist, m->prompt, m->nprompt,
-                c.max_ctx);
+                c.max_ctx, (const BatchPick *)nullptr);
 }
 
 }  // namespace
@@ -1317,6 +1343,7 @@ struct tcb_llama_batch {
   unsigned *count = nullptr;
   int64_t *tok = nullptr;
   tcb::ll::BatchSeq *seq = nullptr;
+  tcb::ll::BatchPick *pick = nullptr;
   int2 *cand = nullptr;
   std::vector<void *> allocs;
   cudaGraph_t graph = nullptr;
@@ -1474,36 +1501,29 @@ int issue_batch_step(tcb_llama_batch *bt, cudaStream_t s) {
   if (rc != TCB_OK) return rc;
   k_rmsnorm<<<B, 1024, 0, s>>>(bt->x, m0->final_norm, bt->h, D, c.eps);
   if ((rc = rows_product(bt, m0->head, bt->head, bt->h, bt->logits, 0, s)) != TCB_OK) return rc;
-  for (int b = 0; b < B; b++)
-    if ((e = launch(k_argmax_part, dim3(kArgBlocks), dim3(256), s, (const float *)(bt->logits + (size_t)b * V), V,
-                    bt->am_v + (size_t)b * kArgBlocks, bt->am_i + (size_t)b * kArgBlocks)) != cudaSuccess)
-      return fail(m0, e);
+  // every sequence's pick in one launch per stage (blockIdx: the sequence)
+  if ((e = launch(k_argmax_part, dim3(kArgBlocks, B), dim3(256), s, (const float *)bt->logits, V, bt->am_v,
+                  bt->am_i)) != cudaSuccess)
+    return fail(m0, e);
   if (m0->tp == 1) {
-    for (int b = 0; b < B; b++) {
-      tcb_llama *m = bt->ms[b];
-      if ((e = launch(k_next_token, dim3(1), dim3(32), s, (const float *)(bt->am_v + (size_t)b * kArgBlocks),
-                      (const int *)(bt->am_i + (size_t)b * kArgBlocks), kArgBlocks, m->pos, m->tok, m->hist,
-                      (const int64_t *)m->prompt, (const int *)m->nprompt, c.max_ctx)) != cudaSuccess)
-        return fail(m0, e);
-    }
+    if ((e = launch(k_next_token, dim3(B), dim3(32), s, (const float *)bt->am_v, (const int *)bt->am_i, kArgBlocks,
+                    (int *)nullptr, (int64_t *)nullptr, (int64_t *)nullptr, (const int64_t *)nullptr,
+                    (const int *)nullptr, c.max_ctx, (const BatchPick *)bt->pick)) != cudaSuccess)
+      return fail(m0, e);
     return TCB_OK;
   }
   // tensor parallelism: each rank's candidate per sequence ([rank][B]), one
   // all-gather, then each sequence's pick over the ranks
-  for (int b = 0; b < B; b++)
-    if ((e = launch(k_local_best, dim3(1), dim3(32), s, (const float *)(bt->am_v + (size_t)b * kArgBlocks),
-                    (const int *)(bt->am_i + (size_t)b * kArgBlocks), kArgBlocks, m0->vocab_off,
-                    bt->cand + (size_t)m0->tr * B + b)) != cudaSuccess)
-      return fail(m0, e);
+  if ((e = launch(k_local_best, dim3(B), dim3(32), s, (const float *)bt->am_v, (const int *)bt->am_i, kArgBlocks,
+                  m0->vocab_off, bt->cand + (size_t)m0->tr * B)) != cudaSuccess)
+    return fail(m0, e);
   if ((m0->nccl_rc = nccl()->all_gather(bt->cand + (size_t)m0->tr * B, bt->cand, 2 * (size_t)B, kNcclInt32, m0->comm,
                                         s)) != 0)
     return fail(m0, cudaErrorUnknown);
-  for (int b = 0; b < B; b++) {
-    tcb_llama *m = bt->ms[b];
-    if ((e = launch(k_pick_tp, dim3(1), dim3(32), s, (const int2 *)(bt->cand + b), m0->tp, B, m->pos, m->tok,
-                    m->hist, (const int64_t *)m->prompt, (const int *)m->nprompt, c.max_ctx)) != cudaSuccess)
-      return fail(m0, e);
-  }
+  if ((e = launch(k_pick_tp, dim3(B), dim3(32), s, (const int2 *)bt->cand, m0->tp, B, (int *)nullptr,
+                  (int64_t *)nullptr, (int64_t *)nullptr, (const int64_t *)nullptr, (const int *)nullptr, c.max_ctx,
+                  (const BatchPick *)bt->pick)) != cudaSuccess)
+    return fail(m0, e);
   return TCB_OK;
 }
 
@@ -1544,6 +1564,9 @@ int tcb_llama_batch_create(tcb_llama *const *ms, int count, tcb_llama_batch **ou
   const size_t qkvn = (size_t)(H + 2 * KVH) * hd;
   std::vector<tcb::ll::BatchSeq> hs(B);
   for (int i = 0; i < B; i++) hs[i] = tcb::ll::BatchSeq{ms[i]->pos, ms[i]->kc, ms[i]->vc, ms[i]->tok};
+  std::vector<tcb::ll::BatchPick> hp(B);
+  for (int i = 0; i < B; i++)
+    hp[i] = tcb::ll::BatchPick{ms[i]->pos, ms[i]->tok, ms[i]->hist, ms[i]->prompt, ms[i]->nprompt};
   if ((e = balloc(bt, &bt->x, (size_t)B * D)) != cudaSuccess || (e = balloc(bt, &bt->h, (size_t)B * D)) != cudaSuccess ||
       (e = balloc(bt, &bt->qkv, (size_t)B * qkvn)) != cudaSuccess ||
       (e = balloc(bt, &bt->att, (size_t)B * H * hd)) != cudaSuccess ||
@@ -1553,10 +1576,11 @@ int tcb_llama_batch_create(tcb_llama *const *ms, int count, tcb_llama_batch **ou
       (e = balloc(bt, &bt->am_v, (size_t)B * tcb::ll::kArgBlocks)) != cudaSuccess ||
       (e = balloc(bt, &bt->am_i, (size_t)B * tcb::ll::kArgBlocks)) != cudaSuccess ||
       (e = balloc(bt, &bt->count, (size_t)B * KVH)) != cudaSuccess || (e = balloc(bt, &bt->tok, (size_t)B)) != cudaSuccess ||
-      (e = balloc(bt, &bt->seq, (size_t)B)) != cudaSuccess ||
+      (e = balloc(bt, &bt->seq, (size_t)B)) != cudaSuccess || (e = balloc(bt, &bt->pick, (size_t)B)) != cudaSuccess ||
       (e = balloc(bt, &bt->cand, (size_t)B * m0->tp)) != cudaSuccess ||
       (e = cudaMemset(bt->count, 0, (size_t)B * KVH * sizeof(unsigned))) != cudaSuccess ||
-      (e = cudaMemcpy(bt->seq, hs.data(), B * sizeof(tcb::ll::BatchSeq), cudaMemcpyHostToDevice)) != cudaSuccess) {
+      (e = cudaMemcpy(bt->seq, hs.data(), B * sizeof(tcb::ll::BatchSeq), cudaMemcpyHostToDevice)) != cudaSuccess ||
+      (e = cudaMemcpy(bt->pick, hp.data(), B * sizeof(tcb::ll::BatchPick), cudaMemcpyHostToDevice)) != cudaSuccess) {
     tcb_llama_batch_destroy(bt);
     return e == cudaErrorMemoryAllocation ? TCB_ERR_NOMEM : fail(m0, e);
   }

@@ -55,10 +55,8 @@ cudaError_t q4k_launch(const MvPlan &pl, int N, int K, const void *w, const void
                        float eps = 0.f, const void *pf = nullptr, size_t pf_bytes = 0, int M = 1, long ldx = 0,
                        long ldc = 0, float *swi = nullptr);
 
-// Q6_K float path (kind 2; taken from kQ6kMinRows rows, the output head).
-// Small N with large K would be split along K (plan.ksplit > 1; the launch
-// then needs plan.split_bytes of scratch that starts zeroed and is left
-// zeroed); at the rows this kernel is routed for the split is never chosen.
+// Q6_K float path (kind 2; taken from kQ6kMinRows rows, the output head;
+// the plan refuses products of fewer tiles than half the SMs).
 MvPlan q6k_plan(int N, int K, const void *w, int sms);
 cudaError_t q6k_launch(const MvPlan &pl, int N, int K, const void *w, const void *x, int xdt, void *c, int cdt,
                        int accumulate, int *err, cudaStream_t s, const void *pf = nullptr, size_t pf_bytes = 0,

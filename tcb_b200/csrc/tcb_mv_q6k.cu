@@ -63,13 +63,10 @@ struct Params {
   int cdt;
   int accumulate;
   int tiles, nch, S;
-  int ksplit, cpk;   // K splits (CTA b takes split b % ksplit), chunks per split
   int *err;
   int soff;
   const void *pf;    // weights of the next kernel of a chain, prefetched into L2 (or nullptr)
   size_t pf_bytes;
-  float *spart;      // [tiles][ksplit][16] split partials (ksplit > 1)
-  unsigned *scnt;    // [tiles] splits finished (zero between launches)
 };
 
 // x region: [nb][kFrag] B fragments (as the Q4_K kernel), [nb][kScl] lane
@@ -116,7 +113,7 @@ __device__ __forceinline__ void load8(const void *x, int e, int xdt, bool vec, f
 // taking elements 8L..8L+7 of a block (as the Q4_K kernel), plus the digit
 // sums of every 16-element sub-block.  Returns false if a sub-block sum of
 // x is not finite.
-// Blocks [b0, b0 + nbl) of x (this CTA's K split), stored at local block
+// Blocks [b0, b0 + nbl) of x (every block: b0 = 0), stored at local block
 // index bg - b0.
 __device__ bool prep_warp(const Params &a, uint8_t *xr, int own, int lane, int b0, int nbl, int nbl_cap,
                           uint64_t *xgo) {
@@ -337,11 +334,11 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq6k(const __grid_constant_
   uint8_t *xr = sm + kXOff;
   uint8_t *stages = sm + a.soff;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  // K split s of tiles t0, t0 + cps, ...; chunks [ch0, ch1)
-  const int split = (int)blockIdx.x % a.ksplit, t0 = (int)blockIdx.x / a.ksplit, cps = (int)gridDim.x / a.ksplit;
+  // tiles t0, t0 + cps, ...; every chunk of K
+  const int t0 = (int)blockIdx.x, cps = (int)gridDim.x;
   const int my_tiles = t0 < a.tiles ? (a.tiles - t0 + cps - 1) / cps : 0;
-  const int ch0 = split * a.cpk, ch1 = min(a.nch, ch0 + a.cpk), nchl = max(0, ch1 - ch0);
-  const int b0 = ch0 * kBlk, nbl = max(0, min(a.nb, ch1 * kBlk) - b0), nbl_cap = a.cpk * kBlk;
+  const int ch0 = 0, ch1 = a.nch, nchl = a.nch;
+  const int b0 = 0, nbl = a.nb, nbl_cap = a.nch * kBlk;
   const int nstages = my_tiles * nchl;
   auto tile_of = [&](int ti) { return t0 + ti * cps; };
 
@@ -388,8 +385,7 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq6k(const __grid_constant_
   const bool slow = *flag != 0;
 
   if (warp == kEpi) {
-    // the 8 partials of each row in block order; with K splits, the last
-    // split of a tile to finish adds the splits' partials in split order
+    // the 8 partials of each row in block order
     const int rot = (int)blockIdx.x & (kBlk - 1);
     for (int ti = 0; ti < my_tiles; ti++) {
       const int tile = tile_of(ti);
@@ -405,20 +401,6 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq6k(const __grid_constant_
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&tfree[slot]);
-      if (a.ksplit > 1) {
-        float *sp = a.spart + (size_t)tile * a.ksplit * kRows;
-        if (lane < kRows) sp[split * kRows + lane] = v;
-        __threadfence();
-        __syncwarp();
-        unsigned old = 0;
-        if (lane == 0) old = atomicAdd(&a.scnt[tile], 1u);
-        if (__shfl_sync(0xFFFFFFFFu, old, 0) != (unsigned)(a.ksplit - 1)) continue;
-        __threadfence();
-        v = 0.f;
-        if (lane < kRows)
-          for (int q = 0; q < a.ksplit; q++) v += __ldcg(sp + q * kRows + lane);
-        if (lane == 0) a.scnt[tile] = 0u;
-      }
       if (mine) store_out(a.c, row, a.cdt, v, a.accumulate != 0);
     }
     return;
@@ -428,7 +410,7 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq6k(const __grid_constant_
   const Lane Q = make_lane(xr, nbl_cap, lane);
   const int own = (warp + (int)blockIdx.x) & (kBlk - 1);
   const int gl = own < a.nb ? (a.nb - 1 - own) / kBlk : -1;  // the warp's last chunk of a row
-  const int last_ch = gl >= ch0 ? min(gl, ch1 - 1) : -1;     // ... within this split
+  const int last_ch = gl >= ch0 ? min(gl, ch1 - 1) : -1;     // ... within the stages
   const int hand_ch = last_ch >= 0 ? last_ch : ch1 - 1;      // where its tile partial is handed over
   if (!slow) {
     // warp w owns block (w + blockIdx) mod 8 of every stage.  All the bytes
@@ -468,8 +450,8 @@ __global__ void __launch_bounds__(32 * kWarps, 2) k_mvq6k(const __grid_constant_
     }
     return;
   }
-  // NaN/Inf in this split's x: release the stages, then TR's float path over
-  // the split's K range for rows w and w + 8 of each tile (the other rows of
+  // NaN/Inf in x: release the stages, then TR's float path over
+  // the K range for rows w and w + 8 of each tile (the other rows of
   // the warp's partial column are zero), through the same hand-over
   for (int it = 0; it < nstages; it++) {
     const int buf = it % a.S;
@@ -522,18 +504,10 @@ MvPlan q6k_plan(int N, int K, const void *w, int sms) {
   auto enc = tensor_map_encoder();
   if (!enc) return pl;
   const int tiles = (N + kRows - 1) / kRows, nch = (nb + kBlk - 1) / kBlk;
-  // K splits only when the rows give fewer tiles than half the SMs (small
-  // N): then enough CTAs to cover the SMs, each digitising and reading only
-  // its share of x.  (For more tiles a split costs more in per-tile
-  // hand-overs than it saves.)
-  int ksplit = 1;
-  if (2 * tiles < sms) {
-    ksplit = (sms + tiles - 1) / tiles;
-    if (ksplit > nch) ksplit = nch;
-  }
-  const int cpk = (nch + ksplit - 1) / ksplit;
-  ksplit = (nch + cpk - 1) / cpk;  // no empty split
-  const int base = (kXOff + x_bytes(cpk * kBlk) + 127) & ~127;
+  // wide products only (the output head): fewer tiles than half the SMs
+  // would leave SMs idle, and those products go to the generic kernel
+  if (2 * tiles < sms) return pl;
+  const int base = (kXOff + x_bytes(nch * kBlk) + 127) & ~127;
   int S, per_sm;
   if (base + 2 * kBoxBytes <= kSmemTwo6) {
     S = (kSmemTwo6 - base) / kBoxBytes;
@@ -546,24 +520,19 @@ MvPlan q6k_plan(int N, int K, const void *w, int sms) {
   }
   if (S < 2) return pl;
   const int slots = per_sm * sms;
-  int cps = slots / ksplit;  // CTAs per split
-  if (cps > tiles) cps = tiles;
-  if (cps < 1) cps = 1;
+  const int cps = slots < tiles ? slots : tiles;
   pl.tiles = tiles;
   pl.nch = nch;
   pl.cbc = kBlk;
-  pl.ksplit = ksplit;
-  pl.cpk = cpk;
-  // counters (one per tile: split only when tiles < sms) in the fixed
-  // counter region, then the partials
-  if (ksplit > 1 && (size_t)tiles * 4 > kScratchCntBytes) return pl;
-  pl.split_bytes = ksplit > 1 ? kScratchCntBytes + (size_t)tiles * ksplit * kRows * 4 : 0;
+  pl.ksplit = 1;
+  pl.cpk = nch;
+  pl.split_bytes = 0;
   pl.stages = S;
   pl.pitch = kPitch;
   pl.xoff = kXOff;
   pl.soff = base;
   pl.smem = base + S * kBoxBytes;
-  pl.grid = cps * ksplit;
+  pl.grid = cps;
   pl.kind = 2;
   CUtensorMap tm;
   cuuint64_t gdim[2] = {(cuuint64_t)(rowBytes / 8), (cuuint64_t)N};
@@ -583,7 +552,7 @@ MvPlan q6k_plan(int N, int K, const void *w, int sms) {
 cudaError_t q6k_launch(const MvPlan &pl, int N, int K, const void *w, const void *x, int xdt, void *c, int cdt,
                        int accumulate, int *err, cudaStream_t s, const void *pf, size_t pf_bytes,
                        void *scratch) {
-  if (pl.ksplit > 1 && !scratch) return cudaErrorInvalidValue;
+  (void)scratch;  // this kernel keeps no state between launches
   using namespace mv6;
   Params a{};
   a.w = static_cast<const uint8_t *>(w);
@@ -602,13 +571,6 @@ cudaError_t q6k_launch(const MvPlan &pl, int N, int K, const void *w, const void
   a.soff = pl.soff;
   a.pf = pf;
   a.pf_bytes = pf_bytes;
-  a.ksplit = pl.ksplit;
-  a.cpk = pl.cpk;
-  if (pl.ksplit > 1) {
-    // [tiles] counters in the counter region, then [tiles][ksplit][16] partials
-    a.scnt = static_cast<unsigned *>(scratch);
-    a.spart = reinterpret_cast<float *>(static_cast<char *>(scratch) + kScratchCntBytes);
-  }
   CUtensorMap tm;
   memcpy(&tm, pl.tmap, sizeof tm);
   cudaError_t e = cudaFuncSetAttribute(k_mvq6k, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem);
