@@ -467,7 +467,7 @@ def decode_tp_bench(ctx, rank: int, world: int, peak_gbs: float, batch16: bool =
     return out
 
 
-def decode_batch_bench(ctx, model, rank: int, world: int, peak_gbs: float, stream, B: int = 16) -> dict:
+def decode_batch_bench(ctx, model, rank: int, world: int, peak_gbs: float, stream, B: int = 16, cfg=None) -> dict:
     """BASELINE config 5 at batch 16: 16 sequences on the same 70B-shape
     weights, each with its own 1024-token random prompt and K/V cache, fed by
     one batched prompt pass (tcb_llama_prefill_batch), then 128 greedy steps
@@ -479,7 +479,7 @@ def decode_batch_bench(ctx, model, rank: int, world: int, peak_gbs: float, strea
 
     from tcb_b200 import llama
 
-    cfg = llama.LLAMA3_70B
+    cfg = cfg or llama.LLAMA3_70B
     engines = [llama.Llama(ctx, model, tp=(world, rank)) for _ in range(B)]
     if world > 1:
         engines[0].tp_init(llama.share_id(llama.nccl_unique_id, rank), peer=False)
@@ -574,6 +574,33 @@ def emit(obj: dict):
     out.flush()
 
 
+def product_bench(ctx, wname: str, n: str, k: str, m: str, act8: bool = False) -> dict:
+    """One product (synthetic weights and activations), 4 warm-up and 10 timed
+    calls on the default stream: the profiling case of a kernel."""
+    import torch
+
+    import tcb_b200 as T
+    from tcb_b200 import synth
+
+    wt = {"q4_k": T.Q4_K, "q6_k": T.Q6_K, "q4_0": T.Q4_0, "q8_0": T.Q8_0}[wname]
+    N, K, M = int(n), int(k), int(m)
+    w = torch.from_numpy(synth.weight(wt, N, K, seed=1)).cuda()
+    x = torch.from_numpy(synth.activations(M, K, seed=2)).cuda()
+    c = torch.zeros((M, N), dtype=torch.float32, device="cuda")
+    for _ in range(4):
+        ctx.qgemm(wt, w, x, c, act8=act8)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(10):
+        ctx.qgemm(wt, w, x, c, act8=act8)
+    e1.record()
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / 10
+    wb = N * K // T.BLOCK[wt][0] * T.BLOCK[wt][1]
+    return {"wtype": wname, "N": N, "K": K, "M": M, "act8": act8, "us_per_call": round(us, 2),
+            "weight_GBs": round(wb / us / 1e3, 1), "device_error": ctx.device_error()}
+
+
 def main():
     claim_stdout()
     ap = argparse.ArgumentParser()
@@ -588,7 +615,14 @@ def main():
     ap.add_argument("--only-model-prefill", action="store_true",
                     help="run only the 8B model prefill and print its object (for profiling)")
     ap.add_argument("--layers", type=int, default=0,
-                    help="with --only-model-prefill: this many layers instead of 32 (small profiling case)")
+                    help="with --only-model-prefill / --only-batch16: this many layers (small profiling case)")
+    ap.add_argument("--only-product", nargs=4, metavar=("WTYPE", "N", "K", "M"),
+                    help="run only one product (q4_k, q6_k, q4_0, q8_0; N x K weight, M rows of x) a few "
+                         "times and print its time (for profiling)")
+    ap.add_argument("--act8", action="store_true", help="with --only-product: the int8-activation product")
+    ap.add_argument("--only-decode", action="store_true", help="run only the 8B decode and print its object")
+    ap.add_argument("--only-batch16", action="store_true",
+                    help="run only the 70B-shape batch-16 decode (with --layers: fewer layers) and print it")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -610,6 +644,23 @@ def main():
     torch.cuda.set_device(dev)
     if args.only_model_prefill:
         emit({"model_prefill": model_prefill_bench(T.Context(local), load_peaks(), args.layers)})
+        return
+    if args.only_product:
+        emit({"product": product_bench(T.Context(local), *args.only_product, act8=args.act8)})
+        return
+    if args.only_decode:
+        emit({"decode": decode_bench(T.Context(local), rank, world, load_peaks()["hbm_gbs"])})
+        return
+    if args.only_batch16:
+        import dataclasses
+
+        from tcb_b200 import llama
+
+        cfg = llama.LLAMA3_70B if not args.layers else dataclasses.replace(llama.LLAMA3_70B, n_layers=args.layers)
+        ctx = T.Context(local)
+        model = llama.device_model(cfg, seed=9, varied=True)
+        emit({"batch16": decode_batch_bench(ctx, model, rank, world, load_peaks()["hbm_gbs"],
+                                            torch.cuda.Stream(dev), cfg=cfg)})
         return
     N, K = WORKLOAD["N"], WORKLOAD["K"]
     config = run_config(world)
