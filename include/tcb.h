@@ -173,6 +173,12 @@ typedef struct tcb_llama_weights {
   const void *const *o;    int o_type;      /* [d, H*hd] */
   const void *const *gate_up; int gate_up_type; /* [2*ffn, d]: gate rows, then up rows */
   const void *const *down; int down_type;   /* [d, ffn] */
+  /* Optional per-layer block types ([n_layers][5]: the q and k rows, the v
+   * rows, o, gate_up, down), overriding the class types above; NULL for
+   * none.  A layer's qkv tensor is then its q and k rows in the first type
+   * followed by its v rows in the second (llama.cpp's Q4_K_M files give some
+   * layers' v and down Q6_K blocks, the others Q4_K). */
+  const int *layer_types;
 } tcb_llama_weights;
 
 int tcb_llama_create(tcb_ctx *ctx, const tcb_llama_config *cfg, const tcb_llama_weights *w, tcb_llama **out);

@@ -41,8 +41,19 @@ def rms(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
     return ((x / np.sqrt(np.float32(ms + np.float32(eps)))) * w).astype(np.float32)
 
 
-def matvec(kind: str, w: np.ndarray, x: np.ndarray, N: int) -> np.ndarray:
-    return O.qgemm_float(TYPES[kind], x.reshape(1, -1).astype(np.float32), w, N)[0]
+def matvec(kind: str, w: np.ndarray, x: np.ndarray, N: int, wt: int | None = None) -> np.ndarray:
+    return O.qgemm_float(TYPES[kind] if wt is None else wt, x.reshape(1, -1).astype(np.float32), w, N)[0]
+
+
+BLOCK = {O.Q8_0: (32, 34), O.Q4_0: (32, 18), Q4_K: (256, 144), Q6_K: (256, 210)}
+
+
+def layer_types(model: dict, l: int) -> tuple:
+    """(qk, v, o, gate_up, down) block types of layer l: model["types"] lists
+    per layer (absent: the class types)."""
+    t = model.get("types") or {}
+    cls = {"qk": "qkv", "v": "qkv", "o": "o", "gate_up": "gate_up", "down": "down"}
+    return tuple(t[k][l] if k in t else TYPES[cls[k]] for k in ("qk", "v", "o", "gate_up", "down"))
 
 
 class Reference:
@@ -61,10 +72,19 @@ class Reference:
         c, m = self.c, self.m
         H, KVH, hd, D, F = c.n_heads, c.n_kv_heads, c.head_dim, c.d_model, c.ffn_dim
         half, G = hd // 2, c.n_heads // c.n_kv_heads
-        x = O.embedding(TYPES["tok_emb"], m["tok_emb"], D, [token])[0].astype(np.float32)
+        ct = m.get("types") or {}
+        x = O.embedding(ct.get("tok_emb", TYPES["tok_emb"]), m["tok_emb"], D, [token])[0].astype(np.float32)
         for l in range(c.n_layers):
+            qk_t, v_t, o_t, gu_t, dn_t = layer_types(m, l)
             h = rms(x, m["attn_norm"][l], c.eps)
-            qkv = matvec("qkv", m["qkv"][l], h, (H + 2 * KVH) * hd).reshape(H + 2 * KVH, hd)
+            if qk_t == v_t:
+                qkv = matvec("qkv", m["qkv"][l], h, (H + 2 * KVH) * hd, qk_t)
+            else:
+                e, b = BLOCK[qk_t]
+                nb = (H + KVH) * hd * (D // e) * b
+                qkv = np.concatenate([matvec("qkv", m["qkv"][l][:nb], h, (H + KVH) * hd, qk_t),
+                                      matvec("qkv", m["qkv"][l][nb:], h, KVH * hd, v_t)])
+            qkv = qkv.reshape(H + 2 * KVH, hd)
             a, b = qkv[:H + KVH, :half], qkv[:H + KVH, half:]
             cs, sn = self.cos[pos], self.sin[pos]
             rot = np.concatenate([a * cs - b * sn, a * sn + b * cs], axis=1).astype(np.float32)
@@ -80,14 +100,14 @@ class Reference:
                 s = (k @ q[hh]) * scale
                 p = np.exp(s - s.max())
                 att[hh] = (p @ v) / p.sum()
-            x = (x + matvec("o", m["o"][l], att.reshape(-1), D)).astype(np.float32)
+            x = (x + matvec("o", m["o"][l], att.reshape(-1), D, o_t)).astype(np.float32)
             h = rms(x, m["ffn_norm"][l], c.eps)
-            gu = matvec("gate_up", m["gate_up"][l], h, 2 * F)
+            gu = matvec("gate_up", m["gate_up"][l], h, 2 * F, gu_t)
             g, u = gu[:F], gu[F:]
             with np.errstate(over="ignore"):  # exp(-g) = inf gives silu = -0, as on the device
                 act = (g / (np.float32(1.0) + np.exp(-g)) * u).astype(np.float32)
-            x = (x + matvec("down", m["down"][l], act, D)).astype(np.float32)
-        return matvec("head", m["head"], rms(x, m["final_norm"], c.eps), c.vocab)
+            x = (x + matvec("down", m["down"][l], act, D, dn_t)).astype(np.float32)
+        return matvec("head", m["head"], rms(x, m["final_norm"], c.eps), c.vocab, ct.get("head"))
 
     def generate(self, prompt, steps: int):
         """Token history (prompt, then greedy), the logits of every step and

@@ -749,6 +749,7 @@ struct tcb_llama {
   std::vector<const float *> attn_norm, ffn_norm;
   Mat head;
   std::vector<Mat> qkv, o, gu, down;
+  std::vector<Mat> qkv_v;  // a layer's v rows when their block type differs from q/k's (N = 0: none)
   // device state
   float *x = nullptr, *h = nullptr, *qkvb = nullptr, *att = nullptr, *gub = nullptr, *a = nullptr, *logits = nullptr;
   float *part = nullptr, *am_v = nullptr, *cosT = nullptr, *sinT = nullptr;
@@ -866,7 +867,15 @@ cudaError_t issue_step(tcb_llama *m, cudaStream_t s) {
   cudaError_t e = tcb::launch_dequant_rows(m->tok_emb_type, m->tok_emb, 1, D, m->tok, m->x, TCB_F32, m->ctx->sms, s);
   for (int l = 0; l < c.n_layers && e == cudaSuccess; l++) {
     __half *kc = m->kc + l * cache_layer, *vc = m->vc + l * cache_layer;
-    if ((e = norm_matvec(m, m->qkv[l], m->attn_norm[l], m->qkvb, s)) != cudaSuccess) break;
+    if (m->qkv_v[l].N) {
+      // q/k and v rows of different block types: the norm once, two products
+      if ((e = launch(k_rmsnorm, dim3(1), dim3(1024), s, m->x, m->attn_norm[l], m->h, D, c.eps)) != cudaSuccess ||
+          (e = matvec(m, m->qkv[l], m->h, m->qkvb, 0, s)) != cudaSuccess ||
+          (e = matvec(m, m->qkv_v[l], m->h, m->qkvb + (size_t)(H + KVH) * hd, 0, s)) != cudaSuccess)
+        break;
+    } else if ((e = norm_matvec(m, m->qkv[l], m->attn_norm[l], m->qkvb, s)) != cudaSuccess) {
+      break;
+    }
     const dim3 ag(KVH, m->nch_max);
     switch (G) {
 #define TCB_ATTN(GG)                                                                                              \
@@ -957,6 +966,19 @@ int tcb_llama_create(tcb_ctx *ctx, const tcb_llama_config *cfg, const tcb_llama_
   if (!kok(w->tok_emb_type, D) || !kok(w->head_type, D) || !kok(w->qkv_type, D) || !kok(w->o_type, H * hd) ||
       !kok(w->gate_up_type, D) || !kok(w->down_type, F))
     return TCB_ERR_SHAPE;
+  // the block types of layer l: q/k rows, v rows, o, gate_up, down
+  auto ltype = [w](int l, int j) {
+    const int cls[5] = {w->qkv_type, w->qkv_type, w->o_type, w->gate_up_type, w->down_type};
+    return w->layer_types ? w->layer_types[5 * l + j] : cls[j];
+  };
+  if (w->layer_types)
+    for (int l = 0; l < c.n_layers; l++) {
+      for (int j = 0; j < 5; j++)
+        if (!wtype_ok(ltype(l, j))) return TCB_ERR_DTYPE;
+      if (!kok(ltype(l, 0), D) || !kok(ltype(l, 1), D) || !kok(ltype(l, 2), H * hd) || !kok(ltype(l, 3), D) ||
+          !kok(ltype(l, 4), F))
+        return TCB_ERR_SHAPE;
+    }
   cudaError_t e = cudaSetDevice(ctx->dev);
   if (e != cudaSuccess) return TCB_ERR_CUDA;
   tcb_llama *m = new tcb_llama();
@@ -977,12 +999,21 @@ int tcb_llama_create(tcb_ctx *ctx, const tcb_llama_config *cfg, const tcb_llama_
     }
     m->attn_norm.push_back(w->attn_norm[l]);
     m->ffn_norm.push_back(w->ffn_norm[l]);
-    m->qkv.push_back(make_mat(w->qkv[l], w->qkv_type, (H + 2 * KVH) * hd, D, ctx->sms));
-    m->o.push_back(make_mat(w->o[l], w->o_type, D, H * hd, ctx->sms));
-    m->gu.push_back(make_mat(w->gate_up[l], w->gate_up_type, 2 * F, D, ctx->sms));
-    if (w->gate_up_type == TCB_Q4_K && F % 16 == 0)
+    const int qk_t = ltype(l, 0), v_t = ltype(l, 1), gu_t = ltype(l, 3);
+    if (qk_t == v_t) {
+      m->qkv.push_back(make_mat(w->qkv[l], qk_t, (H + 2 * KVH) * hd, D, ctx->sms));
+      m->qkv_v.push_back(Mat{});
+    } else {
+      // q and k rows, then the v rows in their own block type
+      m->qkv.push_back(make_mat(w->qkv[l], qk_t, (H + KVH) * hd, D, ctx->sms));
+      const size_t off = (size_t)(H + KVH) * hd * (D / tcb::block_elems(qk_t)) * tcb::block_bytes(qk_t);
+      m->qkv_v.push_back(make_mat(static_cast<const char *>(w->qkv[l]) + off, v_t, KVH * hd, D, ctx->sms));
+    }
+    m->o.push_back(make_mat(w->o[l], ltype(l, 2), D, H * hd, ctx->sms));
+    m->gu.push_back(make_mat(w->gate_up[l], gu_t, 2 * F, D, ctx->sms));
+    if (gu_t == TCB_Q4_K && F % 16 == 0)
       m->gu.back().swi = tcb::q4k_plan(2 * F, D, w->gate_up[l], ctx->sms, 1, F);
-    m->down.push_back(make_mat(w->down[l], w->down_type, D, F, ctx->sms));
+    m->down.push_back(make_mat(w->down[l], ltype(l, 4), D, F, ctx->sms));
   }
   // each matvec streams the next one's weights into L2 (qkv -> o -> gate_up
   // -> down -> next layer's qkv ... -> head -> layer 0's qkv), at most
@@ -992,6 +1023,7 @@ int tcb_llama_create(tcb_ctx *ctx, const tcb_llama_config *cfg, const tcb_llama_
     std::vector<Mat *> chain;
     for (int l = 0; l < c.n_layers; l++) {
       chain.push_back(&m->qkv[l]);
+      if (m->qkv_v[l].N) chain.push_back(&m->qkv_v[l]);
       chain.push_back(&m->o[l]);
       chain.push_back(&m->gu[l]);
       chain.push_back(&m->down[l]);
@@ -1005,7 +1037,7 @@ int tcb_llama_create(tcb_ctx *ctx, const tcb_llama_config *cfg, const tcb_llama_
   }
   size_t sk_bytes = m->head.plan.split_bytes;
   for (int l = 0; l < c.n_layers; l++)
-    for (const Mat *mt : {&m->qkv[l], &m->o[l], &m->gu[l], &m->down[l]})
+    for (const Mat *mt : {&m->qkv[l], &m->qkv_v[l], &m->o[l], &m->gu[l], &m->down[l]})
       sk_bytes = mt->plan.split_bytes > sk_bytes ? mt->plan.split_bytes : sk_bytes;
   m->nch_max = (c.max_ctx + tcb::ll::kChunk - 1) / tcb::ll::kChunk;
   const size_t cache = (size_t)c.n_layers * KVH * c.max_ctx * hd;
@@ -1090,16 +1122,16 @@ namespace {
 // rows out = W · rms(px) for the prompt pass: the RMSNorm in the tensor-core
 // product's activation prologue when that path takes the shape, else a pass
 // of its own into ph
-int norm_gemm(tcb_llama *m, const Mat &mt, const float *nw, int M, float *out, cudaStream_t s) {
+int norm_gemm(tcb_llama *m, const Mat &mt, const float *nw, int M, float *out, long ldo, cudaStream_t s) {
   const tcb_llama_config &c = m->cfg;
   tcb::TcPrologue pro;
   pro.kind = tcb::kTcProRms;
   pro.w = nw;
   pro.eps = c.eps;
-  int rc = tcb::qgemm_tc_prologue(m->ctx, mt.type, M, mt.N, mt.K, mt.w, m->px, c.d_model, out, mt.N, 0, pro, s);
+  int rc = tcb::qgemm_tc_prologue(m->ctx, mt.type, M, mt.N, mt.K, mt.w, m->px, c.d_model, out, ldo, 0, pro, s);
   if (rc != TCB_ERR_UNSUPPORTED) return rc;
   tcb::ll::k_rmsnorm<<<M, 1024, 0, s>>>(m->px, nw, m->ph, c.d_model, c.eps);
-  return tcb_qgemm(m->ctx, mt.type, M, mt.N, mt.K, mt.w, m->ph, TCB_F32, mt.K, out, TCB_F32, mt.N, 0, s);
+  return tcb_qgemm(m->ctx, mt.type, M, mt.N, mt.K, mt.w, m->ph, TCB_F32, mt.K, out, TCB_F32, ldo, 0, s);
 }
 
 // One pass of the prompt over the rows of several sequences that share the
@@ -1135,7 +1167,10 @@ int prefill_pass(tcb_llama *m0, const PfSeq *sq, int ns, cudaStream_t s) {
   int rc = TCB_OK;
   for (int l = 0; l < c.n_layers && rc == TCB_OK; l++) {
     const Mat &q = m0->qkv[l], &o = m0->o[l], &gu = m0->gu[l], &dn = m0->down[l];
-    if ((rc = norm_gemm(m0, q, m0->attn_norm[l], M, m0->pqkv, s)) != TCB_OK) break;
+    if ((rc = norm_gemm(m0, q, m0->attn_norm[l], M, m0->pqkv, qkvn, s)) != TCB_OK) break;
+    const Mat &qv = m0->qkv_v[l];
+    if (qv.N && (rc = norm_gemm(m0, qv, m0->attn_norm[l], M, m0->pqkv + (size_t)(H + KVH) * hd, qkvn, s)) != TCB_OK)
+      break;
     for (int i = 0, r = 0; i < ns; r += sq[i].rows, i++) {
       const tcb_llama *m = sq[i].m;
       __half *kc = m->kc + l * cache_layer, *vc = m->vc + l * cache_layer;
@@ -1149,7 +1184,7 @@ int prefill_pass(tcb_llama *m0, const PfSeq *sq, int ns, cudaStream_t s) {
             TCB_OK ||
         (rc = reduce()) != TCB_OK)
       break;
-    if ((rc = norm_gemm(m0, gu, m0->ffn_norm[l], M, m0->pgu, s)) != TCB_OK) break;
+    if ((rc = norm_gemm(m0, gu, m0->ffn_norm[l], M, m0->pgu, gu.N, s)) != TCB_OK) break;
     // SwiGLU in the down product's activation prologue, else a pass of its own
     tcb::TcPrologue sw;
     sw.kind = tcb::kTcProSwiglu;
@@ -1334,7 +1369,7 @@ struct tcb_llama_batch {
   // the products' launch plans and the scratch they use: owned here, so a
   // captured step never refers to the context's workspace, which later calls
   // may grow (and so move)
-  std::vector<BatchMat> qkv_, o, gu_, down;
+  std::vector<BatchMat> qkv_, qkv_v, o, gu_, down;
   BatchMat head;
   void *ws = nullptr, *sk = nullptr;
   float *x = nullptr, *h = nullptr, *qkv = nullptr, *att = nullptr, *gu = nullptr, *a = nullptr, *logits = nullptr;
@@ -1409,9 +1444,11 @@ BatchMat batch_mat(const tcb_llama *m0, const Mat &mt, int B, size_t &ws, size_t
 }
 
 // rows y (+)= W x_rows for the batch's B rows
+// ldy: the row stride of y (0: mt.N)
 int rows_product(tcb_llama_batch *bt, const Mat &mt, const BatchMat &bm, const float *x, float *y, int acc,
-                 cudaStream_t s) {
+                 cudaStream_t s, long ldy = 0) {
   tcb_llama *m0 = bt->m0;
+  if (ldy == 0) ldy = mt.N;
   const int B = bt->B;
   cudaError_t e = cudaSuccess;
   switch (bm.how) {
@@ -1419,28 +1456,28 @@ int rows_product(tcb_llama_batch *bt, const Mat &mt, const BatchMat &bm, const f
     for (int r0 = 0; r0 < B && e == cudaSuccess; r0 += bm.plan.rows) {
       const int rows = B - r0 < bm.plan.rows ? B - r0 : bm.plan.rows;
       e = tcb::matvec_launch(bm.plan, mt.type, 0, mt.N, mt.K, mt.w, x + (size_t)r0 * mt.K, TCB_F32,
-                             y + (size_t)r0 * mt.N, TCB_F32, acc, m0->ctx->derr, s, nullptr, 0, bt->sk, rows, mt.K,
-                             mt.N);
+                             y + (size_t)r0 * ldy, TCB_F32, acc, m0->ctx->derr, s, nullptr, 0, bt->sk, rows, mt.K,
+                             ldy);
     }
     break;
   case 4:
     for (int r0 = 0; r0 < B && e == cudaSuccess; r0 += bm.plan.rows) {
       const int rows = B - r0 < bm.plan.rows ? B - r0 : bm.plan.rows;
-      e = tcb::rows_launch(bm.plan, mt.N, mt.K, mt.w, x + (size_t)r0 * mt.K, TCB_F32, mt.K, y + (size_t)r0 * mt.N,
-                           TCB_F32, mt.N, acc, rows, m0->ctx->derr, bt->sk, s);
+      e = tcb::rows_launch(bm.plan, mt.N, mt.K, mt.w, x + (size_t)r0 * mt.K, TCB_F32, mt.K, y + (size_t)r0 * ldy,
+                           TCB_F32, ldy, acc, rows, m0->ctx->derr, bt->sk, s);
     }
     break;
   case 1:
-    e = tcb::launch_qgemm_tc(mt.type, mt.w, B, mt.N, mt.K, x, TCB_F32, mt.K, y, TCB_F32, mt.N, acc, bt->ws,
+    e = tcb::launch_qgemm_tc(mt.type, mt.w, B, mt.N, mt.K, x, TCB_F32, mt.K, y, TCB_F32, ldy, acc, bt->ws,
                              m0->ctx->derr, s, nullptr);
     break;
   case 2:
     for (int r = 0; r < B && e == cudaSuccess; r++)
-      e = tcb::matvec_launch(bm.plan, mt.type, 0, mt.N, mt.K, mt.w, x + (size_t)r * mt.K, TCB_F32, y + (size_t)r * mt.N,
+      e = tcb::matvec_launch(bm.plan, mt.type, 0, mt.N, mt.K, mt.w, x + (size_t)r * mt.K, TCB_F32, y + (size_t)r * ldy,
                              TCB_F32, acc, m0->ctx->derr, s, nullptr, 0, bt->sk);
     break;
   default:
-    e = tcb::launch_qgemm_simt(mt.type, mt.w, B, mt.N, mt.K, x, TCB_F32, mt.K, y, TCB_F32, mt.N, acc, m0->ctx->sms, s);
+    e = tcb::launch_qgemm_simt(mt.type, mt.w, B, mt.N, mt.K, x, TCB_F32, mt.K, y, TCB_F32, ldy, acc, m0->ctx->sms, s);
   }
   return e == cudaSuccess ? TCB_OK : fail(m0, e);
 }
@@ -1450,7 +1487,7 @@ int issue_batch_step(tcb_llama_batch *bt, cudaStream_t s) {
   tcb_llama *m0 = bt->m0;
   const tcb_llama_config &c = m0->cfg;
   const int H = c.n_heads, KVH = c.n_kv_heads, hd = c.head_dim, D = c.d_model, F = c.ffn_dim, B = bt->B;
-  const int G = H / KVH, V = c.vocab;
+  const int G = H / KVH, V = c.vocab, qkvn = (H + 2 * KVH) * hd;
   const float scale = 1.0f / sqrtf((float)hd);
   const size_t cache_layer = (size_t)KVH * c.max_ctx * hd;
   // NCCL: rank 0 adds its o/down partial to the residual rows, the others
@@ -1470,7 +1507,10 @@ int issue_batch_step(tcb_llama_batch *bt, cudaStream_t s) {
   int rc = TCB_OK;
   for (int l = 0; l < c.n_layers && rc == TCB_OK; l++) {
     k_rmsnorm<<<B, 1024, 0, s>>>(bt->x, m0->attn_norm[l], bt->h, D, c.eps);
-    if ((rc = rows_product(bt, m0->qkv[l], bt->qkv_[l], bt->h, bt->qkv, 0, s)) != TCB_OK) break;
+    if ((rc = rows_product(bt, m0->qkv[l], bt->qkv_[l], bt->h, bt->qkv, 0, s, qkvn)) != TCB_OK) break;
+    if (m0->qkv_v[l].N && (rc = rows_product(bt, m0->qkv_v[l], bt->qkv_v[l], bt->h, bt->qkv + (size_t)(H + KVH) * hd,
+                                             0, s, qkvn)) != TCB_OK)
+      break;
     const dim3 ag(KVH, m0->nch_max, B);
     switch (G) {
 #define TCB_ATTN(GG)                                                                                              \
@@ -1587,6 +1627,7 @@ int tcb_llama_batch_create(tcb_llama *const *ms, int count, tcb_llama_batch **ou
   size_t ws = 0, sk = 0;
   for (int l = 0; l < c.n_layers; l++) {
     bt->qkv_.push_back(batch_mat(m0, m0->qkv[l], B, ws, sk));
+    bt->qkv_v.push_back(m0->qkv_v[l].N ? batch_mat(m0, m0->qkv_v[l], B, ws, sk) : BatchMat{});
     bt->o.push_back(batch_mat(m0, m0->o[l], B, ws, sk));
     bt->gu_.push_back(batch_mat(m0, m0->gu[l], B, ws, sk));
     bt->down.push_back(batch_mat(m0, m0->down[l], B, ws, sk));

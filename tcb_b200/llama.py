@@ -19,7 +19,7 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from . import BLOCK, Q4_K, Q6_K, TcbError, _stream, lib
+from . import BLOCK, Q4_0, Q4_K, Q6_K, Q8_0, TcbError, _stream, lib
 from . import synth
 
 
@@ -45,7 +45,7 @@ TYPES = {"tok_emb": Q4_K, "qkv": Q4_K, "o": Q6_K, "gate_up": Q4_K, "down": Q6_K,
 # 2.6 (Q4_K) and 13 (Q6_K), and 32 such layers overflow float32; these give
 # weights of standard deviation ~0.02 (TR's default init_std, layers.tr
 # Linear), so activations stay of order one through the stack.
-D_STD = {Q4_K: 7.6e-5, Q6_K: 1.5e-5}
+D_STD = {Q4_K: 7.6e-5, Q6_K: 1.5e-5, Q8_0: 2.7e-4, Q4_0: 4.3e-3}
 
 
 def shapes(cfg: LlamaConfig) -> dict:
@@ -150,29 +150,66 @@ def shard(cfg: LlamaConfig, model: dict, tp: int, r: int) -> dict:
     return out
 
 
-def _d_std(kind: str, varied: bool) -> float:
-    return D_STD[TYPES[kind]] * (VARIED_SCALE.get(kind, 1.0) if varied else 1.0)
+def _d_std(kind: str, varied: bool, wt: int | None = None) -> float:
+    return D_STD[TYPES[kind] if wt is None else wt] * (VARIED_SCALE.get(kind, 1.0) if varied else 1.0)
 
 
-def host_model(cfg: LlamaConfig, seed: int, varied: bool = False) -> dict:
-    """Seeded model as numpy arrays (small configurations: parity tests)."""
+# Per-layer block types (llama.cpp's Q4_K_M files mix Q4_K and Q6_K across
+# layers for the v rows and down): model["types"] maps each of these names to
+# a list of n_layers types; absent names take the class type (TYPES).
+LAYER_KINDS = ("qk", "v", "o", "gate_up", "down")
+_CLASS_OF = {"qk": "qkv", "v": "qkv", "o": "o", "gate_up": "gate_up", "down": "down"}
+
+
+def layer_types(model: dict) -> list:
+    """(qk, v, o, gate_up, down) block types of every layer."""
+    t = model.get("types") or {}
+    L = model["cfg"].n_layers
+    return [tuple(t[k][l] if k in t else TYPES[_CLASS_OF[k]] for k in LAYER_KINDS) for l in range(L)]
+
+
+def qkv_split(cfg: LlamaConfig, qk_type: int) -> int:
+    """Bytes of the q and k rows at the start of a layer's qkv tensor."""
+    e, b = BLOCK[qk_type]
+    return (cfg.n_heads + cfg.n_kv_heads) * cfg.head_dim * (cfg.d_model // e) * b
+
+
+def host_model(cfg: LlamaConfig, seed: int, varied: bool = False, types: dict | None = None) -> dict:
+    """Seeded model as numpy arrays (small configurations: parity tests).
+    types: per-layer block types (LAYER_KINDS -> n_layers types), e.g. a
+    llama.cpp Q4_K_M-like mix; a layer whose v type differs from its q/k
+    type holds its v rows in that type after the q and k rows."""
     sh = shapes(cfg)
     m = {"cfg": cfg}
     rng = np.random.default_rng(seed)
     s = seed * 1000
 
-    def w(kind, sd):
-        wt = TYPES[kind]
-        return synth.weight(wt, *sh[kind], sd, _d_std(kind, varied), centered=varied and wt == Q4_K,
-                            d_band=VARIED_HEAD_BAND if varied and kind == "head" else None)
+    def w(kind, sd, wt=None, rows=None):
+        wt = TYPES[kind] if wt is None else wt
+        n, k = sh[kind]
+        return synth.weight(wt, n if rows is None else rows, k, sd, _d_std(kind, varied, wt),
+                            centered=varied and wt == Q4_K, d_band=VARIED_HEAD_BAND if varied and kind == "head" else None)
 
     m["tok_emb"] = w("tok_emb", s + 1)
     m["head"] = w("head", s + 2)
     m["final_norm"] = (1.0 + 0.1 * rng.standard_normal(cfg.d_model)).astype(np.float32)
     for k in ("attn_norm", "ffn_norm"):
         m[k] = [(1.0 + 0.1 * rng.standard_normal(cfg.d_model)).astype(np.float32) for _ in range(cfg.n_layers)]
-    for j, k in enumerate(("qkv", "o", "gate_up", "down")):
-        m[k] = [w(k, s + 10 + 4 * l + j) for l in range(cfg.n_layers)]
+    if types:
+        m["types"] = {k: list(v) for k, v in types.items()}
+    lt = layer_types(m)
+    hd, H, KVH = cfg.head_dim, cfg.n_heads, cfg.n_kv_heads
+    m["qkv"], m["o"], m["gate_up"], m["down"] = [], [], [], []
+    for l in range(cfg.n_layers):
+        qk_t, v_t, o_t, gu_t, dn_t = lt[l]
+        sd = s + 10 + 4 * l
+        if qk_t == v_t:
+            m["qkv"].append(w("qkv", sd, qk_t))
+        else:
+            m["qkv"].append(np.concatenate([w("qkv", sd, qk_t, (H + KVH) * hd), w("qkv", sd + 500000, v_t, KVH * hd)]))
+        m["o"].append(w("o", sd + 1, o_t))
+        m["gate_up"].append(w("gate_up", sd + 2, gu_t))
+        m["down"].append(w("down", sd + 3, dn_t))
     return m
 
 
@@ -194,10 +231,15 @@ def device_model(cfg: LlamaConfig, seed: int, host: dict | None = None, tp: tupl
         return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
     if host is not None:
+        if host.get("types") and tp[0] > 1:
+            raise NotImplementedError("tensor-parallel shards of a model with per-layer block types")
         host = shard(cfg, host, *tp)
         d = {"cfg": cfg}
         for k, v in host.items():
             if k == "cfg":
+                continue
+            if k == "types":
+                d[k] = v
                 continue
             d[k] = [up(x) for x in v] if isinstance(v, list) else up(v)
         return d
@@ -263,7 +305,8 @@ class _Weights(ctypes.Structure):
     _fields_ = [("tok_emb", ctypes.c_void_p), ("tok_emb_type", ctypes.c_int), ("final_norm", ctypes.c_void_p),
                 ("head", ctypes.c_void_p), ("head_type", ctypes.c_int), ("attn_norm", _PP), ("ffn_norm", _PP),
                 ("qkv", _PP), ("qkv_type", ctypes.c_int), ("o", _PP), ("o_type", ctypes.c_int),
-                ("gate_up", _PP), ("gate_up_type", ctypes.c_int), ("down", _PP), ("down_type", ctypes.c_int)]
+                ("gate_up", _PP), ("gate_up_type", ctypes.c_int), ("down", _PP), ("down_type", ctypes.c_int),
+                ("layer_types", ctypes.POINTER(ctypes.c_int))]
 
 
 def _bind():
@@ -308,12 +351,18 @@ class Llama:
             return (ctypes.c_void_p * len(ts))(*[t.data_ptr() for t in ts])
 
         self._arrs = {k: arr(model[k]) for k in ("attn_norm", "ffn_norm", "qkv", "o", "gate_up", "down")}
-        w = _Weights(model["tok_emb"].data_ptr(), TYPES["tok_emb"], model["final_norm"].data_ptr(),
-                     model["head"].data_ptr(), TYPES["head"],
+        types = model.get("types") or {}
+        self._lt = None
+        if any(k in types for k in LAYER_KINDS):
+            flat = [t for row in layer_types(model) for t in row]
+            self._lt = (ctypes.c_int * len(flat))(*flat)
+        w = _Weights(model["tok_emb"].data_ptr(), types.get("tok_emb", TYPES["tok_emb"]), model["final_norm"].data_ptr(),
+                     model["head"].data_ptr(), types.get("head", TYPES["head"]),
                      ctypes.cast(self._arrs["attn_norm"], _PP), ctypes.cast(self._arrs["ffn_norm"], _PP),
                      ctypes.cast(self._arrs["qkv"], _PP), TYPES["qkv"], ctypes.cast(self._arrs["o"], _PP),
                      TYPES["o"], ctypes.cast(self._arrs["gate_up"], _PP), TYPES["gate_up"],
-                     ctypes.cast(self._arrs["down"], _PP), TYPES["down"])
+                     ctypes.cast(self._arrs["down"], _PP), TYPES["down"],
+                     ctypes.cast(self._lt, ctypes.POINTER(ctypes.c_int)) if self._lt is not None else None)
         h = ctypes.c_void_p()
         self._check(L.tcb_llama_create(ctx.handle, ctypes.byref(c), ctypes.byref(w), ctypes.byref(h)), "create")
         self._h = h

@@ -20,8 +20,13 @@ converter stores the rows of attn_q and attn_k of every head interleaved
 h*hd + 2r holds row r of the head and h*hd + 2r + 1 holds row r + hd/2.  The
 writer applies that order and the loader undoes it (TR's _gguf_satır_sırası).
 Quantized tensors are kept as their verbatim blocks; every one is checked for
-NaN/Inf fp16 scales on load (TR's CheckQuantScales), and only the engine's
-type assignment (llama.TYPES) and F32 norms are accepted.
+NaN/Inf fp16 scales on load (TR's CheckQuantScales).  Block types are taken
+per tensor, as TR's loader does (pretrained.tr 85-141): any of Q8_0, Q4_0,
+Q4_K, Q6_K for the embedding, the head and each layer's products, with
+attn_q/attn_k of one type and ffn_gate/ffn_up of one type (they are merged
+into one product each); attn_v and ffn_down may differ per layer, as in
+llama.cpp's Q4_K_M files.  Types other than the engine's defaults
+(llama.TYPES) are recorded in the model's "types".  Norms are F32.
 """
 from __future__ import annotations
 
@@ -31,7 +36,7 @@ import numpy as np
 
 from . import BLOCK, TcbError, check_scales
 from . import gguf as G
-from .llama import TYPES, LlamaConfig
+from .llama import LAYER_KINDS, TYPES, LlamaConfig, layer_types, qkv_split
 
 ARCH = "llama"
 
@@ -60,33 +65,36 @@ def write(path: str, cfg: LlamaConfig, host: dict, context_length: int | None = 
     b.kv(f"{ARCH}.rope.freq_base", (G.F32V, cfg.rope_theta))
     b.kv(f"{ARCH}.attention.layer_norm_rms_epsilon", (G.F32V, cfg.eps))
 
-    def q(name, kind, rows, K, data):
-        b.tensor(name, TYPES[kind], [K, rows], np.ascontiguousarray(data, dtype=np.uint8).tobytes())
+    def q(name, wt, rows, K, data):
+        b.tensor(name, wt, [K, rows], np.ascontiguousarray(data, dtype=np.uint8).tobytes())
 
     def f32(name, a):
         b.tensor(name, G.F32, [D], np.ascontiguousarray(a, dtype=np.float32).tobytes())
 
-    q("token_embd.weight", "tok_emb", V, D, host["tok_emb"])
-    for l in range(cfg.n_layers):
+    types = host.get("types") or {}
+    q("token_embd.weight", types.get("tok_emb", TYPES["tok_emb"]), V, D, host["tok_emb"])
+    for l, (qk_t, v_t, o_t, gu_t, dn_t) in enumerate(layer_types(host)):
         p = f"blk.{l}."
         f32(p + "attn_norm.weight", host["attn_norm"][l])
-        qkv = _rows(host["qkv"][l], (H + 2 * KVH) * hd)
-        qr, kr, vr = qkv[:H * hd], qkv[H * hd:(H + KVH) * hd], qkv[(H + KVH) * hd:]
+        raw = np.asarray(host["qkv"][l], dtype=np.uint8)
+        nqk = qkv_split(cfg, qk_t)
+        qk = _rows(raw[:nqk], (H + KVH) * hd)
+        qr, kr, vr = qk[:H * hd], qk[H * hd:], _rows(raw[nqk:], KVH * hd)
         fq = np.empty_like(qr)
         fq[_qk_file_order(H, hd)] = qr
         fk = np.empty_like(kr)
         fk[_qk_file_order(KVH, hd)] = kr
-        q(p + "attn_q.weight", "qkv", H * hd, D, fq)
-        q(p + "attn_k.weight", "qkv", KVH * hd, D, fk)
-        q(p + "attn_v.weight", "qkv", KVH * hd, D, vr)
-        q(p + "attn_output.weight", "o", D, H * hd, host["o"][l])
+        q(p + "attn_q.weight", qk_t, H * hd, D, fq)
+        q(p + "attn_k.weight", qk_t, KVH * hd, D, fk)
+        q(p + "attn_v.weight", v_t, KVH * hd, D, vr)
+        q(p + "attn_output.weight", o_t, D, H * hd, host["o"][l])
         f32(p + "ffn_norm.weight", host["ffn_norm"][l])
         gu = _rows(host["gate_up"][l], 2 * F)
-        q(p + "ffn_gate.weight", "gate_up", F, D, gu[:F])
-        q(p + "ffn_up.weight", "gate_up", F, D, gu[F:])
-        q(p + "ffn_down.weight", "down", D, F, host["down"][l])
+        q(p + "ffn_gate.weight", gu_t, F, D, gu[:F])
+        q(p + "ffn_up.weight", gu_t, F, D, gu[F:])
+        q(p + "ffn_down.weight", dn_t, D, F, host["down"][l])
     f32("output_norm.weight", host["final_norm"])
-    q("output.weight", "head", V, D, host["head"])
+    q("output.weight", types.get("head", TYPES["head"]), V, D, host["head"])
     b.write(path)
 
 
@@ -137,42 +145,64 @@ def load(path: str, max_ctx: int | None = None) -> tuple:
                           max_ctx=max_ctx or min(ctx_len, 4096),
                           eps=_f(f, "attention.layer_norm_rms_epsilon"), rope_theta=_f(f, "rope.freq_base", 10000.0))
 
-        def get(name, kind, rows, K):
+        qtypes = set(BLOCK)
+
+        def get(name, quant, rows, K):
+            """(bytes, type) of a quantized tensor, or the F32 vector"""
             try:
                 t = f.tensor(name)
             except KeyError:
                 raise ValueError(f"gguf: missing tensor {name}") from None
-            want = TYPES[kind] if kind else G.F32
-            if t.type != want:
-                raise ValueError(f"gguf: {name} is {G.TYPES[t.type][0]}, the engine takes {G.TYPES[want][0]}")
-            if list(t.dims) != ([K, rows] if kind else [K]):
+            if (t.type in qtypes) != quant:
+                raise ValueError(f"gguf: {name} is {G.TYPES[t.type][0]}, the engine takes "
+                                 f"{'Q8_0, Q4_0, Q4_K or Q6_K' if quant else 'F32'}")
+            if list(t.dims) != ([K, rows] if quant else [K]):
                 raise ValueError(f"gguf: {name} has dims {t.dims}")
             raw = np.frombuffer(G.tensor_bytes(mm, f, t), dtype=np.uint8).copy()
-            if not kind:
+            if not quant:
                 return raw.view(np.float32)
-            bad = check_scales(want, raw)
+            bad = check_scales(t.type, raw)
             if bad >= 0:
                 raise TcbError(10, f"gguf: {name}: block {bad} has a NaN/Inf scale")
-            return raw
+            return raw, t.type
 
-        m = {"cfg": cfg, "tok_emb": get("token_embd.weight", "tok_emb", V, D),
-             "final_norm": get("output_norm.weight", None, None, D), "head": get("output.weight", "head", V, D)}
+        emb, emb_t = get("token_embd.weight", True, V, D)
+        head, head_t = get("output.weight", True, V, D)
+        m = {"cfg": cfg, "tok_emb": emb, "final_norm": get("output_norm.weight", False, None, D), "head": head}
         for k in ("attn_norm", "ffn_norm", "qkv", "o", "gate_up", "down"):
             m[k] = []
+        lt = {k: [] for k in LAYER_KINDS}
         inv_q, inv_k = _qk_file_order(H, hd), _qk_file_order(KVH, hd)
         for l in range(L):
             p = f"blk.{l}."
-            m["attn_norm"].append(get(p + "attn_norm.weight", None, None, D))
-            qr = _rows(get(p + "attn_q.weight", "qkv", H * hd, D), H * hd)[inv_q]
-            kr = _rows(get(p + "attn_k.weight", "qkv", KVH * hd, D), KVH * hd)[inv_k]
-            vr = _rows(get(p + "attn_v.weight", "qkv", KVH * hd, D), KVH * hd)
-            m["qkv"].append(np.concatenate([qr, kr, vr]).reshape(-1))
-            m["o"].append(get(p + "attn_output.weight", "o", D, H * hd))
-            m["ffn_norm"].append(get(p + "ffn_norm.weight", None, None, D))
-            g = _rows(get(p + "ffn_gate.weight", "gate_up", F, D), F)
-            u = _rows(get(p + "ffn_up.weight", "gate_up", F, D), F)
-            m["gate_up"].append(np.concatenate([g, u]).reshape(-1))
-            m["down"].append(get(p + "ffn_down.weight", "down", D, F))
+            m["attn_norm"].append(get(p + "attn_norm.weight", False, None, D))
+            qb, qt = get(p + "attn_q.weight", True, H * hd, D)
+            kb, kt = get(p + "attn_k.weight", True, KVH * hd, D)
+            vb, vt = get(p + "attn_v.weight", True, KVH * hd, D)
+            if qt != kt:
+                raise ValueError(f"gguf: {p}attn_q and attn_k differ in type (merged into one product)")
+            qr, kr = _rows(qb, H * hd)[inv_q], _rows(kb, KVH * hd)[inv_k]
+            m["qkv"].append(np.concatenate([qr.reshape(-1), kr.reshape(-1), vb]))
+            ob, ot = get(p + "attn_output.weight", True, D, H * hd)
+            m["o"].append(ob)
+            m["ffn_norm"].append(get(p + "ffn_norm.weight", False, None, D))
+            gb, gt = get(p + "ffn_gate.weight", True, F, D)
+            ub, ut = get(p + "ffn_up.weight", True, F, D)
+            if gt != ut:
+                raise ValueError(f"gguf: {p}ffn_gate and ffn_up differ in type (merged into one product)")
+            m["gate_up"].append(np.concatenate([gb, ub]))
+            db, dt = get(p + "ffn_down.weight", True, D, F)
+            m["down"].append(db)
+            for k, t in zip(LAYER_KINDS, (qt, vt, ot, gt, dt)):
+                lt[k].append(t)
+        default = dict(zip(LAYER_KINDS, layer_types({"cfg": cfg})[0])) if L else {}
+        types = {k: v for k, v in lt.items() if any(t != default[k] for t in v)}
+        if emb_t != TYPES["tok_emb"]:
+            types["tok_emb"] = emb_t
+        if head_t != TYPES["head"]:
+            types["head"] = head_t
+        if types:
+            m["types"] = types
         return cfg, m
     finally:
         mm.close()

@@ -171,3 +171,46 @@ def test_llama_load_rejects(tmp_path):
     b.write(path2)
     with pytest.raises(ValueError):
         llama_gguf.load(path2)
+
+
+def test_llama_round_trip_mixed_types(tmp_path):
+    """llama.cpp Q4_K_M-like files: attn_v and ffn_down Q6_K in some layers
+    and Q4_K in others, a Q4_0 head and a Q8_0 output projection in one
+    layer: every tensor keeps its own type and bytes through write and load;
+    q/k (or gate/up) of different types are refused (one merged product)."""
+    import tcb_b200 as T
+    from tcb_b200 import llama, llama_gguf
+
+    cfg = llama.LlamaConfig(n_layers=3, d_model=512, n_heads=4, n_kv_heads=2, head_dim=128, ffn_dim=1024,
+                            vocab=2048, max_ctx=160)
+    types = {"v": [T.Q6_K, T.Q4_K, T.Q6_K], "down": [T.Q6_K, T.Q4_K, T.Q4_K], "o": [T.Q6_K, T.Q8_0, T.Q6_K]}
+    host = llama.host_model(cfg, seed=5, types=types)
+    path = str(tmp_path / "mixed.gguf")
+    llama_gguf.write(path, cfg, host)
+    f = G.decode(open(path, "rb").read())
+    assert f.tensor("blk.0.attn_v.weight").type == T.Q6_K and f.tensor("blk.1.attn_v.weight").type == T.Q4_K
+    assert f.tensor("blk.1.attn_output.weight").type == T.Q8_0
+    assert f.tensor("blk.1.ffn_down.weight").type == T.Q4_K
+    cfg2, host2 = llama_gguf.load(path)
+    assert host2["types"] == types
+    for k in ("qkv", "o", "gate_up", "down"):
+        for a, b in zip(host2[k], host[k]):
+            assert np.array_equal(np.asarray(a), np.asarray(b)), k
+    assert llama.layer_types(host2) == llama.layer_types(host)
+    # q and k of different types cannot be merged
+    b = G.Builder()
+    for k, v in f.values.items():
+        b.kv(k, v.data if isinstance(v.data, str) else (v.type, v.data))
+    raw = open(path, "rb").read()
+    for t in f.tensors:
+        data = G.tensor_bytes(raw, f, t)
+        if t.name == "blk.2.attn_k.weight":
+            # the same rows re-encoded as Q8_0 blocks of zeros: a type the q rows do not share
+            data = np.zeros(t.dims[1] * t.dims[0] // 32 * 34, np.uint8).tobytes()
+            b.tensor(t.name, T.Q8_0, list(t.dims), data)
+        else:
+            b.tensor(t.name, t.type, list(t.dims), data)
+    path2 = str(tmp_path / "qk.gguf")
+    b.write(path2)
+    with pytest.raises(ValueError, match="attn_q and attn_k"):
+        llama_gguf.load(path2)
