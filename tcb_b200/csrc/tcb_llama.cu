@@ -117,24 +117,29 @@ __global__ void k_gather_tok(const BatchSeq *bs, int B, int64_t *tok) {
   if (b < B) tok[b] = *bs[b].tok;
 }
 
-// One layer's attention at position *pos: CTA (KV head blockIdx.x, chunk
-// blockIdx.y of kChunk positions), 256 threads.  In a batched step
+// One layer's attention at position *pos: CTA (query heads GS*blockIdx.x ..
+// + GS - 1, chunk blockIdx.y of kChunk positions), 256 threads.  The G query
+// heads of a KV head are spread over gsplit = G/GS CTAs (KV head
+// blockIdx.x / gsplit), chosen by the host so that the grid fills the SMs
+// when the KV heads are few (a tensor-parallel rank holds one of the 70B
+// model's eight).  In a batched step
 // (bs != nullptr) blockIdx.z is the sequence: its position and cache come
 // from bs[z] (plus layer_off), and its qkv row, output row, chunk partials
 // and chunk counters are z strides into the batch's buffers.  Every cached K and V byte of
 // the chunk is requested before the dependency wait (K: thread = (position
 // t/4, 32 dimensions (t%4)*32); V: thread = (dimensions (t%32)*4, positions
 // t/32 + 8j)), so the loads overlap the qkv product.  The CTA rotates the
-// query rows of its G query heads; the CTA whose chunk holds pos also
-// rotates the new key, stores it and the new value into the fp16 cache and
-// uses them from shared memory for that position.  Each CTA writes its
-// chunk's (max, sum, unnormalised output) per query head; the last CTA of a
-// KV head to finish (a counter per KV head, reset by that CTA) merges the
-// chunks in chunk order, so the result does not depend on timing.
-template <int G>
+// query rows of its GS query heads; the CTAs whose chunk holds pos also
+// rotate the new key and use it and the new value from shared memory for
+// that position, and the first of the KV head's CTAs stores both into the
+// fp16 cache.  Each CTA writes its chunk's (max, sum, unnormalised output)
+// per query head; the last CTA of a head group to finish (a counter per
+// group, reset by that CTA) merges the chunks in chunk order, so the result
+// does not depend on timing.
+template <int GS>
 __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cosT, const float *sinT, const int *pos,
                                               __half *kc, __half *vc, float *part, unsigned *count, float *out, int H,
-                                              int KVH, int max_ctx, int nch_max, float scale, const BatchSeq *bs,
+                                              int KVH, int gsplit, int max_ctx, int nch_max, float scale, const BatchSeq *bs,
                                               size_t layer_off) {
   constexpr int half = kHd / 2;
   if (bs) {
@@ -145,20 +150,21 @@ __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cos
     qkv += (size_t)z * (H + 2 * KVH) * kHd;
     out += (size_t)z * H * kHd;
     part += (size_t)z * H * nch_max * (2 + kHd);
-    count += (size_t)z * KVH;
+    count += (size_t)z * H;
   }
-  __shared__ __align__(16) float qs[G][kHd];
+  __shared__ __align__(16) float qs[GS][kHd];
   __shared__ float knew[kHd], vnew[kHd];
-  __shared__ float sc[G][kChunk];
-  __shared__ float gm[G], gl[G];
-  __shared__ float wo[8][G][kHd];
+  __shared__ float sc[GS][kChunk];
+  __shared__ float gm[GS], gl[GS];
+  __shared__ float wo[8][GS][kHd];
   __shared__ int last;
   // The position and the cached K/V rows before it were written by earlier
   // steps (every step starts with a plain launch, after the previous one has
   // completed) or by the prompt pass: they are read before the dependency
   // wait, while the qkv product finishes.  Row p is this step's, written
   // below by the CTA that holds it.
-  const int p = *pos, n = p + 1, kh = blockIdx.x, c = blockIdx.y, t0 = c * kChunk;
+  const int p = *pos, n = p + 1, kh = blockIdx.x / gsplit, c = blockIdx.y, t0 = c * kChunk;
+  const int hq = blockIdx.x * GS;  // the CTA's first query head
   if (t0 >= n) return;
   const int tid = threadIdx.x;
   const __half *kbase = kc + (size_t)kh * max_ctx * kHd, *vbase = vc + (size_t)kh * max_ctx * kHd;
@@ -181,9 +187,9 @@ __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cos
   // not depend on this one, and it waits for this grid before reading `out`
   mv::pdl_launch_dependents();
   const float *cs = cosT + (size_t)p * half, *sn = sinT + (size_t)p * half;
-  for (int i = tid; i < G * half; i += blockDim.x) {
+  for (int i = tid; i < GS * half; i += blockDim.x) {
     const int g = i / half, j = i % half;
-    const float *row = qkv + (size_t)(kh * G + g) * kHd;
+    const float *row = qkv + (size_t)(hq + g) * kHd;
     const float a = row[j], b = row[j + half];
     qs[g][j] = __fsub_rn(__fmul_rn(a, cs[j]), __fmul_rn(b, sn[j]));
     qs[g][j + half] = __fadd_rn(__fmul_rn(a, sn[j]), __fmul_rn(b, cs[j]));
@@ -196,22 +202,24 @@ __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cos
       const float a = krow[tid], b = krow[tid + half];
       const __half ka = __float2half_rn(__fsub_rn(__fmul_rn(a, cs[tid]), __fmul_rn(b, sn[tid])));
       const __half kb = __float2half_rn(__fadd_rn(__fmul_rn(a, sn[tid]), __fmul_rn(b, cs[tid])));
-      kd[tid] = ka;
-      kd[tid + half] = kb;
+      if (blockIdx.x % gsplit == 0) {
+        kd[tid] = ka;
+        kd[tid + half] = kb;
+      }
       knew[tid] = __half2float(ka);
       knew[tid + half] = __half2float(kb);
     } else if (tid < half + kHd) {
       const __half v = __float2half_rn(vrow[tid - half]);
-      vd[tid - half] = v;
+      if (blockIdx.x % gsplit == 0) vd[tid - half] = v;
       vnew[tid - half] = __half2float(v);
     }
   }
   __syncthreads();
   // scores: four threads per position, 32 dimensions each
   {
-    float s[G];
+    float s[GS];
 #pragma unroll
-    for (int g = 0; g < G; g++) s[g] = 0.f;
+    for (int g = 0; g < GS; g++) s[g] = 0.f;
     if (tk < n) {
       float kv[32];
       if (tk == p) {
@@ -229,12 +237,12 @@ __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cos
           }
         }
       }
-      // 16-byte q loads (a broadcast among the lanes of one sk) and the G
+      // 16-byte q loads (a broadcast among the lanes of one sk) and the GS
       // heads' chains interleaved
 #pragma unroll
       for (int i4 = 0; i4 < 8; i4++)
 #pragma unroll
-        for (int g = 0; g < G; g++) {
+        for (int g = 0; g < GS; g++) {
           const float4 q4 = *reinterpret_cast<const float4 *>(&qs[g][32 * sk + 4 * i4]);
           s[g] = fmaf(q4.x, kv[4 * i4], s[g]);
           s[g] = fmaf(q4.y, kv[4 * i4 + 1], s[g]);
@@ -243,7 +251,7 @@ __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cos
         }
     }
 #pragma unroll
-    for (int g = 0; g < G; g++) {
+    for (int g = 0; g < GS; g++) {
       s[g] += __shfl_xor_sync(0xFFFFFFFFu, s[g], 1);
       s[g] += __shfl_xor_sync(0xFFFFFFFFu, s[g], 2);
       if (sk == 0) sc[g][tid >> 2] = tk < n ? s[g] * scale : -INFINITY;
@@ -253,7 +261,7 @@ __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cos
   // chunk softmax: warp g, two positions per lane
   {
     const int w = tid >> 5, lane = tid & 31;
-    if (w < G) {
+    if (w < GS) {
       const float a = sc[w][lane], b = sc[w][lane + 32];
       const float m = warp_max(fmaxf(a, b));
       const float ea = a == -INFINITY ? 0.f : __expf(a - m), eb = b == -INFINITY ? 0.f : __expf(b - m);
@@ -269,9 +277,9 @@ __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cos
   __syncthreads();
   // values: thread = 4 dimensions x positions tv + 8j
   {
-    float o[G][4];
+    float o[GS][4];
 #pragma unroll
-    for (int g = 0; g < G; g++) o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
+    for (int g = 0; g < GS; g++) o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
 #pragma unroll
     for (int j = 0; j < kChunk / 8; j++) {
       const int t = tv + 8 * j;
@@ -286,24 +294,24 @@ __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cos
         v[0] = a.x, v[1] = a.y, v[2] = b.x, v[3] = b.y;
       }
 #pragma unroll
-      for (int g = 0; g < G; g++) {
+      for (int g = 0; g < GS; g++) {
         const float pj = sc[g][t - t0];
 #pragma unroll
         for (int i = 0; i < 4; i++) o[g][i] = fmaf(pj, v[i], o[g][i]);
       }
     }
 #pragma unroll
-    for (int g = 0; g < G; g++)
+    for (int g = 0; g < GS; g++)
 #pragma unroll
       for (int i = 0; i < 4; i++) wo[tid >> 5][g][dv + i] = o[g][i];
   }
   __syncthreads();
-  for (int i = tid; i < G * kHd; i += blockDim.x) {
+  for (int i = tid; i < GS * kHd; i += blockDim.x) {
     const int g = i / kHd, d = i % kHd;
     float O = 0.f;
 #pragma unroll
     for (int w = 0; w < 8; w++) O += wo[w][g][d];
-    float *pp = part + ((size_t)(kh * G + g) * nch_max + c) * (2 + kHd);
+    float *pp = part + ((size_t)(hq + g) * nch_max + c) * (2 + kHd);
     pp[2 + d] = O;
     if (d == 0) {
       pp[0] = gm[g];
@@ -314,7 +322,7 @@ __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cos
   __threadfence();
   __syncthreads();
   const int nch = (n + kChunk - 1) / kChunk;
-  if (tid == 0) last = atomicAdd(&count[kh], 1u) == (unsigned)(nch - 1);
+  if (tid == 0) last = atomicAdd(&count[blockIdx.x], 1u) == (unsigned)(nch - 1);
   __syncthreads();
   if (!last) return;
   __threadfence();
@@ -322,17 +330,17 @@ __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cos
   // output buffer is free again), one warp per query head forms the chunk
   // weights exp(m_c - M) and L, then each thread sums its output element over
   // the chunks in chunk order with the loads issued ahead
-  float *cw = &wo[0][0][0], *cl = cw + G * nch;  // [G][nch] each
-  for (int i = tid; i < G * nch; i += blockDim.x) {
+  float *cw = &wo[0][0][0], *cl = cw + GS * nch;  // [GS][nch] each
+  for (int i = tid; i < GS * nch; i += blockDim.x) {
     const int g = i / nch, cc = i % nch;
-    const float *pc = part + ((size_t)(kh * G + g) * nch_max + cc) * (2 + kHd);
+    const float *pc = part + ((size_t)(hq + g) * nch_max + cc) * (2 + kHd);
     cw[i] = __ldcg(pc);
     cl[i] = __ldcg(pc + 1);
   }
   __syncthreads();
   {
     const int w = tid >> 5, lane = tid & 31;
-    if (w < G) {
+    if (w < GS) {
       float M = -INFINITY;
       for (int cc = lane; cc < nch; cc += 32) M = fmaxf(M, cw[w * nch + cc]);
       M = warp_max(M);
@@ -347,9 +355,9 @@ __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cos
     }
   }
   __syncthreads();
-  for (int i = tid; i < G * kHd; i += blockDim.x) {
+  for (int i = tid; i < GS * kHd; i += blockDim.x) {
     const int g = i / kHd, d = i % kHd;
-    const float *ph = part + (size_t)(kh * G + g) * nch_max * (2 + kHd) + 2 + d;
+    const float *ph = part + (size_t)(hq + g) * nch_max * (2 + kHd) + 2 + d;
     float O = 0.f;
     int cc = 0;
     for (; cc + 4 <= nch; cc += 4) {
@@ -361,9 +369,9 @@ __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cos
       O = fmaf(o3, cw[g * nch + cc + 3], O);
     }
     for (; cc < nch; cc++) O = fmaf(__ldcg(ph + (size_t)cc * (2 + kHd)), cw[g * nch + cc], O);
-    out[(size_t)(kh * G + g) * kHd + d] = __fdiv_rn(O, gl[g]);
+    out[(size_t)(hq + g) * kHd + d] = __fdiv_rn(O, gl[g]);
   }
-  if (tid == 0) count[kh] = 0u;
+  if (tid == 0) count[blockIdx.x] = 0u;
 }
 
 // ---- all-reduce of the residual over peer memory (tensor parallelism)
@@ -731,11 +739,19 @@ namespace {
 struct Mat {
   const void *w = nullptr;
   int type = 0, N = 0, K = 0;
+  // Q6_K rows of 210 * K/256 bytes, not a multiple of 16 (a tensor-parallel
+  // shard of o or down, e.g. K = 1024 or 3584) or not 16-byte aligned, cannot
+  // be mapped by TMA: the engine keeps a copy with every row padded to ldw
+  // bytes (a multiple of 16) for the matvec kernels, and plan reads it
+  const void *wp = nullptr;
+  long ldw = 0;
   tcb::MvPlan plan{};
   tcb::MvPlan swi{};         // gate_up (Q4_K): the launch that writes silu(g) * u itself
   const void *pf = nullptr;  // the next matvec's weights in the step (L2 prefetch while this one runs)
   size_t pf_bytes = 0;
   size_t bytes() const { return (size_t)N * K / tcb::block_elems(type) * tcb::block_bytes(type); }
+  const void *wk() const { return wp ? wp : w; }                    // the weights the matvec plans read
+  size_t kbytes() const { return wp ? (size_t)N * ldw : bytes(); }  // and their size
 };
 
 }  // namespace
@@ -754,7 +770,8 @@ struct tcb_llama {
   float *x = nullptr, *h = nullptr, *qkvb = nullptr, *att = nullptr, *gub = nullptr, *a = nullptr, *logits = nullptr;
   float *part = nullptr, *am_v = nullptr, *cosT = nullptr, *sinT = nullptr;
   int *am_i = nullptr, *pos = nullptr, *nprompt = nullptr;
-  unsigned *acount = nullptr;  // per KV head: attention chunks finished
+  unsigned *acount = nullptr;  // per attention head group: chunks finished
+  int gsplit = 1;              // attention CTAs per KV head (query heads split between them)
   __half *kc = nullptr, *vc = nullptr;
   int64_t *tok = nullptr, *hist = nullptr, *prompt = nullptr;
   int nch_max = 0;
@@ -823,7 +840,7 @@ Mat make_mat(const void *w, int type, int N, int K, int sms) {
 // y (+)= W x for one row of activations (f32 in, f32 out)
 cudaError_t matvec(tcb_llama *m, const Mat &mt, const float *x, float *y, int accumulate, cudaStream_t s) {
   if (mt.plan.ok)
-    return tcb::matvec_launch(mt.plan, mt.type, 0, mt.N, mt.K, mt.w, x, TCB_F32, y, TCB_F32, accumulate,
+    return tcb::matvec_launch(mt.plan, mt.type, 0, mt.N, mt.K, mt.wk(), x, TCB_F32, y, TCB_F32, accumulate,
                               m->ctx->derr, s, mt.pf, mt.pf_bytes, m->sk);
   return tcb::launch_qgemm_simt(mt.type, mt.w, 1, mt.N, mt.K, x, TCB_F32, mt.K, y, TCB_F32, mt.N, accumulate,
                                 m->ctx->sms, s);
@@ -854,6 +871,17 @@ cudaError_t all_reduce_x(tcb_llama *m, cudaStream_t s) {
   return m->nccl_rc ? cudaErrorUnknown : cudaSuccess;
 }
 
+// Attention CTAs per KV head: the most (a power of two dividing the G query
+// heads of a KV head) that keep the grid of every chunk of B sequences
+// within two CTAs per SM.  A CTA's time is a chain of dependent steps over
+// its G/gsplit heads, so with few KV heads (a tensor-parallel rank) spreading
+// the heads over more SMs shortens the launch.
+int attn_split(int G, int KVH, int nch_max, int B, int sms) {
+  int gs = 1;
+  while (G % (2 * gs) == 0 && (long)KVH * 2 * gs * nch_max * B <= 2L * sms) gs *= 2;
+  return gs;
+}
+
 cudaError_t issue_step(tcb_llama *m, cudaStream_t s) {
   using namespace tcb::ll;
   const tcb_llama_config &c = m->cfg;
@@ -876,12 +904,12 @@ cudaError_t issue_step(tcb_llama *m, cudaStream_t s) {
     } else if ((e = norm_matvec(m, m->qkv[l], m->attn_norm[l], m->qkvb, s)) != cudaSuccess) {
       break;
     }
-    const dim3 ag(KVH, m->nch_max);
-    switch (G) {
+    const dim3 ag(KVH * m->gsplit, m->nch_max);
+    switch (G / m->gsplit) {
 #define TCB_ATTN(GG)                                                                                              \
   case GG:                                                                                                        \
     e = launch(k_attn<GG>, ag, dim3(256), s, m->qkvb, m->cosT, m->sinT, m->pos, kc, vc, m->part, m->acount, m->att, H, \
-               KVH, c.max_ctx, m->nch_max, scale, (const BatchSeq *)nullptr, (size_t)0);                          \
+               KVH, m->gsplit, c.max_ctx, m->nch_max, scale, (const BatchSeq *)nullptr, (size_t)0);               \
     break;
       TCB_ATTN(1)
       TCB_ATTN(2)
@@ -1015,6 +1043,29 @@ int tcb_llama_create(tcb_ctx *ctx, const tcb_llama_config *cfg, const tcb_llama_
       m->gu.back().swi = tcb::q4k_plan(2 * F, D, w->gate_up[l], ctx->sms, 1, F);
     m->down.push_back(make_mat(w->down[l], ltype(l, 4), D, F, ctx->sms));
   }
+  // Q6_K matrices the TMA kernels cannot map in place: a row-padded copy
+  {
+    std::vector<Mat *> all{&m->head};
+    for (int l = 0; l < c.n_layers; l++)
+      for (Mat *mt : {&m->qkv[l], &m->qkv_v[l], &m->o[l], &m->gu[l], &m->down[l]}) all.push_back(mt);
+    for (Mat *mt : all) {
+      if (!mt->N || mt->plan.ok || mt->type != TCB_Q6_K) continue;
+      const long rb = (long)(mt->K / 256) * 210, ldw = (rb + 15) & ~15L;
+      uint8_t *wp = nullptr;
+      if ((e = alloc(m, &wp, (size_t)mt->N * ldw)) != cudaSuccess ||
+          (e = cudaMemset(wp, 0, (size_t)mt->N * ldw)) != cudaSuccess ||
+          (e = cudaMemcpy2D(wp, ldw, mt->w, rb, rb, mt->N, cudaMemcpyDeviceToDevice)) != cudaSuccess) {
+        tcb_llama_destroy(m);
+        return e == cudaErrorMemoryAllocation ? TCB_ERR_NOMEM : TCB_ERR_CUDA;
+      }
+      const tcb::MvPlan pl = tcb::matvec_plan(mt->type, 0, 1, mt->N, mt->K, wp, ctx->sms, ldw);
+      if (pl.ok) {
+        mt->wp = wp;
+        mt->ldw = ldw;
+        mt->plan = pl;
+      }
+    }
+  }
   // each matvec streams the next one's weights into L2 (qkv -> o -> gate_up
   // -> down -> next layer's qkv ... -> head -> layer 0's qkv), at most
   // kPrefetchMax bytes of them, half the L2
@@ -1031,8 +1082,8 @@ int tcb_llama_create(tcb_ctx *ctx, const tcb_llama_config *cfg, const tcb_llama_
     chain.push_back(&m->head);
     for (size_t i = 0; i < chain.size(); i++) {
       const Mat *nx = chain[(i + 1) % chain.size()];
-      chain[i]->pf = nx->w;
-      chain[i]->pf_bytes = nx->bytes() < kPrefetchMax ? nx->bytes() : kPrefetchMax;
+      chain[i]->pf = nx->wk();
+      chain[i]->pf_bytes = nx->kbytes() < kPrefetchMax ? nx->kbytes() : kPrefetchMax;
     }
   }
   size_t sk_bytes = m->head.plan.split_bytes;
@@ -1040,6 +1091,7 @@ int tcb_llama_create(tcb_ctx *ctx, const tcb_llama_config *cfg, const tcb_llama_
     for (const Mat *mt : {&m->qkv[l], &m->qkv_v[l], &m->o[l], &m->gu[l], &m->down[l]})
       sk_bytes = mt->plan.split_bytes > sk_bytes ? mt->plan.split_bytes : sk_bytes;
   m->nch_max = (c.max_ctx + tcb::ll::kChunk - 1) / tcb::ll::kChunk;
+  m->gsplit = attn_split(H / KVH, KVH, m->nch_max, 1, ctx->sms);
   const size_t cache = (size_t)c.n_layers * KVH * c.max_ctx * hd;
   const int qkvn = (H + 2 * KVH) * hd;
   if ((e = alloc(m, &m->x, D)) != cudaSuccess || (e = alloc(m, &m->h, D)) != cudaSuccess ||
@@ -1054,7 +1106,7 @@ int tcb_llama_create(tcb_ctx *ctx, const tcb_llama_config *cfg, const tcb_llama_
       (e = alloc(m, &m->vc, cache)) != cudaSuccess || (e = alloc(m, &m->pos, 1)) != cudaSuccess ||
       (e = alloc(m, &m->nprompt, 1)) != cudaSuccess || (e = alloc(m, &m->tok, 1)) != cudaSuccess ||
       (e = alloc(m, &m->hist, c.max_ctx)) != cudaSuccess || (e = alloc(m, &m->prompt, c.max_ctx)) != cudaSuccess ||
-      (e = alloc(m, &m->acount, KVH)) != cudaSuccess || (e = alloc(m, &m->cand, tp)) != cudaSuccess ||
+      (e = alloc(m, &m->acount, H)) != cudaSuccess || (e = alloc(m, &m->cand, tp)) != cudaSuccess ||
       (e = alloc(m, reinterpret_cast<char **>(&m->sk), sk_bytes + 256)) != cudaSuccess) {
     tcb_llama_destroy(m);
     return e == cudaErrorMemoryAllocation ? TCB_ERR_NOMEM : TCB_ERR_CUDA;
@@ -1074,7 +1126,7 @@ int tcb_llama_create(tcb_ctx *ctx, const tcb_llama_config *cfg, const tcb_llama_
   if ((e = cudaMemcpy(m->cosT, ct.data(), ct.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
       (e = cudaMemcpy(m->sinT, st.data(), st.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
       (e = cudaMemset(m->kc, 0, cache * 2)) != cudaSuccess || (e = cudaMemset(m->vc, 0, cache * 2)) != cudaSuccess ||
-      (e = cudaMemset(m->acount, 0, KVH * sizeof(unsigned))) != cudaSuccess ||
+      (e = cudaMemset(m->acount, 0, H * sizeof(unsigned))) != cudaSuccess ||
       (e = cudaMemset(m->sk, 0, sk_bytes + 256)) != cudaSuccess) {
     tcb_llama_destroy(m);
     return TCB_ERR_CUDA;
@@ -1376,6 +1428,7 @@ struct tcb_llama_batch {
   float *part = nullptr, *am_v = nullptr;
   int *am_i = nullptr;
   unsigned *count = nullptr;
+  int gsplit = 1;  // attention CTAs per KV head
   int64_t *tok = nullptr;
   tcb::ll::BatchSeq *seq = nullptr;
   tcb::ll::BatchPick *pick = nullptr;
@@ -1428,7 +1481,7 @@ BatchMat batch_mat(const tcb_llama *m0, const Mat &mt, int B, size_t &ws, size_t
                   tcb::tc_workspace_bytes(mt.type, B, mt.N, mt.K) <= ((size_t)1 << 30);
   if (B > 1 && !(tc && B >= kBatchTcRows))
     for (int mr = 8; mr >= 2 && !bm.plan.ok; mr /= 2)
-      if (mr <= 2 * B - 1 || mr == 2) bm.plan = tcb::matvec_plan_rows(mt.type, 0, mt.N, mt.K, mt.w, sms, mr);
+      if (mr <= 2 * B - 1 || mr == 2) bm.plan = tcb::matvec_plan_rows(mt.type, 0, mt.N, mt.K, mt.wk(), sms, mr, mt.ldw);
   if (bm.plan.ok) {
     bm.how = 0;
   } else if (tc) {
@@ -1436,7 +1489,7 @@ BatchMat batch_mat(const tcb_llama *m0, const Mat &mt, int B, size_t &ws, size_t
     const size_t w = tcb::tc_workspace_bytes(mt.type, B, mt.N, mt.K);
     ws = w > ws ? w : ws;
   } else {
-    bm.plan = tcb::matvec_plan(mt.type, 0, 1, mt.N, mt.K, mt.w, sms);
+    bm.plan = tcb::matvec_plan(mt.type, 0, 1, mt.N, mt.K, mt.wk(), sms, mt.ldw);
     bm.how = bm.plan.ok ? 2 : 3;
   }
   if (bm.plan.ok && bm.plan.split_bytes > sk) sk = bm.plan.split_bytes;
@@ -1455,7 +1508,7 @@ int rows_product(tcb_llama_batch *bt, const Mat &mt, const BatchMat &bm, const f
   case 0:
     for (int r0 = 0; r0 < B && e == cudaSuccess; r0 += bm.plan.rows) {
       const int rows = B - r0 < bm.plan.rows ? B - r0 : bm.plan.rows;
-      e = tcb::matvec_launch(bm.plan, mt.type, 0, mt.N, mt.K, mt.w, x + (size_t)r0 * mt.K, TCB_F32,
+      e = tcb::matvec_launch(bm.plan, mt.type, 0, mt.N, mt.K, mt.wk(), x + (size_t)r0 * mt.K, TCB_F32,
                              y + (size_t)r0 * ldy, TCB_F32, acc, m0->ctx->derr, s, nullptr, 0, bt->sk, rows, mt.K,
                              ldy);
     }
@@ -1473,7 +1526,7 @@ int rows_product(tcb_llama_batch *bt, const Mat &mt, const BatchMat &bm, const f
     break;
   case 2:
     for (int r = 0; r < B && e == cudaSuccess; r++)
-      e = tcb::matvec_launch(bm.plan, mt.type, 0, mt.N, mt.K, mt.w, x + (size_t)r * mt.K, TCB_F32, y + (size_t)r * ldy,
+      e = tcb::matvec_launch(bm.plan, mt.type, 0, mt.N, mt.K, mt.wk(), x + (size_t)r * mt.K, TCB_F32, y + (size_t)r * ldy,
                              TCB_F32, acc, m0->ctx->derr, s, nullptr, 0, bt->sk);
     break;
   default:
@@ -1511,14 +1564,14 @@ int issue_batch_step(tcb_llama_batch *bt, cudaStream_t s) {
     if (m0->qkv_v[l].N && (rc = rows_product(bt, m0->qkv_v[l], bt->qkv_v[l], bt->h, bt->qkv + (size_t)(H + KVH) * hd,
                                              0, s, qkvn)) != TCB_OK)
       break;
-    const dim3 ag(KVH, m0->nch_max, B);
-    switch (G) {
+    const dim3 ag(KVH * bt->gsplit, m0->nch_max, B);
+    switch (G / bt->gsplit) {
 #define TCB_ATTN(GG)                                                                                              \
   case GG:                                                                                                        \
     e = launch(k_attn<GG>, ag, dim3(256), s, (const float *)bt->qkv, (const float *)m0->cosT,                    \
                (const float *)m0->sinT, (const int *)nullptr, (__half *)nullptr, (__half *)nullptr, bt->part,    \
-               bt->count, bt->att, H, KVH, c.max_ctx, m0->nch_max, scale, (const BatchSeq *)bt->seq,             \
-               (size_t)l * cache_layer);                                                                          \
+               bt->count, bt->att, H, KVH, bt->gsplit, c.max_ctx, m0->nch_max, scale,                            \
+               (const BatchSeq *)bt->seq, (size_t)l * cache_layer);                                              \
     break;
       TCB_ATTN(1)
       TCB_ATTN(2)
@@ -1602,6 +1655,7 @@ int tcb_llama_batch_create(tcb_llama *const *ms, int count, tcb_llama_batch **ou
   bt->B = count;
   const int H = c.n_heads, KVH = c.n_kv_heads, hd = c.head_dim, D = c.d_model, F = c.ffn_dim, B = count;
   const size_t qkvn = (size_t)(H + 2 * KVH) * hd;
+  bt->gsplit = attn_split(H / KVH, KVH, m0->nch_max, B, m0->ctx->sms);
   std::vector<tcb::ll::BatchSeq> hs(B);
   for (int i = 0; i < B; i++) hs[i] = tcb::ll::BatchSeq{ms[i]->pos, ms[i]->kc, ms[i]->vc, ms[i]->tok};
   std::vector<tcb::ll::BatchPick> hp(B);
@@ -1615,10 +1669,10 @@ int tcb_llama_batch_create(tcb_llama *const *ms, int count, tcb_llama_batch **ou
       (e = balloc(bt, &bt->part, (size_t)B * H * m0->nch_max * (2 + hd))) != cudaSuccess ||
       (e = balloc(bt, &bt->am_v, (size_t)B * tcb::ll::kArgBlocks)) != cudaSuccess ||
       (e = balloc(bt, &bt->am_i, (size_t)B * tcb::ll::kArgBlocks)) != cudaSuccess ||
-      (e = balloc(bt, &bt->count, (size_t)B * KVH)) != cudaSuccess || (e = balloc(bt, &bt->tok, (size_t)B)) != cudaSuccess ||
+      (e = balloc(bt, &bt->count, (size_t)B * H)) != cudaSuccess || (e = balloc(bt, &bt->tok, (size_t)B)) != cudaSuccess ||
       (e = balloc(bt, &bt->seq, (size_t)B)) != cudaSuccess || (e = balloc(bt, &bt->pick, (size_t)B)) != cudaSuccess ||
       (e = balloc(bt, &bt->cand, (size_t)B * m0->tp)) != cudaSuccess ||
-      (e = cudaMemset(bt->count, 0, (size_t)B * KVH * sizeof(unsigned))) != cudaSuccess ||
+      (e = cudaMemset(bt->count, 0, (size_t)B * H * sizeof(unsigned))) != cudaSuccess ||
       (e = cudaMemcpy(bt->seq, hs.data(), B * sizeof(tcb::ll::BatchSeq), cudaMemcpyHostToDevice)) != cudaSuccess ||
       (e = cudaMemcpy(bt->pick, hp.data(), B * sizeof(tcb::ll::BatchPick), cudaMemcpyHostToDevice)) != cudaSuccess) {
     tcb_llama_batch_destroy(bt);

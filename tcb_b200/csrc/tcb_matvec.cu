@@ -843,13 +843,15 @@ namespace {
 
 constexpr int kSmemMax = 227 * 1024;
 
-// [N rows, rowBytes/8 eight-byte elements] view of the block store
+// [N rows, rowBytes/8 eight-byte elements] view of the block store, rows
+// ldw bytes apart (a padded row's last element may hold up to 7 pad bytes,
+// which no block reads)
 template <int W, bool ACT8>
-bool encode_weight_map(CUtensorMap *tm, const void *w, int N, long rowBytes) {
+bool encode_weight_map(CUtensorMap *tm, const void *w, int N, long rowBytes, long ldw) {
   auto enc = tensor_map_encoder();
   if (!enc) return false;
-  cuuint64_t gdim[2] = {(cuuint64_t)(rowBytes / 8), (cuuint64_t)N};
-  cuuint64_t gstride[1] = {(cuuint64_t)rowBytes};
+  cuuint64_t gdim[2] = {(cuuint64_t)((rowBytes + 7) / 8), (cuuint64_t)N};
+  cuuint64_t gstride[1] = {(cuuint64_t)ldw};
   cuuint32_t box[2] = {(cuuint32_t)mv::Pol<W>::BOX8, 16};
   cuuint32_t estr[2] = {1, 1};
   return enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void *>(w), gdim, gstride, box, estr,
@@ -865,7 +867,7 @@ cudaError_t plan_launch(const MvPlan &pl, const void *w, int N, int K, const voi
   mv::Params a{};
   a.w = static_cast<const uint8_t *>(w);
   a.nb = K / mv::Pol<W>::E;
-  a.rowBytes = (long)a.nb * mv::Pol<W>::B;
+  a.rowBytes = pl.ldw;
   a.N = N;
   a.K = K;
   a.x = x;
@@ -913,13 +915,14 @@ cudaError_t plan_launch(const MvPlan &pl, const void *w, int N, int K, const voi
 
 // mr (1, 2, 4, 8; 1 on the int8 path): the most rows of x a launch takes
 template <int W, bool ACT8>
-MvPlan plan_w(int N, int K, const void *w, int sms, int mr = 1) {
+MvPlan plan_w(int N, int K, const void *w, int sms, int mr = 1, long ldw = 0) {
   using P = mv::Pol<W>;
   MvPlan pl{};
   if (mr != 1 && mr != 2 && mr != 4 && mr != 8) return pl;
   const int nb = K / P::E;
   const long rowBytes = (long)nb * P::B;
-  if (rowBytes % 16 || reinterpret_cast<uintptr_t>(w) % 16 || nb == 0) return pl;
+  if (ldw == 0) ldw = rowBytes;
+  if (ldw % 16 || ldw < rowBytes || reinterpret_cast<uintptr_t>(w) % 16 || nb == 0) return pl;
   if (P::RB == 8 && nb % 8) return pl;  // Q8_0 / Q4_0 rounds are 8 blocks
   if (!tensor_map_encoder()) return pl;
   pl.cbc = P::NBOX * P::BPB;
@@ -941,8 +944,9 @@ MvPlan plan_w(int N, int K, const void *w, int sms, int mr = 1) {
   pl.tiles = (N + 15) / 16;
   pl.grid = pl.tiles < sms ? pl.tiles : sms;
   pl.rows = mr;
+  pl.ldw = ldw;
   CUtensorMap tm;
-  if (!encode_weight_map<W, ACT8>(&tm, w, N, rowBytes)) return pl;
+  if (!encode_weight_map<W, ACT8>(&tm, w, N, rowBytes, ldw)) return pl;
   memcpy(pl.tmap, &tm, sizeof tm);
   pl.ok = true;
   return pl;
@@ -950,9 +954,10 @@ MvPlan plan_w(int N, int K, const void *w, int sms, int mr = 1) {
 
 }  // namespace
 
-MvPlan matvec_plan(int wtype, int act8, int M, int N, int K, const void *w, int sms) {
+MvPlan matvec_plan(int wtype, int act8, int M, int N, int K, const void *w, int sms, long ldw) {
   MvPlan none{};
   if (M != 1 || N <= 0 || K <= 0) return none;
+  if (ldw) return wtype == TCB_Q6_K && !act8 ? plan_w<TCB_Q6_K, false>(N, K, w, sms, 1, ldw) : none;
   switch (wtype) {
   case TCB_Q4_K: return act8 ? plan_w<TCB_Q4_K, true>(N, K, w, sms) : q4k_plan(N, K, w, sms);
   case TCB_Q6_K:
@@ -967,9 +972,10 @@ MvPlan matvec_plan(int wtype, int act8, int M, int N, int K, const void *w, int 
   return none;
 }
 
-MvPlan matvec_plan_rows(int wtype, int act8, int N, int K, const void *w, int sms, int mr) {
+MvPlan matvec_plan_rows(int wtype, int act8, int N, int K, const void *w, int sms, int mr, long ldw) {
   MvPlan none{};
   if (N <= 0 || K <= 0) return none;
+  if (ldw) return wtype == TCB_Q6_K && !act8 && K <= 8192 ? plan_w<TCB_Q6_K, false>(N, K, w, sms, mr, ldw) : none;
   if (act8) {
     switch (wtype) {
     case TCB_Q4_K: return plan_w<TCB_Q4_K, true>(N, K, w, sms, mr);

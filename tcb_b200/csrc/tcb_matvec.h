@@ -20,6 +20,8 @@ struct MvPlan {
   size_t split_bytes;          // device scratch a launch needs (zeroed once; launches leave it zeroed), 0 if none
   int rows, xstride;           // kind 1: rows of x a launch takes, bytes between their digit regions
   int pair;                    // kind 1: F when the launch pairs gate and up rows for SwiGLU, else 0
+  long ldw;                    // kind 0: bytes from one weight row to the next (the packed row size,
+                               // or a padded pitch given to the planner)
   alignas(64) unsigned char tmap[128];  // TMA descriptor of the weight (CUtensorMap)
 };
 
@@ -33,11 +35,16 @@ constexpr int kQ6kMinRows = 32768;
 // launch's partials never land on another's counters.
 constexpr size_t kScratchCntBytes = 1024;
 
-MvPlan matvec_plan(int wtype, int act8, int M, int N, int K, const void *w, int sms);
+// ldw: bytes between weight rows when they are not packed (0: packed).  A
+// 2-D TMA map needs a row stride that is a multiple of 16 bytes, which a
+// Q6_K row (210 bytes a block) is only for a multiple of 8 blocks; a copy
+// with each row padded to a multiple of 16 bytes is read through the generic
+// kernel with ldw = its pitch (Q6_K float path only; other cases refuse).
+MvPlan matvec_plan(int wtype, int act8, int M, int N, int K, const void *w, int sms, long ldw = 0);
 // up to mr (2, 4, 8) rows of x per launch streaming the weights once, float
 // or int8-activation path (ok = false when the rows' x regions leave too
 // little shared memory, or for the wide Q6_K kernel)
-MvPlan matvec_plan_rows(int wtype, int act8, int N, int K, const void *w, int sms, int mr);
+MvPlan matvec_plan_rows(int wtype, int act8, int N, int K, const void *w, int sms, int mr, long ldw = 0);
 
 // Q4_K float path (kind 1).  With nw, the product is W * rms(x): an
 // RMSNorm (x / sqrt(mean(x^2) + eps) * nw, K elements, f32 x, finite x
