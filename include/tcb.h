@@ -198,6 +198,11 @@ int tcb_llama_start(tcb_llama *m, const int64_t *prompt, int n, void *stream);
  * Tensor parallelism sums the residual rows with NCCL.  Returns
  * TCB_ERR_UNSUPPORTED when a step has already run since the start. */
 int tcb_llama_prefill(tcb_llama *m, void *stream);
+/* Rows per pass of tcb_llama_prefill (rows >= 1; 0 restores the default
+ * 2048).  Fewer rows need smaller row buffers; a prompt longer than rows + 1
+ * positions then takes several passes with the same result (the tests use
+ * it to cover pass boundaries).  TR's generate has no such setting. */
+int tcb_llama_set_prefill_rows(tcb_llama *m, int rows);
 /* The prompt pass of several sequences at once (TR's generate over a batch
  * of prompts): count engines made from the same weights and shapes, each
  * started with its own prompt (tcb_llama_start), are fed as one set of rows

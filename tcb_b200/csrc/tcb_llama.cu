@@ -796,6 +796,7 @@ struct tcb_llama {
   unsigned *ar_epoch = nullptr, *ar_done = nullptr;
   // prompt pass (tcb_llama_prefill): row buffers of pf_rows rows, made on first use
   int host_n = 0;                    // prompt length given to tcb_llama_start
+  int pf_pass = 0;                   // rows per pass (tcb_llama_set_prefill_rows; 0: kPrefillRows)
   int pf_rows = 0;
   float *px = nullptr, *ph = nullptr, *pqkv = nullptr, *patt = nullptr, *pgu = nullptr, *pa = nullptr;
 };
@@ -1309,6 +1310,13 @@ int finish_prefill(tcb_llama *m, cudaStream_t s) {
 }
 }  // namespace
 
+int tcb_llama_set_prefill_rows(tcb_llama *m, int rows) {
+  if (!m) return TCB_ERR_NULL;
+  if (rows < 0) return TCB_ERR_SHAPE;
+  m->pf_pass = rows;
+  return TCB_OK;
+}
+
 int tcb_llama_prefill(tcb_llama *m, void *stream) {
   if (!m) return TCB_ERR_NULL;
   const int n = m->host_n;
@@ -1318,10 +1326,7 @@ int tcb_llama_prefill(tcb_llama *m, void *stream) {
   cudaError_t e = cudaSetDevice(m->ctx->dev);
   if (e != cudaSuccess) return fail(m, e);
   if (m->tp > 1 && (!nccl() || !m->comm)) return fail(m, cudaErrorNotReady);
-  // TCB_PREFILL_ROWS overrides the rows per pass (tests use it to cover
-  // prompts that take several passes)
-  const char *ev = getenv("TCB_PREFILL_ROWS");
-  int rows = ev && atoi(ev) > 0 ? atoi(ev) : tcb::ll::kPrefillRows;
+  int rows = m->pf_pass > 0 ? m->pf_pass : tcb::ll::kPrefillRows;
   if (rows > n - 1) rows = n - 1;
   int rc = m->pf_rows >= rows ? TCB_OK : pf_alloc(m, rows, s);
   for (int p0 = 0; p0 < n - 1 && rc == TCB_OK; p0 += rows) {

@@ -319,6 +319,7 @@ def _bind():
     L.tcb_llama_start.argtypes = [P, P, ctypes.c_int, P]
     L.tcb_llama_step.argtypes = [P, P]
     L.tcb_llama_prefill.argtypes = [P, P]
+    L.tcb_llama_set_prefill_rows.argtypes = [P, ctypes.c_int]
     L.tcb_llama_prefill_batch.argtypes = [P, ctypes.c_int, P]
     L.tcb_llama_capture.argtypes = [P, P]
     L.tcb_llama_step_kernels.argtypes = [P, ctypes.POINTER(ctypes.c_int)]
@@ -378,6 +379,10 @@ class Llama:
     def start(self, prompt, stream=None):
         p = np.ascontiguousarray(prompt, dtype=np.int64)
         self._check(self._L.tcb_llama_start(self._h, p.ctypes.data, p.size, _stream(stream)), "start")
+
+    def set_prefill_rows(self, rows: int):
+        """Rows per pass of prefill (0: the default 2048)."""
+        self._check(self._L.tcb_llama_set_prefill_rows(self._h, rows), "set_prefill_rows")
 
     def prefill(self, stream=None):
         """Feed all but the last prompt token in row batches (directly after

@@ -75,10 +75,11 @@ def setup(request, oracle):
     return cfg, ctx, host, dev, prompt, ref_toks[:NPROMPT + gen], ref_logits, tol
 
 
-def run_prefill(ctx, dev, prompt, gen):
-    """prefill, then gen eager steps one at a time: every step's logits and
-    the token history"""
+def run_prefill(ctx, dev, prompt, gen, rows=0):
+    """prefill (rows per pass: 0 for the default), then gen eager steps one at
+    a time: every step's logits and the token history"""
     m = llama.Llama(ctx, dev)
+    m.set_prefill_rows(rows)
     m.start(prompt)
     m.prefill()
     logits = []
@@ -110,12 +111,11 @@ def test_prefill_against_reference(setup):
         assert list(toks) == list(ref_toks)
 
 
-def test_prefill_in_several_passes(setup, monkeypatch):
+def test_prefill_in_several_passes(setup):
     cfg, ctx, host, dev, prompt, ref_toks, ref_logits, tol = setup
     # 80-row passes: batches start at positions 80, 160, 240 (off the 64-row
     # tile grid); the last has 59 rows (below the tensor-core path's minimum)
-    monkeypatch.setenv("TCB_PREFILL_ROWS", "80")
-    logits, toks = run_prefill(ctx, dev, prompt, len(ref_toks) - NPROMPT)
+    logits, toks = run_prefill(ctx, dev, prompt, len(ref_toks) - NPROMPT, rows=80)
     check_run(host, logits, toks, prompt, tol)
 
 
