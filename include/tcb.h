@@ -84,6 +84,27 @@ int tcb_qgemm(tcb_ctx *ctx, int wtype, int M, int N, int K, const void *w,
               const void *x, int xdtype, long ldx, void *c, int cdtype,
               long ldc, int accumulate, void *stream);
 
+/* tcb_qgemm over host buffers: x and c in host memory (w on the device, as
+ * uploaded by tcb_quant_upload).  TR's CPU backend runs quantGemm over host
+ * slices (tensor/cpu_quant.go:47-160, the same (M, N, K, a, b, c, over)
+ * arguments); this entry lets such a caller run the product on the GPU
+ * without managing device buffers.  The results are tcb_qgemm's, bit for bit.
+ *   - pinned x (page-locked or registered) is copied to the device by a kernel
+ *     that reads host memory, and the product starts behind it without a
+ *     copy-engine hand-off; pageable x goes through cudaMemcpyAsync (which
+ *     then returns only once x has been read);
+ *   - pinned c is written by the product in place, over the host link;
+ *     pageable c is computed in a device buffer and copied back (the call
+ *     then returns after the copy);
+ *   - device pointers are used in place.
+ * With pinned buffers the call is asynchronous on stream: read c after the
+ * stream synchronises.  The device copies live in the context and are shared
+ * by its calls: order calls on one context on one stream. */
+int tcb_qgemm_host(tcb_ctx *ctx, int wtype, int M, int N, int K,
+                   const void *w, const void *x, int xdtype, long ldx,
+                   void *c, int cdtype, long ldc, int accumulate,
+                   void *stream);
+
 /* The int8-activation product of TR's TR_quantized_activations block:
  * every finite row of x is quantised per weight block (quantizeQ8,
  * tensor/cpu_quant_q8.go:39-68), dotted in integers per block and folded

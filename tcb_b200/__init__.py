@@ -75,6 +75,7 @@ def lib() -> ctypes.CDLL:
     L.tcb_block_shape.argtypes = [I, ctypes.POINTER(I), ctypes.POINTER(I)]
     L.tcb_qgemm.argtypes = [P, I, I, I, I, P, P, I, Lg, P, I, Lg, I, P]
     L.tcb_qgemm_act8.argtypes = [P, I, I, I, I, P, P, I, Lg, P, I, Lg, I, P]
+    L.tcb_qgemm_host.argtypes = [P, I, I, I, I, P, P, I, Lg, P, I, Lg, I, P]
     L.tcb_qgemm_act8_static.argtypes = [I, I, I, I, P, P, I, Lg, P, I, Lg, I, P]
     L.tcb_qdequant.argtypes = [P, I, P, Lg, P, I, P]
     L.tcb_qembed.argtypes = [P, I, P, Lg, I, P, I, P, P]
@@ -175,6 +176,17 @@ class Context:
         rc = fn(self._h, wtype, M, N, K, _ptr(w), _ptr(x), _dtype_code(x), x.stride(0), _ptr(c),
                 _dtype_code(c), c.stride(0), int(bool(accumulate)), _stream(stream))
         self._check(rc, "tcb_qgemm_act8" if act8 else "tcb_qgemm")
+        return c
+
+    def qgemm_host(self, wtype, w, x, c, accumulate=False, stream=None):
+        """tcb_qgemm_host: x and c torch CPU tensors (pinned or pageable, 2-D,
+        row-contiguous), w a uint8 CUDA tensor.  With pinned c, read c after
+        the stream synchronises."""
+        M, K = x.shape
+        N = c.shape[1]
+        rc = lib().tcb_qgemm_host(self._h, wtype, M, N, K, _ptr(w), _ptr(x), _dtype_code(x), x.stride(0), _ptr(c),
+                                  _dtype_code(c), c.stride(0), int(bool(accumulate)), _stream(stream))
+        self._check(rc, "tcb_qgemm_host")
         return c
 
     def qgemm_act8(self, wtype, w, x, c, accumulate=True, stream=None):

@@ -6,6 +6,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "../../include/tcb.h"
@@ -58,6 +59,70 @@ int ensure_ws(tcb_ctx *ctx, size_t bytes) {
   }
   ctx->ws_cap = cap;
   return TCB_OK;
+}
+
+// grow one of the context's staging buffers (tcb_qgemm_host) to `bytes`
+int ensure_buf(tcb_ctx *ctx, void **buf, size_t *cap, size_t bytes) {
+  if (bytes <= *cap) return TCB_OK;
+  if (*buf) {
+    cudaError_t e = cudaFree(*buf);
+    *buf = nullptr;
+    *cap = 0;
+    if (e != cudaSuccess) return cuda_fail(ctx, e);
+  }
+  const size_t c = bytes < (64u << 10) ? (64u << 10) : bytes + (bytes >> 2);
+  cudaError_t e = cudaMalloc(buf, c);
+  if (e != cudaSuccess) {
+    cuda_fail(ctx, e);
+    (void)cudaGetLastError();
+    return TCB_ERR_NOMEM;
+  }
+  *cap = c;
+  return TCB_OK;
+}
+
+// Where memory p lives, for tcb_qgemm_host: kMemDevice (device or managed
+// memory, used in place), kMemPinned (page-locked or registered host memory;
+// *view is the address at which the GPU reaches it) or kMemPageable.
+constexpr int kMemPageable = 0, kMemPinned = 1, kMemDevice = 2;
+int mem_kind(const void *p, const void **view) {
+  cudaPointerAttributes a{};
+  *view = nullptr;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return kMemPageable;
+  }
+  if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) {
+    *view = p;
+    return kMemDevice;
+  }
+  if (a.type == cudaMemoryTypeHost && a.devicePointer) {
+    *view = a.devicePointer;
+    return kMemPinned;
+  }
+  return kMemPageable;
+}
+
+// rows of x from memory the GPU reaches (pinned host memory) into a dense
+// device buffer.  The previous call's product may still read dst, so the copy
+// waits for the previous kernel of the stream first; the product that follows
+// may launch at once (it waits for this grid before reading x).
+__global__ void k_stage_rows(const uint8_t *src, long sstride, uint8_t *dst, long rowbytes, int rows) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
+  const bool vec = (reinterpret_cast<uintptr_t>(src) | (uintptr_t)sstride | reinterpret_cast<uintptr_t>(dst) |
+                    (uintptr_t)rowbytes) % 16 == 0;
+  const long t0 = (long)blockIdx.x * blockDim.x + threadIdx.x, nt = (long)gridDim.x * blockDim.x;
+  for (int r = blockIdx.y; r < rows; r += gridDim.y) {
+    const uint8_t *s = src + r * sstride;
+    uint8_t *d = dst + r * rowbytes;
+    if (vec) {
+      for (long i = t0; i < rowbytes / 16; i += nt)
+        reinterpret_cast<uint4 *>(d)[i] = reinterpret_cast<const uint4 *>(s)[i];
+    } else {
+      for (long i = t0; i < rowbytes; i += nt) d[i] = s[i];
+    }
+  }
 }
 
 // grow the matvec kernels' scratch to at least `bytes` (zeroed; launches
@@ -266,7 +331,7 @@ int tcb_ctx_destroy(tcb_ctx *ctx) {
   if (!ctx) return TCB_OK;
   int rc = TCB_OK;
   if (cudaSetDevice(ctx->dev) != cudaSuccess) rc = TCB_ERR_CUDA;
-  for (void *p : {ctx->ws, (void *)ctx->derr, ctx->sk})
+  for (void *p : {ctx->ws, (void *)ctx->derr, ctx->sk, ctx->hx, ctx->hc})
     if (p && cudaFree(p) != cudaSuccess) rc = TCB_ERR_CUDA;
   delete ctx;
   return rc;
@@ -291,6 +356,67 @@ int tcb_qgemm(tcb_ctx *ctx, int wtype, int M, int N, int K, const void *w, const
   }
   cudaError_t e = tcb::launch_qgemm_simt(wtype, w, M, N, K, x, xdtype, ldx, c, cdtype, ldc, accumulate, ctx->sms, s);
   if (e != cudaSuccess) return cuda_fail(ctx, e);
+  return TCB_OK;
+}
+
+int tcb_qgemm_host(tcb_ctx *ctx, int wtype, int M, int N, int K, const void *w, const void *x, int xdtype, long ldx,
+                   void *c, int cdtype, long ldc, int accumulate, void *stream) {
+  if (!ctx) return TCB_ERR_NULL;
+  int rc = check_gemm_args(wtype, M, N, K, w, x, xdtype, ldx, c, cdtype, ldc);
+  if (rc != TCB_OK || M == 0 || N == 0) return rc;
+  if ((rc = bind(ctx)) != TCB_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t xe = elem_size(xdtype), ce = elem_size(cdtype);
+  // x: a dense device copy, made by a kernel that reads pinned memory (the
+  // product then follows it without a copy-engine hand-off) or by a runtime
+  // copy from pageable memory; device memory is read in place
+  const void *xd = x;
+  long ldxd = ldx;
+  const void *view = nullptr;
+  if (K > 0 && mem_kind(x, &view) != kMemDevice) {
+    const long rowb = (long)K * (long)xe;
+    {
+      std::lock_guard<std::mutex> lock(ctx->mu);
+      if ((rc = ensure_buf(ctx, &ctx->hx, &ctx->hx_cap, (size_t)M * rowb)) != TCB_OK) return rc;
+    }
+    if (view) {
+      const long units = (rowb % 16 == 0 ? rowb / 16 : rowb);
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)std::min<long>(32, std::max<long>(1, (units + 255) / 256)),
+                         (unsigned)std::min(M, 65535));
+      cfg.blockDim = dim3(256);
+      cfg.stream = s;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      at[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      TCB_CU(ctx, cudaLaunchKernelEx(&cfg, k_stage_rows, static_cast<const uint8_t *>(view), ldx * (long)xe,
+                                     static_cast<uint8_t *>(ctx->hx), rowb, M));
+    } else {
+      TCB_CU(ctx, cudaMemcpy2DAsync(ctx->hx, rowb, x, ldx * xe, rowb, M, cudaMemcpyHostToDevice, s));
+    }
+    xd = ctx->hx;
+    ldxd = K;
+  }
+  // c: written in place where the GPU reaches it (device or pinned memory),
+  // else through a device copy
+  const int ck = mem_kind(c, &view);
+  void *cd = ck == kMemPageable ? nullptr : const_cast<void *>(view);
+  long ldcd = ldc;
+  const long crow = (long)N * (long)ce;
+  if (ck == kMemPageable) {
+    {
+      std::lock_guard<std::mutex> lock(ctx->mu);
+      if ((rc = ensure_buf(ctx, &ctx->hc, &ctx->hc_cap, (size_t)M * crow)) != TCB_OK) return rc;
+    }
+    cd = ctx->hc;
+    ldcd = N;
+    if (accumulate) TCB_CU(ctx, cudaMemcpy2DAsync(cd, crow, c, ldc * ce, crow, M, cudaMemcpyHostToDevice, s));
+  }
+  rc = tcb_qgemm(ctx, wtype, M, N, K, w, xd, xdtype, ldxd, cd, cdtype, ldcd, accumulate, stream);
+  if (rc != TCB_OK) return rc;
+  if (ck == kMemPageable) TCB_CU(ctx, cudaMemcpy2DAsync(c, ldc * ce, cd, crow, crow, M, cudaMemcpyDeviceToHost, s));
   return TCB_OK;
 }
 

@@ -13,6 +13,10 @@ struct tcb_ctx {
   int *derr = nullptr;  // device error word (bounded waits that gave up)
   void *sk = nullptr;   // split-K scratch of the matvec kernels (zeroed; kernels leave it zeroed)
   size_t sk_cap = 0;
+  void *hx = nullptr;   // tcb_qgemm_host: x staged on the device
+  size_t hx_cap = 0;
+  void *hc = nullptr;   // tcb_qgemm_host: c of a caller whose c the GPU cannot reach
+  size_t hc_cap = 0;
   std::mutex mu;
   char err[256] = {0};
 };
