@@ -377,78 +377,69 @@ __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cos
 // ---- all-reduce of the residual over peer memory (tensor parallelism)
 //
 // Every rank's exchange buffer (cudaMalloc'd, mapped into the other ranks by
-// CUDA IPC) holds flags [2][tp][kArBlocks] and slots [2][tp][D].  Call e (a
+// CUDA IPC) holds slots [2][tp][D] of 8-byte words: the low half a value's
+// bits, the high half the number e of the call that wrote it.  Call e (a
 // per-rank counter that all ranks advance alike) uses parity e & 1.  Block b
-// of rank r stores its slice of r's partial into slot [par][r] of every rank
-// (peer stores over NVLink), raises flag [par][r][b] = e on every rank, waits
-// until its own buffer holds flag e from all ranks for block b, and adds the
-// ranks' slices in rank order to the residual: x += ((y_0 + y_1) + ...) --
-// the same operations on every rank, so the ranks keep identical residuals.
-// A slot parity is written again only two calls later, when every rank has
+// of rank r stores its slice of r's partial, each value paired with e in
+// one 8-byte store, into slot [par][r] of every rank (peer stores over
+// NVLink); it then polls the same slice of its own slots [par][r'] until
+// every word carries e, and adds the ranks' values in rank order to the
+// residual: x += ((y_0 + y_1) + ...) -- the same operations on every rank, so
+// the ranks keep identical residuals.  An aligned 8-byte store is seen whole
+// or not at all, so a word that carries e carries e's value: no fence or
+// flag sits between the data and the signal that it is there.  A slot
+// parity is written again only two calls later, when every rank has
 // finished the call in between and therefore read the old contents.  Waits
 // are bounded (about a second); a timeout records TCB_ERR_TIMEOUT.
 constexpr int kArBlocks = 16, kArThreads = 128, kMaxTp = 8;
 struct PeerBufs {
-  float *slot[kMaxTp];      // rank r's slots [2][tp][D] (this process's mapping)
-  unsigned *flag[kMaxTp];   // rank r's flags [2][tp][kArBlocks]
+  unsigned long long *slot[kMaxTp];  // rank r's slots [2][tp][D] (this process's mapping)
 };
 
-__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_words(unsigned long long *p, unsigned long long a, unsigned long long b) {
+  asm volatile("st.relaxed.sys.global.v2.b64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
 }
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+__device__ __forceinline__ void ld_words(const unsigned long long *p, unsigned long long &a, unsigned long long &b) {
+  asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 
-constexpr unsigned kArPolls = 1u << 22;  // flag polls before a wait gives up (about a second)
+constexpr unsigned kArPolls = 1u << 22;  // polls of a word pair before a wait gives up (about a second)
 __global__ void __launch_bounds__(kArThreads) k_peer_ar(const __grid_constant__ PeerBufs pb, const float *yp, float *x, int D, int tp,
                                                        int rank, unsigned *epoch, unsigned *done, int *err, unsigned polls) {
   mv::pdl_wait();
   mv::pdl_launch_dependents();
   const unsigned e = *reinterpret_cast<volatile unsigned *>(epoch) + 1u;
   const int par = (int)(e & 1u), b = blockIdx.x, nb = gridDim.x;
-  const int per = ((D + nb - 1) / nb + 3) & ~3;
+  const int per = ((D + nb - 1) / nb + 1) & ~1;
   const int i0 = b * per, i1 = min(D, i0 + per);
-  for (int r = 0; r < tp; r++) {
-    float *dst = pb.slot[r] + ((size_t)par * tp + rank) * D;
-    for (int i = i0 + 4 * threadIdx.x; i < i1; i += 4 * blockDim.x)
-      *reinterpret_cast<float4 *>(dst + i) = *reinterpret_cast<const float4 *>(yp + i);
+  const unsigned long long tag = (unsigned long long)e << 32;
+  for (int i = i0 + 2 * (int)threadIdx.x; i < i1; i += 2 * blockDim.x) {
+    const float2 v = *reinterpret_cast<const float2 *>(yp + i);
+    const unsigned long long a = tag | __float_as_uint(v.x), c = tag | __float_as_uint(v.y);
+    for (int r = 0; r < tp; r++) st_words(pb.slot[r] + ((size_t)par * tp + rank) * D + i, a, c);
   }
-  __threadfence_system();
-  __syncthreads();
-  if ((int)threadIdx.x < tp) st_release_sys(pb.flag[threadIdx.x] + ((size_t)par * tp + rank) * nb + b, e);
-  if ((int)threadIdx.x < tp) {
-    const unsigned *f = pb.flag[rank] + ((size_t)par * tp + threadIdx.x) * nb + b;
-    bool ok = false;
-    for (uint32_t it = 0; it < polls; it++) {
-      if (ld_acquire_sys(f) == e) {
-        ok = true;
-        break;
+  const unsigned long long *mine = pb.slot[rank] + (size_t)par * tp * D;
+  bool ok = true;
+  for (int i = i0 + 2 * (int)threadIdx.x; i < i1; i += 2 * blockDim.x) {
+    float s0 = 0.f, s1 = 0.f;
+    for (int r = 0; r < tp; r++) {
+      unsigned long long a = 0, c = 0;
+      for (uint32_t it = 0; ok; it++) {
+        ld_words(mine + (size_t)r * D + i, a, c);
+        if ((unsigned)(a >> 32) == e && (unsigned)(c >> 32) == e) break;
+        if (it + 1 >= polls) ok = false;  // gave up: no further waits in this call
+        else __nanosleep(32);
       }
-      __nanosleep(32);
+      const float va = __uint_as_float((unsigned)a), vc = __uint_as_float((unsigned)c);
+      s0 = r == 0 ? va : __fadd_rn(s0, va);
+      s1 = r == 0 ? vc : __fadd_rn(s1, vc);
     }
-    if (!ok) atomicExch(err, TCB_ERR_TIMEOUT);
+    float2 xv = *reinterpret_cast<float2 *>(x + i);
+    xv.x = __fadd_rn(xv.x, s0);
+    xv.y = __fadd_rn(xv.y, s1);
+    *reinterpret_cast<float2 *>(x + i) = xv;
   }
-  __syncthreads();
-  const float *mine = pb.slot[rank] + (size_t)par * tp * D;
-  for (int i = i0 + 4 * threadIdx.x; i < i1; i += 4 * blockDim.x) {
-    float4 acc = __ldcg(reinterpret_cast<const float4 *>(mine + i));
-    for (int r = 1; r < tp; r++) {
-      const float4 v = __ldcg(reinterpret_cast<const float4 *>(mine + (size_t)r * D + i));
-      acc.x = __fadd_rn(acc.x, v.x);
-      acc.y = __fadd_rn(acc.y, v.y);
-      acc.z = __fadd_rn(acc.z, v.z);
-      acc.w = __fadd_rn(acc.w, v.w);
-    }
-    float4 xv = *reinterpret_cast<float4 *>(x + i);
-    xv.x = __fadd_rn(xv.x, acc.x);
-    xv.y = __fadd_rn(xv.y, acc.y);
-    xv.z = __fadd_rn(xv.z, acc.z);
-    xv.w = __fadd_rn(xv.w, acc.w);
-    *reinterpret_cast<float4 *>(x + i) = xv;
-  }
+  if (!ok) atomicExch(err, TCB_ERR_TIMEOUT);
   // the last block to finish advances the counter (every block has read it)
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -1796,8 +1787,7 @@ int tcb_llama_peer_handle(tcb_llama *m, unsigned char *handle64) {
   if (m->tp > tcb::ll::kMaxTp || m->cfg.d_model % 4) return TCB_ERR_UNSUPPORTED;
   cudaError_t e = cudaSetDevice(m->ctx->dev);
   if (e == cudaSuccess && !m->xbuf) {
-    const size_t flags = ((size_t)2 * m->tp * tcb::ll::kArBlocks * 4 + 255) & ~(size_t)255;
-    m->xbuf_bytes = flags + (size_t)2 * m->tp * m->cfg.d_model * 4;
+    m->xbuf_bytes = (size_t)2 * m->tp * m->cfg.d_model * 8;
     if ((e = alloc(m, &m->xbuf, m->xbuf_bytes)) == cudaSuccess && (e = cudaMemset(m->xbuf, 0, m->xbuf_bytes)) == cudaSuccess &&
         (e = alloc(m, &m->yp, (size_t)m->cfg.d_model)) == cudaSuccess && (e = alloc(m, &m->ar_epoch, 2)) == cudaSuccess)
       e = cudaMemset(m->ar_epoch, 0, 2 * sizeof(unsigned));
@@ -1819,7 +1809,6 @@ int tcb_llama_peer_init(tcb_llama *m, const unsigned char *handles) {
   }
   if (m->peer) return TCB_OK;
   cudaError_t e = cudaSetDevice(m->ctx->dev);
-  const size_t flags = ((size_t)2 * m->tp * tcb::ll::kArBlocks * 4 + 255) & ~(size_t)255;
   for (int r = 0; r < m->tp && e == cudaSuccess; r++) {
     char *base = m->xbuf;
     if (r != m->tr) {
@@ -1830,8 +1819,7 @@ int tcb_llama_peer_init(tcb_llama *m, const unsigned char *handles) {
       m->opened.push_back(p);
       base = static_cast<char *>(p);
     }
-    m->pb.flag[r] = reinterpret_cast<unsigned *>(base);
-    m->pb.slot[r] = reinterpret_cast<float *>(base + flags);
+    m->pb.slot[r] = reinterpret_cast<unsigned long long *>(base);
   }
   if (e != cudaSuccess) {
     for (void *p : m->opened) cudaIpcCloseMemHandle(p);
@@ -1855,9 +1843,8 @@ int tcb_peer_ar_selftest(tcb_ctx *ctx, int tp, int rank, int d_model, unsigned p
   if (e != cudaSuccess) return cuda_fail(e);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // every rank's exchange buffer local to this device; nothing but this
-  // call writes them, so the other ranks' flags never arrive
-  const size_t flags = ((size_t)2 * tp * kArBlocks * 4 + 255) & ~(size_t)255;
-  const size_t bytes = flags + (size_t)2 * tp * d_model * 4;
+  // call writes them, so the other ranks' values never arrive
+  const size_t bytes = (size_t)2 * tp * d_model * 8;
   char *buf = nullptr;
   float *vec = nullptr;
   unsigned *cnt = nullptr;
@@ -1866,10 +1853,7 @@ int tcb_peer_ar_selftest(tcb_ctx *ctx, int tp, int rank, int d_model, unsigned p
       (e = cudaMalloc(&cnt, 2 * sizeof(unsigned))) == cudaSuccess && (e = cudaMemsetAsync(buf, 0, bytes * tp, s)) == cudaSuccess &&
       (e = cudaMemsetAsync(vec, 0, (size_t)2 * d_model * 4, s)) == cudaSuccess &&
       (e = cudaMemsetAsync(cnt, 0, 2 * sizeof(unsigned), s)) == cudaSuccess) {
-    for (int r = 0; r < tp; r++) {
-      pb.flag[r] = reinterpret_cast<unsigned *>(buf + bytes * r);
-      pb.slot[r] = reinterpret_cast<float *>(buf + bytes * r + flags);
-    }
+    for (int r = 0; r < tp; r++) pb.slot[r] = reinterpret_cast<unsigned long long *>(buf + bytes * r);
     e = launch(k_peer_ar, dim3(kArBlocks), dim3(kArThreads), s, pb, (const float *)vec, vec + d_model, d_model, tp, rank,
                cnt, cnt + 1, ctx->derr, polls);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
