@@ -266,10 +266,10 @@ int tcb_llama_peer_init(tcb_llama *m, const unsigned char *handles);
 
 /* Self-test of the peer all-reduce's bounded wait, on one device: runs the
  * all-reduce kernel once as rank `rank` of `tp` with every rank's exchange
- * buffer allocated locally, so for tp > 1 the other ranks' flags never
- * arrive and each wait gives up after `polls` polls, leaving
+ * buffer allocated locally, so for tp > 1 the other ranks' values never
+ * arrive and the wait gives up after `polls` polls, leaving
  * TCB_ERR_TIMEOUT in the device error word (tcb_device_error); with tp = 1
- * the rank's own flag completes the wait.  Synchronises the stream; the
+ * the rank's own values complete the wait.  Synchronises the stream; the
  * context stays usable.  No counterpart in TR. */
 int tcb_peer_ar_selftest(tcb_ctx *ctx, int tp, int rank, int d_model, unsigned polls, void *stream);
 

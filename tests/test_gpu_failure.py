@@ -3,10 +3,11 @@ runs out records TCB_ERR_TIMEOUT in the context's device error word, the
 kernel returns, and the context stays usable.
 
 The peer all-reduce of the tensor-parallel decoder (k_peer_ar) waits for
-every other rank's flag.  tcb_peer_ar_selftest runs it as rank 0 of 2 with
-both exchange buffers on this device, so rank 1's flag never arrives (a
-flag that nothing sets) and the wait gives up after a short poll limit;
-with one rank its own flag completes the wait.  A rank that leaves a real
+every other rank's values (each word carrying the call number).
+tcb_peer_ar_selftest runs it as rank r of tp with every exchange buffer on
+this device, so the other ranks' values never arrive (words that nothing
+writes) and the wait gives up after a short poll limit; with one rank its
+own values complete the wait.  A rank that leaves a real
 tensor-parallel run is detected the same way on the remaining ranks.
 """
 import time
@@ -28,7 +29,7 @@ def ctx():
     return T.Context(0)
 
 
-def test_peer_wait_completes_with_its_flag(ctx):
+def test_peer_wait_completes_with_its_own_values(ctx):
     ctx.device_error(clear=True)
     ctx.peer_ar_selftest(1, 0, 4096, 1 << 15)
     assert ctx.device_error() == 0
