@@ -481,7 +481,7 @@ def decode_batch_bench(ctx, model, rank: int, world: int, peak_gbs: float, strea
     cfg = cfg or llama.LLAMA3_70B
     engines = [llama.Llama(ctx, model, tp=(world, rank)) for _ in range(B)]
     if world > 1:
-        engines[0].tp_init(llama.share_id(llama.nccl_unique_id, rank), peer=False)
+        engines[0].tp_init(llama.share_id(llama.nccl_unique_id, rank))
     rng = np.random.default_rng(19)
     prompts = [rng.integers(0, cfg.vocab, 1024) for _ in range(B)]
     for e, p in zip(engines, prompts):
@@ -504,12 +504,15 @@ def decode_batch_bench(ctx, model, rank: int, world: int, peak_gbs: float, strea
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, pms = float(t[0].item()), float(t[1].item())
     toks = [e.tokens(1152, stream) for e in engines]
+    # the engine sums the residual rows over peer memory up to 16 sequences
+    allreduce = ("none (one GPU)" if world == 1 else
+                 "peer memory (NVLink)" if getattr(engines[0], "peer_active", False) and B <= 16 else "nccl")
     batch.close()
     for e in engines:
         e.close()
     bpt = llama.weight_bytes_per_token(cfg)
     per_gpu_step = bpt / world
-    return {"batch": B, "prompt_tokens": 1024, "generated_tokens": 128,
+    return {"batch": B, "prompt_tokens": 1024, "generated_tokens": 128, "allreduce": allreduce,
             "tokens_per_s": round(B * 128 / (ms / 1e3), 2), "ms_per_step": round(ms / 128, 4),
             "prompt_pass_ms": round(pms, 2),
             "roofline": {"bound": "hbm", "achieved_per_gpu": round(per_gpu_step / (ms / 1e3 / 128) / 1e9, 2),

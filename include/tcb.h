@@ -260,7 +260,9 @@ int tcb_llama_tp_init(tcb_llama *m, const unsigned char *id128);
  * exports a 64-byte CUDA IPC handle of it, the caller gathers all ranks'
  * handles in rank order (tp_size * 64 bytes) and passes them to
  * tcb_llama_peer_init, before the first step or capture.  Without it the
- * step uses NCCL.  The greedy pick's all-gather stays on NCCL. */
+ * step uses NCCL.  A batch (tcb_llama_batch_create) of up to 16 engines led
+ * by this one, created after the set-up, sums its residual rows the same
+ * way.  The greedy pick's all-gather stays on NCCL. */
 int tcb_llama_peer_handle(tcb_llama *m, unsigned char *handle64);
 int tcb_llama_peer_init(tcb_llama *m, const unsigned char *handles);
 

@@ -377,7 +377,9 @@ __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cos
 // ---- all-reduce of the residual over peer memory (tensor parallelism)
 //
 // Every rank's exchange buffer (cudaMalloc'd, mapped into the other ranks by
-// CUDA IPC) holds slots [2][tp][D] of 8-byte words: the low half a value's
+// CUDA IPC) holds slots [2][tp][stride] of 8-byte words, of which a call uses
+// the first D of each (stride is fixed per buffer, so a call of D values
+// never reaches into the other parity, whatever D the calls around it had): the low half a value's
 // bits, the high half the number e of the call that wrote it.  Call e (a
 // per-rank counter that all ranks advance alike) uses parity e & 1.  Block b
 // of rank r stores its slice of r's partial, each value paired with e in
@@ -392,8 +394,9 @@ __global__ void __launch_bounds__(256) k_attn(const float *qkv, const float *cos
 // finished the call in between and therefore read the old contents.  Waits
 // are bounded (about a second); a timeout records TCB_ERR_TIMEOUT.
 constexpr int kArBlocks = 16, kArThreads = 128, kMaxTp = 8;
+constexpr int kPeerRows = 16;  // rows of d_model values a slot holds (a batched step of up to 16 sequences)
 struct PeerBufs {
-  unsigned long long *slot[kMaxTp];  // rank r's slots [2][tp][D] (this process's mapping)
+  unsigned long long *slot[kMaxTp];  // rank r's slots [2][tp][stride] (this process's mapping)
 };
 
 __device__ __forceinline__ void st_words(unsigned long long *p, unsigned long long a, unsigned long long b) {
@@ -404,8 +407,9 @@ __device__ __forceinline__ void ld_words(const unsigned long long *p, unsigned l
 }
 
 constexpr unsigned kArPolls = 1u << 22;  // polls of a word pair before a wait gives up (about a second)
-__global__ void __launch_bounds__(kArThreads) k_peer_ar(const __grid_constant__ PeerBufs pb, const float *yp, float *x, int D, int tp,
-                                                       int rank, unsigned *epoch, unsigned *done, int *err, unsigned polls) {
+__global__ void __launch_bounds__(kArThreads) k_peer_ar(const __grid_constant__ PeerBufs pb, const float *yp, float *x, int D, long stride,
+                                                       int tp, int rank, unsigned *epoch, unsigned *done, int *err,
+                                                       unsigned polls) {
   mv::pdl_wait();
   mv::pdl_launch_dependents();
   const unsigned e = *reinterpret_cast<volatile unsigned *>(epoch) + 1u;
@@ -416,16 +420,16 @@ __global__ void __launch_bounds__(kArThreads) k_peer_ar(const __grid_constant__ 
   for (int i = i0 + 2 * (int)threadIdx.x; i < i1; i += 2 * blockDim.x) {
     const float2 v = *reinterpret_cast<const float2 *>(yp + i);
     const unsigned long long a = tag | __float_as_uint(v.x), c = tag | __float_as_uint(v.y);
-    for (int r = 0; r < tp; r++) st_words(pb.slot[r] + ((size_t)par * tp + rank) * D + i, a, c);
+    for (int r = 0; r < tp; r++) st_words(pb.slot[r] + ((size_t)par * tp + rank) * stride + i, a, c);
   }
-  const unsigned long long *mine = pb.slot[rank] + (size_t)par * tp * D;
+  const unsigned long long *mine = pb.slot[rank] + (size_t)par * tp * stride;
   bool ok = true;
   for (int i = i0 + 2 * (int)threadIdx.x; i < i1; i += 2 * blockDim.x) {
     float s0 = 0.f, s1 = 0.f;
     for (int r = 0; r < tp; r++) {
       unsigned long long a = 0, c = 0;
       for (uint32_t it = 0; ok; it++) {
-        ld_words(mine + (size_t)r * D + i, a, c);
+        ld_words(mine + (size_t)r * stride + i, a, c);
         if ((unsigned)(a >> 32) == e && (unsigned)(c >> 32) == e) break;
         if (it + 1 >= polls) ok = false;  // gave up: no further waits in this call
         else __nanosleep(32);
@@ -778,7 +782,7 @@ struct tcb_llama {
   void *sk = nullptr;    // split-K scratch shared by the step's matvecs (they run one after another)
   int nccl_rc = 0;       // last NCCL error
   // peer-memory all-reduce (tcb_llama_peer_init); NCCL's when not set up
-  char *xbuf = nullptr;              // this rank's exchange buffer (flags, then slots)
+  char *xbuf = nullptr;              // this rank's exchange buffer (slots of the peer all-reduce)
   size_t xbuf_bytes = 0;
   tcb::ll::PeerBufs pb{};
   std::vector<void *> opened;        // peers' buffers opened through CUDA IPC
@@ -855,7 +859,8 @@ cudaError_t all_reduce_x(tcb_llama *m, cudaStream_t s) {
   if (m->tp == 1) return cudaSuccess;
   if (m->peer)
     return tcb::ll::launch(tcb::ll::k_peer_ar, dim3(tcb::ll::kArBlocks), dim3(tcb::ll::kArThreads), s, m->pb,
-                           (const float *)m->yp, m->x, m->cfg.d_model, m->tp, m->tr, m->ar_epoch, m->ar_done,
+                           (const float *)m->yp, m->x, m->cfg.d_model, (long)tcb::ll::kPeerRows * m->cfg.d_model,
+                           m->tp, m->tr, m->ar_epoch, m->ar_done,
                            m->ctx->derr, tcb::ll::kArPolls);
   const Nccl *nc = nccl();
   if (!nc || !m->comm) return cudaErrorNotReady;
@@ -1423,6 +1428,7 @@ struct tcb_llama_batch {
   BatchMat head;
   void *ws = nullptr, *sk = nullptr;
   float *x = nullptr, *h = nullptr, *qkv = nullptr, *att = nullptr, *gu = nullptr, *a = nullptr, *logits = nullptr;
+  float *yp = nullptr;  // tensor parallelism over peer memory: this rank's o / down partial rows
   float *part = nullptr, *am_v = nullptr;
   int *am_i = nullptr;
   unsigned *count = nullptr;
@@ -1543,9 +1549,21 @@ int issue_batch_step(tcb_llama_batch *bt, cudaStream_t s) {
   const size_t cache_layer = (size_t)KVH * c.max_ctx * hd;
   // NCCL: rank 0 adds its o/down partial to the residual rows, the others
   // write theirs, and the in-place all-reduce of B rows sums them
-  const int acc = m0->tr == 0;
+  // NCCL: rank 0 adds its partial to the residual rows, the others write
+  // theirs, and the in-place all-reduce sums them.  Peer memory (up to
+  // kPeerRows sequences): every rank writes its partial rows to yp and the
+  // peer all-reduce adds the ranks' partials to the residual rows.
+  const bool peer = bt->yp != nullptr;
+  const int acc = peer ? 0 : m0->tr == 0;
+  float *dst = peer ? bt->yp : bt->x;
   auto reduce = [&]() -> int {
     if (m0->tp == 1) return TCB_OK;
+    if (peer) {
+      const int nb = kArBlocks * B < 4 * m0->ctx->sms ? kArBlocks * B : 4 * m0->ctx->sms;
+      cudaError_t le = launch(k_peer_ar, dim3(nb), dim3(kArThreads), s, m0->pb, (const float *)bt->yp, bt->x, B * D,
+                              (long)kPeerRows * D, m0->tp, m0->tr, m0->ar_epoch, m0->ar_done, m0->ctx->derr, kArPolls);
+      return le == cudaSuccess ? TCB_OK : fail(m0, le);
+    }
     m0->nccl_rc = nccl()->all_reduce(bt->x, bt->x, (size_t)B * D, kNcclFloat32, kNcclSum, m0->comm, s);
     return m0->nccl_rc ? fail(m0, cudaErrorUnknown) : TCB_OK;
   };
@@ -1579,13 +1597,13 @@ int issue_batch_step(tcb_llama_batch *bt, cudaStream_t s) {
     default: e = cudaErrorInvalidValue;
     }
     if (e != cudaSuccess) return fail(m0, e);
-    if ((rc = rows_product(bt, m0->o[l], bt->o[l], bt->att, bt->x, acc, s)) != TCB_OK || (rc = reduce()) != TCB_OK)
+    if ((rc = rows_product(bt, m0->o[l], bt->o[l], bt->att, dst, acc, s)) != TCB_OK || (rc = reduce()) != TCB_OK)
       break;
     k_rmsnorm<<<B, 1024, 0, s>>>(bt->x, m0->ffn_norm[l], bt->h, D, c.eps);
     if ((rc = rows_product(bt, m0->gu[l], bt->gu_[l], bt->h, bt->gu, 0, s)) != TCB_OK) break;
     const long na = (long)B * F;
     k_swiglu_rows<<<(int)((na + 255) / 256 < 4096 ? (na + 255) / 256 : 4096), 256, 0, s>>>(bt->gu, bt->a, F, na);
-    if ((rc = rows_product(bt, m0->down[l], bt->down[l], bt->a, bt->x, acc, s)) != TCB_OK ||
+    if ((rc = rows_product(bt, m0->down[l], bt->down[l], bt->a, dst, acc, s)) != TCB_OK ||
         (rc = reduce()) != TCB_OK)
       break;
   }
@@ -1672,7 +1690,9 @@ int tcb_llama_batch_create(tcb_llama *const *ms, int count, tcb_llama_batch **ou
       (e = balloc(bt, &bt->cand, (size_t)B * m0->tp)) != cudaSuccess ||
       (e = cudaMemset(bt->count, 0, (size_t)B * H * sizeof(unsigned))) != cudaSuccess ||
       (e = cudaMemcpy(bt->seq, hs.data(), B * sizeof(tcb::ll::BatchSeq), cudaMemcpyHostToDevice)) != cudaSuccess ||
-      (e = cudaMemcpy(bt->pick, hp.data(), B * sizeof(tcb::ll::BatchPick), cudaMemcpyHostToDevice)) != cudaSuccess) {
+      (e = cudaMemcpy(bt->pick, hp.data(), B * sizeof(tcb::ll::BatchPick), cudaMemcpyHostToDevice)) != cudaSuccess ||
+      // the residual rows' sums over peer memory when every row fits a slot
+      (m0->peer && B <= tcb::ll::kPeerRows && (e = balloc(bt, &bt->yp, (size_t)B * D)) != cudaSuccess)) {
     tcb_llama_batch_destroy(bt);
     return e == cudaErrorMemoryAllocation ? TCB_ERR_NOMEM : fail(m0, e);
   }
@@ -1787,7 +1807,7 @@ int tcb_llama_peer_handle(tcb_llama *m, unsigned char *handle64) {
   if (m->tp > tcb::ll::kMaxTp || m->cfg.d_model % 4) return TCB_ERR_UNSUPPORTED;
   cudaError_t e = cudaSetDevice(m->ctx->dev);
   if (e == cudaSuccess && !m->xbuf) {
-    m->xbuf_bytes = (size_t)2 * m->tp * m->cfg.d_model * 8;
+    m->xbuf_bytes = (size_t)2 * m->tp * tcb::ll::kPeerRows * m->cfg.d_model * 8;
     if ((e = alloc(m, &m->xbuf, m->xbuf_bytes)) == cudaSuccess && (e = cudaMemset(m->xbuf, 0, m->xbuf_bytes)) == cudaSuccess &&
         (e = alloc(m, &m->yp, (size_t)m->cfg.d_model)) == cudaSuccess && (e = alloc(m, &m->ar_epoch, 2)) == cudaSuccess)
       e = cudaMemset(m->ar_epoch, 0, 2 * sizeof(unsigned));
@@ -1854,7 +1874,8 @@ int tcb_peer_ar_selftest(tcb_ctx *ctx, int tp, int rank, int d_model, unsigned p
       (e = cudaMemsetAsync(vec, 0, (size_t)2 * d_model * 4, s)) == cudaSuccess &&
       (e = cudaMemsetAsync(cnt, 0, 2 * sizeof(unsigned), s)) == cudaSuccess) {
     for (int r = 0; r < tp; r++) pb.slot[r] = reinterpret_cast<unsigned long long *>(buf + bytes * r);
-    e = launch(k_peer_ar, dim3(kArBlocks), dim3(kArThreads), s, pb, (const float *)vec, vec + d_model, d_model, tp, rank,
+    e = launch(k_peer_ar, dim3(kArBlocks), dim3(kArThreads), s, pb, (const float *)vec, vec + d_model, d_model,
+               (long)d_model, tp, rank,
                cnt, cnt + 1, ctx->derr, polls);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   }

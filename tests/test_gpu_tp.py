@@ -83,14 +83,17 @@ def test_tp2_matches_reference(oracle, tmp_path, mode):
 
 
 @pytest.mark.skipif(NGPU < 2, reason="needs 2 GPUs")
-def test_tp2_batch_matches_reference(oracle, tmp_path):
-    """tcb_llama_batch over 2 ranks: every sequence's history against the CPU
-    reference fed it (logits at every step, every greedy token)"""
+@pytest.mark.parametrize("mode", ["batch", "batch_peer"])
+def test_tp2_batch_matches_reference(oracle, tmp_path, mode):
+    """tcb_llama_batch over 2 ranks, the residual rows summed by NCCL or by
+    the peer all-reduce: every sequence's history against the CPU reference
+    fed it (logits at every step, every greedy token)"""
     from tcb_b200 import llama
 
     import tp_worker
 
-    d = run_worker(tmp_path, 2, "batch")
+    d = run_worker(tmp_path, 2, mode)
+    assert bool(d["peer"]) == (mode == "batch_peer")
     host = llama.host_model(tp_worker.CFG, seed=tp_worker.SEED, varied=True)
     for i, p in enumerate(tp_worker.BATCH_PROMPTS):
         toks = d["eager"][i]

@@ -58,11 +58,13 @@ BATCH_PROMPTS = [np.random.default_rng(41).integers(0, CFG.vocab, n).astype(np.i
 BATCH_STEPS = 36
 
 
-def batch_main(ctx, rank, world, out_path):
+def batch_main(ctx, rank, world, out_path, peer):
     host = llama.host_model(CFG, seed=SEED, varied=True)
     dev = llama.device_model(CFG, SEED, host, tp=(world, rank))
     engines = [llama.Llama(ctx, dev, tp=(world, rank)) for _ in BATCH_PROMPTS]
-    engines[0].tp_init(llama.share_id(llama.nccl_unique_id, rank), peer=False)
+    # the residual rows summed by NCCL, or by the peer all-reduce (five
+    # sequences fit its slots)
+    engines[0].tp_init(llama.share_id(llama.nccl_unique_id, rank), peer=peer)
     runs = {}
     for mode in ("eager", "graph"):
         for e, p in zip(engines, BATCH_PROMPTS):
@@ -88,7 +90,8 @@ def batch_main(ctx, rank, world, out_path):
     dist.all_gather_object(err, ctx.device_error())
     if rank == 0:
         np.savez(out_path, eager=np.stack(runs["eager"][0]), graph=np.stack(runs["graph"][0]),
-                 logits=runs["eager"][1], same_on_ranks=all(t == all_tok[0] for t in all_tok), peer=False,
+                 logits=runs["eager"][1], same_on_ranks=all(t == all_tok[0] for t in all_tok),
+                 peer=bool(getattr(engines[0], "peer_active", False)),
                  device_errors=np.array(err, np.int64), first=0)
     for e in engines:
         e.close()
@@ -103,8 +106,8 @@ def main():
     dist.init_process_group("gloo")
     out_path, mode = sys.argv[1], sys.argv[2]
     ctx = T.Context(local)
-    if mode == "batch":
-        return batch_main(ctx, rank, world, out_path)
+    if mode in ("batch", "batch_peer"):
+        return batch_main(ctx, rank, world, out_path, peer=mode == "batch_peer")
     if mode == "shape70":
         cfg = CFG70
         dev = llama.device_model(cfg, SEED70, tp=(world, rank), varied=True)
