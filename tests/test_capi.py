@@ -33,6 +33,7 @@ def test_null_context_is_refused():
     assert L.tcb_qgemm_act8(None, T.Q4_K, 1, 1, 256, None, None, 0, 256, None, 0, 1, 1, None) == 1
     assert L.tcb_qdequant(None, T.Q4_K, None, 256, None, 0, None) == 1
     assert L.tcb_llama_set_prefill_rows(None, 80) == 1
+    assert L.tcb_qgemm_host(None, T.Q4_K, 1, 1, 256, None, None, 0, 256, None, 0, 1, 1, None) == 1
 
 
 @pytest.mark.parametrize("w", [T.Q8_0, T.Q4_0, T.Q4_K, T.Q6_K])
